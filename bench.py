@@ -1,0 +1,463 @@
+#!/usr/bin/env python
+"""Benchmark of the connectome hop path on B200: one JSON line (rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload infer|infer32|train] [--impl ours|reference]
+  (N > 1: python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N)
+
+Workloads (the reference's BASELINE configs, synthetic inputs: the seeded 2,992,734-edge 3-hop graph of
+flyguy_b200.synth, obs ~ N(0,1), teacher logits ~ N(0,2^2)):
+  infer    (default) config 2 - rollout inference, bf16 states / fp32 accumulation / fp32 weights, global batch 65,536
+           sharded over the N GPUs with no collective; metric decisions/sec
+  infer32  config 1 - fp32 forward, batch 4,096 per GPU; metric decisions/sec
+  train    config 3 - distillation step (forward, fused KL loss, backward, Adam lr 3e-4), global batch 16,384 data-parallel
+           with one NCCL all-reduce (average) of the flat fp32 gradient per step; metric train samples/sec
+
+A step is one pass of the hop path over the rank's batch with its inputs resident in HBM; the L2 is flushed (a 256 MiB
+write) between timed steps, outside the timed events. `value` = all ranks' units / the max over ranks of the summed
+per-step device time. `e2e` = the same metric through the library's host-buffer entry points (fg_forward_host; for
+train: pinned H2D of obs + teacher, fg_teach, all-reduce, fc_step, D2H of the loss), host copies inside the timed
+region. `roofline` = the dominant kernel class's algorithmic bytes / its CUDA-event time over the timed region.
+`--impl reference` times the reference's own CPU implementation (flyguy/native/fly_infer.cpp built from source into
+oracle/_ref; for training, which the reference does in torch on the CPU, the oracle's C port) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+WORKLOADS = {
+    "infer": dict(cfg=2, batch=65536, per_gpu=False, flags="bf16", metric="decisions/sec", unit="decisions/s",
+                  dtype="bf16", desc="config 2: bf16-state forward (fp32 accumulation, fp32 weights), global batch "
+                                     "65,536 batch-sharded, no collective"),
+    "infer32": dict(cfg=1, batch=4096, per_gpu=True, flags="fp32", metric="decisions/sec", unit="decisions/s",
+                    dtype="f32", desc="config 1: fp32 forward, batch 4,096 per GPU"),
+    "train": dict(cfg=3, batch=16384, per_gpu=False, flags="train", metric="train samples/sec", unit="samples/s",
+                  dtype="f32", desc="config 3: distillation step (forward, KL loss, backward, Adam) fp32, global "
+                                    "batch 16,384 data-parallel, one NCCL all-reduce of the flat gradient per step"),
+}
+LR = 3e-4
+FALLBACK_HBM_GBS = 6650.0
+
+
+def args_():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="infer")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="wall time budget of the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+    a.warmup = max(3, a.warmup)
+    return a
+
+
+# ------------------------------------------------------------------ helpers
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, burst copy)"
+    return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.path = index, None, None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL,
+                                         stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or not f[0].isdigit() or int(f[0]) != self.index:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), float(f[3]), f[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower().startswith("active")})
+        load = [r for r in rows if r[2] > 300.0] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in load), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows), "samples_under_load": len(load),
+                "power_w_max": max(r[2] for r in rows), "gpu_index": self.index}
+
+
+def algo_bytes(cls: str, s, B: int, act: int) -> float:
+    """Algorithmic HBM bytes of one step's launches of a kernel class: every layer read / written once, edge arrays
+    (int32 source + fp32 weight) and row pointers once."""
+    n, K = s["sizes"], s["hops"]
+    E = s.edges()
+    rows = sum(n[1:])
+    if cls == "hop_fwd":
+        return act * B * sum(n[k] + n[k + 1] for k in range(K)) + 8 * E + 4 * rows
+    if cls == "hop_bwd_t":                       # read gz of layer k, write gh of layer k-1
+        return 4 * B * sum(n[k] + n[k + 1] for k in range(K)) + 8 * E + 4 * sum(n[:K])
+    if cls == "sddmm":                           # read gz of layer k and the states of layer k-1, write the grads
+        return 4 * B * sum(n[k] + n[k + 1] for k in range(K)) + 12 * E
+    if cls == "act_bwd":                         # read gh and h, write gz
+        return 3 * 4 * B * rows
+    if cls == "plug_fwd":
+        return (s["obs_dim"] * 4 + n[0] * act) * B
+    if cls == "out_fwd":
+        return (n[K] * act + s["n_act"] * 4) * B
+    return 0.0
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(a, W, rank, world, dev, torch, dist):
+    from flyguy_b200 import native, synth
+    s, P = synth.make_synthetic()
+    Bg = W["batch"] * (world if W["per_gpu"] else 1)
+    B = Bg // world
+    assert B % 32 == 0 and B * world == Bg, "the batch must split into multiples of 32"
+    flags = {"bf16": native.FG_ACT_BF16, "fp32": native.FG_INFER_ONLY, "train": 0}[W["flags"]]
+    h = native.Handle(s, B, flags, device=dev)
+    h.set_params(P, 0)
+    h.set_params(P, 1)
+    obs_np, teacher_np = synth.make_batch(B, seed=1000 + rank)
+    obs = torch.from_numpy(obs_np).to(dev)
+    teacher = torch.from_numpy(teacher_np).to(dev)
+    logits = torch.empty(B, s["n_act"], device=dev)
+    flush = torch.empty(64 * 2 ** 20, dtype=torch.float32, device=dev)      # 256 MiB > 126 MB L2
+    train = W["flags"] == "train"
+    grad = h.flat(4) if train else None
+
+    def step():
+        if train:
+            h.zero_grad()
+            h.teach(obs, teacher, 1.0, logits=None, stats=False)
+            if world > 1:
+                dist.all_reduce(grad, op=dist.ReduceOp.AVG)
+            h.step(LR, 0.3 * LR, LR, 0.0, 0.999)
+        else:
+            h.forward(obs, 0, out=logits)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    # ---- timed region (device time, per-step CUDA events; L2 flushed between steps outside the events)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    h.timing(True)
+    launches0 = h.launches()
+    with Clocks(int(os.environ.get("LOCAL_RANK", dev.index or 0))) as clk:
+        barrier()
+        torch.cuda.synchronize(dev)
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record()
+            step()
+            e1.record()
+        torch.cuda.synchronize(dev)
+        barrier()
+    launches = h.launches() - launches0
+    kern = h.timing_read()
+    h.timing(False)
+    t_dev = sum(e0.elapsed_time(e1) for e0, e1 in evs) / 1e3
+    t_max = max_over_ranks(t_dev)
+    value = Bg * a.steps / t_max
+    clocks = clk.summary()
+    # ---- roofline of the dominant kernel class
+    kern_step = {k: (ms / a.steps, n // a.steps) for k, (ms, n) in kern.items() if n}
+    dom = max(kern_step, key=lambda k: kern_step[k][0])
+    act = 2 if W["flags"] == "bf16" else 4
+    byts = algo_bytes(dom, s, B, act)
+    peak, peak_src = peaks()
+    achieved = byts / (kern_step[dom][0] / 1e3) / 1e9 if byts else None
+    roof = {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1) if achieved else None, "peak": peak,
+            "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None, "traffic": traffic_of(dom, W),
+            "algorithmic_bytes_per_step": byts, "launches_per_step": kern_step[dom][1],
+            "ms_per_step": round(kern_step[dom][0], 4), "peak_source": peak_src}
+    # whole-step view: the path's algorithmic bytes per unit (SURVEY formula) x rate
+    N_rows, E = sum(s["sizes"]), s.edges()
+    if train:
+        per_unit = 5 * 4 * N_rows + s["obs_dim"] * 4 + s["n_act"] * 4 + (28 * E + 28 * sum(h.sizes)) / B
+    else:
+        per_unit = 2 * act * N_rows + s["obs_dim"] * 4 + s["n_act"] * 4 + (8 * E + 4 * sum(s["sizes"][1:])) / B
+    step_roof = {"bytes_per_unit": round(per_unit, 1), "achieved_gbs_per_gpu": round(per_unit * value / world / 1e9, 1),
+                 "frac": round(per_unit * value / world / 1e9 / peak, 4)}
+    # ---- e2e through the host-buffer entry points
+    e2e = run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier, max_over_ranks, grad)
+    # ---- CPU baseline (rank 0, N = 1)
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_baseline(W, s, P, a.cpu_seconds)
+    out = {"metric": W["metric"], "value": round(value, 1), "unit": W["unit"], "n_gpus": world, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": round(t_max / a.steps * 1e3, 4), "higher_is_better": True,
+           "scaling": "weak" if W["per_gpu"] else "strong", "vs_baseline": None, "dtype": W["dtype"],
+           "data": "synthetic: seeded 3-hop graph (16,894/46,393/37,748/1,332 neurons, 2,992,734 edges, lognormal "
+                   "in-degree mean 35, Zipf(1.5) sources), obs ~ N(0,1), teacher ~ N(0,4)",
+           "config": {"workload": W["desc"], "baseline_config": W["cfg"], "global_batch": Bg, "per_gpu_batch": B,
+                      "parallelism": (f"dp{world}" if train else f"batch-sharded x{world}, no collective"),
+                      "l2": "flushed between timed steps (256 MiB write, outside the step events)",
+                      "graph": "synthetic flyguy-sized 3-hop", "edges": E},
+           "roofline": roof, "step_roofline": step_roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+           "gpu_launches": int(launches),
+           "kernels_ms_per_step": {k: round(v[0], 4) for k, v in kern_step.items()}}
+    return out
+
+
+def traffic_of(cls: str, W) -> float | None:
+    """Per-step DRAM bytes of the kernel class from the committed ncu summary (profiles/traffic.json), if any."""
+    p = REPO / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    v = d.get(W["flags"], {}).get(cls)
+    return float(v) if v is not None else None
+
+
+def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier, max_over_ranks, grad):
+    train = W["flags"] == "train"
+    obs_h = torch.from_numpy(obs_np).pin_memory()
+    out_h = torch.empty(B, s["n_act"]).pin_memory()
+    if train:
+        teach_h = torch.from_numpy(teacher_np).pin_memory()
+        obs_d = torch.empty_like(obs_h, device=dev)
+        teach_d = torch.empty_like(teach_h, device=dev)
+
+        def step():
+            obs_d.copy_(obs_h, non_blocking=True)
+            teach_d.copy_(teach_h, non_blocking=True)
+            h.zero_grad()
+            st = h.teach(obs_d, teach_d, 1.0, logits=None, stats=world == 1)
+            if world > 1:
+                dist.all_reduce(grad, op=dist.ReduceOp.AVG)
+                h.step(LR, 0.3 * LR, LR, 0.0, 0.999)
+                h.sync()                             # the loss sums come back after the step
+            else:
+                h.step(LR, 0.3 * LR, LR, 0.0, 0.999)
+                h.sync()
+            return st
+        h2d, d2h = (obs_np.nbytes + teacher_np.nbytes), 16
+    else:
+        def step():
+            h.forward_host(obs_h, out_h)
+        h2d, d2h = obs_np.nbytes, out_h.numel() * 4
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    t = 0.0
+    for _ in range(a.steps):
+        t0 = time.perf_counter()
+        step()
+        t += time.perf_counter() - t0
+    barrier()
+    t = max_over_ranks(t)
+    return {"value": round(Bg * a.steps / t, 1), "unit": W["unit"], "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h),
+            "path": ("obs/teacher H2D (pinned) + fg_teach + fc_step + D2H loss" if train
+                     else "fg_forward_host (pinned host obs -> host logits, copies overlapped in 4 chunks)")}
+
+
+# ------------------------------------------------------------------ CPU baseline / reference arm
+def _ref_forward(s, P, threads):
+    from oracle.oracle import REF_LIB, Oracle, RefInfer
+    if REF_LIB.exists():
+        return RefInfer(s, P, threads=threads), "reference", "flyguy/native/fly_infer.cpp (oracle/_ref, g++ -O3 " \
+            "-march=x86-64-v3 -ffast-math), one handle per thread"
+    o = Oracle(s, threads=threads)
+    return type("O", (), {"forward": lambda self, x: o.forward(P, x), "close": lambda self: None})(), "port", \
+        "oracle/fly_oracle.c forward (OpenMP)"
+
+
+def cpu_baseline(W, s, P, budget: float):
+    """The reference's CPU path timed on this host's cores on a bounded sample sized to ~`budget` seconds."""
+    from flyguy_b200 import synth
+    threads = os.cpu_count() or 1
+    if W["flags"] == "train":
+        return _cpu_train(s, P, threads, budget, steps=1)
+    r, kind, what = _ref_forward(s, P, threads)
+    obs, _ = synth.make_batch(threads * 8, seed=7)
+    t0 = time.perf_counter()
+    r.forward(obs)
+    dt = time.perf_counter() - t0
+    n = int(max(threads, min(200_000, budget / max(dt, 1e-6) * len(obs))))
+    obs, _ = synth.make_batch(n, seed=8)
+    t0 = time.perf_counter()
+    r.forward(obs)
+    dt = time.perf_counter() - t0
+    r.close()
+    return {"value": round(n / dt, 1), "unit": W["unit"], "cores": threads, "kind": kind,
+            "sample": f"{n} decisions of the same workload (synthetic graph, obs ~ N(0,1)) in {dt:.1f} s; {what}",
+            "cpu": _cpu_model()}
+
+
+def _cpu_train(s, P, threads, budget, steps):
+    """The oracle's C port of the training step: forward + KL loss + backward on a sample, then Adam over every
+    weight (the reference trains on the CPU through torch, which is not available on the GPU box)."""
+    from flyguy_b200 import synth
+    from oracle.oracle import Oracle, adam, loss
+    o = Oracle(s, threads=threads)
+    M = [np.zeros_like(p) for p in P]
+    V = [np.zeros_like(p) for p in P]
+    E = [p.copy() for p in P]
+    Q = [p.copy() for p in P]
+
+    def one(n, seed):
+        obs, teacher = synth.make_batch(n, seed=seed)
+        lg = o.forward(Q, obs)
+        _, _, dl = loss(lg, teacher, 1.0)
+        G = o.backward(Q, obs, dl)
+        adam(Q, G, M, V, E, 1, LR, 0.3 * LR, LR)
+    n = threads * 2
+    t0 = time.perf_counter()
+    one(n, 7)
+    dt = time.perf_counter() - t0
+    n = int(max(threads, min(16384, budget / max(dt, 1e-6) * n / steps)))
+    n = max(32, n // 32 * 32)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        one(n, 9 + i)
+    dt = time.perf_counter() - t0
+    return {"value": round(n * steps / dt, 1), "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} training step(s) of {n} samples (forward, KL loss, backward, Adam over all "
+                      f"{sum(len(p) for p in P):,} weights) in {dt:.1f} s; oracle/fly_oracle.c (OpenMP, double sums)",
+            "cpu": _cpu_model()}
+
+
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(a, W):
+    """The reference's CPU implementation of the path, W warm-up + K timed steps of a bounded sample each."""
+    from flyguy_b200 import synth
+    s, P = synth.make_synthetic()
+    threads = os.cpu_count() or 1
+    Bg = W["batch"]
+    if W["flags"] == "train":
+        cb = _cpu_train(s, P, threads, budget=max(2.0, 90.0 / (a.steps + a.warmup)), steps=1)
+        n = int(cb["sample"].split(" samples")[0].split()[-1])
+        from oracle.oracle import Oracle, adam, loss
+        o = Oracle(s, threads=threads)
+        M, V, E, Q = [np.zeros_like(p) for p in P], [np.zeros_like(p) for p in P], [p.copy() for p in P], \
+            [p.copy() for p in P]
+
+        def step(i):
+            obs, teacher = synth.make_batch(n, seed=100 + i)
+            lg = o.forward(Q, obs)
+            _, _, dl = loss(lg, teacher, 1.0)
+            adam(Q, o.backward(Q, obs, dl), M, V, E, i + 1, LR, 0.3 * LR, LR)
+        kind, what = "port", "oracle/fly_oracle.c training step (OpenMP)"
+        r = None
+    else:
+        r, kind, what = _ref_forward(s, P, threads)
+        obs0, _ = synth.make_batch(threads * 8, seed=5)
+        t0 = time.perf_counter()
+        r.forward(obs0)
+        per = (time.perf_counter() - t0) / len(obs0)
+        n = int(max(threads, min(Bg, max(2.0, 90.0 / (a.steps + a.warmup)) / per)))
+        obs, _ = synth.make_batch(n, seed=6)
+
+        def step(i):
+            r.forward(obs)
+    for i in range(a.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(a.steps):
+        step(a.warmup + i)
+    dt = time.perf_counter() - t0
+    if r is not None:
+        r.close()
+    value = n * a.steps / dt
+    return {"impl": "reference", "metric": W["metric"], "value": round(value, 1), "unit": W["unit"],
+            "n_gpus": 0, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt / a.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak" if W["per_gpu"] else "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (same graph and obs distribution as our arm)",
+            "config": {"workload": W["desc"], "baseline_config": W["cfg"], "global_batch": Bg,
+                       "sample_per_step": n, "parallelism": f"{threads} host threads"},
+            "cpu_baseline": {"value": round(value, 1), "unit": W["unit"], "cores": threads, "kind": kind,
+                             "sample": f"{n} units per step; {what}", "cpu": _cpu_model()},
+            "e2e": {"value": round(value, 1), "unit": W["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    a = args_()
+    W = WORKLOADS[a.workload]
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if a.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(a, W)), flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        local = int(os.environ.get("LOCAL_RANK", rank))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", torch.cuda.current_device())
+    try:
+        out = run_ours(a, W, rank, world, dev, torch, dist)
+        if rank == 0:
+            print(json.dumps(out), flush=True)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,59 @@
+"""Build recipe of libflyguy_b200.so (sm_100a only), in-tree next to the package.
+
+  python -m flyguy_b200.csrc.build [--ptxas-v]
+
+nvcc compiles for the B200 architecture-specific target (-gencode arch=compute_100a,code=sm_100a); the CUDA runtime is
+linked statically, so the library needs only the driver at run time and shares torch's primary context.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+PKG = HERE.parent
+REPO = PKG.parent
+LIB = PKG / "libflyguy_b200.so"
+SOURCES = [HERE / "fg_core.cu"]
+DEPS = SOURCES + [HERE / "fg_kernels.cuh", REPO / "include" / "flyguy_b200.h"]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc() -> str:
+    for c in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if c and Path(c).exists():
+            return c
+    raise FileNotFoundError("nvcc not found (the CUDA toolkit is needed to build libflyguy_b200.so)")
+
+
+def stale() -> bool:
+    return not LIB.exists() or any(d.stat().st_mtime > LIB.stat().st_mtime for d in DEPS)
+
+
+def build(force: bool = False, ptxas_v: bool = False, out: Path = LIB) -> Path:
+    if not force and out == LIB and not stale():
+        return out
+    tmp = out.with_suffix(".so.tmp")
+    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
+           "-I", str(REPO / "include"), "-o", str(tmp), *map(str, SOURCES)]
+    if ptxas_v:
+        cmd += ["-Xptxas", "-v"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode:
+        raise RuntimeError(f"nvcc failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+    if ptxas_v:
+        sys.stderr.write(r.stderr)
+    os.replace(tmp, out)
+    return out
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ptxas-v", action="store_true")
+    ap.add_argument("--force", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force or a.ptxas_v, ptxas_v=a.ptxas_v))

@@ -1,0 +1,800 @@
+// flyguy_b200 host side: NET.bin loading, the merged-pair plans, device buffers and the C-ABI of
+// include/flyguy_b200.h. The reference's equivalent is the host half of flyguy/native/flyguy_train.cu (load_net
+// 230-256, alloc_batch 308-317, forward_logits 320-332, backward 339-359, fc_* 553-629).
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <numeric>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "fg_kernels.cuh"
+#include "flyguy_b200.h"
+
+using namespace fg;
+
+namespace {
+
+struct Err : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+#define CK(call)                                                                                      \
+    do {                                                                                              \
+        cudaError_t e_ = (call);                                                                      \
+        if (e_ != cudaSuccess) throw Err(std::string(#call) + ": " + cudaGetErrorString(e_));         \
+    } while (0)
+#define LAUNCHED() CK(cudaGetLastError())
+
+thread_local std::string g_create_error;    // fg_last_error(NULL): why the last create on this thread failed
+
+struct Hop {
+    int rows = 0, n_src = 0, E = 0, P = 0;
+    long long pbase = 0;                     // first merged pair of this hop in the concatenated arrays
+    long long rbase = 0;                     // first row of this hop's layer in the per-row arrays
+    bool widx_unique = true, redrive = false;
+    int *d_nid = nullptr, *d_drow = nullptr, *d_sched = nullptr, *d_pptr = nullptr;
+    int *d_tsched = nullptr, *d_tptr = nullptr;
+    void* d_h = nullptr;                     // states [rows, ld]
+};
+
+// kernel classes timed by fg_timing (CUDA events around every launch of the class, on the handle's stream)
+enum KClass { K_TRANSPOSE, K_FOLD, K_PLUG_FWD, K_HOP_FWD, K_OUT_FWD, K_LOSS, K_OUT_BWD, K_ACT_BWD, K_SDDMM, K_HOP_BWD,
+              K_PLUG_BWD, K_ADAM, K_NORM, K_NCLASS };
+
+struct Timer {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;
+    size_t used = 0;
+    struct Rec { int cls; cudaEvent_t a, b; };
+    std::vector<Rec> recs;
+};
+
+struct Core {
+    int obs_dim = 0, n_act = 0, hops = 0, n_neurons = 0, n_w = 0, n_s = 0, fan = 0, n_dn = 0;
+    std::vector<int> sizes;
+    int maxB = 0, flags = 0;
+    bool bf16 = false, train = true, redrive = false;
+    int *d_in_crow = nullptr, *d_in_col = nullptr, *d_n0 = nullptr, *d_dn = nullptr;
+    std::vector<Hop> hop;
+    long long R = 0, Ptot = 0, Etot = 0;
+    int* d_row_nid = nullptr;
+    float *d_rgain = nullptr, *d_rthr = nullptr, *d_rsig = nullptr;
+    int2 *d_pairs = nullptr, *d_tpairs = nullptr;
+    int *d_gptr = nullptr, *d_gw = nullptr, *d_tpi = nullptr;
+    long long off[8] = {0};
+    float *P = nullptr, *G = nullptr, *M = nullptr, *V = nullptr, *EMA = nullptr;
+    long long adam_t = 0;
+    float *x = nullptr, *drive = nullptr, *lg = nullptr, *dl = nullptr;
+    void* h0 = nullptr;
+    float *gh_a = nullptr, *gh_b = nullptr, *gz = nullptr, *gdrive = nullptr, *part = nullptr;
+    float *kl_s = nullptr, *ag_s = nullptr, *stats = nullptr, *norm_part = nullptr, *norm = nullptr;
+    int* live = nullptr;
+    int out_splits = 1;
+    float *obs_dev = nullptr, *logits_dev = nullptr;   // fg_forward_host staging
+    cudaStream_t st = 0, h2d = nullptr, d2h = nullptr;
+    int folded = -1;                                    // 0: derived arrays from P, 1: from EMA, -1: stale
+    int lastB = 0;
+    int status = 0;
+    std::string err;
+    std::vector<void*> allocs;
+    int device = 0;
+    long long launches = 0;
+    Timer timer;
+};
+
+cudaEvent_t pool_event(Core& c) {
+    if (c.timer.used == c.timer.pool.size()) {
+        cudaEvent_t e;
+        CK(cudaEventCreate(&e));
+        c.timer.pool.push_back(e);
+    }
+    return c.timer.pool[c.timer.used++];
+}
+// every kernel of the library goes through here: counted, and timed when fg_timing is on
+template <class F>
+void launch(Core& c, int cls, F&& f) {
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (c.timer.on) {
+        a = pool_event(c);
+        b = pool_event(c);
+        CK(cudaEventRecord(a, c.st));
+    }
+    f();
+    CK(cudaGetLastError());
+    ++c.launches;
+    if (c.timer.on) {
+        CK(cudaEventRecord(b, c.st));
+        c.timer.recs.push_back({cls, a, b});
+    }
+}
+
+template <class X>
+X* dalloc(Core& c, size_t n) {
+    void* p = nullptr;
+    CK(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(X)));
+    c.allocs.push_back(p);
+    return static_cast<X*>(p);
+}
+template <class X>
+X* upload(Core& c, const std::vector<X>& v) {
+    X* p = dalloc<X>(c, v.size());
+    if (!v.empty()) CK(cudaMemcpy(p, v.data(), v.size() * sizeof(X), cudaMemcpyHostToDevice));
+    return p;
+}
+
+// ---------------------------------------------------------------- NET.bin
+struct Reader {
+    std::vector<int> v;
+    size_t at = 0;
+    std::vector<int> take(long long n, const char* what) {
+        if (n < 0 || at + (size_t)n > v.size()) throw Err(std::string("NET.bin too short reading ") + what);
+        std::vector<int> out(v.begin() + at, v.begin() + at + n);
+        at += n;
+        return out;
+    }
+};
+
+void check_range(const std::vector<int>& a, long long lo, long long hi, const char* what) {
+    for (int x : a)
+        if (x < lo || x >= hi) throw Err(std::string("NET.bin: ") + what + " index out of range");
+}
+void check_ptr(const std::vector<int>& p, long long n, const char* what) {
+    if (p.empty() || p[0] != 0 || p.back() != n) throw Err(std::string("NET.bin: bad row pointer ") + what);
+    for (size_t i = 1; i < p.size(); ++i)
+        if (p[i] < p[i - 1]) throw Err(std::string("NET.bin: row pointer not ascending ") + what);
+}
+
+// merged pairs of one hop: pair = the edges of one (row, source); returns host arrays appended to the global ones
+void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::vector<int>& col,
+                    const std::vector<int>& widx, std::vector<int2>& pairs, std::vector<int>& gptr,
+                    std::vector<int>& gw, std::vector<int2>& tpairs, std::vector<int>& tpi, std::vector<char>& mark) {
+    const int rows = h.rows;
+    std::vector<int> pptr(rows + 1, 0), order;
+    const long long pbase = (long long)pairs.size();
+    h.pbase = pbase;
+    std::vector<int> psrc;
+    for (int t = 0; t < rows; ++t) {
+        order.resize(crow[t + 1] - crow[t]);
+        std::iota(order.begin(), order.end(), crow[t]);
+        std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return col[a] < col[b]; });
+        for (size_t i = 0; i < order.size(); ++i) {
+            const int e = order[i];
+            if (i == 0 || col[e] != col[order[i - 1]]) {
+                psrc.push_back(col[e]);
+                gptr.push_back((int)gw.size());
+            }
+            gw.push_back(widx[e]);
+            if (mark[widx[e]]) h.widx_unique = false;
+            mark[widx[e]] = 1;
+        }
+        pptr[t + 1] = (int)psrc.size();
+    }
+    for (int w : widx) mark[w] = 0;
+    h.P = (int)psrc.size();
+    for (int p = 0; p < h.P; ++p) pairs.push_back(make_int2(psrc[p], 0));
+    // transposed: by source, destinations ascending
+    std::vector<int> tptr(h.n_src + 1, 0);
+    for (int s : psrc) ++tptr[s + 1];
+    for (int s = 0; s < h.n_src; ++s) tptr[s + 1] += tptr[s];
+    std::vector<int> fill(tptr.begin(), tptr.end() - 1);
+    std::vector<int2> tp(h.P);
+    std::vector<int> ti(h.P);
+    for (int t = 0; t < rows; ++t)
+        for (int p = pptr[t]; p < pptr[t + 1]; ++p) {
+            const int q = fill[psrc[p]]++;
+            tp[q] = make_int2(t, 0);
+            ti[q] = (int)(pbase + p);
+        }
+    tpairs.insert(tpairs.end(), tp.begin(), tp.end());
+    tpi.insert(tpi.end(), ti.begin(), ti.end());
+    // schedules: rows (sources) with most pairs first, so the long ones start early
+    std::vector<int> sched(rows), tsched(h.n_src);
+    std::iota(sched.begin(), sched.end(), 0);
+    std::stable_sort(sched.begin(), sched.end(),
+                     [&](int a, int b) { return pptr[a + 1] - pptr[a] > pptr[b + 1] - pptr[b]; });
+    std::iota(tsched.begin(), tsched.end(), 0);
+    std::stable_sort(tsched.begin(), tsched.end(),
+                     [&](int a, int b) { return tptr[a + 1] - tptr[a] > tptr[b + 1] - tptr[b]; });
+    h.d_pptr = upload(c, pptr);
+    h.d_sched = upload(c, sched);
+    h.d_tptr = upload(c, tptr);
+    h.d_tsched = upload(c, tsched);
+}
+
+// the file's arrays, read and checked on the host before anything touches the GPU
+struct NetHost {
+    std::vector<int> in_crow, in_col, n0, dn;
+    std::vector<int> E;
+    struct H { std::vector<int> nid, crow, col, widx, drow; };
+    std::vector<H> hop;
+};
+
+NetHost parse_net(Core& c, const char* path) {
+    FILE* f = fopen(path, "rb");
+    if (!f) throw Err(std::string("cannot open ") + path);
+    fseek(f, 0, SEEK_END);
+    long sz = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    if (sz < 36 || sz % 4) { fclose(f); throw Err("NET.bin: bad size"); }
+    Reader r;
+    r.v.resize(sz / 4);
+    size_t got = fread(r.v.data(), 4, r.v.size(), f);
+    fclose(f);
+    if (got != r.v.size()) throw Err("NET.bin: short read");
+    if (memcmp(r.v.data(), "FLY1", 4)) throw Err("NET.bin: not a FLY1 file");
+    r.at = 1;
+    auto hd = r.take(8, "header");
+    c.obs_dim = hd[0]; c.n_act = hd[1]; c.hops = hd[2]; c.n_neurons = hd[3];
+    c.n_w = hd[4]; c.n_s = hd[5]; c.fan = hd[6]; c.n_dn = hd[7];
+    if (c.obs_dim <= 0 || c.n_act <= 0 || c.n_act > kMaxAct || c.hops <= 0 || c.hops > 32 || c.n_neurons <= 0 ||
+        c.n_w < 0 || c.n_s <= 0 || c.fan < 0 || c.n_dn <= 0)
+        throw Err("NET.bin: bad header");
+    NetHost n;
+    c.sizes = r.take(c.hops + 1, "sizes");
+    n.E = r.take(c.hops, "edge counts");
+    if (c.sizes[0] != c.n_s) throw Err("NET.bin: sizes[0] != n_s");
+    for (int k = 0; k <= c.hops; ++k) if (c.sizes[k] <= 0) throw Err("NET.bin: empty layer");
+    for (int k = 0; k < c.hops; ++k) if (n.E[k] < 0) throw Err("NET.bin: negative edge count");
+    const long long e_in = (long long)c.n_s * c.fan;
+    n.in_crow = r.take(c.n_s + 1, "in_crow");
+    n.in_col = r.take(e_in, "in_col");
+    r.take(c.obs_dim + 1, "in_tcrow"); r.take(e_in, "in_tcol"); r.take(e_in, "in_tperm");
+    n.n0 = r.take(c.n_s, "n0");
+    check_ptr(n.in_crow, e_in, "in_crow");
+    check_range(n.in_col, 0, c.obs_dim, "in_col");
+    check_range(n.n0, 0, c.n_neurons, "n0");
+    n.hop.resize(c.hops);
+    for (int k = 0; k < c.hops; ++k) {
+        const int rows = c.sizes[k + 1], n_src = c.sizes[k], E = n.E[k];
+        NetHost::H& h = n.hop[k];
+        h.nid = r.take(rows, "nid");
+        h.crow = r.take(rows + 1, "crow");
+        h.col = r.take(E, "col");
+        h.widx = r.take(E, "widx");
+        r.take(n_src + 1, "tcrow"); r.take(E, "tcol"); r.take(E, "twidx");
+        h.drow = r.take(rows, "drow");
+        check_range(h.nid, 0, c.n_neurons, "nid");
+        check_ptr(h.crow, E, "crow");
+        check_range(h.col, 0, n_src, "col");
+        check_range(h.widx, 0, c.n_w, "widx");
+        check_range(h.drow, -1, c.n_s, "drow");
+    }
+    n.dn = r.take(c.n_dn, "dn_rows");
+    check_range(n.dn, 0, c.sizes[c.hops], "dn_rows");
+    r.take(c.n_w, "wmap");
+    if (r.at != r.v.size()) throw Err("NET.bin: trailing bytes");
+    return n;
+}
+
+void upload_net(Core& c, NetHost& n) {
+    c.d_in_crow = upload(c, n.in_crow);
+    c.d_in_col = upload(c, n.in_col);
+    c.d_n0 = upload(c, n.n0);
+    std::vector<int> row_nid(n.n0);
+    std::vector<int2> pairs, tpairs;
+    std::vector<int> gptr, gw, tpi;
+    std::vector<char> mark(std::max(c.n_w, 1), 0);
+    c.hop.resize(c.hops);
+    long long rbase = c.n_s;
+    for (int k = 0; k < c.hops; ++k) {
+        Hop& h = c.hop[k];
+        NetHost::H& src = n.hop[k];
+        h.rows = c.sizes[k + 1]; h.n_src = c.sizes[k]; h.E = n.E[k]; h.rbase = rbase;
+        for (int d : src.drow) if (d >= 0) h.redrive = true;
+        c.redrive |= h.redrive;
+        h.d_nid = upload(c, src.nid);
+        h.d_drow = h.redrive ? upload(c, src.drow) : nullptr;
+        row_nid.insert(row_nid.end(), src.nid.begin(), src.nid.end());
+        build_hop_plan(c, h, src.crow, src.col, src.widx, pairs, gptr, gw, tpairs, tpi, mark);
+        rbase += h.rows;
+    }
+    c.d_dn = upload(c, n.dn);
+    gptr.push_back((int)gw.size());
+    c.R = (long long)row_nid.size();
+    c.Ptot = (long long)pairs.size();
+    c.Etot = (long long)gw.size();
+    c.d_row_nid = upload(c, row_nid);
+    c.d_rgain = dalloc<float>(c, c.R);
+    c.d_rthr = dalloc<float>(c, c.R);
+    c.d_rsig = dalloc<float>(c, c.R);
+    c.d_pairs = upload(c, pairs);
+    c.d_tpairs = upload(c, tpairs);
+    c.d_gptr = upload(c, gptr);
+    c.d_gw = upload(c, gw);
+    c.d_tpi = upload(c, tpi);
+}
+
+size_t act_bytes(const Core& c) { return c.bf16 ? 2 : 4; }
+
+void alloc_all(Core& c) {
+    const long long ps[7] = {c.n_w, c.n_neurons, c.n_neurons, (long long)c.n_s * c.fan, c.n_s,
+                             (long long)c.n_act * c.n_dn, c.n_act};
+    c.off[0] = 0;
+    for (int i = 0; i < 7; ++i) c.off[i + 1] = c.off[i] + ps[i];
+    const long long n = c.off[7];
+    c.P = dalloc<float>(c, n);
+    c.EMA = dalloc<float>(c, n);
+    CK(cudaMemset(c.P, 0, n * 4));
+    CK(cudaMemset(c.EMA, 0, n * 4));
+    if (c.train) {
+        c.G = dalloc<float>(c, n); c.M = dalloc<float>(c, n); c.V = dalloc<float>(c, n);
+        CK(cudaMemset(c.G, 0, n * 4)); CK(cudaMemset(c.M, 0, n * 4)); CK(cudaMemset(c.V, 0, n * 4));
+    }
+    const size_t B = c.maxB;
+    int max_rows = c.n_s;
+    for (auto& h : c.hop) max_rows = std::max(max_rows, h.rows);
+    c.x = dalloc<float>(c, (size_t)c.obs_dim * B);
+    if (c.train || c.redrive) c.drive = dalloc<float>(c, (size_t)c.n_s * B);
+    c.h0 = dalloc<char>(c, (size_t)c.n_s * B * act_bytes(c));
+    for (auto& h : c.hop) h.d_h = dalloc<char>(c, (size_t)h.rows * B * act_bytes(c));
+    c.lg = dalloc<float>(c, (size_t)c.n_act * B);
+    c.norm_part = dalloc<float>(c, 1024);
+    c.norm = dalloc<float>(c, 4);
+    c.stats = dalloc<float>(c, 4);
+    if (c.train) {
+        c.dl = dalloc<float>(c, (size_t)c.n_act * B);
+        c.gh_a = dalloc<float>(c, (size_t)max_rows * B);
+        c.gh_b = dalloc<float>(c, (size_t)max_rows * B);
+        c.gz = dalloc<float>(c, (size_t)max_rows * B);
+        c.gdrive = dalloc<float>(c, (size_t)c.n_s * B);
+        c.live = dalloc<int>(c, max_rows);
+        c.out_splits = std::max(1, std::min(64, (int)((B + 1023) / 1024)));
+        c.part = dalloc<float>(c, (size_t)c.out_splits * c.n_act * (c.n_dn + 1));
+        c.kl_s = dalloc<float>(c, B);
+        c.ag_s = dalloc<float>(c, B);
+    }
+}
+
+void set_smem_limits(const Core& c) {
+    const int smem = (32 * c.n_act + 128 * (c.n_act + 1)) * 4;
+    CK(cudaFuncSetAttribute(k_out_fwd<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_out_fwd<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+}
+
+inline unsigned blocks(long long n, int t = 256) { return (unsigned)((n + t - 1) / t); }
+
+// derived per-version arrays: per-row gain / threshold / sigmoid, merged pair weights (forward and transposed)
+void fold(Core& c, int which) {
+    if (c.folded == which) return;
+    const float* src = which ? c.EMA : c.P;
+    launch(c, K_FOLD, [&]() { k_fold_neurons<<<blocks(c.R), 256, 0, c.st>>>(c.d_row_nid, src + c.off[1], src + c.off[2], c.d_rgain, c.d_rthr,
+                                                  c.d_rsig, (int)c.R); });
+    if (c.Ptot) {
+        launch(c, K_FOLD, [&]() { k_fold_pairs<<<blocks(c.Ptot), 256, 0, c.st>>>(c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, (int)c.Ptot); });
+        launch(c, K_FOLD, [&]() { k_fold_tpairs<<<blocks(c.Ptot), 256, 0, c.st>>>(c.d_tpi, c.d_pairs, c.d_tpairs, (int)c.Ptot); });
+    }
+    c.folded = which;
+}
+
+void check_batch(const Core& c, int B) {
+    if (B <= 0 || B % 32 || B > c.maxB)
+        throw Err("batch " + std::to_string(B) + " is not a positive multiple of 32 up to max_batch " +
+                  std::to_string(c.maxB));
+}
+
+// obs_nm: already neuron-major in c.x when obs == nullptr
+template <class T>
+void forward_t(Core& c, const float* obs, int B, float* logits, int ema, bool keep_lg) {
+    constexpr int V = Act<T>::V;
+    fold(c, ema ? 1 : 0);
+    const float* Pw = ema ? c.EMA : c.P;
+    if (obs) {
+        launch(c, K_TRANSPOSE, [&]() { k_to_neuron_major<<<dim3((B + 31) / 32, (c.obs_dim + 31) / 32), dim3(32, 8), 0, c.st>>>(obs, c.x, c.obs_dim, B, B); });
+    }
+    const unsigned chunks = (unsigned)((B + 32 * V - 1) / (32 * V));
+    const dim3 g0((c.n_s + kWarps - 1) / kWarps, chunks);
+    if (c.drive)
+        launch(c, K_PLUG_FWD, [&]() { k_plug_fwd<T, true><<<g0, kThreads, 0, c.st>>>(c.d_in_crow, c.d_in_col, Pw + c.off[3], Pw + c.off[4], c.d_rgain,
+                                                       c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, B); });
+    else
+        launch(c, K_PLUG_FWD, [&]() { k_plug_fwd<T, false><<<g0, kThreads, 0, c.st>>>(c.d_in_crow, c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+                                                        c.d_rgain, c.d_rthr, c.x, nullptr, (T*)c.h0, c.n_s, B); });
+    const T* hp = (const T*)c.h0;
+    for (auto& h : c.hop) {
+        const dim3 g((h.rows + kWarps - 1) / kWarps, chunks);
+        launch(c, K_HOP_FWD, [&]() { k_hop_fwd<T><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase, hp, c.d_rgain + h.rbase,
+                                               c.d_rthr + h.rbase, h.d_drow, c.drive, (T*)h.d_h, h.rows, B); });
+        hp = (const T*)h.d_h;
+    }
+    const int groups = (c.n_act + kActGroup - 1) / kActGroup;
+    const int smem = (32 * c.n_act + 128 * (c.n_act + 1)) * 4;
+    launch(c, K_OUT_FWD, [&]() { k_out_fwd<T><<<(B + 127) / 128, 128 * groups, smem, c.st>>>(Pw + c.off[5], Pw + c.off[6], c.d_dn, hp,
+                                                                 keep_lg ? c.lg : nullptr, logits, c.n_act, c.n_dn, B, B); });
+    c.lastB = B;
+}
+
+void forward(Core& c, const float* obs, int B, float* logits, int ema, bool keep_lg) {
+    if (c.bf16) forward_t<__nv_bfloat16>(c, obs, B, logits, ema, keep_lg);
+    else forward_t<float>(c, obs, B, logits, ema, keep_lg);
+}
+
+// gradient of the loss whose d/dlogits is in c.dl [n_act, B], through the states of the last forward; ADDED to G
+void backward(Core& c, int B) {
+    if (!c.train) throw Err("this handle was created for inference only");
+    if (B != c.lastB) throw Err("fc_backward batch differs from the last forward's");
+    fold(c, 0);
+    const float* W = c.P;
+    CK(cudaMemsetAsync(c.gdrive, 0, (size_t)c.n_s * B * 4, c.st));
+    const Hop& top = c.hop.back();
+    const float* hK = (const float*)top.d_h;
+    const int splits = std::max(1, std::min(c.out_splits, (B + 1023) / 1024));
+    const int split_len = ((B + splits - 1) / splits + 31) / 32 * 32;
+    launch(c, K_OUT_BWD, [&]() { k_out_bwd_w<float><<<dim3((c.n_dn + 1 + 31) / 32, (c.n_act + 31) / 32, splits), 256, 0, c.st>>>(
+        c.dl, hK, c.d_dn, c.part, c.n_act, c.n_dn, B, B, split_len); });
+    launch(c, K_OUT_BWD, [&]() { k_out_bwd_reduce<<<blocks((long long)c.n_act * (c.n_dn + 1)), 256, 0, c.st>>>(c.part, c.G + c.off[5],
+                                                                                 c.G + c.off[6], c.n_act, c.n_dn, splits); });
+    float* gh = c.gh_a;
+    float* gh_next = c.gh_b;
+    if (c.n_dn < top.rows) CK(cudaMemsetAsync(gh, 0, (size_t)top.rows * B * 4, c.st));
+    const int jper = 64;
+    launch(c, K_OUT_BWD, [&]() { k_out_bwd_h<<<dim3((B + 127) / 128, (c.n_dn + jper - 1) / jper), 128, jper * c.n_act * 4, c.st>>>(
+        W + c.off[5], c.dl, c.d_dn, gh, c.n_act, c.n_dn, B, B, jper); });
+    for (int k = c.hops - 1; k >= 0; --k) {
+        const Hop& h = c.hop[k];
+        const float* hk = (const float*)h.d_h;
+        const float* hprev = k ? (const float*)c.hop[k - 1].d_h : (const float*)c.h0;
+        launch(c, K_ACT_BWD, [&]() { k_act_bwd<float><<<h.rows, kThreads, 0, c.st>>>(gh, hk, h.d_nid, h.d_drow, c.d_rgain + h.rbase,
+                                                        c.d_rthr + h.rbase, c.d_rsig + h.rbase, c.gz, c.G + c.off[1],
+                                                        c.G + c.off[2], c.gdrive, c.live, B, B); });
+        if (h.widx_unique)
+            launch(c, K_SDDMM, [&]() { k_sddmm<float, false><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase,
+                                                                 c.d_gw, c.gz, hprev, c.live, c.G + c.off[0], B, B); });
+        else
+            launch(c, K_SDDMM, [&]() { k_sddmm<float, true><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase,
+                                                                c.d_gw, c.gz, hprev, c.live, c.G + c.off[0], B, B); });
+        launch(c, K_HOP_BWD, [&]() { k_hop_bwd_t<<<dim3((h.n_src + kWarps - 1) / kWarps, (B + 127) / 128), kThreads, 0, c.st>>>(
+            h.d_tsched, h.d_tptr, c.d_tpairs + h.pbase, c.gz, gh_next, h.n_src, B); });
+        std::swap(gh, gh_next);
+    }
+    launch(c, K_PLUG_BWD, [&]() { k_plug_bwd<float><<<c.n_s, kThreads, 0, c.st>>>(gh, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_crow,
+                                                    c.d_in_col, c.x, c.d_rgain, c.d_rsig, c.G + c.off[1],
+                                                    c.G + c.off[2], c.G + c.off[3], c.G + c.off[4], B, B); });
+}
+
+float grad_norm(Core& c, float max_norm) {
+    const long long n = c.off[7];
+    const int nb = (int)std::min<long long>(1024, std::max<long long>(1, blocks(n)));
+    launch(c, K_NORM, [&]() { k_sumsq<<<nb, 256, 0, c.st>>>(c.G, n, c.norm_part); });
+    launch(c, K_NORM, [&]() { k_norm_final<<<1, 256, 0, c.st>>>(c.norm_part, nb, max_norm, c.norm); });
+    float g = 0.f;
+    CK(cudaMemcpyAsync(&g, c.norm, 4, cudaMemcpyDeviceToHost, c.st));
+    CK(cudaStreamSynchronize(c.st));
+    return g;
+}
+
+float* flat(Core& c, int which) {
+    switch (which) {
+        case 0: return c.P;
+        case 1: return c.EMA;
+        case 2: return c.M;
+        case 3: return c.V;
+        case 4: return c.G;
+    }
+    return nullptr;
+}
+
+Core* as_core(void* h) { return static_cast<Core*>(h); }
+
+template <class F>
+auto guarded(void* h, F&& fn, decltype(fn()) fail) -> decltype(fn()) {
+    Core* c = as_core(h);
+    if (!c) { g_create_error = "null handle"; return fail; }
+    if (c->status) return fail;
+    try {
+        CK(cudaSetDevice(c->device));
+        return fn();
+    } catch (const std::exception& e) {
+        c->status = 1;
+        c->err = e.what();
+        return fail;
+    }
+}
+
+void destroy(Core* c) {
+    if (!c) return;
+    if (c->allocs.empty() && !c->h2d && !c->d2h) { delete c; return; }
+    cudaSetDevice(c->device);
+    if (c->st) cudaStreamSynchronize(c->st);
+    for (void* p : c->allocs) cudaFree(p);
+    for (auto e : c->timer.pool) cudaEventDestroy(e);
+    if (c->h2d) cudaStreamDestroy(c->h2d);
+    if (c->d2h) cudaStreamDestroy(c->d2h);
+    delete c;
+}
+
+void* create(const char* path, int max_batch, int flags) {
+    Core* c = new Core;
+    try {
+        if (!path) throw Err("no network file");
+        if (max_batch <= 0 || max_batch % 32) throw Err("max_batch must be a positive multiple of 32");
+        c->maxB = max_batch;
+        c->flags = flags;
+        c->bf16 = flags & FG_ACT_BF16;
+        c->train = !(flags & (FG_ACT_BF16 | FG_INFER_ONLY));
+        NetHost n = parse_net(*c, path);     // (a bad file fails here, before the GPU is touched)
+        CK(cudaGetDevice(&c->device));
+        upload_net(*c, n);
+        alloc_all(*c);
+        set_smem_limits(*c);
+        CK(cudaDeviceSynchronize());
+        return c;
+    } catch (const std::exception& e) {
+        g_create_error = e.what();
+        destroy(c);
+        return nullptr;
+    }
+}
+
+}  // namespace
+
+// ================================================================ C ABI
+extern "C" {
+
+void* fc_create(const char* net_path, int max_batch) { return create(net_path, max_batch, 0); }
+void* fg_create(const char* net_path, int max_batch, int flags) { return create(net_path, max_batch, flags); }
+void fg_destroy(void* h) { destroy(as_core(h)); }
+
+int fg_status(void* h) { return h ? as_core(h)->status : (g_create_error.empty() ? 0 : 1); }
+const char* fg_last_error(void* h) { return h ? as_core(h)->err.c_str() : g_create_error.c_str(); }
+void fg_clear_error(void* h) {
+    if (!h) { g_create_error.clear(); return; }
+    as_core(h)->status = 0;
+    as_core(h)->err.clear();
+}
+
+void fc_sizes(void* h, long long* out) {
+    guarded(h, [&]() {
+        Core& c = *as_core(h);
+        for (int i = 0; i < 7; ++i) out[i] = c.off[i + 1] - c.off[i];
+        out[7] = c.obs_dim; out[8] = c.n_act; out[9] = c.maxB;
+        return 0;
+    }, 0);
+}
+
+void fg_offsets(void* h, long long* off) {
+    guarded(h, [&]() { for (int i = 0; i < 8; ++i) off[i] = as_core(h)->off[i]; return 0; }, 0);
+}
+
+int fg_layout(void* h, int* sizes, long long* pairs) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        for (int k = 0; k <= c.hops; ++k) if (sizes) sizes[k] = c.sizes[k];
+        for (int k = 0; k < c.hops; ++k) if (pairs) pairs[k] = c.hop[k].P;
+        return c.hops;
+    }, -1);
+}
+
+void fc_set_stream(void* h, void* stream) {
+    guarded(h, [&]() { as_core(h)->st = static_cast<cudaStream_t>(stream); return 0; }, 0);
+}
+
+int fg_flat(void* h, int which, float** ptr, long long* n) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        float* p = flat(c, which);
+        if (!p) throw Err("no such array in this handle (which " + std::to_string(which) + ")");
+        *ptr = p;
+        *n = c.off[7];
+        if (which <= 1) c.folded = -1;       // the caller may write the weights through this pointer
+        return 0;
+    }, -1);
+}
+
+void fc_copy(void* h, int which, int to_core, float** ptrs) {
+    guarded(h, [&]() {
+        Core& c = *as_core(h);
+        float* A = flat(c, which);
+        if (!A) throw Err("fc_copy: no such array in this handle (which " + std::to_string(which) + ")");
+        for (int i = 0; i < 7; ++i) {
+            if (!ptrs[i]) continue;
+            float* mine = A + c.off[i];
+            const size_t bytes = (size_t)(c.off[i + 1] - c.off[i]) * 4;
+            if (to_core) CK(cudaMemcpyAsync(mine, ptrs[i], bytes, cudaMemcpyDeviceToDevice, c.st));
+            else CK(cudaMemcpyAsync(ptrs[i], mine, bytes, cudaMemcpyDeviceToDevice, c.st));
+        }
+        if (to_core && which <= 1) c.folded = -1;
+        return 0;
+    }, 0);
+}
+
+void fc_forward(void* h, const float* obs, int B, float* logits, int ema) {
+    guarded(h, [&]() {
+        Core& c = *as_core(h);
+        check_batch(c, B);
+        forward(c, obs, B, logits, ema, c.train);
+        return 0;
+    }, 0);
+}
+
+void fc_zero_grad(void* h) {
+    guarded(h, [&]() {
+        Core& c = *as_core(h);
+        if (!c.train) throw Err("this handle was created for inference only");
+        CK(cudaMemsetAsync(c.G, 0, c.off[7] * 4, c.st));
+        return 0;
+    }, 0);
+}
+
+void fc_backward(void* h, const float* dlogits, int B) {
+    guarded(h, [&]() {
+        Core& c = *as_core(h);
+        check_batch(c, B);
+        if (!c.train) throw Err("this handle was created for inference only");
+        launch(c, K_TRANSPOSE, [&]() { k_to_neuron_major<<<dim3((B + 31) / 32, (c.n_act + 31) / 32), dim3(32, 8), 0, c.st>>>(dlogits, c.dl, c.n_act,
+                                                                                            B, B); });
+        backward(c, B);
+        return 0;
+    }, 0);
+}
+
+float fc_grad_norm(void* h) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        if (!c.train) throw Err("this handle was created for inference only");
+        return grad_norm(c, 0.f);
+    }, 0.f);
+}
+
+float fc_step(void* h, float lr, float lr_neuron, float lr_plug, float max_norm, float ema) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        if (!c.train) throw Err("this handle was created for inference only");
+        float g = 0.f;
+        const float* scale = nullptr;
+        if (max_norm > 0) { g = grad_norm(c, max_norm); scale = c.norm; }
+        ++c.adam_t;
+        const long long tc = std::min<long long>(c.adam_t, 100000);
+        const float c1 = 1.f - (float)pow(0.9, (double)tc), c2 = 1.f - (float)pow(0.999, (double)tc);
+        const long long n = c.off[7];
+        launch(c, K_ADAM, [&]() { k_adam<<<(unsigned)std::min<long long>(blocks(n), 148 * 16), 256, 0, c.st>>>(
+            c.P, c.G, c.M, c.V, c.EMA, n, c.off[1], c.off[3], lr, lr_neuron, lr_plug, c1, c2, scale, ema); });
+        c.folded = -1;
+        return g;
+    }, 0.f);
+}
+
+long long fc_adam_t(void* h, long long set) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        if (set >= 0) c.adam_t = set;
+        return c.adam_t;
+    }, (long long)0);
+}
+
+void fc_sync(void* h) {
+    guarded(h, [&]() { CK(cudaStreamSynchronize(as_core(h)->st)); return 0; }, 0);
+}
+
+int fg_teach(void* h, const float* obs, const float* teacher, int B, float inv_temp, float* logits, double* stats) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        check_batch(c, B);
+        if (!c.train) throw Err("this handle was created for inference only");
+        forward(c, obs, B, logits, 0, true);
+        CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
+        launch(c, K_LOSS, [&]() { k_loss<<<blocks(B), 256, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp); });
+        launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
+        backward(c, B);
+        if (stats) {
+            float s[2];
+            CK(cudaMemcpyAsync(s, c.stats, 8, cudaMemcpyDeviceToHost, c.st));
+            CK(cudaStreamSynchronize(c.st));
+            stats[0] = s[0];
+            stats[1] = s[1];
+        }
+        return 0;
+    }, -1);
+}
+
+int fg_forward_host(void* h, const float* obs_host, int B, float* logits_host, int ema) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        check_batch(c, B);
+        if (!c.obs_dev) {
+            c.obs_dev = dalloc<float>(c, (size_t)c.maxB * c.obs_dim);
+            c.logits_dev = dalloc<float>(c, (size_t)c.maxB * c.n_act);
+            CK(cudaStreamCreateWithFlags(&c.h2d, cudaStreamNonBlocking));
+            CK(cudaStreamCreateWithFlags(&c.d2h, cudaStreamNonBlocking));
+        }
+        const int nch = B >= 4 * 256 ? 4 : 1;
+        const int chunk = ((B + nch - 1) / nch + 255) / 256 * 256;
+        std::vector<cudaEvent_t> ev;
+        auto event = [&]() {
+            cudaEvent_t e;
+            CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+            ev.push_back(e);
+            return e;
+        };
+        try {
+            cudaEvent_t start = event();
+            CK(cudaEventRecord(start, c.st));          // the copies start after the handle's earlier work
+            CK(cudaStreamWaitEvent(c.h2d, start, 0));
+            std::vector<cudaEvent_t> in_done, out_done;
+            for (int b0 = 0; b0 < B; b0 += chunk) {
+                const int n = std::min(chunk, B - b0);
+                CK(cudaMemcpyAsync(c.obs_dev + (size_t)b0 * c.obs_dim, obs_host + (size_t)b0 * c.obs_dim,
+                                   (size_t)n * c.obs_dim * 4, cudaMemcpyHostToDevice, c.h2d));
+                cudaEvent_t e = event();
+                CK(cudaEventRecord(e, c.h2d));
+                in_done.push_back(e);
+            }
+            int i = 0;
+            for (int b0 = 0; b0 < B; b0 += chunk, ++i) {
+                const int n = std::min(chunk, B - b0);
+                CK(cudaStreamWaitEvent(c.st, in_done[i], 0));
+                forward(c, c.obs_dev + (size_t)b0 * c.obs_dim, n, c.logits_dev + (size_t)b0 * c.n_act, ema, false);
+                cudaEvent_t e = event();
+                CK(cudaEventRecord(e, c.st));
+                CK(cudaStreamWaitEvent(c.d2h, e, 0));
+                CK(cudaMemcpyAsync(logits_host + (size_t)b0 * c.n_act, c.logits_dev + (size_t)b0 * c.n_act,
+                                   (size_t)n * c.n_act * 4, cudaMemcpyDeviceToHost, c.d2h));
+            }
+            cudaEvent_t done = event();
+            CK(cudaEventRecord(done, c.d2h));
+            CK(cudaStreamWaitEvent(c.st, done, 0));     // later work of the handle waits for the copies
+            CK(cudaEventSynchronize(done));
+        } catch (...) {
+            for (auto e : ev) cudaEventDestroy(e);
+            throw;
+        }
+        for (auto e : ev) cudaEventDestroy(e);
+        c.lastB = 0;                                    // chunked states: no backward through them
+        return 0;
+    }, -1);
+}
+
+long long fg_launches(void* h) {
+    return guarded(h, [&]() { return as_core(h)->launches; }, (long long)-1);
+}
+
+int fg_timing(void* h, int on) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        if (!on && !c.timer.recs.empty()) throw Err("fg_timing: read the recorded times (fg_timing_read) first");
+        c.timer.on = on != 0;
+        return 0;
+    }, -1);
+}
+
+int fg_timing_read(void* h, double* ms, long long* count, int n) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        for (int i = 0; i < n; ++i) { ms[i] = 0.0; count[i] = 0; }
+        CK(cudaStreamSynchronize(c.st));
+        for (auto& r : c.timer.recs) {
+            float t = 0.f;
+            CK(cudaEventElapsedTime(&t, r.a, r.b));
+            if (r.cls < n) { ms[r.cls] += t; ++count[r.cls]; }
+        }
+        c.timer.recs.clear();
+        c.timer.used = 0;
+        return (int)K_NCLASS;
+    }, -1);
+}
+
+int fg_layer(void* h, int k, float* out, int B) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        if (k < 0 || k > c.hops) throw Err("no such layer");
+        if (B != c.lastB) throw Err("fg_layer: batch differs from the last forward's");
+        const void* src = k ? c.hop[k - 1].d_h : c.h0;
+        const size_t n = (size_t)c.sizes[k] * B;
+        if (!c.bf16) {
+            CK(cudaMemcpyAsync(out, src, n * 4, cudaMemcpyDeviceToDevice, c.st));
+        } else {
+            std::vector<float> tmp;   // small layers in tests only: convert on the host
+            std::vector<__nv_bfloat16> hb(n);
+            CK(cudaMemcpyAsync(hb.data(), src, n * 2, cudaMemcpyDeviceToHost, c.st));
+            CK(cudaStreamSynchronize(c.st));
+            tmp.resize(n);
+            for (size_t i = 0; i < n; ++i) tmp[i] = __bfloat162float(hb[i]);
+            CK(cudaMemcpyAsync(out, tmp.data(), n * 4, cudaMemcpyHostToDevice, c.st));
+            CK(cudaStreamSynchronize(c.st));
+        }
+        return 0;
+    }, -1);
+}
+
+}  // extern "C"

@@ -1,0 +1,625 @@
+// flyguy_b200 device code: the hop path's kernels for sm_100a.
+//
+// Layout: every layer's states are neuron-major [rows][ld] (ld = the batch), so one warp reads 32*V consecutive
+// samples of ONE source neuron as a single coalesced 16-byte-per-lane load (V = 4 fp32 or 8 bf16 values per lane).
+// The forward and transposed products walk MERGED edge runs: the edges of one (destination, source) pair are folded
+// into one weight once per weight version (k_fold_pairs), so a duplicate-heavy graph does each (row, source) product
+// once. Reductions over the batch (neuron, plug and weight gradients) are owned by one CTA each and reduced in a
+// fixed order - no float atomics, bit-reproducible for a given batch.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fg {
+
+constexpr int kWarps = 8;                 // warps per CTA of the row kernels
+constexpr int kThreads = 32 * kWarps;
+
+template <class T> struct Act;
+template <> struct Act<float> { static constexpr int V = 4; };
+template <> struct Act<__nv_bfloat16> { static constexpr int V = 8; };
+
+// ---- 16-byte vector loads / stores of V activations as fp32
+__device__ __forceinline__ void ld_act(const float* p, float (&v)[4]) {
+    float4 q = __ldg(reinterpret_cast<const float4*>(p));
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+}
+__device__ __forceinline__ void ld_act(const __nv_bfloat16* p, float (&v)[8]) {
+    uint4 q = __ldg(reinterpret_cast<const uint4*>(p));
+    // bf16 -> fp32 is exact: the 16 bits become the high half of the fp32 word
+    v[0] = __uint_as_float(q.x << 16); v[1] = __uint_as_float(q.x & 0xffff0000u);
+    v[2] = __uint_as_float(q.y << 16); v[3] = __uint_as_float(q.y & 0xffff0000u);
+    v[4] = __uint_as_float(q.z << 16); v[5] = __uint_as_float(q.z & 0xffff0000u);
+    v[6] = __uint_as_float(q.w << 16); v[7] = __uint_as_float(q.w & 0xffff0000u);
+}
+__device__ __forceinline__ void st_act(float* p, const float (&v)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&b);
+}
+__device__ __forceinline__ void st_act(__nv_bfloat16* p, const float (&v)[8]) {
+    uint4 q;
+    q.x = pack_bf16(v[0], v[1]); q.y = pack_bf16(v[2], v[3]);
+    q.z = pack_bf16(v[4], v[5]); q.w = pack_bf16(v[6], v[7]);
+    *reinterpret_cast<uint4*>(p) = q;
+}
+__device__ __forceinline__ float ld1(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float ld1(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+// sum of N values over the CTA (fixed order); result valid in every thread. `red` holds kWarps*N floats.
+template <int N>
+__device__ __forceinline__ void block_sum(float (&v)[N], float* red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = warp_sum(v[i]);
+    __syncthreads();
+    if (lane == 0) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) red[i * kWarps + warp] = v[i];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) s += red[i * kWarps + w];
+        v[i] = s;
+    }
+}
+
+// ---------------------------------------------------------------- weight-version folds
+// per row of every layer: its neuron's gain and threshold softplus(theta)
+__global__ void k_fold_neurons(const int* __restrict__ nid, const float* __restrict__ gain,
+                               const float* __restrict__ theta, float* __restrict__ rgain, float* __restrict__ rthr,
+                               float* __restrict__ rsig, int n) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    int id = nid[i];
+    float th = theta[id];
+    rgain[i] = gain[id];
+    rthr[i] = softplus_f(th);
+    rsig[i] = sigmoid_f(th);
+}
+// merged pair weight = sum of the weights of its edges (edges of one (row, source) pair are contiguous)
+__global__ void k_fold_pairs(const int* __restrict__ gptr, const int* __restrict__ gw, const float* __restrict__ W,
+                             int2* __restrict__ pairs, int n) {
+    int p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= n) return;
+    float s = 0.f;
+    for (int j = gptr[p]; j < gptr[p + 1]; ++j) s += __ldg(&W[gw[j]]);
+    pairs[p].y = __float_as_int(s);
+}
+__global__ void k_fold_tpairs(const int* __restrict__ tpi, const int2* __restrict__ pairs, int2* __restrict__ tpairs,
+                              int n) {
+    int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= n) return;
+    tpairs[q].y = pairs[tpi[q]].y;
+}
+
+// ---------------------------------------------------------------- layout changes at the API boundary
+// in [B, D] (sample-major, the caller's) -> out [D, ld] (neuron-major); 32x32 tiles through shared memory
+__global__ void k_to_neuron_major(const float* __restrict__ in, float* __restrict__ out, int D, int B, int ld) {
+    __shared__ float tile[32][33];
+    int b0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        int b = b0 + r, d = d0 + threadIdx.x;
+        tile[r][threadIdx.x] = (b < B && d < D) ? in[(size_t)b * D + d] : 0.f;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        int d = d0 + r, b = b0 + threadIdx.x;
+        if (d < D && b < B) out[(size_t)d * ld + b] = tile[threadIdx.x][r];
+    }
+}
+
+// ---------------------------------------------------------------- forward
+// input plug + sensory activation: drive[s,b] = in_b[s] + sum_j in_w[s*fan+j] * x[col, b];
+// h0 = relu(gain*drive - thr). One warp per (row, 32V-sample chunk).
+template <class T, bool SAVE_DRIVE>
+__global__ void __launch_bounds__(kThreads) k_plug_fwd(const int* __restrict__ in_crow, const int* __restrict__ in_col,
+                                                       const float* __restrict__ in_w, const float* __restrict__ in_b,
+                                                       const float* __restrict__ rgain, const float* __restrict__ rthr,
+                                                       const float* __restrict__ x, float* __restrict__ drive,
+                                                       T* __restrict__ h0, int n_s, int ld) {
+    constexpr int V = Act<T>::V;
+    const int row = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= n_s) return;
+    const int c = (blockIdx.y * 32 + lane) * V;
+    if (c >= ld) return;
+    float acc[V];
+    const float bias = __ldg(&in_b[row]);
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] = bias;
+    const int e1 = in_crow[row + 1];
+    for (int e = in_crow[row]; e < e1; ++e) {
+        const float w = __ldg(&in_w[e]);
+        const float* xs = x + (size_t)__ldg(&in_col[e]) * ld + c;
+#pragma unroll
+        for (int i = 0; i < V; i += 4) {
+            float4 q = __ldg(reinterpret_cast<const float4*>(xs + i));
+            acc[i] = fmaf(w, q.x, acc[i]); acc[i + 1] = fmaf(w, q.y, acc[i + 1]);
+            acc[i + 2] = fmaf(w, q.z, acc[i + 2]); acc[i + 3] = fmaf(w, q.w, acc[i + 3]);
+        }
+    }
+    const size_t o = (size_t)row * ld + c;
+    if (SAVE_DRIVE) {
+#pragma unroll
+        for (int i = 0; i < V; i += 4)
+            *reinterpret_cast<float4*>(drive + o + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+    }
+    const float g = __ldg(&rgain[row]), th = __ldg(&rthr[row]);
+    float hv[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) hv[i] = fmaxf(fmaf(g, acc[i], -th), 0.f);
+    st_act(h0 + o, hv);
+}
+
+// one hop: z[t,b] = sum over merged pairs (src, w) of row t of w * hp[src, b] (+ drive[drow[t], b]);
+// h = relu(gain*z - thr). One warp per (row, 32V-sample chunk); rows in degree-descending schedule order.
+template <class T>
+__global__ void __launch_bounds__(kThreads) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
+                                                      const int2* __restrict__ pairs, const T* __restrict__ hp,
+                                                      const float* __restrict__ rgain, const float* __restrict__ rthr,
+                                                      const int* __restrict__ drow, const float* __restrict__ drive,
+                                                      T* __restrict__ h, int n_rows, int ld) {
+    constexpr int V = Act<T>::V;
+    const int slot = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (slot >= n_rows) return;
+    const int t = __ldg(&sched[slot]);
+    const int c = (blockIdx.y * 32 + lane) * V;
+    if (c >= ld) return;
+    float acc[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) acc[i] = 0.f;
+    const int e0 = __ldg(&pptr[t]), e1 = __ldg(&pptr[t + 1]);
+    const T* base = hp + c;
+    int e = e0;
+    for (; e + 4 <= e1; e += 4) {                        // four pairs in flight
+        int2 p[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) p[u] = __ldg(&pairs[e + u]);
+        float v[4][V];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) ld_act(base + (size_t)p[u].x * ld, v[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float w = __int_as_float(p[u].y);
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[i] = fmaf(w, v[u][i], acc[i]);
+        }
+    }
+    for (; e < e1; ++e) {
+        const int2 p = __ldg(&pairs[e]);
+        float v[V];
+        ld_act(base + (size_t)p.x * ld, v);
+        const float w = __int_as_float(p.y);
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = fmaf(w, v[i], acc[i]);
+    }
+    if (drow) {
+        const int d = __ldg(&drow[t]);
+        if (d >= 0) {
+            const float* dr = drive + (size_t)d * ld + c;
+#pragma unroll
+            for (int i = 0; i < V; i += 4) {
+                float4 q = __ldg(reinterpret_cast<const float4*>(dr + i));
+                acc[i] += q.x; acc[i + 1] += q.y; acc[i + 2] += q.z; acc[i + 3] += q.w;
+            }
+        }
+    }
+    const float g = __ldg(&rgain[t]), th = __ldg(&rthr[t]);
+    float hv[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) hv[i] = fmaxf(fmaf(g, acc[i], -th), 0.f);
+    st_act(h + (size_t)t * ld + c, hv);
+}
+
+// output plug: logits[a,b] = out_b[a] + sum_j out_w[a,j] * hK[dn[j], b]. A CTA owns 128 samples; its threads
+// split the actions into groups of kActGroup; out_w is staged transposed through shared memory 32 columns at a time.
+// Writes the neuron-major copy lg [n_act, ld] (for the loss) and/or the caller's [B, n_act] rows.
+constexpr int kActGroup = 48;
+template <class T>
+__global__ void __launch_bounds__(256) k_out_fwd(const float* __restrict__ ow, const float* __restrict__ ob,
+                                                 const int* __restrict__ dn, const T* __restrict__ hK,
+                                                 float* __restrict__ lg, float* __restrict__ out, int n_act, int n_dn,
+                                                 int B, int ld) {
+    extern __shared__ float sm[];                         // wT[32][n_act] then stage[128][n_act+1]
+    float* wT = sm;
+    float* stage = sm + 32 * n_act;
+    const int groups = (n_act + kActGroup - 1) / kActGroup;
+    const int tb = threadIdx.x & 127, grp = threadIdx.x >> 7;
+    const int b = blockIdx.x * 128 + tb;
+    const int a0 = grp * kActGroup;
+    const bool on = grp < groups && b < B;
+    float acc[kActGroup];
+#pragma unroll
+    for (int i = 0; i < kActGroup; ++i) acc[i] = (a0 + i < n_act) ? __ldg(&ob[a0 + i]) : 0.f;
+    for (int j0 = 0; j0 < n_dn; j0 += 32) {
+        const int nj = min(32, n_dn - j0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < 32 * n_act; i += blockDim.x) {
+            int jj = i / n_act, a = i - jj * n_act;
+            wT[i] = jj < nj ? __ldg(&ow[(size_t)a * n_dn + j0 + jj]) : 0.f;
+        }
+        __syncthreads();
+        if (on) {
+            for (int jj = 0; jj < nj; ++jj) {
+                const float hv = ld1(hK + (size_t)__ldg(&dn[j0 + jj]) * ld + b);
+                const float* w = wT + jj * n_act + a0;
+                if (a0 + kActGroup <= n_act) {
+#pragma unroll
+                    for (int i = 0; i < kActGroup; ++i) acc[i] = fmaf(w[i], hv, acc[i]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < kActGroup; ++i) if (a0 + i < n_act) acc[i] = fmaf(w[i], hv, acc[i]);
+                }
+            }
+        }
+    }
+    if (lg && on) {
+#pragma unroll
+        for (int i = 0; i < kActGroup; ++i) if (a0 + i < n_act) lg[(size_t)(a0 + i) * ld + b] = acc[i];
+    }
+    if (out) {
+        __syncthreads();
+        if (grp < groups) {
+#pragma unroll
+            for (int i = 0; i < kActGroup; ++i) if (a0 + i < n_act) stage[tb * (n_act + 1) + a0 + i] = acc[i];
+        }
+        __syncthreads();
+        const int nb = min(128, B - blockIdx.x * 128);
+        float* o = out + (size_t)blockIdx.x * 128 * n_act;
+        for (int i = threadIdx.x; i < nb * n_act; i += blockDim.x) {
+            int bb = i / n_act, a = i - bb * n_act;
+            o[i] = stage[bb * (n_act + 1) + a];
+        }
+    }
+}
+
+// ---------------------------------------------------------------- loss
+// per sample: p_t = softmax(teacher * it); kl = sum p_t (log p_t - log softmax(s)); dl = (softmax(s) - p_t) / B;
+// argmax agreement. teacher is the caller's [B, n_act]; lg and dl are neuron-major.
+__global__ void k_loss(const float* __restrict__ lg, const float* __restrict__ teacher, float* __restrict__ dl,
+                       float* __restrict__ kl_s, float* __restrict__ ag_s, int n_act, int B, int ld, float it) {
+    int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const float* t = teacher + (size_t)b * n_act;
+    float ms = -INFINITY, mt = -INFINITY;
+    int as = 0, at = 0;
+    for (int a = 0; a < n_act; ++a) {
+        float s = lg[(size_t)a * ld + b], tv = t[a] * it;
+        if (s > ms) { ms = s; as = a; }
+        if (tv > mt) { mt = tv; at = a; }
+    }
+    float zs = 0.f, zt = 0.f;
+    for (int a = 0; a < n_act; ++a) { zs += expf(lg[(size_t)a * ld + b] - ms); zt += expf(t[a] * it - mt); }
+    const float ls = ms + logf(zs), lt = mt + logf(zt), inv_b = 1.f / (float)B;
+    float kl = 0.f;
+    for (int a = 0; a < n_act; ++a) {
+        float lps = lg[(size_t)a * ld + b] - ls, lpt = t[a] * it - lt, pt = expf(lpt);
+        kl += pt * (lpt - lps);
+        dl[(size_t)a * ld + b] = (expf(lps) - pt) * inv_b;
+    }
+    kl_s[b] = kl;
+    ag_s[b] = as == at ? 1.f : 0.f;
+}
+// stats[0] = sum kl, stats[1] = sum agree (one CTA, fixed order)
+__global__ void k_loss_stats(const float* __restrict__ kl_s, const float* __restrict__ ag_s, float* __restrict__ stats,
+                             int B) {
+    __shared__ float red[2 * kWarps];
+    float v[2] = {0.f, 0.f};
+    for (int b = threadIdx.x; b < B; b += blockDim.x) { v[0] += kl_s[b]; v[1] += ag_s[b]; }
+    block_sum<2>(v, red);
+    if (threadIdx.x == 0) { stats[0] += v[0]; stats[1] += v[1]; }
+}
+
+// ---------------------------------------------------------------- backward: output plug
+// split-K partial sums over the batch: part[s][a][j] = sum_{b in split s} dl[a,b] * hK[dn[j], b] for j < n_dn and
+// sum_b dl[a,b] for j == n_dn. A CTA owns a 32x32 (action, column) tile and one batch split.
+template <class T>
+__global__ void __launch_bounds__(256) k_out_bwd_w(const float* __restrict__ dl, const T* __restrict__ hK,
+                                                   const int* __restrict__ dn, float* __restrict__ part, int n_act,
+                                                   int n_dn, int B, int ld, int split_len) {
+    __shared__ float sd[32][33], sh[32][33];
+    const int a0 = blockIdx.y * 32, j0 = blockIdx.x * 32, s = blockIdx.z;
+    const int b_lo = s * split_len, b_hi = min(B, b_lo + split_len);
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 8 rows of threads, each does 4 actions
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int b0 = b_lo; b0 < b_hi; b0 += 32) {
+        __syncthreads();
+        for (int r = ty; r < 32; r += 8) {
+            int a = a0 + r, j = j0 + r, b = b0 + tx;
+            sd[r][tx] = (a < n_act && b < b_hi) ? dl[(size_t)a * ld + b] : 0.f;
+            float hv = 0.f;
+            if (b < b_hi) {
+                if (j < n_dn) hv = ld1(hK + (size_t)__ldg(&dn[j]) * ld + b);
+                else if (j == n_dn) hv = 1.f;
+            }
+            sh[r][tx] = hv;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) {
+            const float hv = sh[tx][k];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[i] = fmaf(sd[ty + 8 * i][k], hv, acc[i]);
+        }
+    }
+    const int j = j0 + tx, n_col = n_dn + 1;
+    if (j < n_col) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            int a = a0 + ty + 8 * i;
+            if (a < n_act) part[((size_t)s * n_act + a) * n_col + j] = acc[i];
+        }
+    }
+}
+// G_out_w[a*n_dn + j] += sum_s part[s][a][j]; G_out_b[a] += sum_s part[s][a][n_dn]
+__global__ void k_out_bwd_reduce(const float* __restrict__ part, float* __restrict__ gow, float* __restrict__ gob,
+                                 int n_act, int n_dn, int splits) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int n_col = n_dn + 1;
+    if (i >= n_act * n_col) return;
+    float s = 0.f;
+    for (int k = 0; k < splits; ++k) s += part[(size_t)k * n_act * n_col + i];
+    int a = i / n_col, j = i - a * n_col;
+    if (j < n_dn) gow[(size_t)a * n_dn + j] += s; else gob[a] += s;
+}
+// gh[dn[j], b] = sum_a out_w[a, j] * dl[a, b]: a thread per sample holds dl[., b] in registers (n_act <= 96)
+constexpr int kMaxAct = 96;
+__global__ void __launch_bounds__(128) k_out_bwd_h(const float* __restrict__ ow, const float* __restrict__ dl,
+                                                   const int* __restrict__ dn, float* __restrict__ gh, int n_act,
+                                                   int n_dn, int B, int ld, int j_per_cta) {
+    extern __shared__ float w_s[];                        // [j_per_cta][n_act]
+    const int b = blockIdx.x * 128 + threadIdx.x, jb = blockIdx.y * j_per_cta;
+    const int nj = min(j_per_cta, n_dn - jb);
+    for (int i = threadIdx.x; i < nj * n_act; i += blockDim.x) {
+        int jj = i / n_act, a = i - jj * n_act;
+        w_s[i] = __ldg(&ow[(size_t)a * n_dn + jb + jj]);
+    }
+    __syncthreads();
+    if (b >= B) return;
+    float d[kMaxAct];
+#pragma unroll
+    for (int a = 0; a < kMaxAct; ++a) d[a] = a < n_act ? dl[(size_t)a * ld + b] : 0.f;
+    for (int jj = 0; jj < nj; ++jj) {
+        const float* w = w_s + jj * n_act;
+        float s = 0.f;
+#pragma unroll
+        for (int a = 0; a < kMaxAct; ++a) if (a < n_act) s = fmaf(w[a], d[a], s);
+        gh[(size_t)__ldg(&dn[jb + jj]) * ld + b] = s;
+    }
+}
+
+// ---------------------------------------------------------------- backward: through the neurons
+// one CTA per row: g = gh * [h > 0]; gz = g * gain -> gz; gain grad += sum g*z with z = (h + thr) / gain (exact where
+// h > 0, the only place it counts); theta grad += sum -g * sigmoid(theta); gdrive[drow] += gz. Returns through
+// `live[row]` whether any g was non-zero (rows that never fire are skipped by the weight gradient).
+template <class T>
+__global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ gh, const T* __restrict__ h,
+                                                      const int* __restrict__ nid, const int* __restrict__ drow,
+                                                      const float* __restrict__ rgain, const float* __restrict__ rthr,
+                                                      const float* __restrict__ rsig, float* __restrict__ gz,
+                                                      float* __restrict__ ggain, float* __restrict__ gtheta,
+                                                      float* __restrict__ gdrive, int* __restrict__ live, int B,
+                                                      int ld) {
+    __shared__ float red[3 * kWarps];
+    const int t = blockIdx.x;
+    const float gn = rgain[t], th = rthr[t];
+    const float inv_g = gn != 0.f ? 1.f / gn : 0.f;
+    const int d = drow ? drow[t] : -1;
+    const size_t o = (size_t)t * ld;
+    float s[3] = {0.f, 0.f, 0.f};                        // sum g*z, sum g, any
+    for (int b = threadIdx.x * 4; b < B; b += kThreads * 4) {
+        float4 q = __ldg(reinterpret_cast<const float4*>(gh + o + b));
+        float hv[4] = {ld1(h + o + b), ld1(h + o + b + 1), ld1(h + o + b + 2), ld1(h + o + b + 3)};
+        float gv[4] = {q.x, q.y, q.z, q.w};
+        float zo[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float g = hv[i] > 0.f ? gv[i] : 0.f;
+            s[0] = fmaf(g, (hv[i] + th) * inv_g, s[0]);
+            s[1] += g;
+            s[2] += g != 0.f ? 1.f : 0.f;
+            zo[i] = g * gn;
+        }
+        *reinterpret_cast<float4*>(gz + o + b) = make_float4(zo[0], zo[1], zo[2], zo[3]);
+        if (d >= 0) {
+            float4* gd = reinterpret_cast<float4*>(gdrive + (size_t)d * ld + b);
+            float4 c = *gd;
+            c.x += zo[0]; c.y += zo[1]; c.z += zo[2]; c.w += zo[3];
+            *gd = c;
+        }
+    }
+    block_sum<3>(s, red);
+    if (threadIdx.x == 0) {
+        const int id = nid[t];
+        ggain[id] += s[0];
+        gtheta[id] += -s[1] * rsig[t];
+        live[t] = s[2] > 0.f;
+    }
+}
+
+// per merged pair p of row t: gp = sum_b gz[t,b] * hp[src_p, b], added to the gradient of every edge weight of the
+// pair. One CTA per row, the row's pairs 8 at a time.
+template <class T, bool ATOMIC>
+__global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ pptr, const int2* __restrict__ pairs,
+                                                    const int* __restrict__ gptr, const int* __restrict__ gw,
+                                                    const float* __restrict__ gz, const T* __restrict__ hp,
+                                                    const int* __restrict__ live, float* __restrict__ gW, int B,
+                                                    int ld) {
+    __shared__ float red[8 * kWarps];
+    const int t = blockIdx.x;
+    if (!live[t]) return;
+    const int e0 = pptr[t], e1 = pptr[t + 1];
+    const float* g = gz + (size_t)t * ld;
+    for (int p0 = e0; p0 < e1; p0 += 8) {
+        const int np = min(8, e1 - p0);
+        int src[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) src[u] = u < np ? __ldg(&pairs[p0 + u].x) : 0;
+        float acc[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+        for (int b = threadIdx.x * 4; b < B; b += kThreads * 4) {
+            float4 q = __ldg(reinterpret_cast<const float4*>(g + b));
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (u < np) {
+                    const T* hs = hp + (size_t)src[u] * ld + b;
+                    float h0 = ld1(hs), h1 = ld1(hs + 1), h2 = ld1(hs + 2), h3 = ld1(hs + 3);
+                    acc[u] = fmaf(q.x, h0, fmaf(q.y, h1, fmaf(q.z, h2, fmaf(q.w, h3, acc[u]))));
+                }
+            }
+        }
+        block_sum<8>(acc, red);
+        if (threadIdx.x < np) {
+            const int p = p0 + threadIdx.x;
+            float v = 0.f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) if (u == (int)threadIdx.x) v = acc[u];
+            for (int j = gptr[p]; j < gptr[p + 1]; ++j) {
+                if (ATOMIC) atomicAdd(&gW[gw[j]], v); else gW[gw[j]] += v;
+            }
+        }
+    }
+}
+
+// transposed hop: gh[s, b] = sum over merged pairs (dst, w) of source row s of w * gz[dst, b]. One warp per
+// (row, 128-sample chunk), rows in degree-descending schedule order.
+__global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int* __restrict__ sched, const int* __restrict__ tptr,
+                                                        const int2* __restrict__ tpairs, const float* __restrict__ gz,
+                                                        float* __restrict__ gh, int n_rows, int ld) {
+    const int slot = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (slot >= n_rows) return;
+    const int s = __ldg(&sched[slot]);
+    const int c = (blockIdx.y * 32 + lane) * 4;
+    if (c >= ld) return;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int e0 = __ldg(&tptr[s]), e1 = __ldg(&tptr[s + 1]);
+    const float* base = gz + c;
+    int e = e0;
+    for (; e + 4 <= e1; e += 4) {
+        int2 p[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) p[u] = __ldg(&tpairs[e + u]);
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = __ldg(reinterpret_cast<const float4*>(base + (size_t)p[u].x * ld));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float w = __int_as_float(p[u].y);
+            acc[0] = fmaf(w, v[u].x, acc[0]); acc[1] = fmaf(w, v[u].y, acc[1]);
+            acc[2] = fmaf(w, v[u].z, acc[2]); acc[3] = fmaf(w, v[u].w, acc[3]);
+        }
+    }
+    for (; e < e1; ++e) {
+        const int2 p = __ldg(&tpairs[e]);
+        const float4 v = __ldg(reinterpret_cast<const float4*>(base + (size_t)p.x * ld));
+        const float w = __int_as_float(p.y);
+        acc[0] = fmaf(w, v.x, acc[0]); acc[1] = fmaf(w, v.y, acc[1]);
+        acc[2] = fmaf(w, v.z, acc[2]); acc[3] = fmaf(w, v.w, acc[3]);
+    }
+    *reinterpret_cast<float4*>(gh + (size_t)s * ld + c) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+// sensory layer and plug, one CTA per sensory row s: g0 = gh0 * [h0 > 0]; gain grad += sum g0 * drive; theta grad +=
+// sum -g0 * sigmoid(theta); gd = gdrive (re-drive from later hops) + g0 * gain; in_b grad += sum gd;
+// in_w grad[e] += sum gd * x[col_e] for the row's fan edges (fan <= 32).
+template <class T>
+__global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__ gh0, const T* __restrict__ h0,
+                                                       const float* __restrict__ drive, const float* __restrict__ gdrive,
+                                                       const int* __restrict__ n0, const int* __restrict__ in_crow,
+                                                       const int* __restrict__ in_col, const float* __restrict__ x,
+                                                       const float* __restrict__ rgain, const float* __restrict__ rsig,
+                                                       float* __restrict__ ggain, float* __restrict__ gtheta,
+                                                       float* __restrict__ gin_w, float* __restrict__ gin_b, int B,
+                                                       int ld) {
+    constexpr int F = 16;                                 // fan handled per pass
+    __shared__ float red[(F + 3) * kWarps];
+    const int s = blockIdx.x;
+    const float gn = rgain[s];
+    const size_t o = (size_t)s * ld;
+    const int e0 = in_crow[s], e1 = in_crow[s + 1];
+    for (int f0 = e0; f0 < e1 || f0 == e0; f0 += F) {
+        const int nf = max(0, min(F, e1 - f0));
+        int col[F];
+#pragma unroll
+        for (int u = 0; u < F; ++u) col[u] = u < nf ? in_col[f0 + u] : 0;
+        float v[F + 3];
+#pragma unroll
+        for (int u = 0; u < F + 3; ++u) v[u] = 0.f;
+        for (int b = threadIdx.x; b < B; b += kThreads) {
+            float g = ld1(h0 + o + b) > 0.f ? gh0[o + b] : 0.f;
+            float gd = gdrive[o + b] + g * gn;
+            v[F] += g * drive[o + b];
+            v[F + 1] += g;
+            v[F + 2] += gd;
+#pragma unroll
+            for (int u = 0; u < F; ++u) if (u < nf) v[u] = fmaf(gd, x[(size_t)col[u] * ld + b], v[u]);
+        }
+        block_sum<F + 3>(v, red);
+        if (threadIdx.x == 0) {
+            if (f0 == e0) {
+                const int id = n0[s];
+                ggain[id] += v[F];
+                gtheta[id] += -v[F + 1] * rsig[s];
+                gin_b[s] += v[F + 2];
+            }
+            for (int u = 0; u < nf; ++u) gin_w[f0 + u] += v[u];
+        }
+        if (nf == 0) break;
+    }
+}
+
+// ---------------------------------------------------------------- optimiser
+// partial sums of squares of the flat gradient (one per CTA); the host or k_norm_final adds them in order
+__global__ void k_sumsq(const float* __restrict__ g, long long n, float* __restrict__ part) {
+    __shared__ float red[kWarps];
+    float v[1] = {0.f};
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        v[0] = fmaf(g[i], g[i], v[0]);
+    block_sum<1>(v, red);
+    if (threadIdx.x == 0) part[blockIdx.x] = v[0];
+}
+// norm[0] = sqrt(sum of part); norm[1] = gradient scale for clipping to max_norm (1 if not clipping)
+__global__ void k_norm_final(const float* __restrict__ part, int n, float max_norm, float* __restrict__ norm) {
+    __shared__ float red[kWarps];
+    float v[1] = {0.f};
+    for (int i = threadIdx.x; i < n; i += blockDim.x) v[0] += part[i];
+    block_sum<1>(v, red);
+    if (threadIdx.x == 0) {
+        float g = sqrtf(v[0]);
+        norm[0] = g;
+        norm[1] = (max_norm > 0.f && g > max_norm) ? max_norm / g : 1.f;
+    }
+}
+// Adam over the flat parameter buffer: segments [0, seg1) at lr0 (strengths), [seg1, seg2) at lr1 (gain, theta),
+// the rest at lr2 (plugs). Gradient scale from norm[1] when `scale` is given.
+__global__ void k_adam(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
+                       float* __restrict__ ema, long long n, long long seg1, long long seg2, float lr0, float lr1,
+                       float lr2, float c1, float c2, const float* __restrict__ scale, float decay) {
+    const float gs = scale ? scale[1] : 1.f;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float lr = i < seg1 ? lr0 : (i < seg2 ? lr1 : lr2);
+        const float gr = g[i] * gs;
+        const float mi = 0.9f * m[i] + 0.1f * gr, vi = 0.999f * v[i] + 0.001f * gr * gr;
+        m[i] = mi; v[i] = vi;
+        const float pi = p[i] - lr * (mi / c1) / (sqrtf(vi / c2) + 1e-8f);
+        p[i] = pi;
+        ema[i] = decay * ema[i] + (1.f - decay) * pi;
+    }
+}
+
+}  // namespace fg

@@ -1,0 +1,274 @@
+"""ctypes binding of libflyguy_b200.so (the C-ABI of include/flyguy_b200.h) and a torch-facing handle.
+
+The library is loaded from the package directory (built in-tree by flyguy_b200/csrc/build.py). There is no CPU or
+eager fallback: if the library is missing or fails to load, `lib()` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+from .netfile import Structure, read_net, write_net
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libflyguy_b200.so"
+FG_ACT_BF16, FG_INFER_ONLY = 1, 2
+_lib = None
+
+# the exported symbols and their ctypes signatures: (restype, argtypes)
+_vp, _ci, _cf, _cll = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_longlong
+SIGNATURES = {
+    "fc_create": (_vp, [ctypes.c_char_p, _ci]),
+    "fc_sizes": (None, [_vp, ctypes.POINTER(_cll)]),
+    "fc_copy": (None, [_vp, _ci, _ci, ctypes.POINTER(_vp)]),
+    "fc_forward": (None, [_vp, _vp, _ci, _vp, _ci]),
+    "fc_zero_grad": (None, [_vp]),
+    "fc_backward": (None, [_vp, _vp, _ci]),
+    "fc_grad_norm": (_cf, [_vp]),
+    "fc_step": (_cf, [_vp, _cf, _cf, _cf, _cf, _cf]),
+    "fc_adam_t": (_cll, [_vp, _cll]),
+    "fc_sync": (None, [_vp]),
+    "fg_create": (_vp, [ctypes.c_char_p, _ci, _ci]),
+    "fg_destroy": (None, [_vp]),
+    "fg_status": (_ci, [_vp]),
+    "fg_last_error": (ctypes.c_char_p, [_vp]),
+    "fg_clear_error": (None, [_vp]),
+    "fc_set_stream": (None, [_vp, _vp]),
+    "fg_flat": (_ci, [_vp, _ci, ctypes.POINTER(_vp), ctypes.POINTER(_cll)]),
+    "fg_offsets": (None, [_vp, ctypes.POINTER(_cll)]),
+    "fg_layout": (_ci, [_vp, ctypes.POINTER(_ci), ctypes.POINTER(_cll)]),
+    "fg_teach": (_ci, [_vp, _vp, _vp, _ci, _cf, _vp, ctypes.POINTER(ctypes.c_double)]),
+    "fg_forward_host": (_ci, [_vp, _vp, _ci, _vp, _ci]),
+    "fg_layer": (_ci, [_vp, _ci, _vp, _ci]),
+    "fg_launches": (_cll, [_vp]),
+    "fg_timing": (_ci, [_vp, _ci]),
+    "fg_timing_read": (_ci, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_cll), _ci]),
+}
+KERNEL_CLASSES = ("layout", "fold", "plug_fwd", "hop_fwd", "out_fwd", "loss", "out_bwd", "act_bwd", "sddmm",
+                  "hop_bwd_t", "plug_bwd", "adam", "norm")
+
+
+class FlyguyError(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises if it is not built or does not load."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise FlyguyError(f"{LIB_PATH} is not built: run `python -m flyguy_b200.csrc.build` (or "
+                              "__graft_entry__.build()); flyguy_b200 has no fallback path")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = L
+    return _lib
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+class Handle:
+    """One network in the library, bound to torch tensors on one CUDA device.
+
+    Arrays are exchanged as torch CUDA tensors (fp32, contiguous). `flags` 0: fp32 states, training buffers;
+    FG_ACT_BF16: bf16 states, forward only; FG_INFER_ONLY: fp32 states, forward only."""
+
+    def __init__(self, s: Structure | str | Path, max_batch: int, flags: int = 0, device=None):
+        """s: a Structure, or the path of a NET.bin file."""
+        import torch
+        self.torch = torch
+        self.L = lib()
+        self.max_batch, self.flags = int(max_batch), int(flags)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        with torch.cuda.device(self.device), tempfile.TemporaryDirectory() as tmp:
+            if isinstance(s, (str, Path)):
+                path = Path(s)
+                s = read_net(path)
+            else:
+                path = Path(tmp) / "net.bin"
+                write_net(s, path)
+            self.s = s
+            torch.cuda.synchronize()
+            self.h = self.L.fg_create(str(path).encode(), self.max_batch, self.flags)
+        if not self.h:
+            raise FlyguyError(f"fg_create: {self.L.fg_last_error(None).decode()}")
+        sizes = (ctypes.c_longlong * 10)()
+        self.L.fc_sizes(self.h, sizes)
+        self.sizes = [int(v) for v in sizes[:7]]
+        off = (ctypes.c_longlong * 8)()
+        self.L.fg_offsets(self.h, off)
+        self.offsets = [int(v) for v in off]
+        self.check()
+
+    # ---- plumbing
+    def check(self) -> None:
+        if self.L.fg_status(self.h):
+            msg = self.L.fg_last_error(self.h).decode()
+            self.L.fg_clear_error(self.h)
+            raise FlyguyError(msg)
+
+    def bind_stream(self) -> None:
+        self.L.fc_set_stream(self.h, self.torch.cuda.current_stream(self.device).cuda_stream)
+
+    def close(self) -> None:
+        if getattr(self, "h", None):
+            self.L.fg_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def flat(self, which: int):
+        """The library's flat array (0 weights, 1 average, 2 m, 3 v, 4 gradient) as a zero-copy torch tensor."""
+        p, n = ctypes.c_void_p(), ctypes.c_longlong()
+        if self.L.fg_flat(self.h, which, ctypes.byref(p), ctypes.byref(n)):
+            self.check()
+        return _wrap(p.value, int(n.value), self.device)
+
+    def layout(self):
+        sizes = (ctypes.c_int * 64)()
+        pairs = (ctypes.c_longlong * 64)()
+        K = self.L.fg_layout(self.h, sizes, pairs)
+        self.check()
+        return [int(v) for v in sizes[:K + 1]], [int(v) for v in pairs[:K]]
+
+    # ---- weights
+    def set_params(self, params, which: int = 0) -> None:
+        torch = self.torch
+        ts = [torch.as_tensor(np.asarray(p, np.float32).reshape(-1)).to(self.device) for p in params]
+        assert [t.numel() for t in ts] == self.sizes, "weights do not fit this network"
+        self.copy(which, 1, ts)
+
+    def copy(self, which: int, to_core: int, tensors) -> None:
+        for t in tensors:
+            if t is not None:
+                assert t.is_cuda and t.is_contiguous() and t.dtype == self.torch.float32
+        arr = (ctypes.c_void_p * 7)(*[_ptr(t) for t in tensors])
+        self.bind_stream()
+        self.L.fc_copy(self.h, which, to_core, arr)
+        self.check()
+
+    def get(self, which: int):
+        out = [self.torch.empty(n, device=self.device) for n in self.sizes]
+        self.copy(which, 0, out)
+        return out
+
+    # ---- compute
+    def forward(self, obs, ema: int = 0, out=None):
+        torch = self.torch
+        B = obs.shape[0]
+        out = torch.empty(B, self.s["n_act"], device=self.device) if out is None else out
+        self.bind_stream()
+        self.L.fc_forward(self.h, _ptr(obs), B, _ptr(out), ema)
+        self.check()
+        return out
+
+    def backward(self, dlogits) -> None:
+        self.bind_stream()
+        self.L.fc_backward(self.h, _ptr(dlogits), dlogits.shape[0])
+        self.check()
+
+    def zero_grad(self) -> None:
+        self.bind_stream()
+        self.L.fc_zero_grad(self.h)
+        self.check()
+
+    def step(self, lr, lr_neuron, lr_plug, max_norm=0.0, ema=0.999) -> float:
+        self.bind_stream()
+        g = self.L.fc_step(self.h, lr, lr_neuron, lr_plug, max_norm, ema)
+        self.check()
+        return float(g)
+
+    def grad_norm(self) -> float:
+        self.bind_stream()
+        g = self.L.fc_grad_norm(self.h)
+        self.check()
+        return float(g)
+
+    def adam_t(self, set_to: int = -1) -> int:
+        v = self.L.fc_adam_t(self.h, int(set_to))
+        self.check()
+        return int(v)
+
+    def teach(self, obs, teacher, inv_temp: float = 1.0, logits=None, stats: bool = True):
+        self.bind_stream()
+        st = (ctypes.c_double * 2)() if stats else None
+        rc = self.L.fg_teach(self.h, _ptr(obs), _ptr(teacher), obs.shape[0], float(inv_temp), _ptr(logits), st)
+        if rc:
+            self.check()
+        return (float(st[0]), float(st[1])) if stats else None
+
+    def forward_host(self, obs_host, logits_host, ema: int = 0) -> None:
+        """obs_host / logits_host: contiguous CPU tensors (pinned for overlap)."""
+        self.bind_stream()
+        rc = self.L.fg_forward_host(self.h, obs_host.data_ptr(), obs_host.shape[0], logits_host.data_ptr(), ema)
+        if rc:
+            self.check()
+
+    def layer(self, k: int, B: int):
+        rows = self.s["sizes"][k]
+        out = self.torch.empty(rows, B, device=self.device)
+        self.bind_stream()
+        if self.L.fg_layer(self.h, k, _ptr(out), B):
+            self.check()
+        return out
+
+    def launches(self) -> int:
+        return int(self.L.fg_launches(self.h))
+
+    def timing(self, on: bool) -> None:
+        if self.L.fg_timing(self.h, int(on)):
+            self.check()
+
+    def timing_read(self) -> dict:
+        """{kernel class: (milliseconds, launches)} since the last read."""
+        n = len(KERNEL_CLASSES)
+        ms, cnt = (ctypes.c_double * n)(), (ctypes.c_longlong * n)()
+        if self.L.fg_timing_read(self.h, ms, cnt, n) < 0:
+            self.check()
+        return {k: (float(ms[i]), int(cnt[i])) for i, k in enumerate(KERNEL_CLASSES)}
+
+    def sync(self) -> None:
+        self.L.fc_sync(self.h)
+        self.check()
+
+
+class _CudaArray:
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+def _wrap(ptr: int, n: int, device):
+    import torch
+    with torch.cuda.device(device):
+        return torch.as_tensor(_CudaArray(ptr, n), device=device)
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)
+
+
+def header_symbols(path: Path | None = None) -> list[str]:
+    """The entry points include/flyguy_b200.h declares."""
+    import re
+    path = path or PKG.parent / "include" / "flyguy_b200.h"
+    text = Path(path).read_text()
+    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b((?:fc|fg)_\w+)\s*\(", text, re.M)))
+
+
+def default_threads() -> int:
+    return os.cpu_count() or 1

@@ -1,0 +1,120 @@
+/* flyguy_b200 - the connectome hop path of flyguy on B200 (sm_100a), as a C-ABI shared library.
+ *
+ * libflyguy_b200.so replaces the reference's whole-network GPU library `fc_*` (adventure-gpt/flyguy,
+ * flyguy/native/flyguy_train.cu:553-629, built with -DFLYGUY_CORE, loaded by ctypes in flyguy/fly_native.py:127-159).
+ * Every fc_* entry point below keeps the reference's name, argument order and meaning, so the reference's ctypes
+ * binding loads this library by path alone. The fg_* entry points are additions (status codes instead of exiting
+ * the process, an explicit stream, bf16 activations, zero-copy gradient for the data-parallel all-reduce, the fused
+ * teaching step, host-buffer forward).
+ *
+ * Conventions (all entry points):
+ *  - Pointers named obs / logits / dlogits / teacher are DEVICE memory owned by the caller (torch tensors), fp32,
+ *    row-major [B, obs_dim] / [B, n_act], contiguous - except fg_forward_host, which takes HOST memory.
+ *  - B is a multiple of 32 and at most the max_batch given at creation.
+ *  - Work is queued on the handle's stream (fc_set_stream; default: the legacy default stream) in order; calls return
+ *    before the GPU finishes unless they return a value that needs the GPU (fc_grad_norm, fc_step with max_norm > 0,
+ *    fg_teach with stats != NULL).
+ *  - Errors never end the process: a failing call records a message in the handle, later calls on the handle
+ *    return at once, and fg_status / fg_last_error report it. A NULL handle from create: fg_last_error(NULL).
+ *  - A handle is not thread-safe; use one per thread.
+ */
+#ifndef FLYGUY_B200_H
+#define FLYGUY_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- reference-compatible entry points (flyguy/native/flyguy_train.cu) ---------------------------------------- */
+
+/* Loads NET.bin ("FLY1", flyguy/native/export.py:9-16) and allocates weights, gradient, Adam state, running average
+ * and fp32 states for batches up to max_batch. Replaces fc_create (flyguy_train.cu:569-575). NULL on failure. */
+void* fc_create(const char* net_path, int max_batch);
+
+/* out[0..6]: lengths of the seven weight arrays (W in play, gain, theta, in_w, in_b, out_w, out_b); out[7] obs_dim,
+ * out[8] n_act, out[9] max_batch. Replaces fc_sizes (flyguy_train.cu:577-581). */
+void fc_sizes(void* h, long long* out);
+
+/* which: 0 weights, 1 running average, 2 / 3 Adam's first / second moments, 4 gradient. ptrs: seven device arrays
+ * (NULL = skip). to_core 1: read them into the library; 0: write the library's arrays into them.
+ * Replaces fc_copy (flyguy_train.cu:584-589). */
+void fc_copy(void* h, int which, int to_core, float** ptrs);
+
+/* obs [B, obs_dim] -> logits [B, n_act] with the weights (ema 0) or their running average (ema 1). The states stay
+ * for fc_backward. Replaces fc_forward (flyguy_train.cu:592-598). */
+void fc_forward(void* h, const float* obs, int B, float* logits, int ema);
+
+/* gradient = 0. Replaces fc_zero_grad (flyguy_train.cu:599-602). */
+void fc_zero_grad(void* h);
+
+/* dlogits [B, n_act]: gradient of a loss w.r.t. the logits of the batch the last fc_forward(.., ema 0) went through;
+ * the weights' gradients are ADDED to the library's gradient. Replaces fc_backward (flyguy_train.cu:604-609). */
+void fc_backward(void* h, const float* dlogits, int B);
+
+/* Euclidean norm of the whole gradient (waits for the GPU). Replaces fc_grad_norm (flyguy_train.cu:610-616). */
+float fc_grad_norm(void* h);
+
+/* One Adam step (betas 0.9 / 0.999, eps 1e-8) from the gradient; strengths at lr, gain / theta at lr_neuron, plugs
+ * at lr_plug; the gradient is scaled to max_norm first if longer (0 = no clipping); the running average follows with
+ * decay `ema`. Returns the gradient norm before clipping (0 when max_norm is 0).
+ * Replaces fc_step (flyguy_train.cu:619-627). */
+float fc_step(void* h, float lr, float lr_neuron, float lr_plug, float max_norm, float ema);
+
+/* Adam's step count; set >= 0 sets it. Replaces fc_adam_t (flyguy_train.cu:628). */
+long long fc_adam_t(void* h, long long set);
+
+/* Waits for the handle's stream. Replaces fc_sync (flyguy_train.cu:629). */
+void fc_sync(void* h);
+
+/* ---- additions ------------------------------------------------------------------------------------------------ */
+
+#define FG_ACT_BF16 1     /* states stored as bf16 (fp32 accumulation, fp32 weights); forward only */
+#define FG_INFER_ONLY 2   /* no gradient / optimiser buffers: fc_backward and fc_step fail */
+
+/* fc_create with flags (FG_ACT_BF16 implies FG_INFER_ONLY). */
+void* fg_create(const char* net_path, int max_batch, int flags);
+/* Frees the handle and its device memory (the reference never frees its handle). */
+void fg_destroy(void* h);
+/* 0 = fine; otherwise the handle is in error and fg_last_error says why. */
+int fg_status(void* h);
+const char* fg_last_error(void* h);
+/* Clears a recorded error (after the caller handled it). */
+void fg_clear_error(void* h);
+/* All later work of the handle goes to this cudaStream_t (e.g. torch.cuda.current_stream().cuda_stream). */
+void fc_set_stream(void* h, void* stream);
+/* Device pointer and length of one flat array (which as in fc_copy): the seven arrays back to back in fc_sizes
+ * order. The gradient (which 4) is what a data-parallel trainer all-reduces in place before fc_step. */
+int fg_flat(void* h, int which, float** ptr, long long* n);
+/* The seven arrays' offsets into the flat arrays: off[0..7] (off[7] = total). */
+void fg_offsets(void* h, long long* off);
+/* Layer sizes: sizes[0..hops] (returns hops); merged (destination, source) pairs per hop into pairs[0..hops-1]. */
+int fg_layout(void* h, int* sizes, long long* pairs);
+
+/* The distillation step's device half, fused: forward with the weights, KL(softmax(teacher * inv_temp) ||
+ * softmax(logits)) averaged over the batch, its gradient through the network ADDED to the gradient.
+ * obs [B, obs_dim], teacher [B, n_act] device; logits [B, n_act] device or NULL. stats: host double[2] (sum of KL over
+ * the batch, number of argmax agreements), or NULL to not wait for the GPU. Returns 0 or -1 (see fg_last_error). */
+int fg_teach(void* h, const float* obs, const float* teacher, int B, float inv_temp, float* logits, double* stats);
+
+/* Forward from HOST memory: obs_host [B, obs_dim] -> logits_host [B, n_act], host<->device copies overlapped with the
+ * compute in chunks (pinned host memory makes the copies asynchronous). Waits for the result. Returns 0 or -1. */
+int fg_forward_host(void* h, const float* obs_host, int B, float* logits_host, int ema);
+
+/* Neuron-major states of layer k (0 = sensory ... hops) of the last forward: [sizes[k], B] fp32, device. */
+int fg_layer(void* h, int k, float* out, int B);
+
+/* Number of kernels this handle has launched so far. */
+long long fg_launches(void* h);
+/* on 1: every later kernel launch is bracketed by CUDA events on the handle's stream (for live per-kernel timing);
+ * on 0: stop (after reading). */
+int fg_timing(void* h, int on);
+/* Waits for the stream; sums the recorded times per kernel class into ms[0..n-1] (milliseconds) and count[0..n-1]
+ * (launches), then forgets them. Classes: 0 layout change, 1 weight folds, 2 input plug, 3 hop forward, 4 output
+ * plug, 5 loss, 6 output-plug backward, 7 neuron backward, 8 weight gradient, 9 transposed hop, 10 plug backward,
+ * 11 Adam, 12 gradient norm. Returns the number of classes. */
+int fg_timing_read(void* h, double* ms, long long* count, int n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
