@@ -41,6 +41,9 @@ WORKLOADS = {
     "infer": dict(cfg=2, batch=65536, per_gpu=False, flags="bf16", metric="decisions/sec", unit="decisions/s",
                   dtype="bf16", desc="config 2: bf16-state forward (fp32 accumulation, fp32 weights), global batch "
                                      "65,536 batch-sharded, no collective"),
+    "infer16": dict(cfg=2, batch=65536, per_gpu=False, flags="f16", metric="decisions/sec", unit="decisions/s",
+                    dtype="f16", desc="config 2 with fp16 states (the reference's 16-bit state format; fp32 "
+                                      "accumulation, fp32 weights), global batch 65,536 batch-sharded, no collective"),
     "infer32": dict(cfg=1, batch=4096, per_gpu=True, flags="fp32", metric="decisions/sec", unit="decisions/s",
                     dtype="f32", desc="config 1: fp32 forward, batch 4,096 per GPU"),
     "train": dict(cfg=3, batch=16384, per_gpu=False, flags="train", metric="train samples/sec", unit="samples/s",
@@ -60,6 +63,8 @@ def args_():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="wall time budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling of a small case only)")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -151,10 +156,11 @@ def algo_bytes(cls: str, s, B: int, act: int) -> float:
 def run_ours(a, W, rank, world, dev, torch, dist):
     from flyguy_b200 import native, synth
     s, P = synth.make_synthetic()
-    Bg = W["batch"] * (world if W["per_gpu"] else 1)
+    Bg = (a.batch or W["batch"]) * (world if W["per_gpu"] else 1)
     B = Bg // world
     assert B % 32 == 0 and B * world == Bg, "the batch must split into multiples of 32"
-    flags = {"bf16": native.FG_ACT_BF16, "fp32": native.FG_INFER_ONLY, "train": 0}[W["flags"]]
+    flags = {"bf16": native.FG_ACT_BF16, "f16": native.FG_ACT_F16, "fp32": native.FG_INFER_ONLY,
+             "train": 0}[W["flags"]]
     h = native.Handle(s, B, flags, device=dev)
     h.set_params(P, 0)
     h.set_params(P, 1)
@@ -214,7 +220,7 @@ def run_ours(a, W, rank, world, dev, torch, dist):
     # ---- roofline of the dominant kernel class
     kern_step = {k: (ms / a.steps, n // a.steps) for k, (ms, n) in kern.items() if n}
     dom = max(kern_step, key=lambda k: kern_step[k][0])
-    act = 2 if W["flags"] == "bf16" else 4
+    act = 2 if W["flags"] in ("bf16", "f16") else 4
     byts = algo_bytes(dom, s, B, act)
     peak, peak_src = peaks()
     achieved = byts / (kern_step[dom][0] / 1e3) / 1e9 if byts else None
@@ -231,7 +237,8 @@ def run_ours(a, W, rank, world, dev, torch, dist):
     step_roof = {"bytes_per_unit": round(per_unit, 1), "achieved_gbs_per_gpu": round(per_unit * value / world / 1e9, 1),
                  "frac": round(per_unit * value / world / 1e9 / peak, 4)}
     # ---- e2e through the host-buffer entry points
-    e2e = run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier, max_over_ranks, grad)
+    e2e = None if a.no_e2e else run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier,
+                                          max_over_ranks, grad)
     # ---- CPU baseline (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:

@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstring>
 #include <numeric>
+#include <type_traits>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -36,8 +37,13 @@ struct Hop {
     bool widx_unique = true, redrive = false;
     int *d_nid = nullptr, *d_drow = nullptr, *d_sched = nullptr, *d_pptr = nullptr;
     int *d_tsched = nullptr, *d_tptr = nullptr;
+    int4 *d_segs = nullptr, *d_reds = nullptr;   // transposed product: segments of source rows, split-row reductions
+    int n_segs = 0, n_reds = 0, n_slots = 0;
     void* d_h = nullptr;                     // states [rows, ld]
+    bool out_f32 = false;                    // this hop's layer is stored in fp32 (the last layer always is)
 };
+
+constexpr int kSegLen = 512;                 // pairs per transposed segment
 
 // kernel classes timed by fg_timing (CUDA events around every launch of the class, on the handle's stream)
 enum KClass { K_TRANSPOSE, K_FOLD, K_PLUG_FWD, K_HOP_FWD, K_OUT_FWD, K_LOSS, K_OUT_BWD, K_ACT_BWD, K_SDDMM, K_HOP_BWD,
@@ -55,7 +61,9 @@ struct Core {
     int obs_dim = 0, n_act = 0, hops = 0, n_neurons = 0, n_w = 0, n_s = 0, fan = 0, n_dn = 0;
     std::vector<int> sizes;
     int maxB = 0, flags = 0;
-    bool bf16 = false, train = true, redrive = false;
+    bool bf16 = false, f16 = false, train = true, redrive = false;
+    float* owT = nullptr;                                // out_w transposed, padded to kOutA actions
+    float* seg_part = nullptr;                           // partial rows of split transposed segments
     int *d_in_crow = nullptr, *d_in_col = nullptr, *d_n0 = nullptr, *d_dn = nullptr;
     std::vector<Hop> hop;
     long long R = 0, Ptot = 0, Etot = 0;
@@ -197,6 +205,22 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
     std::iota(tsched.begin(), tsched.end(), 0);
     std::stable_sort(tsched.begin(), tsched.end(),
                      [&](int a, int b) { return tptr[a + 1] - tptr[a] > tptr[b + 1] - tptr[b]; });
+    std::vector<int4> segs, reds;
+    for (int s = 0; s < h.n_src; ++s) {
+        const int n = tptr[s + 1] - tptr[s];
+        if (n <= kSegLen) { segs.push_back(make_int4(s, tptr[s], tptr[s + 1], -1)); continue; }
+        const int nseg = (n + kSegLen - 1) / kSegLen;
+        reds.push_back(make_int4(s, h.n_slots, nseg, 0));
+        for (int i = 0; i < nseg; ++i)
+            segs.push_back(make_int4(s, tptr[s] + i * kSegLen, std::min(tptr[s + 1], tptr[s] + (i + 1) * kSegLen),
+                                     h.n_slots + i));
+        h.n_slots += nseg;
+    }
+    std::stable_sort(segs.begin(), segs.end(), [](const int4& a, const int4& b) { return a.z - a.y > b.z - b.y; });
+    h.n_segs = (int)segs.size();
+    h.n_reds = (int)reds.size();
+    h.d_segs = upload(c, segs);
+    h.d_reds = upload(c, reds);
     h.d_pptr = upload(c, pptr);
     h.d_sched = upload(c, sched);
     h.d_tptr = upload(c, tptr);
@@ -231,6 +255,7 @@ NetHost parse_net(Core& c, const char* path) {
     if (c.obs_dim <= 0 || c.n_act <= 0 || c.n_act > kMaxAct || c.hops <= 0 || c.hops > 32 || c.n_neurons <= 0 ||
         c.n_w < 0 || c.n_s <= 0 || c.fan < 0 || c.n_dn <= 0)
         throw Err("NET.bin: bad header");
+    if ((long long)c.obs_dim * kPlugCols * 4 > 220 * 1024) throw Err("obs_dim too large for the plug's staging");
     NetHost n;
     c.sizes = r.take(c.hops + 1, "sizes");
     n.E = r.take(c.hops, "edge counts");
@@ -306,7 +331,7 @@ void upload_net(Core& c, NetHost& n) {
     c.d_tpi = upload(c, tpi);
 }
 
-size_t act_bytes(const Core& c) { return c.bf16 ? 2 : 4; }
+size_t act_bytes(const Core& c) { return (c.bf16 || c.f16) ? 2 : 4; }
 
 void alloc_all(Core& c) {
     const long long ps[7] = {c.n_w, c.n_neurons, c.n_neurons, (long long)c.n_s * c.fan, c.n_s,
@@ -328,7 +353,12 @@ void alloc_all(Core& c) {
     c.x = dalloc<float>(c, (size_t)c.obs_dim * B);
     if (c.train || c.redrive) c.drive = dalloc<float>(c, (size_t)c.n_s * B);
     c.h0 = dalloc<char>(c, (size_t)c.n_s * B * act_bytes(c));
-    for (auto& h : c.hop) h.d_h = dalloc<char>(c, (size_t)h.rows * B * act_bytes(c));
+    for (size_t k = 0; k < c.hop.size(); ++k) {
+        Hop& h = c.hop[k];
+        h.out_f32 = act_bytes(c) == 4 || k + 1 == c.hop.size();
+        h.d_h = dalloc<char>(c, (size_t)h.rows * B * (h.out_f32 ? 4 : act_bytes(c)));
+    }
+    c.owT = dalloc<float>(c, (size_t)c.n_dn * kOutA);
     c.lg = dalloc<float>(c, (size_t)c.n_act * B);
     c.norm_part = dalloc<float>(c, 1024);
     c.norm = dalloc<float>(c, 4);
@@ -343,14 +373,28 @@ void alloc_all(Core& c) {
         c.out_splits = std::max(1, std::min(64, (int)((B + 1023) / 1024)));
         c.part = dalloc<float>(c, (size_t)c.out_splits * c.n_act * (c.n_dn + 1));
         c.kl_s = dalloc<float>(c, B);
+        int slots = 0;
+        for (auto& h : c.hop) slots = std::max(slots, h.n_slots);
+        c.seg_part = dalloc<float>(c, (size_t)slots * B);
         c.ag_s = dalloc<float>(c, B);
     }
 }
 
+int plug_smem(const Core& c) { return c.obs_dim * kPlugCols * 4; }
+
+template <class T>
+void plug_limits(int smem) {
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+}
+
 void set_smem_limits(const Core& c) {
-    const int smem = (32 * c.n_act + 128 * (c.n_act + 1)) * 4;
-    CK(cudaFuncSetAttribute(k_out_fwd<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    CK(cudaFuncSetAttribute(k_out_fwd<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    const int smem = plug_smem(c);
+    plug_limits<float>(smem);
+    plug_limits<__nv_bfloat16>(smem);
+    plug_limits<__half>(smem);
 }
 
 inline unsigned blocks(long long n, int t = 256) { return (unsigned)((n + t - 1) / t); }
@@ -365,6 +409,8 @@ void fold(Core& c, int which) {
         launch(c, K_FOLD, [&]() { k_fold_pairs<<<blocks(c.Ptot), 256, 0, c.st>>>(c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, (int)c.Ptot); });
         launch(c, K_FOLD, [&]() { k_fold_tpairs<<<blocks(c.Ptot), 256, 0, c.st>>>(c.d_tpi, c.d_pairs, c.d_tpairs, (int)c.Ptot); });
     }
+    launch(c, K_FOLD, [&]() { k_fold_owT<<<blocks((long long)c.n_dn * kOutA), 256, 0, c.st>>>(src + c.off[5], c.owT,
+                                                                                         c.n_act, c.n_dn); });
     c.folded = which;
 }
 
@@ -374,39 +420,66 @@ void check_batch(const Core& c, int B) {
                   std::to_string(c.maxB));
 }
 
-// obs_nm: already neuron-major in c.x when obs == nullptr
+template <class T, bool SAVE>
+void plug_launch(Core& c, const float* Pw, int B) {
+    const dim3 g((c.n_s + kPlugRows - 1) / kPlugRows, (B + kPlugCols - 1) / kPlugCols);
+    const bool vec4 = c.fan % 4 == 0;
+    launch(c, K_PLUG_FWD, [&]() {
+        if (vec4)
+            k_plug_fwd<T, SAVE, true><<<g, kPlugThreads, plug_smem(c), c.st>>>(
+                c.d_in_crow, c.d_in_col, Pw + c.off[3], Pw + c.off[4], c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0,
+                c.n_s, c.obs_dim, B);
+        else
+            k_plug_fwd<T, SAVE, false><<<g, kPlugThreads, plug_smem(c), c.st>>>(
+                c.d_in_crow, c.d_in_col, Pw + c.off[3], Pw + c.off[4], c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0,
+                c.n_s, c.obs_dim, B);
+    });
+}
+
+template <class TI, class TO>
+void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
+    constexpr int V = Act<TI>::V;
+    const dim3 g((h.rows + kWarps - 1) / kWarps, (unsigned)((B + 32 * V - 1) / (32 * V)));
+    launch(c, K_HOP_FWD, [&]() {
+        k_hop_fwd<TI, TO><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase, (const TI*)hp,
+                                                    c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive,
+                                                    (TO*)h.d_h, h.rows, B);
+    });
+}
+
+// obs == nullptr: the states start from c.x as it is
 template <class T>
 void forward_t(Core& c, const float* obs, int B, float* logits, int ema, bool keep_lg) {
-    constexpr int V = Act<T>::V;
     fold(c, ema ? 1 : 0);
     const float* Pw = ema ? c.EMA : c.P;
     if (obs) {
-        launch(c, K_TRANSPOSE, [&]() { k_to_neuron_major<<<dim3((B + 31) / 32, (c.obs_dim + 31) / 32), dim3(32, 8), 0, c.st>>>(obs, c.x, c.obs_dim, B, B); });
+        launch(c, K_TRANSPOSE, [&]() {
+            k_to_neuron_major<<<dim3((B + 31) / 32, (c.obs_dim + 31) / 32), dim3(32, 8), 0, c.st>>>(obs, c.x, c.obs_dim,
+                                                                                                B, B);
+        });
     }
-    const unsigned chunks = (unsigned)((B + 32 * V - 1) / (32 * V));
-    const dim3 g0((c.n_s + kWarps - 1) / kWarps, chunks);
-    if (c.drive)
-        launch(c, K_PLUG_FWD, [&]() { k_plug_fwd<T, true><<<g0, kThreads, 0, c.st>>>(c.d_in_crow, c.d_in_col, Pw + c.off[3], Pw + c.off[4], c.d_rgain,
-                                                       c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, B); });
-    else
-        launch(c, K_PLUG_FWD, [&]() { k_plug_fwd<T, false><<<g0, kThreads, 0, c.st>>>(c.d_in_crow, c.d_in_col, Pw + c.off[3], Pw + c.off[4],
-                                                        c.d_rgain, c.d_rthr, c.x, nullptr, (T*)c.h0, c.n_s, B); });
-    const T* hp = (const T*)c.h0;
+    if (c.drive) plug_launch<T, true>(c, Pw, B);
+    else plug_launch<T, false>(c, Pw, B);
+    const void* hp = c.h0;
+    bool hp_f32 = std::is_same<T, float>::value;
     for (auto& h : c.hop) {
-        const dim3 g((h.rows + kWarps - 1) / kWarps, chunks);
-        launch(c, K_HOP_FWD, [&]() { k_hop_fwd<T><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase, hp, c.d_rgain + h.rbase,
-                                               c.d_rthr + h.rbase, h.d_drow, c.drive, (T*)h.d_h, h.rows, B); });
-        hp = (const T*)h.d_h;
+        if (hp_f32) hop_launch<float, float>(c, h, hp, B);
+        else if (h.out_f32) hop_launch<T, float>(c, h, hp, B);
+        else hop_launch<T, T>(c, h, hp, B);
+        hp = h.d_h;
+        hp_f32 = h.out_f32;
     }
-    const int groups = (c.n_act + kActGroup - 1) / kActGroup;
-    const int smem = (32 * c.n_act + 128 * (c.n_act + 1)) * 4;
-    launch(c, K_OUT_FWD, [&]() { k_out_fwd<T><<<(B + 127) / 128, 128 * groups, smem, c.st>>>(Pw + c.off[5], Pw + c.off[6], c.d_dn, hp,
-                                                                 keep_lg ? c.lg : nullptr, logits, c.n_act, c.n_dn, B, B); });
+    launch(c, K_OUT_FWD, [&]() {
+        k_out_fwd<float><<<(B + kOutB - 1) / kOutB, 256, 0, c.st>>>(c.owT, Pw + c.off[6], c.d_dn, (const float*)hp,
+                                                                  keep_lg ? c.lg : nullptr, logits, c.n_act, c.n_dn, B,
+                                                                  B);
+    });
     c.lastB = B;
 }
 
 void forward(Core& c, const float* obs, int B, float* logits, int ema, bool keep_lg) {
     if (c.bf16) forward_t<__nv_bfloat16>(c, obs, B, logits, ema, keep_lg);
+    else if (c.f16) forward_t<__half>(c, obs, B, logits, ema, keep_lg);
     else forward_t<float>(c, obs, B, logits, ema, keep_lg);
 }
 
@@ -444,11 +517,18 @@ void backward(Core& c, int B) {
         else
             launch(c, K_SDDMM, [&]() { k_sddmm<float, true><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase,
                                                                 c.d_gw, c.gz, hprev, c.live, c.G + c.off[0], B, B); });
-        launch(c, K_HOP_BWD, [&]() { k_hop_bwd_t<<<dim3((h.n_src + kWarps - 1) / kWarps, (B + 127) / 128), kThreads, 0, c.st>>>(
-            h.d_tsched, h.d_tptr, c.d_tpairs + h.pbase, c.gz, gh_next, h.n_src, B); });
+        launch(c, K_HOP_BWD, [&]() {
+            k_hop_bwd_t<<<dim3((h.n_segs + kWarps - 1) / kWarps, (B + 127) / 128), kThreads, 0, c.st>>>(
+                h.d_segs, c.d_tpairs + h.pbase, c.gz, gh_next, c.seg_part, h.n_segs, B);
+        });
+        if (h.n_reds)
+            launch(c, K_HOP_BWD, [&]() {
+                k_seg_reduce<<<dim3((h.n_reds + kWarps - 1) / kWarps, (B + 127) / 128), kThreads, 0, c.st>>>(
+                    h.d_reds, c.seg_part, gh_next, h.n_reds, B);
+            });
         std::swap(gh, gh_next);
     }
-    launch(c, K_PLUG_BWD, [&]() { k_plug_bwd<float><<<c.n_s, kThreads, 0, c.st>>>(gh, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_crow,
+    launch(c, K_PLUG_BWD, [&]() { k_plug_bwd<<<c.n_s, kThreads, 0, c.st>>>(gh, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_crow,
                                                     c.d_in_col, c.x, c.d_rgain, c.d_rsig, c.G + c.off[1],
                                                     c.G + c.off[2], c.G + c.off[3], c.G + c.off[4], B, B); });
 }
@@ -512,7 +592,8 @@ void* create(const char* path, int max_batch, int flags) {
         c->maxB = max_batch;
         c->flags = flags;
         c->bf16 = flags & FG_ACT_BF16;
-        c->train = !(flags & (FG_ACT_BF16 | FG_INFER_ONLY));
+        c->f16 = (flags & FG_ACT_F16) && !c->bf16;
+        c->train = !(flags & (FG_ACT_BF16 | FG_ACT_F16 | FG_INFER_ONLY));
         NetHost n = parse_net(*c, path);     // (a bad file fails here, before the GPU is touched)
         CK(cudaGetDevice(&c->device));
         upload_net(*c, n);
@@ -781,7 +862,16 @@ int fg_layer(void* h, int k, float* out, int B) {
         if (B != c.lastB) throw Err("fg_layer: batch differs from the last forward's");
         const void* src = k ? c.hop[k - 1].d_h : c.h0;
         const size_t n = (size_t)c.sizes[k] * B;
-        if (!c.bf16) {
+        const bool f32 = act_bytes(c) == 4 || (k > 0 && c.hop[k - 1].out_f32);
+        if (!f32 && c.f16) {
+            std::vector<__half> hb(n);
+            CK(cudaMemcpyAsync(hb.data(), src, n * 2, cudaMemcpyDeviceToHost, c.st));
+            CK(cudaStreamSynchronize(c.st));
+            std::vector<float> tmp(n);
+            for (size_t i = 0; i < n; ++i) tmp[i] = __half2float(hb[i]);
+            CK(cudaMemcpyAsync(out, tmp.data(), n * 4, cudaMemcpyHostToDevice, c.st));
+            CK(cudaStreamSynchronize(c.st));
+        } else if (f32) {
             CK(cudaMemcpyAsync(out, src, n * 4, cudaMemcpyDeviceToDevice, c.st));
         } else {
             std::vector<float> tmp;   // small layers in tests only: convert on the host

@@ -8,6 +8,7 @@
 // fixed order - no float atomics, bit-reproducible for a given batch.
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -19,6 +20,7 @@ constexpr int kThreads = 32 * kWarps;
 template <class T> struct Act;
 template <> struct Act<float> { static constexpr int V = 4; };
 template <> struct Act<__nv_bfloat16> { static constexpr int V = 8; };
+template <> struct Act<__half> { static constexpr int V = 8; };
 
 // ---- 16-byte vector loads / stores of V activations as fp32
 __device__ __forceinline__ void ld_act(const float* p, float (&v)[4]) {
@@ -33,6 +35,15 @@ __device__ __forceinline__ void ld_act(const __nv_bfloat16* p, float (&v)[8]) {
     v[4] = __uint_as_float(q.z << 16); v[5] = __uint_as_float(q.z & 0xffff0000u);
     v[6] = __uint_as_float(q.w << 16); v[7] = __uint_as_float(q.w & 0xffff0000u);
 }
+__device__ __forceinline__ void ld_act(const __half* p, float (&v)[8]) {
+    uint4 q = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        v[2 * i] = f.x; v[2 * i + 1] = f.y;
+    }
+}
 __device__ __forceinline__ void st_act(float* p, const float (&v)[4]) {
     *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
 }
@@ -46,7 +57,37 @@ __device__ __forceinline__ void st_act(__nv_bfloat16* p, const float (&v)[8]) {
     q.z = pack_bf16(v[4], v[5]); q.w = pack_bf16(v[6], v[7]);
     *reinterpret_cast<uint4*>(p) = q;
 }
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+    __half2 b = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&b);
+}
+__device__ __forceinline__ void st_act(__half* p, const float (&v)[8]) {
+    uint4 q;
+    q.x = pack_f16(v[0], v[1]); q.y = pack_f16(v[2], v[3]);
+    q.z = pack_f16(v[4], v[5]); q.w = pack_f16(v[6], v[7]);
+    *reinterpret_cast<uint4*>(p) = q;
+}
+// V fp32 values stored as the layer's type (V = that type's vector width)
+template <class TO, int V>
+__device__ __forceinline__ void st_vals(TO* p, const float (&v)[V]);
+template <>
+__device__ __forceinline__ void st_vals<float, 8>(float* p, const float (&v)[8]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+template <>
+__device__ __forceinline__ void st_vals<float, 4>(float* p, const float (&v)[4]) { st_act(p, v); }
+template <>
+__device__ __forceinline__ void st_vals<__nv_bfloat16, 8>(__nv_bfloat16* p, const float (&v)[8]) { st_act(p, v); }
+template <>
+__device__ __forceinline__ void st_vals<__half, 8>(__half* p, const float (&v)[8]) { st_act(p, v); }
+__device__ __forceinline__ void store2(float* p, float a, float b) { *reinterpret_cast<float2*>(p) = make_float2(a, b); }
+__device__ __forceinline__ void store2(__nv_bfloat16* p, float a, float b) {
+    *reinterpret_cast<uint32_t*>(p) = pack_bf16(a, b);
+}
+__device__ __forceinline__ void store2(__half* p, float a, float b) { *reinterpret_cast<uint32_t*>(p) = pack_f16(a, b); }
 __device__ __forceinline__ float ld1(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float ld1(const __half* p) { return __half2float(*p); }
 __device__ __forceinline__ float ld1(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(expf(x)); }
@@ -107,6 +148,14 @@ __global__ void k_fold_tpairs(const int* __restrict__ tpi, const int2* __restric
     tpairs[q].y = pairs[tpi[q]].y;
 }
 
+// out_w [n_act][n_dn] -> owT [n_dn][kOutA] (actions padded with zeros), the output plug's operand layout
+__global__ void k_fold_owT(const float* __restrict__ ow, float* __restrict__ owT, int n_act, int n_dn) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_dn * 96) return;
+    int j = i / 96, a = i - j * 96;
+    owT[i] = a < n_act ? ow[(size_t)a * n_dn + j] : 0.f;
+}
+
 // ---------------------------------------------------------------- layout changes at the API boundary
 // in [B, D] (sample-major, the caller's) -> out [D, ld] (neuron-major); 32x32 tiles through shared memory
 __global__ void k_to_neuron_major(const float* __restrict__ in, float* __restrict__ out, int D, int B, int ld) {
@@ -125,55 +174,76 @@ __global__ void k_to_neuron_major(const float* __restrict__ in, float* __restric
 
 // ---------------------------------------------------------------- forward
 // input plug + sensory activation: drive[s,b] = in_b[s] + sum_j in_w[s*fan+j] * x[col, b];
-// h0 = relu(gain*drive - thr). One warp per (row, 32V-sample chunk).
-template <class T, bool SAVE_DRIVE>
-__global__ void __launch_bounds__(kThreads) k_plug_fwd(const int* __restrict__ in_crow, const int* __restrict__ in_col,
-                                                       const float* __restrict__ in_w, const float* __restrict__ in_b,
-                                                       const float* __restrict__ rgain, const float* __restrict__ rthr,
-                                                       const float* __restrict__ x, float* __restrict__ drive,
-                                                       T* __restrict__ h0, int n_s, int ld) {
-    constexpr int V = Act<T>::V;
-    const int row = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (row >= n_s) return;
-    const int c = (blockIdx.y * 32 + lane) * V;
-    if (c >= ld) return;
-    float acc[V];
-    const float bias = __ldg(&in_b[row]);
+// h0 = relu(gain*drive - thr). A CTA stages x for 64 samples (all obs_dim rows, fp32) in shared memory once and
+// computes a range of kPlugRows sensory rows from it; lane l of a warp owns samples 2l, 2l+1.
+constexpr int kPlugCols = 64, kPlugRows = 1024, kPlugThreads = 512;
+template <class T, bool SAVE_DRIVE, bool VEC4>
+__global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict__ in_crow,
+                                                           const int* __restrict__ in_col,
+                                                           const float* __restrict__ in_w,
+                                                           const float* __restrict__ in_b,
+                                                           const float* __restrict__ rgain,
+                                                           const float* __restrict__ rthr, const float* __restrict__ x,
+                                                           float* __restrict__ drive, T* __restrict__ h0, int n_s,
+                                                           int obs_dim, int ld) {
+    extern __shared__ float xs[];                         // [obs_dim][kPlugCols]
+    const int b0 = blockIdx.y * kPlugCols;
+    const int nb = min(kPlugCols, ld - b0);
+    for (int i = threadIdx.x; i < obs_dim * (kPlugCols / 4); i += blockDim.x) {
+        const int f = i / (kPlugCols / 4), q = (i - f * (kPlugCols / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (q < nb) v = __ldg(reinterpret_cast<const float4*>(x + (size_t)f * ld + b0 + q));
+        *reinterpret_cast<float4*>(xs + f * kPlugCols + q) = v;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r_lo = blockIdx.x * kPlugRows, r_hi = min(n_s, r_lo + kPlugRows);
+    const int bl = 2 * lane;
+    if (bl >= nb) return;
+    for (int row = r_lo + warp; row < r_hi; row += kPlugThreads / 32) {
+        const float bias = __ldg(&in_b[row]);
+        float a0 = bias, a1 = bias;
+        const int e0 = __ldg(&in_crow[row]), e1 = __ldg(&in_crow[row + 1]);
+        if (VEC4) {
+            for (int e = e0; e < e1; e += 4) {
+                const int4 cc = __ldg(reinterpret_cast<const int4*>(in_col + e));
+                const float4 ww = __ldg(reinterpret_cast<const float4*>(in_w + e));
+                const int cs[4] = {cc.x, cc.y, cc.z, cc.w};
+                const float ws[4] = {ww.x, ww.y, ww.z, ww.w};
 #pragma unroll
-    for (int i = 0; i < V; ++i) acc[i] = bias;
-    const int e1 = in_crow[row + 1];
-    for (int e = in_crow[row]; e < e1; ++e) {
-        const float w = __ldg(&in_w[e]);
-        const float* xs = x + (size_t)__ldg(&in_col[e]) * ld + c;
-#pragma unroll
-        for (int i = 0; i < V; i += 4) {
-            float4 q = __ldg(reinterpret_cast<const float4*>(xs + i));
-            acc[i] = fmaf(w, q.x, acc[i]); acc[i + 1] = fmaf(w, q.y, acc[i + 1]);
-            acc[i + 2] = fmaf(w, q.z, acc[i + 2]); acc[i + 3] = fmaf(w, q.w, acc[i + 3]);
+                for (int u = 0; u < 4; ++u) {
+                    const float2 xv = *reinterpret_cast<const float2*>(xs + cs[u] * kPlugCols + bl);
+                    a0 = fmaf(ws[u], xv.x, a0);
+                    a1 = fmaf(ws[u], xv.y, a1);
+                }
+            }
+        } else {
+            for (int e = e0; e < e1; ++e) {
+                const int cc = __ldg(&in_col[e]);
+                const float ww = __ldg(&in_w[e]);
+                const float2 xv = *reinterpret_cast<const float2*>(xs + cc * kPlugCols + bl);
+                a0 = fmaf(ww, xv.x, a0);
+                a1 = fmaf(ww, xv.y, a1);
+            }
         }
+        const size_t o = (size_t)row * ld + b0 + bl;
+        if (SAVE_DRIVE) *reinterpret_cast<float2*>(drive + o) = make_float2(a0, a1);
+        const float g = __ldg(&rgain[row]), th = __ldg(&rthr[row]);
+        const float v0 = fmaxf(fmaf(g, a0, -th), 0.f), v1 = fmaxf(fmaf(g, a1, -th), 0.f);
+        store2(h0 + o, v0, v1);
     }
-    const size_t o = (size_t)row * ld + c;
-    if (SAVE_DRIVE) {
-#pragma unroll
-        for (int i = 0; i < V; i += 4)
-            *reinterpret_cast<float4*>(drive + o + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-    }
-    const float g = __ldg(&rgain[row]), th = __ldg(&rthr[row]);
-    float hv[V];
-#pragma unroll
-    for (int i = 0; i < V; ++i) hv[i] = fmaxf(fmaf(g, acc[i], -th), 0.f);
-    st_act(h0 + o, hv);
 }
 
 // one hop: z[t,b] = sum over merged pairs (src, w) of row t of w * hp[src, b] (+ drive[drow[t], b]);
 // h = relu(gain*z - thr). One warp per (row, 32V-sample chunk); rows in degree-descending schedule order.
-template <class T>
+// TI: the source layer's type, TO: this layer's (the last layer of a 16-bit network is fp32).
+template <class TI, class TO>
 __global__ void __launch_bounds__(kThreads) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
-                                                      const int2* __restrict__ pairs, const T* __restrict__ hp,
+                                                      const int2* __restrict__ pairs, const TI* __restrict__ hp,
                                                       const float* __restrict__ rgain, const float* __restrict__ rthr,
                                                       const int* __restrict__ drow, const float* __restrict__ drive,
-                                                      T* __restrict__ h, int n_rows, int ld) {
-    constexpr int V = Act<T>::V;
+                                                      TO* __restrict__ h, int n_rows, int ld) {
+    constexpr int V = Act<TI>::V;
     const int slot = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (slot >= n_rows) return;
     const int t = __ldg(&sched[slot]);
@@ -183,7 +253,7 @@ __global__ void __launch_bounds__(kThreads) k_hop_fwd(const int* __restrict__ sc
 #pragma unroll
     for (int i = 0; i < V; ++i) acc[i] = 0.f;
     const int e0 = __ldg(&pptr[t]), e1 = __ldg(&pptr[t + 1]);
-    const T* base = hp + c;
+    const TI* base = hp + c;
     int e = e0;
     for (; e + 4 <= e1; e += 4) {                        // four pairs in flight
         int2 p[4];
@@ -222,67 +292,99 @@ __global__ void __launch_bounds__(kThreads) k_hop_fwd(const int* __restrict__ sc
     float hv[V];
 #pragma unroll
     for (int i = 0; i < V; ++i) hv[i] = fmaxf(fmaf(g, acc[i], -th), 0.f);
-    st_act(h + (size_t)t * ld + c, hv);
+    st_vals<TO, V>(h + (size_t)t * ld + c, hv);
 }
 
-// output plug: logits[a,b] = out_b[a] + sum_j out_w[a,j] * hK[dn[j], b]. A CTA owns 128 samples; its threads
-// split the actions into groups of kActGroup; out_w is staged transposed through shared memory 32 columns at a time.
-// Writes the neuron-major copy lg [n_act, ld] (for the loss) and/or the caller's [B, n_act] rows.
-constexpr int kActGroup = 48;
+// output plug: logits[a,b] = out_b[a] + sum_j out_w[a,j] * hK[dn[j], b], a register-blocked product: a CTA owns
+// 96 actions x 128 samples, each thread 6 actions x 8 samples; owT is out_w transposed and padded to 96 actions
+// ([n_dn][96], refreshed with the weights), staged with hK 32 columns at a time. Writes the neuron-major copy
+// lg [n_act, ld] (for the loss) and/or the caller's rows out [B, n_act].
+constexpr int kOutA = 96, kOutB = 128, kOutK = 32;
 template <class T>
-__global__ void __launch_bounds__(256) k_out_fwd(const float* __restrict__ ow, const float* __restrict__ ob,
+__global__ void __launch_bounds__(256) k_out_fwd(const float* __restrict__ owT, const float* __restrict__ ob,
                                                  const int* __restrict__ dn, const T* __restrict__ hK,
                                                  float* __restrict__ lg, float* __restrict__ out, int n_act, int n_dn,
                                                  int B, int ld) {
-    extern __shared__ float sm[];                         // wT[32][n_act] then stage[128][n_act+1]
-    float* wT = sm;
-    float* stage = sm + 32 * n_act;
-    const int groups = (n_act + kActGroup - 1) / kActGroup;
-    const int tb = threadIdx.x & 127, grp = threadIdx.x >> 7;
-    const int b = blockIdx.x * 128 + tb;
-    const int a0 = grp * kActGroup;
-    const bool on = grp < groups && b < B;
-    float acc[kActGroup];
+    __shared__ __align__(16) float sm[kOutK * kOutA + kOutK * kOutB];   // 28 KB; reused for the output rows
+    float* Ws = sm;
+    float* Hs = sm + kOutK * kOutA;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int b0 = blockIdx.x * kOutB;
+    float acc[6][8];
 #pragma unroll
-    for (int i = 0; i < kActGroup; ++i) acc[i] = (a0 + i < n_act) ? __ldg(&ob[a0 + i]) : 0.f;
-    for (int j0 = 0; j0 < n_dn; j0 += 32) {
-        const int nj = min(32, n_dn - j0);
+    for (int i = 0; i < 6; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int k0 = 0; k0 < n_dn; k0 += kOutK) {
+        const int nk = min(kOutK, n_dn - k0);
         __syncthreads();
-        for (int i = threadIdx.x; i < 32 * n_act; i += blockDim.x) {
-            int jj = i / n_act, a = i - jj * n_act;
-            wT[i] = jj < nj ? __ldg(&ow[(size_t)a * n_dn + j0 + jj]) : 0.f;
+        for (int i = threadIdx.x; i < kOutK * kOutA / 4; i += 256) {
+            const int k = i / (kOutA / 4);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (k < nk) v = __ldg(reinterpret_cast<const float4*>(owT + (size_t)(k0 + k) * kOutA) + (i - k * (kOutA / 4)));
+            reinterpret_cast<float4*>(Ws)[i] = v;
+        }
+        for (int i = threadIdx.x; i < kOutK * kOutB; i += 256) {
+            const int k = i / kOutB, b = i - k * kOutB;
+            Hs[i] = (k < nk && b0 + b < B) ? ld1(hK + (size_t)__ldg(&dn[k0 + k]) * ld + b0 + b) : 0.f;
         }
         __syncthreads();
-        if (on) {
-            for (int jj = 0; jj < nj; ++jj) {
-                const float hv = ld1(hK + (size_t)__ldg(&dn[j0 + jj]) * ld + b);
-                const float* w = wT + jj * n_act + a0;
-                if (a0 + kActGroup <= n_act) {
+#pragma unroll 4
+        for (int k = 0; k < kOutK; ++k) {
+            const float4 h0 = *reinterpret_cast<const float4*>(Hs + k * kOutB + tx * 8);
+            const float4 h1 = *reinterpret_cast<const float4*>(Hs + k * kOutB + tx * 8 + 4);
+            const float2 w01 = *reinterpret_cast<const float2*>(Ws + k * kOutA + ty * 6);
+            const float2 w23 = *reinterpret_cast<const float2*>(Ws + k * kOutA + ty * 6 + 2);
+            const float2 w45 = *reinterpret_cast<const float2*>(Ws + k * kOutA + ty * 6 + 4);
+            const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            const float wv[6] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y};
 #pragma unroll
-                    for (int i = 0; i < kActGroup; ++i) acc[i] = fmaf(w[i], hv, acc[i]);
-                } else {
+            for (int i = 0; i < 6; ++i)
 #pragma unroll
-                    for (int i = 0; i < kActGroup; ++i) if (a0 + i < n_act) acc[i] = fmaf(w[i], hv, acc[i]);
-                }
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(wv[i], hv[j], acc[i][j]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+        const int a = ty * 6 + i;
+        const float bias = a < n_act ? __ldg(&ob[a]) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] += bias;
+    }
+    if (lg) {
+#pragma unroll
+        for (int i = 0; i < 6; ++i) {
+            const int a = ty * 6 + i;
+            if (a >= n_act) continue;
+            float* row = lg + (size_t)a * ld + b0 + tx * 8;
+            if (b0 + tx * 8 + 8 <= B) {
+                *reinterpret_cast<float4*>(row) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+                *reinterpret_cast<float4*>(row + 4) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+            } else {
+                for (int j = 0; j < 8; ++j) if (b0 + tx * 8 + j < B) row[j] = acc[i][j];
             }
         }
     }
-    if (lg && on) {
-#pragma unroll
-        for (int i = 0; i < kActGroup; ++i) if (a0 + i < n_act) lg[(size_t)(a0 + i) * ld + b] = acc[i];
-    }
-    if (out) {
+    if (out) {                                            // [128 samples][n_act] rows, staged for coalesced stores
         __syncthreads();
-        if (grp < groups) {
+        float* st = sm;                                   // needs kOutB * (kOutA + 1) floats: reuse + spill below
+        const int stride = kOutA + 1;
+        for (int half = 0; half < 2; ++half) {            // 64 samples at a time fit the 28 KB buffer
+            __syncthreads();
+            if ((tx >> 3) == half) {
 #pragma unroll
-            for (int i = 0; i < kActGroup; ++i) if (a0 + i < n_act) stage[tb * (n_act + 1) + a0 + i] = acc[i];
-        }
-        __syncthreads();
-        const int nb = min(128, B - blockIdx.x * 128);
-        float* o = out + (size_t)blockIdx.x * 128 * n_act;
-        for (int i = threadIdx.x; i < nb * n_act; i += blockDim.x) {
-            int bb = i / n_act, a = i - bb * n_act;
-            o[i] = stage[bb * (n_act + 1) + a];
+                for (int i = 0; i < 6; ++i)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) st[((tx & 7) * 8 + j) * stride + ty * 6 + i] = acc[i][j];
+            }
+            __syncthreads();
+            const int sb = b0 + half * 64;
+            const int nbb = max(0, min(64, B - sb));
+            float* o = out + (size_t)sb * n_act;
+            for (int i = threadIdx.x; i < nbb * n_act; i += 256) {
+                const int bb = i / n_act, a = i - bb * n_act;
+                o[i] = st[bb * stride + a];
+            }
         }
     }
 }
@@ -496,21 +598,22 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ pptr
     }
 }
 
-// transposed hop: gh[s, b] = sum over merged pairs (dst, w) of source row s of w * gz[dst, b]. One warp per
-// (row, 128-sample chunk), rows in degree-descending schedule order.
-__global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int* __restrict__ sched, const int* __restrict__ tptr,
-                                                        const int2* __restrict__ tpairs, const float* __restrict__ gz,
-                                                        float* __restrict__ gh, int n_rows, int ld) {
-    const int slot = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (slot >= n_rows) return;
-    const int s = __ldg(&sched[slot]);
+// transposed hop: gh[s, b] = sum over merged pairs (dst, w) of source row s of w * gz[dst, b]. The source rows are
+// cut into segments of at most a fixed number of pairs (hub sources have tens of thousands); a segment of a row
+// that has one writes gh directly, the others write a partial row that k_seg_reduce adds up in order.
+// One warp per (segment, 128-sample chunk); segments longest first. seg = {row, first pair, end pair, slot or -1}.
+__global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__ segs, const int2* __restrict__ tpairs,
+                                                        const float* __restrict__ gz, float* __restrict__ gh,
+                                                        float* __restrict__ part, int n_segs, int ld) {
+    const int sidx = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (sidx >= n_segs) return;
+    const int4 sg = __ldg(&segs[sidx]);
     const int c = (blockIdx.y * 32 + lane) * 4;
     if (c >= ld) return;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const int e0 = __ldg(&tptr[s]), e1 = __ldg(&tptr[s + 1]);
     const float* base = gz + c;
-    int e = e0;
-    for (; e + 4 <= e1; e += 4) {
+    int e = sg.y;
+    for (; e + 4 <= sg.z; e += 4) {
         int2 p[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) p[u] = __ldg(&tpairs[e + u]);
@@ -524,21 +627,37 @@ __global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int* __restrict__ 
             acc[2] = fmaf(w, v[u].z, acc[2]); acc[3] = fmaf(w, v[u].w, acc[3]);
         }
     }
-    for (; e < e1; ++e) {
+    for (; e < sg.z; ++e) {
         const int2 p = __ldg(&tpairs[e]);
         const float4 v = __ldg(reinterpret_cast<const float4*>(base + (size_t)p.x * ld));
         const float w = __int_as_float(p.y);
         acc[0] = fmaf(w, v.x, acc[0]); acc[1] = fmaf(w, v.y, acc[1]);
         acc[2] = fmaf(w, v.z, acc[2]); acc[3] = fmaf(w, v.w, acc[3]);
     }
-    *reinterpret_cast<float4*>(gh + (size_t)s * ld + c) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    float* dst = sg.w < 0 ? gh + (size_t)sg.x * ld : part + (size_t)sg.w * ld;
+    *reinterpret_cast<float4*>(dst + c) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+// red = {row, first slot, slot count, -}: gh[row] = sum of its partial rows, in slot order
+__global__ void __launch_bounds__(kThreads) k_seg_reduce(const int4* __restrict__ red, const float* __restrict__ part,
+                                                         float* __restrict__ gh, int n_red, int ld) {
+    const int ridx = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (ridx >= n_red) return;
+    const int4 r = __ldg(&red[ridx]);
+    const int c = (blockIdx.y * 32 + lane) * 4;
+    if (c >= ld) return;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < r.z; ++i) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(part + (size_t)(r.y + i) * ld + c));
+        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+    }
+    *reinterpret_cast<float4*>(gh + (size_t)r.x * ld + c) = s;
 }
 
 // sensory layer and plug, one CTA per sensory row s: g0 = gh0 * [h0 > 0]; gain grad += sum g0 * drive; theta grad +=
 // sum -g0 * sigmoid(theta); gd = gdrive (re-drive from later hops) + g0 * gain; in_b grad += sum gd;
-// in_w grad[e] += sum gd * x[col_e] for the row's fan edges (fan <= 32).
-template <class T>
-__global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__ gh0, const T* __restrict__ h0,
+// in_w grad[e] += sum gd * x[col_e] for the row's fan edges, kPlugFan at a time. Four samples per thread per step.
+constexpr int kPlugFan = 16;
+__global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__ gh0, const float* __restrict__ h0,
                                                        const float* __restrict__ drive, const float* __restrict__ gdrive,
                                                        const int* __restrict__ n0, const int* __restrict__ in_crow,
                                                        const int* __restrict__ in_col, const float* __restrict__ x,
@@ -546,32 +665,47 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__
                                                        float* __restrict__ ggain, float* __restrict__ gtheta,
                                                        float* __restrict__ gin_w, float* __restrict__ gin_b, int B,
                                                        int ld) {
-    constexpr int F = 16;                                 // fan handled per pass
+    constexpr int F = kPlugFan;
     __shared__ float red[(F + 3) * kWarps];
     const int s = blockIdx.x;
     const float gn = rgain[s];
     const size_t o = (size_t)s * ld;
     const int e0 = in_crow[s], e1 = in_crow[s + 1];
-    for (int f0 = e0; f0 < e1 || f0 == e0; f0 += F) {
+    int f0 = e0;
+    do {
         const int nf = max(0, min(F, e1 - f0));
+        const bool first = f0 == e0;
         int col[F];
 #pragma unroll
         for (int u = 0; u < F; ++u) col[u] = u < nf ? in_col[f0 + u] : 0;
         float v[F + 3];
 #pragma unroll
         for (int u = 0; u < F + 3; ++u) v[u] = 0.f;
-        for (int b = threadIdx.x; b < B; b += kThreads) {
-            float g = ld1(h0 + o + b) > 0.f ? gh0[o + b] : 0.f;
-            float gd = gdrive[o + b] + g * gn;
-            v[F] += g * drive[o + b];
-            v[F + 1] += g;
-            v[F + 2] += gd;
+        for (int b = threadIdx.x * 4; b < B; b += kThreads * 4) {
+            const float4 gh = __ldg(reinterpret_cast<const float4*>(gh0 + o + b));
+            const float4 hh = __ldg(reinterpret_cast<const float4*>(h0 + o + b));
+            const float4 gr = __ldg(reinterpret_cast<const float4*>(gdrive + o + b));
+            const float g[4] = {hh.x > 0.f ? gh.x : 0.f, hh.y > 0.f ? gh.y : 0.f, hh.z > 0.f ? gh.z : 0.f,
+                                hh.w > 0.f ? gh.w : 0.f};
+            const float gd[4] = {fmaf(g[0], gn, gr.x), fmaf(g[1], gn, gr.y), fmaf(g[2], gn, gr.z),
+                                 fmaf(g[3], gn, gr.w)};
+            if (first) {
+                const float4 dr = __ldg(reinterpret_cast<const float4*>(drive + o + b));
+                v[F] += g[0] * dr.x + g[1] * dr.y + g[2] * dr.z + g[3] * dr.w;
+                v[F + 1] += g[0] + g[1] + g[2] + g[3];
+                v[F + 2] += gd[0] + gd[1] + gd[2] + gd[3];
+            }
 #pragma unroll
-            for (int u = 0; u < F; ++u) if (u < nf) v[u] = fmaf(gd, x[(size_t)col[u] * ld + b], v[u]);
+            for (int u = 0; u < F; ++u) {
+                if (u < nf) {
+                    const float4 xv = __ldg(reinterpret_cast<const float4*>(x + (size_t)col[u] * ld + b));
+                    v[u] += gd[0] * xv.x + gd[1] * xv.y + gd[2] * xv.z + gd[3] * xv.w;
+                }
+            }
         }
         block_sum<F + 3>(v, red);
         if (threadIdx.x == 0) {
-            if (f0 == e0) {
+            if (first) {
                 const int id = n0[s];
                 ggain[id] += v[F];
                 gtheta[id] += -v[F + 1] * rsig[s];
@@ -579,8 +713,8 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__
             }
             for (int u = 0; u < nf; ++u) gin_w[f0 + u] += v[u];
         }
-        if (nf == 0) break;
-    }
+        f0 += F;
+    } while (f0 < e1);
 }
 
 // ---------------------------------------------------------------- optimiser

@@ -16,7 +16,7 @@ from .netfile import Structure, read_net, write_net
 
 PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libflyguy_b200.so"
-FG_ACT_BF16, FG_INFER_ONLY = 1, 2
+FG_ACT_BF16, FG_INFER_ONLY, FG_ACT_F16 = 1, 2, 4
 _lib = None
 
 # the exported symbols and their ctypes signatures: (restype, argtypes)

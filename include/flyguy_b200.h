@@ -70,8 +70,10 @@ void fc_sync(void* h);
 
 #define FG_ACT_BF16 1     /* states stored as bf16 (fp32 accumulation, fp32 weights); forward only */
 #define FG_INFER_ONLY 2   /* no gradient / optimiser buffers: fc_backward and fc_step fail */
+#define FG_ACT_F16 4      /* states stored as IEEE fp16 (the reference's 16-bit "cuda16" states); forward only */
+/* In both 16-bit modes the last layer (the descending neurons the output plug reads) stays fp32. */
 
-/* fc_create with flags (FG_ACT_BF16 implies FG_INFER_ONLY). */
+/* fc_create with flags (FG_ACT_BF16 and FG_ACT_F16 imply FG_INFER_ONLY). */
 void* fg_create(const char* net_path, int max_batch, int flags);
 /* Frees the handle and its device memory (the reference never frees its handle). */
 void fg_destroy(void* h);

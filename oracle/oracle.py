@@ -67,7 +67,7 @@ class Oracle:
     """The oracle bound to one network structure (a netfile.Structure)."""
 
     def __init__(self, s, threads: int = 0):
-        self.s, self.threads = s, int(threads or os.cpu_count() or 1)
+        self.s, self.threads = s, int(threads or min(os.cpu_count() or 1, 16))
         self._keep = []
         K = s["hops"]
 
