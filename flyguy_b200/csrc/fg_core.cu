@@ -71,12 +71,14 @@ struct Core {
     float *d_rgain = nullptr, *d_rthr = nullptr, *d_rsig = nullptr;
     int2 *d_pairs = nullptr, *d_tpairs = nullptr;
     int *d_gptr = nullptr, *d_gw = nullptr, *d_tpi = nullptr;
-    long long off[8] = {0};
+    long long off[8] = {0};                             // segment starts in the flat arrays (256-byte aligned)
+    long long psize[7] = {0};                           // the seven arrays' true lengths
     float *P = nullptr, *G = nullptr, *M = nullptr, *V = nullptr, *EMA = nullptr;
     long long adam_t = 0;
     float *x = nullptr, *drive = nullptr, *lg = nullptr, *dl = nullptr;
     void* h0 = nullptr;
-    float *gh_a = nullptr, *gh_b = nullptr, *gz = nullptr, *gdrive = nullptr, *part = nullptr;
+    float *gz_a = nullptr, *gz_b = nullptr, *gdrive = nullptr, *part = nullptr;
+    float *nsum = nullptr, *plug_part = nullptr;
     float *kl_s = nullptr, *ag_s = nullptr, *stats = nullptr, *norm_part = nullptr, *norm = nullptr;
     int* live = nullptr;
     int out_splits = 1;
@@ -255,7 +257,7 @@ NetHost parse_net(Core& c, const char* path) {
     if (c.obs_dim <= 0 || c.n_act <= 0 || c.n_act > kMaxAct || c.hops <= 0 || c.hops > 32 || c.n_neurons <= 0 ||
         c.n_w < 0 || c.n_s <= 0 || c.fan < 0 || c.n_dn <= 0)
         throw Err("NET.bin: bad header");
-    if ((long long)c.obs_dim * kPlugCols * 4 > 220 * 1024) throw Err("obs_dim too large for the plug's staging");
+    if ((long long)c.obs_dim * 64 * 4 + 8192LL * 8 > 220 * 1024) throw Err("obs_dim too large for the plug's staging");
     NetHost n;
     c.sizes = r.take(c.hops + 1, "sizes");
     n.E = r.take(c.hops, "edge counts");
@@ -337,7 +339,10 @@ void alloc_all(Core& c) {
     const long long ps[7] = {c.n_w, c.n_neurons, c.n_neurons, (long long)c.n_s * c.fan, c.n_s,
                              (long long)c.n_act * c.n_dn, c.n_act};
     c.off[0] = 0;
-    for (int i = 0; i < 7; ++i) c.off[i + 1] = c.off[i] + ps[i];
+    for (int i = 0; i < 7; ++i) {
+        c.psize[i] = ps[i];
+        c.off[i + 1] = (c.off[i] + ps[i] + 63) / 64 * 64;   // every array starts on a 256-byte boundary
+    }
     const long long n = c.off[7];
     c.P = dalloc<float>(c, n);
     c.EMA = dalloc<float>(c, n);
@@ -365,11 +370,12 @@ void alloc_all(Core& c) {
     c.stats = dalloc<float>(c, 4);
     if (c.train) {
         c.dl = dalloc<float>(c, (size_t)c.n_act * B);
-        c.gh_a = dalloc<float>(c, (size_t)max_rows * B);
-        c.gh_b = dalloc<float>(c, (size_t)max_rows * B);
-        c.gz = dalloc<float>(c, (size_t)max_rows * B);
+        c.gz_a = dalloc<float>(c, (size_t)max_rows * B);
+        c.gz_b = dalloc<float>(c, (size_t)max_rows * B);
         c.gdrive = dalloc<float>(c, (size_t)c.n_s * B);
         c.live = dalloc<int>(c, max_rows);
+        c.nsum = dalloc<float>(c, (size_t)max_rows * ((B + 255) / 256) * 3);
+        c.plug_part = dalloc<float>(c, (size_t)c.n_s * kPlugSplits * (c.fan + 3));
         c.out_splits = std::max(1, std::min(64, (int)((B + 1023) / 1024)));
         c.part = dalloc<float>(c, (size_t)c.out_splits * c.n_act * (c.n_dn + 1));
         c.kl_s = dalloc<float>(c, B);
@@ -380,21 +386,21 @@ void alloc_all(Core& c) {
     }
 }
 
-int plug_smem(const Core& c) { return c.obs_dim * kPlugCols * 4; }
+int plug_rows(const Core& c) { return std::max(16, std::min(512, 8192 / std::max(c.fan, 1))); }
+template <class T>
+int plug_smem(const Core& c) { return c.obs_dim * PlugCfg<T>::cols * (int)sizeof(T) + plug_rows(c) * c.fan * 8; }
 
 template <class T>
-void plug_limits(int smem) {
-    CK(cudaFuncSetAttribute(k_plug_fwd<T, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    CK(cudaFuncSetAttribute(k_plug_fwd<T, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    CK(cudaFuncSetAttribute(k_plug_fwd<T, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    CK(cudaFuncSetAttribute(k_plug_fwd<T, false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+void plug_limits(const Core& c) {
+    const int smem = plug_smem<T>(c);
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
 }
 
 void set_smem_limits(const Core& c) {
-    const int smem = plug_smem(c);
-    plug_limits<float>(smem);
-    plug_limits<__nv_bfloat16>(smem);
-    plug_limits<__half>(smem);
+    plug_limits<float>(c);
+    plug_limits<__nv_bfloat16>(c);
+    plug_limits<__half>(c);
 }
 
 inline unsigned blocks(long long n, int t = 256) { return (unsigned)((n + t - 1) / t); }
@@ -422,24 +428,19 @@ void check_batch(const Core& c, int B) {
 
 template <class T, bool SAVE>
 void plug_launch(Core& c, const float* Pw, int B) {
-    const dim3 g((c.n_s + kPlugRows - 1) / kPlugRows, (B + kPlugCols - 1) / kPlugCols);
-    const bool vec4 = c.fan % 4 == 0;
+    const int rows = plug_rows(c);
+    const dim3 g((c.n_s + rows - 1) / rows, (B + PlugCfg<T>::cols - 1) / PlugCfg<T>::cols);
     launch(c, K_PLUG_FWD, [&]() {
-        if (vec4)
-            k_plug_fwd<T, SAVE, true><<<g, kPlugThreads, plug_smem(c), c.st>>>(
-                c.d_in_crow, c.d_in_col, Pw + c.off[3], Pw + c.off[4], c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0,
-                c.n_s, c.obs_dim, B);
-        else
-            k_plug_fwd<T, SAVE, false><<<g, kPlugThreads, plug_smem(c), c.st>>>(
-                c.d_in_crow, c.d_in_col, Pw + c.off[3], Pw + c.off[4], c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0,
-                c.n_s, c.obs_dim, B);
+        k_plug_fwd<T, SAVE><<<g, kPlugThreads, plug_smem<T>(c), c.st>>>(
+            c.d_in_col, Pw + c.off[3], Pw + c.off[4], c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows,
+            c.obs_dim, B);
     });
 }
 
 template <class TI, class TO>
 void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
-    constexpr int V = Act<TI>::V;
-    const dim3 g((h.rows + kWarps - 1) / kWarps, (unsigned)((B + 32 * V - 1) / (32 * V)));
+    constexpr int N = Lane32<TI>::N;
+    const dim3 g((h.rows + kWarps - 1) / kWarps, (unsigned)((B + 32 * N - 1) / (32 * N)));
     launch(c, K_HOP_FWD, [&]() {
         k_hop_fwd<TI, TO><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase, (const TI*)hp,
                                                     c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive,
@@ -483,7 +484,9 @@ void forward(Core& c, const float* obs, int B, float* logits, int ema, bool keep
     else forward_t<float>(c, obs, B, logits, ema, keep_lg);
 }
 
-// gradient of the loss whose d/dlogits is in c.dl [n_act, B], through the states of the last forward; ADDED to G
+// gradient of the loss whose d/dlogits is in c.dl [n_act, B], through the states of the last forward; ADDED to G.
+// Per hop k (top down): the weight gradient of its merged pairs from gz_k and the states below, then the transposed
+// product into the layer below with that layer's neuron backward fused in (for the sensory layer: gh0 for the plug).
 void backward(Core& c, int B) {
     if (!c.train) throw Err("this handle was created for inference only");
     if (B != c.lastB) throw Err("fc_backward batch differs from the last forward's");
@@ -494,43 +497,84 @@ void backward(Core& c, int B) {
     const float* hK = (const float*)top.d_h;
     const int splits = std::max(1, std::min(c.out_splits, (B + 1023) / 1024));
     const int split_len = ((B + splits - 1) / splits + 31) / 32 * 32;
-    launch(c, K_OUT_BWD, [&]() { k_out_bwd_w<float><<<dim3((c.n_dn + 1 + 31) / 32, (c.n_act + 31) / 32, splits), 256, 0, c.st>>>(
-        c.dl, hK, c.d_dn, c.part, c.n_act, c.n_dn, B, B, split_len); });
-    launch(c, K_OUT_BWD, [&]() { k_out_bwd_reduce<<<blocks((long long)c.n_act * (c.n_dn + 1)), 256, 0, c.st>>>(c.part, c.G + c.off[5],
-                                                                                 c.G + c.off[6], c.n_act, c.n_dn, splits); });
-    float* gh = c.gh_a;
-    float* gh_next = c.gh_b;
-    if (c.n_dn < top.rows) CK(cudaMemsetAsync(gh, 0, (size_t)top.rows * B * 4, c.st));
+    launch(c, K_OUT_BWD, [&]() {
+        k_out_bwd_w<float><<<dim3((c.n_dn + 1 + 31) / 32, (c.n_act + 31) / 32, splits), 256, 0, c.st>>>(
+            c.dl, hK, c.d_dn, c.part, c.n_act, c.n_dn, B, B, split_len);
+    });
+    launch(c, K_OUT_BWD, [&]() {
+        k_out_bwd_reduce<<<blocks((long long)c.n_act * (c.n_dn + 1)), 256, 0, c.st>>>(c.part, c.G + c.off[5],
+                                                                                     c.G + c.off[6], c.n_act, c.n_dn,
+                                                                                     splits);
+    });
+    float* gz = c.gz_a;                      // gz of the layer being processed
+    float* nxt = c.gz_b;                     // gz (or gh0) of the layer below
+    if (c.n_dn < top.rows) CK(cudaMemsetAsync(nxt, 0, (size_t)top.rows * B * 4, c.st));
     const int jper = 64;
-    launch(c, K_OUT_BWD, [&]() { k_out_bwd_h<<<dim3((B + 127) / 128, (c.n_dn + jper - 1) / jper), 128, jper * c.n_act * 4, c.st>>>(
-        W + c.off[5], c.dl, c.d_dn, gh, c.n_act, c.n_dn, B, B, jper); });
+    launch(c, K_OUT_BWD, [&]() {
+        k_out_bwd_h<<<dim3((B + 127) / 128, (c.n_dn + jper - 1) / jper), 128, jper * c.n_act * 4, c.st>>>(
+            W + c.off[5], c.dl, c.d_dn, nxt, c.n_act, c.n_dn, B, B, jper);
+    });
+    launch(c, K_ACT_BWD, [&]() {
+        k_act_bwd<float><<<top.rows, kThreads, 0, c.st>>>(nxt, hK, top.d_nid, top.d_drow, c.d_rgain + top.rbase,
+                                                          c.d_rthr + top.rbase, c.d_rsig + top.rbase, gz,
+                                                          c.G + c.off[1], c.G + c.off[2], c.gdrive, c.live, B, B);
+    });
+    const int chunks = (B + 255) / 256;
     for (int k = c.hops - 1; k >= 0; --k) {
         const Hop& h = c.hop[k];
-        const float* hk = (const float*)h.d_h;
         const float* hprev = k ? (const float*)c.hop[k - 1].d_h : (const float*)c.h0;
-        launch(c, K_ACT_BWD, [&]() { k_act_bwd<float><<<h.rows, kThreads, 0, c.st>>>(gh, hk, h.d_nid, h.d_drow, c.d_rgain + h.rbase,
-                                                        c.d_rthr + h.rbase, c.d_rsig + h.rbase, c.gz, c.G + c.off[1],
-                                                        c.G + c.off[2], c.gdrive, c.live, B, B); });
         if (h.widx_unique)
-            launch(c, K_SDDMM, [&]() { k_sddmm<float, false><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase,
-                                                                 c.d_gw, c.gz, hprev, c.live, c.G + c.off[0], B, B); });
-        else
-            launch(c, K_SDDMM, [&]() { k_sddmm<float, true><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase,
-                                                                c.d_gw, c.gz, hprev, c.live, c.G + c.off[0], B, B); });
-        launch(c, K_HOP_BWD, [&]() {
-            k_hop_bwd_t<<<dim3((h.n_segs + kWarps - 1) / kWarps, (B + 127) / 128), kThreads, 0, c.st>>>(
-                h.d_segs, c.d_tpairs + h.pbase, c.gz, gh_next, c.seg_part, h.n_segs, B);
-        });
-        if (h.n_reds)
-            launch(c, K_HOP_BWD, [&]() {
-                k_seg_reduce<<<dim3((h.n_reds + kWarps - 1) / kWarps, (B + 127) / 128), kThreads, 0, c.st>>>(
-                    h.d_reds, c.seg_part, gh_next, h.n_reds, B);
+            launch(c, K_SDDMM, [&]() {
+                k_sddmm<float, false><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase,
+                                                                     c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live,
+                                                                     c.G + c.off[0], B, B);
             });
-        std::swap(gh, gh_next);
+        else
+            launch(c, K_SDDMM, [&]() {
+                k_sddmm<float, true><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase,
+                                                                    c.d_gw, gz, hprev, c.live, c.G + c.off[0], B, B);
+            });
+        const dim3 gs((h.n_segs + kWarps - 1) / kWarps, chunks), gr((h.n_reds + kWarps - 1) / kWarps, chunks);
+        if (k >= 1) {                        // the layer below is a hop's: its neuron backward rides along
+            const Hop& lo = c.hop[k - 1];
+            NeuronEpi ep{hprev, c.d_rgain + lo.rbase, c.d_rthr + lo.rbase, lo.d_drow, c.gdrive, c.nsum, chunks};
+            launch(c, K_HOP_BWD, [&]() {
+                k_hop_bwd_t<true><<<gs, kThreads, 0, c.st>>>(h.d_segs, c.d_tpairs + h.pbase, gz, nxt, c.seg_part,
+                                                             h.n_segs, B, ep);
+            });
+            if (h.n_reds)
+                launch(c, K_HOP_BWD, [&]() {
+                    k_seg_reduce<true><<<gr, kThreads, 0, c.st>>>(h.d_reds, c.seg_part, nxt, h.n_reds, B, ep);
+                });
+            launch(c, K_ACT_BWD, [&]() {
+                k_neuron_reduce<<<blocks(lo.rows), 256, 0, c.st>>>(c.nsum, lo.d_nid, c.d_rsig + lo.rbase,
+                                                                  c.G + c.off[1], c.G + c.off[2], c.live, lo.rows,
+                                                                  chunks);
+            });
+        } else {
+            NeuronEpi ep{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, chunks};
+            launch(c, K_HOP_BWD, [&]() {
+                k_hop_bwd_t<false><<<gs, kThreads, 0, c.st>>>(h.d_segs, c.d_tpairs + h.pbase, gz, nxt, c.seg_part,
+                                                              h.n_segs, B, ep);
+            });
+            if (h.n_reds)
+                launch(c, K_HOP_BWD, [&]() {
+                    k_seg_reduce<false><<<gr, kThreads, 0, c.st>>>(h.d_reds, c.seg_part, nxt, h.n_reds, B, ep);
+                });
+        }
+        std::swap(gz, nxt);
     }
-    launch(c, K_PLUG_BWD, [&]() { k_plug_bwd<<<c.n_s, kThreads, 0, c.st>>>(gh, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_crow,
-                                                    c.d_in_col, c.x, c.d_rgain, c.d_rsig, c.G + c.off[1],
-                                                    c.G + c.off[2], c.G + c.off[3], c.G + c.off[4], B, B); });
+    // gz now holds gh0 (the sensory layer's incoming gradient)
+    launch(c, K_PLUG_BWD, [&]() {
+        k_plug_bwd<<<dim3(c.n_s, kPlugSplits), kThreads, 0, c.st>>>(gz, (const float*)c.h0, c.drive, c.gdrive,
+                                                                    c.d_in_crow, c.d_in_col, c.x, c.d_rgain,
+                                                                    c.plug_part, c.fan, B, B);
+    });
+    launch(c, K_PLUG_BWD, [&]() {
+        k_plug_reduce<<<blocks((long long)c.n_s * (c.fan + 3)), 256, 0, c.st>>>(
+            c.plug_part, c.d_n0, c.d_rsig, c.G + c.off[1], c.G + c.off[2], c.G + c.off[3], c.G + c.off[4], c.n_s,
+            c.fan);
+    });
 }
 
 float grad_norm(Core& c, float max_norm) {
@@ -628,7 +672,7 @@ void fg_clear_error(void* h) {
 void fc_sizes(void* h, long long* out) {
     guarded(h, [&]() {
         Core& c = *as_core(h);
-        for (int i = 0; i < 7; ++i) out[i] = c.off[i + 1] - c.off[i];
+        for (int i = 0; i < 7; ++i) out[i] = c.psize[i];
         out[7] = c.obs_dim; out[8] = c.n_act; out[9] = c.maxB;
         return 0;
     }, 0);
@@ -671,7 +715,7 @@ void fc_copy(void* h, int which, int to_core, float** ptrs) {
         for (int i = 0; i < 7; ++i) {
             if (!ptrs[i]) continue;
             float* mine = A + c.off[i];
-            const size_t bytes = (size_t)(c.off[i + 1] - c.off[i]) * 4;
+            const size_t bytes = (size_t)c.psize[i] * 4;
             if (to_core) CK(cudaMemcpyAsync(mine, ptrs[i], bytes, cudaMemcpyDeviceToDevice, c.st));
             else CK(cudaMemcpyAsync(ptrs[i], mine, bytes, cudaMemcpyDeviceToDevice, c.st));
         }

@@ -174,125 +174,197 @@ __global__ void k_to_neuron_major(const float* __restrict__ in, float* __restric
 
 // ---------------------------------------------------------------- forward
 // input plug + sensory activation: drive[s,b] = in_b[s] + sum_j in_w[s*fan+j] * x[col, b];
-// h0 = relu(gain*drive - thr). A CTA stages x for 64 samples (all obs_dim rows, fp32) in shared memory once and
-// computes a range of kPlugRows sensory rows from it; lane l of a warp owns samples 2l, 2l+1.
-constexpr int kPlugCols = 64, kPlugRows = 1024, kPlugThreads = 512;
-template <class T, bool SAVE_DRIVE, bool VEC4>
-__global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict__ in_crow,
-                                                           const int* __restrict__ in_col,
+// h0 = relu(gain*drive - thr). A CTA stages x for a chunk of samples (all obs_dim rows; in the state type for 16-bit
+// states - 128 samples - or fp32 - 64 samples) and its rows' plug columns and weights in shared memory, then every warp
+// computes rows from there: lane l owns the chunk's samples [NS*l, NS*l + NS).
+constexpr int kPlugThreads = 512;
+template <class T> struct PlugCfg { static constexpr int cols = sizeof(T) == 4 ? 64 : 128; };
+__device__ __forceinline__ void cvt_store4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+__device__ __forceinline__ void cvt_store4(__nv_bfloat16* p, float4 v) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+}
+__device__ __forceinline__ void cvt_store4(__half* p, float4 v) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
+}
+// NS consecutive staged values as fp32 (NS = 2 for fp32, 4 for 16-bit types)
+__device__ __forceinline__ void lds_ns(const float* p, float (&v)[2]) {
+    const float2 q = *reinterpret_cast<const float2*>(p);
+    v[0] = q.x; v[1] = q.y;
+}
+__device__ __forceinline__ void lds_ns(const __nv_bfloat16* p, float (&v)[4]) {
+    const uint2 q = *reinterpret_cast<const uint2*>(p);
+    v[0] = __uint_as_float(q.x << 16); v[1] = __uint_as_float(q.x & 0xffff0000u);
+    v[2] = __uint_as_float(q.y << 16); v[3] = __uint_as_float(q.y & 0xffff0000u);
+}
+__device__ __forceinline__ void lds_ns(const __half* p, float (&v)[4]) {
+    const uint2 q = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&q.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&q.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+__device__ __forceinline__ void st_ns(float* p, const float (&v)[2]) { *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]); }
+__device__ __forceinline__ void st_ns(__nv_bfloat16* p, const float (&v)[4]) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]));
+}
+__device__ __forceinline__ void st_ns(__half* p, const float (&v)[4]) {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]));
+}
+
+template <class T, bool SAVE_DRIVE>
+__global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict__ in_col,
                                                            const float* __restrict__ in_w,
                                                            const float* __restrict__ in_b,
                                                            const float* __restrict__ rgain,
                                                            const float* __restrict__ rthr, const float* __restrict__ x,
                                                            float* __restrict__ drive, T* __restrict__ h0, int n_s,
-                                                           int obs_dim, int ld) {
-    extern __shared__ float xs[];                         // [obs_dim][kPlugCols]
-    const int b0 = blockIdx.y * kPlugCols;
-    const int nb = min(kPlugCols, ld - b0);
-    for (int i = threadIdx.x; i < obs_dim * (kPlugCols / 4); i += blockDim.x) {
-        const int f = i / (kPlugCols / 4), q = (i - f * (kPlugCols / 4)) * 4;
+                                                           int fan, int rows_per_cta, int obs_dim, int ld) {
+    constexpr int C = PlugCfg<T>::cols, NS = C / 32;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T* xs = reinterpret_cast<T*>(smem_raw);                                   // [obs_dim][C]
+    int* cs = reinterpret_cast<int*>(smem_raw + (size_t)obs_dim * C * sizeof(T));   // [rows][fan]
+    float* ws = reinterpret_cast<float*>(cs + rows_per_cta * fan);                 // [rows][fan]
+    const int b0 = blockIdx.y * C;
+    const int r_lo = blockIdx.x * rows_per_cta, r_hi = min(n_s, r_lo + rows_per_cta);
+    for (int i = threadIdx.x; i < obs_dim * (C / 4); i += blockDim.x) {
+        const int f = i / (C / 4), q = (i - f * (C / 4)) * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (q < nb) v = __ldg(reinterpret_cast<const float4*>(x + (size_t)f * ld + b0 + q));
-        *reinterpret_cast<float4*>(xs + f * kPlugCols + q) = v;
+        if (b0 + q < ld) v = __ldg(reinterpret_cast<const float4*>(x + (size_t)f * ld + b0 + q));
+        cvt_store4(xs + f * C + q, v);
+    }
+    const int ne = (r_hi - r_lo) * fan;
+    const size_t e_lo = (size_t)r_lo * fan;
+    for (int i = threadIdx.x; i < ne; i += blockDim.x) {
+        cs[i] = __ldg(&in_col[e_lo + i]);
+        ws[i] = __ldg(&in_w[e_lo + i]);
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int r_lo = blockIdx.x * kPlugRows, r_hi = min(n_s, r_lo + kPlugRows);
-    const int bl = 2 * lane;
-    if (bl >= nb) return;
+    const int bl = NS * lane;
+    if (b0 + bl >= ld) return;
     for (int row = r_lo + warp; row < r_hi; row += kPlugThreads / 32) {
+        float a[NS];
         const float bias = __ldg(&in_b[row]);
-        float a0 = bias, a1 = bias;
-        const int e0 = __ldg(&in_crow[row]), e1 = __ldg(&in_crow[row + 1]);
-        if (VEC4) {
-            for (int e = e0; e < e1; e += 4) {
-                const int4 cc = __ldg(reinterpret_cast<const int4*>(in_col + e));
-                const float4 ww = __ldg(reinterpret_cast<const float4*>(in_w + e));
-                const int cs[4] = {cc.x, cc.y, cc.z, cc.w};
-                const float ws[4] = {ww.x, ww.y, ww.z, ww.w};
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float2 xv = *reinterpret_cast<const float2*>(xs + cs[u] * kPlugCols + bl);
-                    a0 = fmaf(ws[u], xv.x, a0);
-                    a1 = fmaf(ws[u], xv.y, a1);
-                }
-            }
-        } else {
-            for (int e = e0; e < e1; ++e) {
-                const int cc = __ldg(&in_col[e]);
-                const float ww = __ldg(&in_w[e]);
-                const float2 xv = *reinterpret_cast<const float2*>(xs + cc * kPlugCols + bl);
-                a0 = fmaf(ww, xv.x, a0);
-                a1 = fmaf(ww, xv.y, a1);
-            }
+        for (int i = 0; i < NS; ++i) a[i] = bias;
+        const int* rc = cs + (row - r_lo) * fan;
+        const float* rw = ws + (row - r_lo) * fan;
+        for (int j = 0; j < fan; ++j) {
+            float v[NS];
+            lds_ns(xs + rc[j] * C + bl, v);
+            const float w = rw[j];
+#pragma unroll
+            for (int i = 0; i < NS; ++i) a[i] = fmaf(w, v[i], a[i]);
         }
         const size_t o = (size_t)row * ld + b0 + bl;
-        if (SAVE_DRIVE) *reinterpret_cast<float2*>(drive + o) = make_float2(a0, a1);
+        if (SAVE_DRIVE) {
+#pragma unroll
+            for (int i = 0; i < NS; i += 2) *reinterpret_cast<float2*>(drive + o + i) = make_float2(a[i], a[i + 1]);
+        }
         const float g = __ldg(&rgain[row]), th = __ldg(&rthr[row]);
-        const float v0 = fmaxf(fmaf(g, a0, -th), 0.f), v1 = fmaxf(fmaf(g, a1, -th), 0.f);
-        store2(h0 + o, v0, v1);
+        float hv[NS];
+#pragma unroll
+        for (int i = 0; i < NS; ++i) hv[i] = fmaxf(fmaf(g, a[i], -th), 0.f);
+        st_ns(h0 + o, hv);
     }
 }
 
 // one hop: z[t,b] = sum over merged pairs (src, w) of row t of w * hp[src, b] (+ drive[drow[t], b]);
-// h = relu(gain*z - thr). One warp per (row, 32V-sample chunk); rows in degree-descending schedule order.
+// h = relu(gain*z - thr). One warp per (row, 32*2V-sample chunk): each lane loads 32 bytes of the source row per pair
+// (16 bf16/fp16 or 8 fp32 states) so the pair's own load and address math are shared by many FMAs, and multiplies
+// with packed fp32x2 FMAs (sm_100). Rows run in degree-descending schedule order.
 // TI: the source layer's type, TO: this layer's (the last layer of a 16-bit network is fp32).
+__device__ __forceinline__ void unpack2(const __nv_bfloat16*, uint32_t x, float2& f) {
+    f = make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
+}
+__device__ __forceinline__ void unpack2(const __half*, uint32_t x, float2& f) {
+    f = __half22float2(*reinterpret_cast<const __half2*>(&x));
+}
+// 32 bytes at p as N/2 float2 pairs (N = 16 for 16-bit types, 8 for fp32)
+template <class T, int N>
+__device__ __forceinline__ void ld32(const T* p, float2 (&v)[N / 2]) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+    if constexpr (sizeof(T) == 4) {
+        v[0] = make_float2(__uint_as_float(a.x), __uint_as_float(a.y));
+        v[1] = make_float2(__uint_as_float(a.z), __uint_as_float(a.w));
+        v[2] = make_float2(__uint_as_float(b.x), __uint_as_float(b.y));
+        v[3] = make_float2(__uint_as_float(b.z), __uint_as_float(b.w));
+    } else {
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) unpack2(p, w[i], v[i]);
+    }
+}
+template <class T> struct Lane32 { static constexpr int N = 32 / sizeof(T); };   // states per lane per pair
+
 template <class TI, class TO>
 __global__ void __launch_bounds__(kThreads) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
                                                       const int2* __restrict__ pairs, const TI* __restrict__ hp,
                                                       const float* __restrict__ rgain, const float* __restrict__ rthr,
                                                       const int* __restrict__ drow, const float* __restrict__ drive,
                                                       TO* __restrict__ h, int n_rows, int ld) {
-    constexpr int V = Act<TI>::V;
+    constexpr int N = Lane32<TI>::N, H = N / 2;
     const int slot = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (slot >= n_rows) return;
     const int t = __ldg(&sched[slot]);
-    const int c = (blockIdx.y * 32 + lane) * V;
+    const int c = (blockIdx.y * 32 + lane) * N;
     if (c >= ld) return;
-    float acc[V];
+    float2 acc[H];
 #pragma unroll
-    for (int i = 0; i < V; ++i) acc[i] = 0.f;
+    for (int i = 0; i < H; ++i) acc[i] = make_float2(0.f, 0.f);
     const int e0 = __ldg(&pptr[t]), e1 = __ldg(&pptr[t + 1]);
     const TI* base = hp + c;
+    const unsigned row_elems = (unsigned)ld;
     int e = e0;
-    for (; e + 4 <= e1; e += 4) {                        // four pairs in flight
-        int2 p[4];
+    for (; e + 2 <= e1; e += 2) {                        // two pairs (64 bytes per lane) in flight
+        const int2 p0 = __ldg(&pairs[e]), p1 = __ldg(&pairs[e + 1]);
+        float2 v0[H], v1[H];
+        ld32<TI, N>(base + (size_t)((unsigned)p0.x * row_elems), v0);
+        ld32<TI, N>(base + (size_t)((unsigned)p1.x * row_elems), v1);
+        const float2 w0 = make_float2(__int_as_float(p0.y), __int_as_float(p0.y));
+        const float2 w1 = make_float2(__int_as_float(p1.y), __int_as_float(p1.y));
 #pragma unroll
-        for (int u = 0; u < 4; ++u) p[u] = __ldg(&pairs[e + u]);
-        float v[4][V];
+        for (int i = 0; i < H; ++i) acc[i] = __ffma2_rn(w0, v0[i], acc[i]);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) ld_act(base + (size_t)p[u].x * ld, v[u]);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const float w = __int_as_float(p[u].y);
-#pragma unroll
-            for (int i = 0; i < V; ++i) acc[i] = fmaf(w, v[u][i], acc[i]);
-        }
+        for (int i = 0; i < H; ++i) acc[i] = __ffma2_rn(w1, v1[i], acc[i]);
     }
-    for (; e < e1; ++e) {
-        const int2 p = __ldg(&pairs[e]);
-        float v[V];
-        ld_act(base + (size_t)p.x * ld, v);
-        const float w = __int_as_float(p.y);
+    if (e < e1) {
+        const int2 p0 = __ldg(&pairs[e]);
+        float2 v0[H];
+        ld32<TI, N>(base + (size_t)((unsigned)p0.x * row_elems), v0);
+        const float2 w0 = make_float2(__int_as_float(p0.y), __int_as_float(p0.y));
 #pragma unroll
-        for (int i = 0; i < V; ++i) acc[i] = fmaf(w, v[i], acc[i]);
+        for (int i = 0; i < H; ++i) acc[i] = __ffma2_rn(w0, v0[i], acc[i]);
     }
     if (drow) {
         const int d = __ldg(&drow[t]);
         if (d >= 0) {
-            const float* dr = drive + (size_t)d * ld + c;
+            const float4* dr = reinterpret_cast<const float4*>(drive + (size_t)d * ld + c);
 #pragma unroll
-            for (int i = 0; i < V; i += 4) {
-                float4 q = __ldg(reinterpret_cast<const float4*>(dr + i));
-                acc[i] += q.x; acc[i + 1] += q.y; acc[i + 2] += q.z; acc[i + 3] += q.w;
+            for (int i = 0; i < H / 2; ++i) {
+                const float4 q = __ldg(dr + i);
+                acc[2 * i].x += q.x; acc[2 * i].y += q.y; acc[2 * i + 1].x += q.z; acc[2 * i + 1].y += q.w;
             }
         }
     }
     const float g = __ldg(&rgain[t]), th = __ldg(&rthr[t]);
-    float hv[V];
+    float hv[N];
 #pragma unroll
-    for (int i = 0; i < V; ++i) hv[i] = fmaxf(fmaf(g, acc[i], -th), 0.f);
-    st_vals<TO, V>(h + (size_t)t * ld + c, hv);
+    for (int i = 0; i < H; ++i) {
+        hv[2 * i] = fmaxf(fmaf(g, acc[i].x, -th), 0.f);
+        hv[2 * i + 1] = fmaxf(fmaf(g, acc[i].y, -th), 0.f);
+    }
+    TO* o = h + (size_t)t * ld + c;
+    if constexpr (sizeof(TO) == 4) {
+#pragma unroll
+        for (int i = 0; i < N; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(hv[i], hv[i + 1], hv[i + 2], hv[i + 3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < N; i += 8) {
+            float q[8] = {hv[i], hv[i + 1], hv[i + 2], hv[i + 3], hv[i + 4], hv[i + 5], hv[i + 6], hv[i + 7]};
+            st_act(o + i, q);
+        }
+    }
 }
 
 // output plug: logits[a,b] = out_b[a] + sum_j out_w[a,j] * hK[dn[j], b], a register-blocked product: a CTA owns
@@ -599,78 +671,182 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ pptr
 }
 
 // transposed hop: gh[s, b] = sum over merged pairs (dst, w) of source row s of w * gz[dst, b]. The source rows are
-// cut into segments of at most a fixed number of pairs (hub sources have tens of thousands); a segment of a row
-// that has one writes gh directly, the others write a partial row that k_seg_reduce adds up in order.
-// One warp per (segment, 128-sample chunk); segments longest first. seg = {row, first pair, end pair, slot or -1}.
+// cut into segments of at most a fixed number of pairs (hub sources have tens of thousands); a segment of a row that
+// has one finishes the row, the others write a partial row that k_seg_reduce adds up in slot order.
+// One warp per (segment, 256-sample chunk), 32 bytes (8 states) per lane per pair, packed fp32x2 FMAs; segments
+// longest first. seg = {row, first pair, end pair, slot or -1}.
+// Finishing a row (EPI): the source layer's neuron backward is fused in - g = gh * [h > 0]; gz = g * gain is written
+// (not gh), gdrive[drow] += gz, and the row's per-chunk sums of g*z (z = (h + thr) / gain where h > 0), of g and of
+// [g != 0] go to nsum[row][chunk][3] for k_neuron_reduce. Without EPI (the sensory layer) gh itself is written.
+struct NeuronEpi {
+    const float* h;          // the source layer's states [rows, ld]
+    const float* rgain;      // per row
+    const float* rthr;
+    const int* drow;         // re-drive rows (nullable)
+    float* gdrive;           // [n_s, ld]
+    float* nsum;             // [rows][chunks][3]
+    int chunks;
+};
+template <bool EPI>
+__device__ __forceinline__ void finish_row(int s, int chunk, int c, int ld, float (&a)[8], float* out,
+                                           const NeuronEpi& ep, bool on) {
+    float* o = out + (size_t)s * ld + c;
+    if (!EPI) {
+        *reinterpret_cast<float4*>(o) = make_float4(a[0], a[1], a[2], a[3]);
+        *reinterpret_cast<float4*>(o + 4) = make_float4(a[4], a[5], a[6], a[7]);
+        return;
+    }
+    const float gn = __ldg(&ep.rgain[s]), th = __ldg(&ep.rthr[s]);
+    const float inv_g = gn != 0.f ? 1.f / gn : 0.f;
+    float4 h0 = make_float4(0.f, 0.f, 0.f, 0.f), h1 = h0;
+    if (on) {
+        h0 = __ldg(reinterpret_cast<const float4*>(ep.h + (size_t)s * ld + c));
+        h1 = __ldg(reinterpret_cast<const float4*>(ep.h + (size_t)s * ld + c) + 1);
+    }
+    const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    float gz[8], s0 = 0.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float g = hv[i] > 0.f ? a[i] : 0.f;
+        gz[i] = g * gn;
+        s0 = fmaf(g, (hv[i] + th) * inv_g, s0);
+        s1 += g;
+        s2 += g != 0.f ? 1.f : 0.f;
+    }
+    if (on) {
+        *reinterpret_cast<float4*>(o) = make_float4(gz[0], gz[1], gz[2], gz[3]);
+        *reinterpret_cast<float4*>(o + 4) = make_float4(gz[4], gz[5], gz[6], gz[7]);
+    }
+    if (on && ep.drow) {
+        const int d = __ldg(&ep.drow[s]);
+        if (d >= 0) {
+            float4* gd = reinterpret_cast<float4*>(ep.gdrive + (size_t)d * ld + c);
+            float4 u = gd[0], v = gd[1];
+            u.x += gz[0]; u.y += gz[1]; u.z += gz[2]; u.w += gz[3];
+            v.x += gz[4]; v.y += gz[5]; v.z += gz[6]; v.w += gz[7];
+            gd[0] = u; gd[1] = v;
+        }
+    }
+    s0 = warp_sum(s0); s1 = warp_sum(s1); s2 = warp_sum(s2);
+    if ((threadIdx.x & 31) == 0) {
+        float* ns = ep.nsum + ((size_t)s * ep.chunks + chunk) * 3;
+        ns[0] = s0; ns[1] = s1; ns[2] = s2;
+    }
+}
+
+template <bool EPI>
 __global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__ segs, const int2* __restrict__ tpairs,
-                                                        const float* __restrict__ gz, float* __restrict__ gh,
-                                                        float* __restrict__ part, int n_segs, int ld) {
+                                                        const float* __restrict__ gz, float* __restrict__ out,
+                                                        float* __restrict__ part, int n_segs, int ld, NeuronEpi ep) {
     const int sidx = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (sidx >= n_segs) return;
     const int4 sg = __ldg(&segs[sidx]);
-    const int c = (blockIdx.y * 32 + lane) * 4;
-    if (c >= ld) return;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const float* base = gz + c;
+    const int c = (blockIdx.y * 32 + lane) * 8;
+    // every lane stays to the end: the epilogue reduces over the warp (ld is a multiple of 32: lanes past the batch
+    // read and write nothing)
+    const bool on = c < ld;
+    float2 acc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
+    const float* base = gz + (on ? c : 0);
+    const unsigned row_elems = (unsigned)ld;
     int e = sg.y;
-    for (; e + 4 <= sg.z; e += 4) {
-        int2 p[4];
+    if (on) {
+        for (; e + 2 <= sg.z; e += 2) {
+            const int2 p0 = __ldg(&tpairs[e]), p1 = __ldg(&tpairs[e + 1]);
+            float2 v0[4], v1[4];
+            ld32<float, 8>(base + (size_t)((unsigned)p0.x * row_elems), v0);
+            ld32<float, 8>(base + (size_t)((unsigned)p1.x * row_elems), v1);
+            const float2 w0 = make_float2(__int_as_float(p0.y), __int_as_float(p0.y));
+            const float2 w1 = make_float2(__int_as_float(p1.y), __int_as_float(p1.y));
 #pragma unroll
-        for (int u = 0; u < 4; ++u) p[u] = __ldg(&tpairs[e + u]);
-        float4 v[4];
+            for (int i = 0; i < 4; ++i) acc[i] = __ffma2_rn(w0, v0[i], acc[i]);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = __ldg(reinterpret_cast<const float4*>(base + (size_t)p[u].x * ld));
+            for (int i = 0; i < 4; ++i) acc[i] = __ffma2_rn(w1, v1[i], acc[i]);
+        }
+        if (e < sg.z) {
+            const int2 p0 = __ldg(&tpairs[e]);
+            float2 v0[4];
+            ld32<float, 8>(base + (size_t)((unsigned)p0.x * row_elems), v0);
+            const float2 w0 = make_float2(__int_as_float(p0.y), __int_as_float(p0.y));
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const float w = __int_as_float(p[u].y);
-            acc[0] = fmaf(w, v[u].x, acc[0]); acc[1] = fmaf(w, v[u].y, acc[1]);
-            acc[2] = fmaf(w, v[u].z, acc[2]); acc[3] = fmaf(w, v[u].w, acc[3]);
+            for (int i = 0; i < 4; ++i) acc[i] = __ffma2_rn(w0, v0[i], acc[i]);
         }
     }
-    for (; e < sg.z; ++e) {
-        const int2 p = __ldg(&tpairs[e]);
-        const float4 v = __ldg(reinterpret_cast<const float4*>(base + (size_t)p.x * ld));
-        const float w = __int_as_float(p.y);
-        acc[0] = fmaf(w, v.x, acc[0]); acc[1] = fmaf(w, v.y, acc[1]);
-        acc[2] = fmaf(w, v.z, acc[2]); acc[3] = fmaf(w, v.w, acc[3]);
+    float a[8] = {acc[0].x, acc[0].y, acc[1].x, acc[1].y, acc[2].x, acc[2].y, acc[3].x, acc[3].y};
+    if (sg.w >= 0) {
+        if (on) {
+            float* o = part + (size_t)sg.w * ld + c;
+            *reinterpret_cast<float4*>(o) = make_float4(a[0], a[1], a[2], a[3]);
+            *reinterpret_cast<float4*>(o + 4) = make_float4(a[4], a[5], a[6], a[7]);
+        }
+        return;
     }
-    float* dst = sg.w < 0 ? gh + (size_t)sg.x * ld : part + (size_t)sg.w * ld;
-    *reinterpret_cast<float4*>(dst + c) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    if (EPI) {
+        if (!on) {                                         // keep the warp reduction whole; contribute zeros
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a[i] = 0.f;
+        }
+        finish_row<EPI>(sg.x, blockIdx.y, on ? c : 0, ld, a, out, ep, on);
+    } else if (on) {
+        finish_row<EPI>(sg.x, blockIdx.y, c, ld, a, out, ep, true);
+    }
 }
-// red = {row, first slot, slot count, -}: gh[row] = sum of its partial rows, in slot order
+// red = {row, first slot, slot count, -}: the row = the sum of its partial rows in slot order, then finished as above
+template <bool EPI>
 __global__ void __launch_bounds__(kThreads) k_seg_reduce(const int4* __restrict__ red, const float* __restrict__ part,
-                                                         float* __restrict__ gh, int n_red, int ld) {
+                                                         float* __restrict__ out, int n_red, int ld, NeuronEpi ep) {
     const int ridx = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (ridx >= n_red) return;
     const int4 r = __ldg(&red[ridx]);
-    const int c = (blockIdx.y * 32 + lane) * 4;
-    if (c >= ld) return;
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i = 0; i < r.z; ++i) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(part + (size_t)(r.y + i) * ld + c));
-        s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+    const int c = (blockIdx.y * 32 + lane) * 8;
+    const bool on = c < ld;
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (on) {
+        for (int i = 0; i < r.z; ++i) {
+            const float4* q = reinterpret_cast<const float4*>(part + (size_t)(r.y + i) * ld + c);
+            const float4 u = __ldg(q), v = __ldg(q + 1);
+            a[0] += u.x; a[1] += u.y; a[2] += u.z; a[3] += u.w;
+            a[4] += v.x; a[5] += v.y; a[6] += v.z; a[7] += v.w;
+        }
     }
-    *reinterpret_cast<float4*>(gh + (size_t)r.x * ld + c) = s;
+    if (EPI) finish_row<EPI>(r.x, blockIdx.y, on ? c : 0, ld, a, out, ep, on);
+    else if (on) finish_row<EPI>(r.x, blockIdx.y, c, ld, a, out, ep, true);
+}
+// per row of a layer: gain grad += sum over chunks of g*z, theta grad += -(sum of g) * sigmoid(theta); live = any g
+__global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __restrict__ nid,
+                                const float* __restrict__ rsig, float* __restrict__ ggain, float* __restrict__ gtheta,
+                                int* __restrict__ live, int rows, int chunks) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= rows) return;
+    float a = 0.f, b = 0.f, n = 0.f;
+    const float* p = nsum + (size_t)s * chunks * 3;
+    for (int k = 0; k < chunks; ++k) { a += p[3 * k]; b += p[3 * k + 1]; n += p[3 * k + 2]; }
+    const int id = nid[s];
+    ggain[id] += a;
+    gtheta[id] += -b * rsig[s];
+    live[s] = n > 0.f;
 }
 
-// sensory layer and plug, one CTA per sensory row s: g0 = gh0 * [h0 > 0]; gain grad += sum g0 * drive; theta grad +=
-// sum -g0 * sigmoid(theta); gd = gdrive (re-drive from later hops) + g0 * gain; in_b grad += sum gd;
-// in_w grad[e] += sum gd * x[col_e] for the row's fan edges, kPlugFan at a time. Four samples per thread per step.
-constexpr int kPlugFan = 16;
+// sensory layer and plug, one CTA per (sensory row s, batch split): g0 = gh0 * [h0 > 0]; sums over the split of
+// g0 * drive, g0, gd = gdrive (re-drive from later hops) + g0 * gain, and gd * x[col_e] for the row's fan edges
+// (kPlugFan at a time) go to part[s][split][fan + 3]; k_plug_reduce adds the splits in order into the gradients of
+// gain, theta, in_b and in_w. Four samples per thread per step.
+constexpr int kPlugFan = 16, kPlugSplits = 4;
 __global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__ gh0, const float* __restrict__ h0,
                                                        const float* __restrict__ drive, const float* __restrict__ gdrive,
-                                                       const int* __restrict__ n0, const int* __restrict__ in_crow,
-                                                       const int* __restrict__ in_col, const float* __restrict__ x,
-                                                       const float* __restrict__ rgain, const float* __restrict__ rsig,
-                                                       float* __restrict__ ggain, float* __restrict__ gtheta,
-                                                       float* __restrict__ gin_w, float* __restrict__ gin_b, int B,
-                                                       int ld) {
+                                                       const int* __restrict__ in_crow, const int* __restrict__ in_col,
+                                                       const float* __restrict__ x, const float* __restrict__ rgain,
+                                                       float* __restrict__ part, int fan, int B, int ld) {
     constexpr int F = kPlugFan;
     __shared__ float red[(F + 3) * kWarps];
-    const int s = blockIdx.x;
+    const int s = blockIdx.x, split = blockIdx.y;
+    const int span = (B / 4 + kPlugSplits - 1) / kPlugSplits * 4;
+    const int b_lo = split * span, b_hi = min(B, b_lo + span);
     const float gn = rgain[s];
     const size_t o = (size_t)s * ld;
     const int e0 = in_crow[s], e1 = in_crow[s + 1];
+    float* out = part + ((size_t)s * kPlugSplits + split) * (fan + 3);
     int f0 = e0;
     do {
         const int nf = max(0, min(F, e1 - f0));
@@ -681,7 +857,7 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__
         float v[F + 3];
 #pragma unroll
         for (int u = 0; u < F + 3; ++u) v[u] = 0.f;
-        for (int b = threadIdx.x * 4; b < B; b += kThreads * 4) {
+        for (int b = b_lo + threadIdx.x * 4; b < b_hi; b += kThreads * 4) {
             const float4 gh = __ldg(reinterpret_cast<const float4*>(gh0 + o + b));
             const float4 hh = __ldg(reinterpret_cast<const float4*>(h0 + o + b));
             const float4 gr = __ldg(reinterpret_cast<const float4*>(gdrive + o + b));
@@ -705,16 +881,25 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__
         }
         block_sum<F + 3>(v, red);
         if (threadIdx.x == 0) {
-            if (first) {
-                const int id = n0[s];
-                ggain[id] += v[F];
-                gtheta[id] += -v[F + 1] * rsig[s];
-                gin_b[s] += v[F + 2];
-            }
-            for (int u = 0; u < nf; ++u) gin_w[f0 + u] += v[u];
+            if (first) { out[fan] = v[F]; out[fan + 1] = v[F + 1]; out[fan + 2] = v[F + 2]; }
+            for (int u = 0; u < nf; ++u) out[f0 - e0 + u] = v[u];
         }
         f0 += F;
     } while (f0 < e1);
+}
+__global__ void k_plug_reduce(const float* __restrict__ part, const int* __restrict__ n0,
+                              const float* __restrict__ rsig, float* __restrict__ ggain, float* __restrict__ gtheta,
+                              float* __restrict__ gin_w, float* __restrict__ gin_b, int n_s, int fan) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;      // one thread per (row, fan + 3 values)
+    const int per = fan + 3;
+    if (i >= n_s * per) return;
+    const int s = i / per, j = i - s * per;
+    float v = 0.f;
+    for (int k = 0; k < kPlugSplits; ++k) v += part[((size_t)s * kPlugSplits + k) * per + j];
+    if (j < fan) gin_w[(size_t)s * fan + j] += v;
+    else if (j == fan) ggain[n0[s]] += v;
+    else if (j == fan + 1) gtheta[n0[s]] += -v * rsig[s];
+    else gin_b[s] += v;
 }
 
 // ---------------------------------------------------------------- optimiser

@@ -65,19 +65,20 @@ class Engine:
         return self.train
 
     # ---- forward without gradients
-    def infer(self, obs: torch.Tensor, half: bool = False) -> torch.Tensor:
+    def infer(self, obs: torch.Tensor, states: str = "f32") -> torch.Tensor:
+        """Forward without gradients; states "f32", "f16" (the reference's 16-bit "cuda16" states) or "bf16"."""
         B = obs.shape[0]
-        if not half and self.train is not None and B <= self.max_batch:
+        if states == "f32" and self.train is not None and B <= self.max_batch:
             return self._piece(self.training_handle(), obs)
         cap = min(MAX_INFER_BATCH, max(32, (B + 31) // 32 * 32))
-        key = half
-        h = self.infer_h.get(key)
+        h = self.infer_h.get(states)
         if h is None or h.max_batch < cap:
             if h is not None:
                 h.close()
+            flags = {"f32": native.FG_INFER_ONLY, "f16": native.FG_ACT_F16, "bf16": native.FG_ACT_BF16}[states]
             with torch.cuda.device(self.device):
-                h = native.Handle(self.s, cap, native.FG_ACT_BF16 if half else native.FG_INFER_ONLY, device=self.device)
-            self.infer_h[key] = h
+                h = native.Handle(self.s, cap, flags, device=self.device)
+            self.infer_h[states] = h
             self._ver.pop(id(h), None)
         self._fresh(h)
         return torch.cat([self._piece(h, obs[i:i + h.max_batch]) for i in range(0, B, h.max_batch)]) \

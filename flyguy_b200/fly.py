@@ -68,8 +68,9 @@ class FlyActor(nn.Module):
         self.n_neurons, self.n_conn, self.hops, self.obs_dim, self.fan = n, len(pre), hops, obs_dim, fan
         self.whole_graph = "in_total" not in g.files
         self.gather_limit = 60_000_000           # kept for API compatibility (the reference's torch-path switch)
-        self.kernel = "b200"                     # every kernel name of the reference maps to the B200 library;
-        #                                          "cuda16" selects bf16 states for forward without gradients
+        self.kernel = "b200"                     # every kernel name of the reference maps to the B200 library; for
+        #                                          forward without gradients "cuda16" selects fp16 states (as the
+        #                                          reference's cuda16 kernels) and "bf16" bf16 states
         down = reachable(sens, pre, post, n, hops)
         up = reachable(dn, post, pre, n, hops)
         layers = [np.flatnonzero(down[k] & up[hops - k]) for k in range(hops + 1)]
@@ -163,4 +164,4 @@ class FlyActor(nn.Module):
         eng = self.engine()
         if torch.is_grad_enabled() and any(p.requires_grad for p in self.parameters()):
             return eng.logits_autograd(obs)
-        return eng.infer(obs, half=self.kernel == "cuda16")
+        return eng.infer(obs, states={"cuda16": "f16", "bf16": "bf16"}.get(self.kernel, "f32"))

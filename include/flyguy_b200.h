@@ -84,10 +84,11 @@ const char* fg_last_error(void* h);
 void fg_clear_error(void* h);
 /* All later work of the handle goes to this cudaStream_t (e.g. torch.cuda.current_stream().cuda_stream). */
 void fc_set_stream(void* h, void* stream);
-/* Device pointer and length of one flat array (which as in fc_copy): the seven arrays back to back in fc_sizes
- * order. The gradient (which 4) is what a data-parallel trainer all-reduces in place before fc_step. */
+/* Device pointer and length of one flat array (which as in fc_copy): the seven arrays in fc_sizes order, each
+ * starting on a 256-byte boundary (fg_offsets; the gaps stay zero). The gradient (which 4) is what a data-parallel
+ * trainer all-reduces in place before fc_step. */
 int fg_flat(void* h, int which, float** ptr, long long* n);
-/* The seven arrays' offsets into the flat arrays: off[0..7] (off[7] = total). */
+/* The seven arrays' offsets into the flat arrays, in floats: off[0..7] (off[7] = the flat length). */
 void fg_offsets(void* h, long long* off);
 /* Layer sizes: sizes[0..hops] (returns hops); merged (destination, source) pairs per hop into pairs[0..hops-1]. */
 int fg_layout(void* h, int* sizes, long long* pairs);
