@@ -257,7 +257,7 @@ NetHost parse_net(Core& c, const char* path) {
     if (c.obs_dim <= 0 || c.n_act <= 0 || c.n_act > kMaxAct || c.hops <= 0 || c.hops > 32 || c.n_neurons <= 0 ||
         c.n_w < 0 || c.n_s <= 0 || c.fan < 0 || c.n_dn <= 0)
         throw Err("NET.bin: bad header");
-    if ((long long)c.obs_dim * 64 * 4 + 8192LL * 8 > 220 * 1024) throw Err("obs_dim too large for the plug's staging");
+    if ((long long)c.obs_dim * 64 * 4 > 220 * 1024) throw Err("obs_dim too large for the plug's staging");
     NetHost n;
     c.sizes = r.take(c.hops + 1, "sizes");
     n.E = r.take(c.hops, "edge counts");
@@ -386,21 +386,21 @@ void alloc_all(Core& c) {
     }
 }
 
-int plug_rows(const Core& c) { return std::max(16, std::min(512, 8192 / std::max(c.fan, 1))); }
 template <class T>
-int plug_smem(const Core& c) { return c.obs_dim * PlugCfg<T>::cols * (int)sizeof(T) + plug_rows(c) * c.fan * 8; }
+int plug_smem(const Core& c) { return c.obs_dim * PlugCfg<T>::cols * (int)sizeof(T); }
 
-template <class T>
-void plug_limits(const Core& c) {
+template <class T, bool SAVE>
+void plug_limit(const Core& c) {
     const int smem = plug_smem<T>(c);
-    CK(cudaFuncSetAttribute(k_plug_fwd<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    CK(cudaFuncSetAttribute(k_plug_fwd<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
 }
 
 void set_smem_limits(const Core& c) {
-    plug_limits<float>(c);
-    plug_limits<__nv_bfloat16>(c);
-    plug_limits<__half>(c);
+    plug_limit<float, true>(c); plug_limit<float, false>(c);
+    plug_limit<__nv_bfloat16, true>(c); plug_limit<__nv_bfloat16, false>(c);
+    plug_limit<__half, true>(c); plug_limit<__half, false>(c);
 }
 
 inline unsigned blocks(long long n, int t = 256) { return (unsigned)((n + t - 1) / t); }
@@ -428,12 +428,22 @@ void check_batch(const Core& c, int B) {
 
 template <class T, bool SAVE>
 void plug_launch(Core& c, const float* Pw, int B) {
-    const int rows = plug_rows(c);
-    const dim3 g((c.n_s + rows - 1) / rows, (B + PlugCfg<T>::cols - 1) / PlugCfg<T>::cols);
+    const int chunks = (B + PlugCfg<T>::cols - 1) / PlugCfg<T>::cols;
+    // enough row blocks for ~2 waves of CTAs, each block at least 64 rows (the staged chunk is shared by its rows)
+    const int nblk = std::max(1, std::min((c.n_s + 63) / 64, (2 * 148 + chunks - 1) / chunks));
+    const int rows = (c.n_s + nblk - 1) / nblk;
+    const dim3 g(nblk, chunks);
     launch(c, K_PLUG_FWD, [&]() {
-        k_plug_fwd<T, SAVE><<<g, kPlugThreads, plug_smem<T>(c), c.st>>>(
-            c.d_in_col, Pw + c.off[3], Pw + c.off[4], c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows,
-            c.obs_dim, B);
+        const int smem = plug_smem<T>(c);
+        if (c.fan == 8)
+            k_plug_fwd<T, SAVE, 8><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+                c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
+        else if (c.fan == 16)
+            k_plug_fwd<T, SAVE, 16><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+                c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
+        else
+            k_plug_fwd<T, SAVE, 0><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+                c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
     });
 }
 
@@ -534,18 +544,27 @@ void backward(Core& c, int B) {
                 k_sddmm<float, true><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase,
                                                                     c.d_gw, gz, hprev, c.live, c.G + c.off[0], B, B);
             });
-        const dim3 gs((h.n_segs + kWarps - 1) / kWarps, chunks), gr((h.n_reds + kWarps - 1) / kWarps, chunks);
+        const dim3 gr((h.n_reds + kWarps - 1) / kWarps, chunks);
+        // groups of chunks whose gz slab (rows x 256 samples x 4 bytes) stays within ~48 MB of L2
+        const int per = std::max(1, (int)((48LL << 20) / ((long long)h.rows * 256 * 4)));
+        auto transposed = [&](auto epi, const NeuronEpi& ep) {
+            constexpr bool EPI = decltype(epi)::value;
+            for (int ch = 0; ch < chunks; ch += per) {
+                const dim3 gs((h.n_segs + kWarps - 1) / kWarps, std::min(per, chunks - ch));
+                launch(c, K_HOP_BWD, [&]() {
+                    k_hop_bwd_t<EPI><<<gs, kThreads, 0, c.st>>>(h.d_segs, c.d_tpairs + h.pbase, gz, nxt, c.seg_part,
+                                                                h.n_segs, B, ch, ep);
+                });
+            }
+            if (h.n_reds)
+                launch(c, K_HOP_BWD, [&]() {
+                    k_seg_reduce<EPI><<<gr, kThreads, 0, c.st>>>(h.d_reds, c.seg_part, nxt, h.n_reds, B, ep);
+                });
+        };
         if (k >= 1) {                        // the layer below is a hop's: its neuron backward rides along
             const Hop& lo = c.hop[k - 1];
             NeuronEpi ep{hprev, c.d_rgain + lo.rbase, c.d_rthr + lo.rbase, lo.d_drow, c.gdrive, c.nsum, chunks};
-            launch(c, K_HOP_BWD, [&]() {
-                k_hop_bwd_t<true><<<gs, kThreads, 0, c.st>>>(h.d_segs, c.d_tpairs + h.pbase, gz, nxt, c.seg_part,
-                                                             h.n_segs, B, ep);
-            });
-            if (h.n_reds)
-                launch(c, K_HOP_BWD, [&]() {
-                    k_seg_reduce<true><<<gr, kThreads, 0, c.st>>>(h.d_reds, c.seg_part, nxt, h.n_reds, B, ep);
-                });
+            transposed(std::true_type{}, ep);
             launch(c, K_ACT_BWD, [&]() {
                 k_neuron_reduce<<<blocks(lo.rows), 256, 0, c.st>>>(c.nsum, lo.d_nid, c.d_rsig + lo.rbase,
                                                                   c.G + c.off[1], c.G + c.off[2], c.live, lo.rows,
@@ -553,14 +572,7 @@ void backward(Core& c, int B) {
             });
         } else {
             NeuronEpi ep{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, chunks};
-            launch(c, K_HOP_BWD, [&]() {
-                k_hop_bwd_t<false><<<gs, kThreads, 0, c.st>>>(h.d_segs, c.d_tpairs + h.pbase, gz, nxt, c.seg_part,
-                                                              h.n_segs, B, ep);
-            });
-            if (h.n_reds)
-                launch(c, K_HOP_BWD, [&]() {
-                    k_seg_reduce<false><<<gr, kThreads, 0, c.st>>>(h.d_reds, c.seg_part, nxt, h.n_reds, B, ep);
-                });
+            transposed(std::false_type{}, ep);
         }
         std::swap(gz, nxt);
     }

@@ -210,7 +210,27 @@ __device__ __forceinline__ void st_ns(__half* p, const float (&v)[4]) {
     *reinterpret_cast<uint2*>(p) = make_uint2(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]));
 }
 
-template <class T, bool SAVE_DRIVE>
+// the row's plug columns and weights, FAN at a time (FAN % 4 == 0) or one by one (FAN == 0: any fan)
+template <int FAN>
+struct PlugRow {
+    int c[FAN > 0 ? FAN : 1];
+    float w[FAN > 0 ? FAN : 1];
+    __device__ __forceinline__ void load(const int* col, const float* wt, size_t e) {
+        if constexpr (FAN > 0) {
+#pragma unroll
+            for (int j = 0; j < FAN; j += 4) {
+                const int4 q = __ldg(reinterpret_cast<const int4*>(col + e + j));
+                const float4 r = __ldg(reinterpret_cast<const float4*>(wt + e + j));
+                c[j] = q.x; c[j + 1] = q.y; c[j + 2] = q.z; c[j + 3] = q.w;
+                w[j] = r.x; w[j + 1] = r.y; w[j + 2] = r.z; w[j + 3] = r.w;
+            }
+        }
+    }
+};
+
+// A CTA owns one chunk of C samples and a block of rows: x for the chunk is staged once, then each warp walks rows
+// (its next row's columns and weights loaded ahead, in registers) gathering from shared memory.
+template <class T, bool SAVE_DRIVE, int FAN>
 __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict__ in_col,
                                                            const float* __restrict__ in_w,
                                                            const float* __restrict__ in_b,
@@ -221,8 +241,6 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
     constexpr int C = PlugCfg<T>::cols, NS = C / 32;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T* xs = reinterpret_cast<T*>(smem_raw);                                   // [obs_dim][C]
-    int* cs = reinterpret_cast<int*>(smem_raw + (size_t)obs_dim * C * sizeof(T));   // [rows][fan]
-    float* ws = reinterpret_cast<float*>(cs + rows_per_cta * fan);                 // [rows][fan]
     const int b0 = blockIdx.y * C;
     const int r_lo = blockIdx.x * rows_per_cta, r_hi = min(n_s, r_lo + rows_per_cta);
     for (int i = threadIdx.x; i < obs_dim * (C / 4); i += blockDim.x) {
@@ -231,29 +249,37 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
         if (b0 + q < ld) v = __ldg(reinterpret_cast<const float4*>(x + (size_t)f * ld + b0 + q));
         cvt_store4(xs + f * C + q, v);
     }
-    const int ne = (r_hi - r_lo) * fan;
-    const size_t e_lo = (size_t)r_lo * fan;
-    for (int i = threadIdx.x; i < ne; i += blockDim.x) {
-        cs[i] = __ldg(&in_col[e_lo + i]);
-        ws[i] = __ldg(&in_w[e_lo + i]);
-    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bl = NS * lane;
     if (b0 + bl >= ld) return;
-    for (int row = r_lo + warp; row < r_hi; row += kPlugThreads / 32) {
+    constexpr int STEP = kPlugThreads / 32;
+    PlugRow<FAN> cur, nxt;
+    int row = r_lo + warp;
+    if (FAN > 0 && row < r_hi) cur.load(in_col, in_w, (size_t)row * FAN);
+    for (; row < r_hi; row += STEP) {
+        if (FAN > 0 && row + STEP < r_hi) nxt.load(in_col, in_w, (size_t)(row + STEP) * FAN);
         float a[NS];
         const float bias = __ldg(&in_b[row]);
 #pragma unroll
         for (int i = 0; i < NS; ++i) a[i] = bias;
-        const int* rc = cs + (row - r_lo) * fan;
-        const float* rw = ws + (row - r_lo) * fan;
-        for (int j = 0; j < fan; ++j) {
-            float v[NS];
-            lds_ns(xs + rc[j] * C + bl, v);
-            const float w = rw[j];
+        if constexpr (FAN > 0) {
 #pragma unroll
-            for (int i = 0; i < NS; ++i) a[i] = fmaf(w, v[i], a[i]);
+            for (int j = 0; j < FAN; ++j) {
+                float v[NS];
+                lds_ns(xs + cur.c[j] * C + bl, v);
+#pragma unroll
+                for (int i = 0; i < NS; ++i) a[i] = fmaf(cur.w[j], v[i], a[i]);
+            }
+        } else {
+            const size_t e0 = (size_t)row * fan;
+            for (int j = 0; j < fan; ++j) {
+                float v[NS];
+                lds_ns(xs + __ldg(&in_col[e0 + j]) * C + bl, v);
+                const float w = __ldg(&in_w[e0 + j]);
+#pragma unroll
+                for (int i = 0; i < NS; ++i) a[i] = fmaf(w, v[i], a[i]);
+            }
         }
         const size_t o = (size_t)row * ld + b0 + bl;
         if (SAVE_DRIVE) {
@@ -265,13 +291,15 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
 #pragma unroll
         for (int i = 0; i < NS; ++i) hv[i] = fmaxf(fmaf(g, a[i], -th), 0.f);
         st_ns(h0 + o, hv);
+        if constexpr (FAN > 0) cur = nxt;
     }
 }
 
 // one hop: z[t,b] = sum over merged pairs (src, w) of row t of w * hp[src, b] (+ drive[drow[t], b]);
-// h = relu(gain*z - thr). One warp per (row, 32*2V-sample chunk): each lane loads 32 bytes of the source row per pair
-// (16 bf16/fp16 or 8 fp32 states) so the pair's own load and address math are shared by many FMAs, and multiplies
-// with packed fp32x2 FMAs (sm_100). Rows run in degree-descending schedule order.
+// h = relu(gain*z - thr). One warp per (row, chunk of 2*32*V samples): each lane loads two 16-byte groups of the
+// source row per pair, the warp's loads of a group being one contiguous 512-byte run (group g of lane l: samples
+// chunk + g*32V + l*V ... + V-1), so the pair record and its address math are shared by 2V FMAs per lane; products use
+// packed fp32x2 FMAs (sm_100). Rows run in degree-descending schedule order.
 // TI: the source layer's type, TO: this layer's (the last layer of a 16-bit network is fp32).
 __device__ __forceinline__ void unpack2(const __nv_bfloat16*, uint32_t x, float2& f) {
     f = make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
@@ -279,91 +307,97 @@ __device__ __forceinline__ void unpack2(const __nv_bfloat16*, uint32_t x, float2
 __device__ __forceinline__ void unpack2(const __half*, uint32_t x, float2& f) {
     f = __half22float2(*reinterpret_cast<const __half2*>(&x));
 }
-// 32 bytes at p as N/2 float2 pairs (N = 16 for 16-bit types, 8 for fp32)
-template <class T, int N>
-__device__ __forceinline__ void ld32(const T* p, float2 (&v)[N / 2]) {
+// 16 bytes at p as float2 pairs (4 for 16-bit types, 2 for fp32)
+template <class T>
+__device__ __forceinline__ void ld16(const T* p, float2 (&v)[16 / sizeof(T) / 2]) {
     const uint4 a = __ldg(reinterpret_cast<const uint4*>(p));
-    const uint4 b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
     if constexpr (sizeof(T) == 4) {
         v[0] = make_float2(__uint_as_float(a.x), __uint_as_float(a.y));
         v[1] = make_float2(__uint_as_float(a.z), __uint_as_float(a.w));
-        v[2] = make_float2(__uint_as_float(b.x), __uint_as_float(b.y));
-        v[3] = make_float2(__uint_as_float(b.z), __uint_as_float(b.w));
     } else {
-        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) unpack2(p, w[i], v[i]);
+        unpack2(p, a.x, v[0]); unpack2(p, a.y, v[1]); unpack2(p, a.z, v[2]); unpack2(p, a.w, v[3]);
     }
 }
+template <class T> struct Vec16 { static constexpr int V = 16 / sizeof(T), H = V / 2; };
 template <class T> struct Lane32 { static constexpr int N = 32 / sizeof(T); };   // states per lane per pair
+                                                                                 // (warp chunk = 32 * N samples)
+
+template <class TO, int V>
+__device__ __forceinline__ void st16(TO* o, const float* hv) {
+    if constexpr (sizeof(TO) == 4) {
+#pragma unroll
+        for (int i = 0; i < V; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(hv[i], hv[i + 1], hv[i + 2], hv[i + 3]);
+    } else {
+        float q[8] = {hv[0], hv[1], hv[2], hv[3], hv[4], hv[5], hv[6], hv[7]};
+        st_act(o, q);
+    }
+}
 
 template <class TI, class TO>
-__global__ void __launch_bounds__(kThreads) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
-                                                      const int2* __restrict__ pairs, const TI* __restrict__ hp,
-                                                      const float* __restrict__ rgain, const float* __restrict__ rthr,
-                                                      const int* __restrict__ drow, const float* __restrict__ drive,
-                                                      TO* __restrict__ h, int n_rows, int ld) {
-    constexpr int N = Lane32<TI>::N, H = N / 2;
+__global__ void __launch_bounds__(kThreads, 6) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
+                                                         const int2* __restrict__ pairs, const TI* __restrict__ hp,
+                                                         const float* __restrict__ rgain, const float* __restrict__ rthr,
+                                                         const int* __restrict__ drow, const float* __restrict__ drive,
+                                                         TO* __restrict__ h, int n_rows, int ld) {
+    constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H;
     const int slot = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (slot >= n_rows) return;
     const int t = __ldg(&sched[slot]);
-    const int c = (blockIdx.y * 32 + lane) * N;
-    if (c >= ld) return;
-    float2 acc[H];
+    const int c0 = blockIdx.y * 64 * V + lane * V, c1 = c0 + 32 * V;     // the lane's two groups
+    if (c0 >= ld) return;
+    const bool g1 = c1 < ld;
+    float2 a0[H], a1[H];
 #pragma unroll
-    for (int i = 0; i < H; ++i) acc[i] = make_float2(0.f, 0.f);
+    for (int i = 0; i < H; ++i) { a0[i] = make_float2(0.f, 0.f); a1[i] = make_float2(0.f, 0.f); }
     const int e0 = __ldg(&pptr[t]), e1 = __ldg(&pptr[t + 1]);
-    const TI* base = hp + c;
     const unsigned row_elems = (unsigned)ld;
-    int e = e0;
-    for (; e + 2 <= e1; e += 2) {                        // two pairs (64 bytes per lane) in flight
-        const int2 p0 = __ldg(&pairs[e]), p1 = __ldg(&pairs[e + 1]);
+    const TI* b0 = hp + c0;
+    const TI* b1 = hp + (g1 ? c1 : c0);
+    for (int e = e0; e < e1; ++e) {
+        const int2 p = __ldg(&pairs[e]);
+        const size_t ro = (size_t)((unsigned)p.x * row_elems);
         float2 v0[H], v1[H];
-        ld32<TI, N>(base + (size_t)((unsigned)p0.x * row_elems), v0);
-        ld32<TI, N>(base + (size_t)((unsigned)p1.x * row_elems), v1);
-        const float2 w0 = make_float2(__int_as_float(p0.y), __int_as_float(p0.y));
-        const float2 w1 = make_float2(__int_as_float(p1.y), __int_as_float(p1.y));
+        ld16<TI>(b0 + ro, v0);
+        if (g1) ld16<TI>(b1 + ro, v1);
+        const float2 w = make_float2(__int_as_float(p.y), __int_as_float(p.y));
 #pragma unroll
-        for (int i = 0; i < H; ++i) acc[i] = __ffma2_rn(w0, v0[i], acc[i]);
+        for (int i = 0; i < H; ++i) a0[i] = __ffma2_rn(w, v0[i], a0[i]);
+        if (g1) {
 #pragma unroll
-        for (int i = 0; i < H; ++i) acc[i] = __ffma2_rn(w1, v1[i], acc[i]);
-    }
-    if (e < e1) {
-        const int2 p0 = __ldg(&pairs[e]);
-        float2 v0[H];
-        ld32<TI, N>(base + (size_t)((unsigned)p0.x * row_elems), v0);
-        const float2 w0 = make_float2(__int_as_float(p0.y), __int_as_float(p0.y));
-#pragma unroll
-        for (int i = 0; i < H; ++i) acc[i] = __ffma2_rn(w0, v0[i], acc[i]);
+            for (int i = 0; i < H; ++i) a1[i] = __ffma2_rn(w, v1[i], a1[i]);
+        }
     }
     if (drow) {
         const int d = __ldg(&drow[t]);
         if (d >= 0) {
-            const float4* dr = reinterpret_cast<const float4*>(drive + (size_t)d * ld + c);
 #pragma unroll
-            for (int i = 0; i < H / 2; ++i) {
-                const float4 q = __ldg(dr + i);
-                acc[2 * i].x += q.x; acc[2 * i].y += q.y; acc[2 * i + 1].x += q.z; acc[2 * i + 1].y += q.w;
+            for (int gi = 0; gi < 2; ++gi) {
+                if (gi == 1 && !g1) break;
+                float2* a = gi ? a1 : a0;
+                const float4* dr = reinterpret_cast<const float4*>(drive + (size_t)d * ld + (gi ? c1 : c0));
+#pragma unroll
+                for (int i = 0; i < H / 2; ++i) {
+                    const float4 q = __ldg(dr + i);
+                    a[2 * i].x += q.x; a[2 * i].y += q.y; a[2 * i + 1].x += q.z; a[2 * i + 1].y += q.w;
+                }
             }
         }
     }
     const float g = __ldg(&rgain[t]), th = __ldg(&rthr[t]);
-    float hv[N];
+    float hv[V];
 #pragma unroll
     for (int i = 0; i < H; ++i) {
-        hv[2 * i] = fmaxf(fmaf(g, acc[i].x, -th), 0.f);
-        hv[2 * i + 1] = fmaxf(fmaf(g, acc[i].y, -th), 0.f);
+        hv[2 * i] = fmaxf(fmaf(g, a0[i].x, -th), 0.f);
+        hv[2 * i + 1] = fmaxf(fmaf(g, a0[i].y, -th), 0.f);
     }
-    TO* o = h + (size_t)t * ld + c;
-    if constexpr (sizeof(TO) == 4) {
+    st16<TO, V>(h + (size_t)t * ld + c0, hv);
+    if (g1) {
 #pragma unroll
-        for (int i = 0; i < N; i += 4) *reinterpret_cast<float4*>(o + i) = make_float4(hv[i], hv[i + 1], hv[i + 2], hv[i + 3]);
-    } else {
-#pragma unroll
-        for (int i = 0; i < N; i += 8) {
-            float q[8] = {hv[i], hv[i + 1], hv[i + 2], hv[i + 3], hv[i + 4], hv[i + 5], hv[i + 6], hv[i + 7]};
-            st_act(o + i, q);
+        for (int i = 0; i < H; ++i) {
+            hv[2 * i] = fmaxf(fmaf(g, a1[i].x, -th), 0.f);
+            hv[2 * i + 1] = fmaxf(fmaf(g, a1[i].y, -th), 0.f);
         }
+        st16<TO, V>(h + (size_t)t * ld + c1, hv);
     }
 }
 
@@ -630,7 +664,7 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
 template <class T, bool ATOMIC>
 __global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ pptr, const int2* __restrict__ pairs,
                                                     const int* __restrict__ gptr, const int* __restrict__ gw,
-                                                    const float* __restrict__ gz, const T* __restrict__ hp,
+                                                    const float* __restrict__ gz, const float* __restrict__ hp,
                                                     const int* __restrict__ live, float* __restrict__ gW, int B,
                                                     int ld) {
     __shared__ float red[8 * kWarps];
@@ -647,13 +681,13 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ pptr
 #pragma unroll
         for (int u = 0; u < 8; ++u) acc[u] = 0.f;
         for (int b = threadIdx.x * 4; b < B; b += kThreads * 4) {
-            float4 q = __ldg(reinterpret_cast<const float4*>(g + b));
+            const float4 q = __ldg(reinterpret_cast<const float4*>(g + b));
+            if (q.x == 0.f && q.y == 0.f && q.z == 0.f && q.w == 0.f) continue;     // silent samples: nothing to add
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 if (u < np) {
-                    const T* hs = hp + (size_t)src[u] * ld + b;
-                    float h0 = ld1(hs), h1 = ld1(hs + 1), h2 = ld1(hs + 2), h3 = ld1(hs + 3);
-                    acc[u] = fmaf(q.x, h0, fmaf(q.y, h1, fmaf(q.z, h2, fmaf(q.w, h3, acc[u]))));
+                    const float4 hq = __ldg(reinterpret_cast<const float4*>(hp + (size_t)src[u] * ld + b));
+                    acc[u] = fmaf(q.x, hq.x, fmaf(q.y, hq.y, fmaf(q.z, hq.z, fmaf(q.w, hq.w, acc[u]))));
                 }
             }
         }
@@ -673,8 +707,10 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ pptr
 // transposed hop: gh[s, b] = sum over merged pairs (dst, w) of source row s of w * gz[dst, b]. The source rows are
 // cut into segments of at most a fixed number of pairs (hub sources have tens of thousands); a segment of a row that
 // has one finishes the row, the others write a partial row that k_seg_reduce adds up in slot order.
-// One warp per (segment, 256-sample chunk), 32 bytes (8 states) per lane per pair, packed fp32x2 FMAs; segments
-// longest first. seg = {row, first pair, end pair, slot or -1}.
+// One warp per (segment, 256-sample chunk); each lane owns two 4-sample groups 128 samples apart (every warp load is
+// one contiguous 512-byte run); packed fp32x2 FMAs; segments longest first. seg = {row, first pair, end, slot or -1}.
+// The host launches it over groups of chunks (chunk0 = the group's first) small enough that the gz columns a launch
+// gathers from stay in L2: hub rows reach every destination row, so each chunk reads its whole gz column slab.
 // Finishing a row (EPI): the source layer's neuron backward is fused in - g = gh * [h > 0]; gz = g * gain is written
 // (not gh), gdrive[drow] += gz, and the row's per-chunk sums of g*z (z = (h + thr) / gain where h > 0), of g and of
 // [g != 0] go to nsum[row][chunk][3] for k_neuron_reduce. Without EPI (the sensory layer) gh itself is written.
@@ -687,110 +723,101 @@ struct NeuronEpi {
     float* nsum;             // [rows][chunks][3]
     int chunks;
 };
+// one 4-sample group of a finished row: stores, and adds the group's neuron sums into s[3]
 template <bool EPI>
-__device__ __forceinline__ void finish_row(int s, int chunk, int c, int ld, float (&a)[8], float* out,
-                                           const NeuronEpi& ep, bool on) {
+__device__ __forceinline__ void finish_group(int s, int c, int ld, const float (&a)[4], float* out,
+                                             const NeuronEpi& ep, float gn, float th, float inv_g, float (&sum)[3]) {
     float* o = out + (size_t)s * ld + c;
     if (!EPI) {
         *reinterpret_cast<float4*>(o) = make_float4(a[0], a[1], a[2], a[3]);
-        *reinterpret_cast<float4*>(o + 4) = make_float4(a[4], a[5], a[6], a[7]);
         return;
     }
-    const float gn = __ldg(&ep.rgain[s]), th = __ldg(&ep.rthr[s]);
-    const float inv_g = gn != 0.f ? 1.f / gn : 0.f;
-    float4 h0 = make_float4(0.f, 0.f, 0.f, 0.f), h1 = h0;
-    if (on) {
-        h0 = __ldg(reinterpret_cast<const float4*>(ep.h + (size_t)s * ld + c));
-        h1 = __ldg(reinterpret_cast<const float4*>(ep.h + (size_t)s * ld + c) + 1);
-    }
-    const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-    float gz[8], s0 = 0.f, s1 = 0.f, s2 = 0.f;
+    const float4 hq = __ldg(reinterpret_cast<const float4*>(ep.h + (size_t)s * ld + c));
+    const float hv[4] = {hq.x, hq.y, hq.z, hq.w};
+    float gz[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 4; ++i) {
         const float g = hv[i] > 0.f ? a[i] : 0.f;
         gz[i] = g * gn;
-        s0 = fmaf(g, (hv[i] + th) * inv_g, s0);
-        s1 += g;
-        s2 += g != 0.f ? 1.f : 0.f;
+        sum[0] = fmaf(g, (hv[i] + th) * inv_g, sum[0]);
+        sum[1] += g;
+        sum[2] += g != 0.f ? 1.f : 0.f;
     }
-    if (on) {
-        *reinterpret_cast<float4*>(o) = make_float4(gz[0], gz[1], gz[2], gz[3]);
-        *reinterpret_cast<float4*>(o + 4) = make_float4(gz[4], gz[5], gz[6], gz[7]);
-    }
-    if (on && ep.drow) {
+    *reinterpret_cast<float4*>(o) = make_float4(gz[0], gz[1], gz[2], gz[3]);
+    if (ep.drow) {
         const int d = __ldg(&ep.drow[s]);
         if (d >= 0) {
             float4* gd = reinterpret_cast<float4*>(ep.gdrive + (size_t)d * ld + c);
-            float4 u = gd[0], v = gd[1];
+            float4 u = *gd;
             u.x += gz[0]; u.y += gz[1]; u.z += gz[2]; u.w += gz[3];
-            v.x += gz[4]; v.y += gz[5]; v.z += gz[6]; v.w += gz[7];
-            gd[0] = u; gd[1] = v;
+            *gd = u;
         }
     }
-    s0 = warp_sum(s0); s1 = warp_sum(s1); s2 = warp_sum(s2);
-    if ((threadIdx.x & 31) == 0) {
-        float* ns = ep.nsum + ((size_t)s * ep.chunks + chunk) * 3;
-        ns[0] = s0; ns[1] = s1; ns[2] = s2;
+}
+// the lane's two groups of a finished row (valid: in the batch); the warp then reduces the neuron sums
+template <bool EPI>
+__device__ __forceinline__ void finish_row(int s, int chunk, int c0, int c1, bool v0, bool v1, int ld,
+                                           const float (&a0)[4], const float (&a1)[4], float* out,
+                                           const NeuronEpi& ep) {
+    float sum[3] = {0.f, 0.f, 0.f};
+    float gn = 0.f, th = 0.f, inv_g = 0.f;
+    if (EPI) {
+        gn = __ldg(&ep.rgain[s]);
+        th = __ldg(&ep.rthr[s]);
+        inv_g = gn != 0.f ? 1.f / gn : 0.f;
+    }
+    if (v0) finish_group<EPI>(s, c0, ld, a0, out, ep, gn, th, inv_g, sum);
+    if (v1) finish_group<EPI>(s, c1, ld, a1, out, ep, gn, th, inv_g, sum);
+    if (EPI) {
+        sum[0] = warp_sum(sum[0]); sum[1] = warp_sum(sum[1]); sum[2] = warp_sum(sum[2]);
+        if ((threadIdx.x & 31) == 0) {
+            float* ns = ep.nsum + ((size_t)s * ep.chunks + chunk) * 3;
+            ns[0] = sum[0]; ns[1] = sum[1]; ns[2] = sum[2];
+        }
     }
 }
 
 template <bool EPI>
-__global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__ segs, const int2* __restrict__ tpairs,
-                                                        const float* __restrict__ gz, float* __restrict__ out,
-                                                        float* __restrict__ part, int n_segs, int ld, NeuronEpi ep) {
+__global__ void __launch_bounds__(kThreads, 6) k_hop_bwd_t(const int4* __restrict__ segs,
+                                                           const int2* __restrict__ tpairs,
+                                                           const float* __restrict__ gz, float* __restrict__ out,
+                                                           float* __restrict__ part, int n_segs, int ld, int chunk0,
+                                                           NeuronEpi ep) {
     const int sidx = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (sidx >= n_segs) return;
     const int4 sg = __ldg(&segs[sidx]);
-    const int c = (blockIdx.y * 32 + lane) * 8;
-    // every lane stays to the end: the epilogue reduces over the warp (ld is a multiple of 32: lanes past the batch
-    // read and write nothing)
-    const bool on = c < ld;
-    float2 acc[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i] = make_float2(0.f, 0.f);
-    const float* base = gz + (on ? c : 0);
+    const int chunk = chunk0 + blockIdx.y;
+    const int c0 = chunk * 256 + lane * 4, c1 = c0 + 128;
+    // lanes past the batch stay to the end (the epilogue reduces over the warp) but load and store nothing
+    const bool v0 = c0 < ld, v1 = c1 < ld;
+    float2 a0[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)}, a1[2] = {a0[0], a0[1]};
     const unsigned row_elems = (unsigned)ld;
-    int e = sg.y;
-    if (on) {
-        for (; e + 2 <= sg.z; e += 2) {
-            const int2 p0 = __ldg(&tpairs[e]), p1 = __ldg(&tpairs[e + 1]);
-            float2 v0[4], v1[4];
-            ld32<float, 8>(base + (size_t)((unsigned)p0.x * row_elems), v0);
-            ld32<float, 8>(base + (size_t)((unsigned)p1.x * row_elems), v1);
-            const float2 w0 = make_float2(__int_as_float(p0.y), __int_as_float(p0.y));
-            const float2 w1 = make_float2(__int_as_float(p1.y), __int_as_float(p1.y));
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] = __ffma2_rn(w0, v0[i], acc[i]);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] = __ffma2_rn(w1, v1[i], acc[i]);
-        }
-        if (e < sg.z) {
-            const int2 p0 = __ldg(&tpairs[e]);
-            float2 v0[4];
-            ld32<float, 8>(base + (size_t)((unsigned)p0.x * row_elems), v0);
-            const float2 w0 = make_float2(__int_as_float(p0.y), __int_as_float(p0.y));
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] = __ffma2_rn(w0, v0[i], acc[i]);
+    const float* b0 = gz + (v0 ? c0 : 0);
+    const float* b1 = gz + (v1 ? c1 : 0);
+    if (v0) {
+        for (int e = sg.y; e < sg.z; ++e) {
+            const int2 p = __ldg(&tpairs[e]);
+            const size_t ro = (size_t)((unsigned)p.x * row_elems);
+            float2 x0[2], x1[2];
+            ld16<float>(b0 + ro, x0);
+            if (v1) ld16<float>(b1 + ro, x1);
+            const float2 w = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+            a0[0] = __ffma2_rn(w, x0[0], a0[0]);
+            a0[1] = __ffma2_rn(w, x0[1], a0[1]);
+            if (v1) {
+                a1[0] = __ffma2_rn(w, x1[0], a1[0]);
+                a1[1] = __ffma2_rn(w, x1[1], a1[1]);
+            }
         }
     }
-    float a[8] = {acc[0].x, acc[0].y, acc[1].x, acc[1].y, acc[2].x, acc[2].y, acc[3].x, acc[3].y};
+    const float r0[4] = {a0[0].x, a0[0].y, a0[1].x, a0[1].y}, r1[4] = {a1[0].x, a1[0].y, a1[1].x, a1[1].y};
     if (sg.w >= 0) {
-        if (on) {
-            float* o = part + (size_t)sg.w * ld + c;
-            *reinterpret_cast<float4*>(o) = make_float4(a[0], a[1], a[2], a[3]);
-            *reinterpret_cast<float4*>(o + 4) = make_float4(a[4], a[5], a[6], a[7]);
-        }
+        float* o = part + (size_t)sg.w * ld;
+        if (v0) *reinterpret_cast<float4*>(o + c0) = make_float4(r0[0], r0[1], r0[2], r0[3]);
+        if (v1) *reinterpret_cast<float4*>(o + c1) = make_float4(r1[0], r1[1], r1[2], r1[3]);
         return;
     }
-    if (EPI) {
-        if (!on) {                                         // keep the warp reduction whole; contribute zeros
-#pragma unroll
-            for (int i = 0; i < 8; ++i) a[i] = 0.f;
-        }
-        finish_row<EPI>(sg.x, blockIdx.y, on ? c : 0, ld, a, out, ep, on);
-    } else if (on) {
-        finish_row<EPI>(sg.x, blockIdx.y, c, ld, a, out, ep, true);
-    }
+    finish_row<EPI>(sg.x, chunk, c0, c1, v0, v1, ld, r0, r1, out, ep);
 }
 // red = {row, first slot, slot count, -}: the row = the sum of its partial rows in slot order, then finished as above
 template <bool EPI>
@@ -799,19 +826,21 @@ __global__ void __launch_bounds__(kThreads) k_seg_reduce(const int4* __restrict_
     const int ridx = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (ridx >= n_red) return;
     const int4 r = __ldg(&red[ridx]);
-    const int c = (blockIdx.y * 32 + lane) * 8;
-    const bool on = c < ld;
-    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (on) {
-        for (int i = 0; i < r.z; ++i) {
-            const float4* q = reinterpret_cast<const float4*>(part + (size_t)(r.y + i) * ld + c);
-            const float4 u = __ldg(q), v = __ldg(q + 1);
-            a[0] += u.x; a[1] += u.y; a[2] += u.z; a[3] += u.w;
-            a[4] += v.x; a[5] += v.y; a[6] += v.z; a[7] += v.w;
+    const int c0 = blockIdx.y * 256 + lane * 4, c1 = c0 + 128;
+    const bool v0 = c0 < ld, v1 = c1 < ld;
+    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int i = 0; i < r.z; ++i) {
+        const float* q = part + (size_t)(r.y + i) * ld;
+        if (v0) {
+            const float4 u = __ldg(reinterpret_cast<const float4*>(q + c0));
+            a0[0] += u.x; a0[1] += u.y; a0[2] += u.z; a0[3] += u.w;
+        }
+        if (v1) {
+            const float4 u = __ldg(reinterpret_cast<const float4*>(q + c1));
+            a1[0] += u.x; a1[1] += u.y; a1[2] += u.z; a1[3] += u.w;
         }
     }
-    if (EPI) finish_row<EPI>(r.x, blockIdx.y, on ? c : 0, ld, a, out, ep, on);
-    else if (on) finish_row<EPI>(r.x, blockIdx.y, c, ld, a, out, ep, true);
+    finish_row<EPI>(r.x, blockIdx.y, c0, c1, v0, v1, ld, a0, a1, out, ep);
 }
 // per row of a layer: gain grad += sum over chunks of g*z, theta grad += -(sum of g) * sigmoid(theta); live = any g
 __global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __restrict__ nid,

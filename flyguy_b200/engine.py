@@ -118,6 +118,29 @@ class Engine:
         else they accumulate in the library's gradient (NativeFlyActor + NativeAdam)."""
         return _Logits.apply(obs, self.hook, self, to_torch)
 
+    def run_average(self, obs: torch.Tensor) -> torch.Tensor:
+        """Forward with the library's running average of the weights (fc_forward with ema 1), no gradients."""
+        h = self.training_handle()
+        outs = []
+        for i in range(0, obs.shape[0], h.max_batch):
+            x = obs[i:i + h.max_batch]
+            b = x.shape[0]
+            outs.append(h.forward(_pad32(x.float()).contiguous(), 1)[:b])
+            self.gen += 1
+        return torch.cat(outs) if len(outs) > 1 else outs[0]
+
+    def average_state(self):
+        """A copy of the actor (no library handle) holding the library's running average of the weights."""
+        import copy
+        a = copy.deepcopy(self.actor)
+        E = self.train.get(1)
+        with torch.no_grad():
+            a.w[self.wmap.to(a.w.device)] = E[0].to(a.w.device)
+            for p, v in ((a.gain, E[1]), (a.theta, E[2]), (a.in_w, E[3]), (a.in_b, E[4]), (a.out.weight, E[5]),
+                         (a.out.bias, E[6])):
+                p.copy_(v.view_as(p))
+        return a
+
     def pull(self) -> None:
         """The library's weights -> the torch parameters (after a library optimiser step)."""
         a = self.actor

@@ -113,3 +113,29 @@ def test_flyactor_16bit_inference(toy, cuda):
     with torch.no_grad():
         got = f(torch.as_tensor(d["obs"]).cuda()).cpu().numpy()
     assert rel(got, d["logits"]) < 1e-2
+
+
+def test_teach_trainer_learns_and_saves(tmp_path, cuda):
+    """flyguy/teach.py's loop on the library: a student network distils a teacher (a different random fly network)
+    from a FLYD file; the running average gets closer to the teacher and is saved as a checkpoint that loads back."""
+    import argparse
+    from flyguy_b200.model import load_actor, save_actor
+    from flyguy_b200.teach import train, write_moments
+    toy_connectome(tmp_path / "g.npz", 700, 90, 40, 6000, seed=1)
+    cfg = {"fly_graph": str(tmp_path / "g.npz"), "fly_hops": 3, "fly_fan": 8, "fly_kernel": "torch"}
+    torch.manual_seed(5)
+    t = FlyActor(tmp_path / "g.npz", 517, 90, hops=3, fan=8)
+    with torch.no_grad():
+        t.w.abs_().mul_(2.0)
+        t.out.weight.normal_(0, 0.3)
+        t.theta.fill_(-2.5)
+    save_actor(tmp_path / "teacher.pt", t, cfg, 0)
+    rng = np.random.default_rng(0)
+    write_moments(tmp_path / "m.bin", rng.standard_normal((3000, 517)).astype(np.float16))
+    args = argparse.Namespace(data=[tmp_path / "m.bin"], teacher=tmp_path / "teacher.pt", start="fresh", graph="",
+                              graph_root=None, hops=0, steps=150, batch=64, lr=3e-3, temp=1.0, average=0.99,
+                              holdout=0.1, eval_every=150, out=tmp_path / "student.pt", seed=0)
+    r = train(args)
+    assert r["kl"] < r["kl0"], r
+    ck, s = load_actor(tmp_path / "student.pt", native=False, device="cuda")
+    assert ck["taught_steps"] == 150
