@@ -38,12 +38,13 @@ struct Hop {
     int *d_nid = nullptr, *d_drow = nullptr, *d_sched = nullptr, *d_pptr = nullptr;
     int *d_tsched = nullptr, *d_tptr = nullptr;
     int4 *d_segs = nullptr, *d_reds = nullptr;   // transposed product: segments of source rows, split-row reductions
+    int* d_seg_red = nullptr;                    // per segment: its split row's reduction index, or -1
     int n_segs = 0, n_reds = 0, n_slots = 0;
     void* d_h = nullptr;                     // states [rows, ld]
     bool out_f32 = false;                    // this hop's layer is stored in fp32 (the last layer always is)
 };
 
-constexpr int kSegLen = 512;                 // pairs per transposed segment
+constexpr int kSegLen = 256;                 // pairs per transposed segment
 
 // kernel classes timed by fg_timing (CUDA events around every launch of the class, on the handle's stream)
 enum KClass { K_TRANSPOSE, K_FOLD, K_PLUG_FWD, K_HOP_FWD, K_OUT_FWD, K_LOSS, K_OUT_BWD, K_ACT_BWD, K_SDDMM, K_HOP_BWD,
@@ -64,6 +65,7 @@ struct Core {
     bool bf16 = false, f16 = false, train = true, redrive = false;
     float* owT = nullptr;                                // out_w transposed, padded to kOutA actions
     float* seg_part = nullptr;                           // partial rows of split transposed segments
+    int* seg_done = nullptr;                             // arrival counters of split rows' segments [red][chunk]
     int *d_in_crow = nullptr, *d_in_col = nullptr, *d_n0 = nullptr, *d_dn = nullptr;
     std::vector<Hop> hop;
     long long R = 0, Ptot = 0, Etot = 0;
@@ -208,20 +210,34 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
     std::stable_sort(tsched.begin(), tsched.end(),
                      [&](int a, int b) { return tptr[a + 1] - tptr[a] > tptr[b + 1] - tptr[b]; });
     std::vector<int4> segs, reds;
+    std::vector<int> seg_red;
     for (int s = 0; s < h.n_src; ++s) {
         const int n = tptr[s + 1] - tptr[s];
-        if (n <= kSegLen) { segs.push_back(make_int4(s, tptr[s], tptr[s + 1], -1)); continue; }
+        if (n <= kSegLen) {
+            segs.push_back(make_int4(s, tptr[s], tptr[s + 1], -1));
+            seg_red.push_back(-1);
+            continue;
+        }
         const int nseg = (n + kSegLen - 1) / kSegLen;
-        reds.push_back(make_int4(s, h.n_slots, nseg, 0));
-        for (int i = 0; i < nseg; ++i)
+        for (int i = 0; i < nseg; ++i) {
             segs.push_back(make_int4(s, tptr[s] + i * kSegLen, std::min(tptr[s + 1], tptr[s] + (i + 1) * kSegLen),
                                      h.n_slots + i));
+            seg_red.push_back((int)reds.size());
+        }
+        reds.push_back(make_int4(s, h.n_slots, nseg, 0));
         h.n_slots += nseg;
     }
-    std::stable_sort(segs.begin(), segs.end(), [](const int4& a, const int4& b) { return a.z - a.y > b.z - b.y; });
+    std::vector<int> by_len(segs.size());
+    std::iota(by_len.begin(), by_len.end(), 0);
+    std::stable_sort(by_len.begin(), by_len.end(),
+                     [&](int a, int b) { return segs[a].z - segs[a].y > segs[b].z - segs[b].y; });
+    std::vector<int4> segs_s(segs.size());
+    std::vector<int> red_s(segs.size());
+    for (size_t i = 0; i < by_len.size(); ++i) { segs_s[i] = segs[by_len[i]]; red_s[i] = seg_red[by_len[i]]; }
     h.n_segs = (int)segs.size();
     h.n_reds = (int)reds.size();
-    h.d_segs = upload(c, segs);
+    h.d_segs = upload(c, segs_s);
+    h.d_seg_red = upload(c, red_s);
     h.d_reds = upload(c, reds);
     h.d_pptr = upload(c, pptr);
     h.d_sched = upload(c, sched);
@@ -382,6 +398,11 @@ void alloc_all(Core& c) {
         int slots = 0;
         for (auto& h : c.hop) slots = std::max(slots, h.n_slots);
         c.seg_part = dalloc<float>(c, (size_t)slots * B);
+        int reds = 0;
+        for (auto& h : c.hop) reds = std::max(reds, h.n_reds);
+        const size_t n_done = std::max<size_t>(1, (size_t)reds * ((B + 255) / 256));
+        c.seg_done = dalloc<int>(c, n_done);
+        CK(cudaMemset(c.seg_done, 0, n_done * sizeof(int)));
         c.ag_s = dalloc<float>(c, B);
     }
 }
@@ -449,12 +470,18 @@ void plug_launch(Core& c, const float* Pw, int B) {
 
 template <class TI, class TO>
 void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
-    constexpr int N = Lane32<TI>::N;
+    constexpr int N = Lane32<TI>::N;                     // samples per lane; the warp's chunk is 32 N
     const dim3 g((h.rows + kWarps - 1) / kWarps, (unsigned)((B + 32 * N - 1) / (32 * N)));
+    const bool full = B % (32 * N) == 0;
     launch(c, K_HOP_FWD, [&]() {
-        k_hop_fwd<TI, TO><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase, (const TI*)hp,
-                                                    c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive,
-                                                    (TO*)h.d_h, h.rows, B);
+        if (full)
+            k_hop_fwd<TI, TO, true><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase,
+                                                              (const TI*)hp, c.d_rgain + h.rbase, c.d_rthr + h.rbase,
+                                                              h.d_drow, c.drive, (TO*)h.d_h, h.rows, B);
+        else
+            k_hop_fwd<TI, TO, false><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase,
+                                                               (const TI*)hp, c.d_rgain + h.rbase, c.d_rthr + h.rbase,
+                                                               h.d_drow, c.drive, (TO*)h.d_h, h.rows, B);
     });
 }
 
@@ -544,22 +571,20 @@ void backward(Core& c, int B) {
                 k_sddmm<float, true><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase,
                                                                     c.d_gw, gz, hprev, c.live, c.G + c.off[0], B, B);
             });
-        const dim3 gr((h.n_reds + kWarps - 1) / kWarps, chunks);
-        // groups of chunks whose gz slab (rows x 256 samples x 4 bytes) stays within ~48 MB of L2
-        const int per = std::max(1, (int)((48LL << 20) / ((long long)h.rows * 256 * 4)));
+        const bool full = B % 256 == 0;
         auto transposed = [&](auto epi, const NeuronEpi& ep) {
             constexpr bool EPI = decltype(epi)::value;
-            for (int ch = 0; ch < chunks; ch += per) {
-                const dim3 gs((h.n_segs + kWarps - 1) / kWarps, std::min(per, chunks - ch));
-                launch(c, K_HOP_BWD, [&]() {
-                    k_hop_bwd_t<EPI><<<gs, kThreads, 0, c.st>>>(h.d_segs, c.d_tpairs + h.pbase, gz, nxt, c.seg_part,
-                                                                h.n_segs, B, ch, ep);
-                });
-            }
-            if (h.n_reds)
-                launch(c, K_HOP_BWD, [&]() {
-                    k_seg_reduce<EPI><<<gr, kThreads, 0, c.st>>>(h.d_reds, c.seg_part, nxt, h.n_reds, B, ep);
-                });
+            const dim3 gs((h.n_segs + kWarps - 1) / kWarps, chunks);
+            launch(c, K_HOP_BWD, [&]() {
+                if (full)
+                    k_hop_bwd_t<EPI, true><<<gs, kThreads, 0, c.st>>>(h.d_segs, h.d_seg_red, h.d_reds, c.seg_done,
+                                                                      c.d_tpairs + h.pbase, gz, nxt, c.seg_part,
+                                                                      h.n_segs, B, ep);
+                else
+                    k_hop_bwd_t<EPI, false><<<gs, kThreads, 0, c.st>>>(h.d_segs, h.d_seg_red, h.d_reds, c.seg_done,
+                                                                       c.d_tpairs + h.pbase, gz, nxt, c.seg_part,
+                                                                       h.n_segs, B, ep);
+            });
         };
         if (k >= 1) {                        // the layer below is a hop's: its neuron backward rides along
             const Hop& lo = c.hop[k - 1];

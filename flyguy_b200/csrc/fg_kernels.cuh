@@ -178,7 +178,7 @@ __global__ void k_to_neuron_major(const float* __restrict__ in, float* __restric
 // states - 128 samples - or fp32 - 64 samples) and its rows' plug columns and weights in shared memory, then every warp
 // computes rows from there: lane l owns the chunk's samples [NS*l, NS*l + NS).
 constexpr int kPlugThreads = 512;
-template <class T> struct PlugCfg { static constexpr int cols = sizeof(T) == 4 ? 64 : 128; };
+template <class T> struct PlugCfg { static constexpr int cols = sizeof(T) == 4 ? 32 : 64; };   // 66 KB staged
 __device__ __forceinline__ void cvt_store4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 __device__ __forceinline__ void cvt_store4(__nv_bfloat16* p, float4 v) {
     *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
@@ -186,7 +186,22 @@ __device__ __forceinline__ void cvt_store4(__nv_bfloat16* p, float4 v) {
 __device__ __forceinline__ void cvt_store4(__half* p, float4 v) {
     *reinterpret_cast<uint2*>(p) = make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
 }
-// NS consecutive staged values as fp32 (NS = 2 for fp32, 4 for 16-bit types)
+// NS consecutive staged values as fp32 (NS = 1 for fp32, 2 for 16-bit types)
+__device__ __forceinline__ void lds_ns(const float* p, float (&v)[1]) { v[0] = *p; }
+__device__ __forceinline__ void lds_ns(const __nv_bfloat16* p, float (&v)[2]) {
+    const uint32_t q = *reinterpret_cast<const uint32_t*>(p);
+    v[0] = __uint_as_float(q << 16); v[1] = __uint_as_float(q & 0xffff0000u);
+}
+__device__ __forceinline__ void lds_ns(const __half* p, float (&v)[2]) {
+    const uint32_t q = *reinterpret_cast<const uint32_t*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&q));
+    v[0] = a.x; v[1] = a.y;
+}
+__device__ __forceinline__ void st_ns(float* p, const float (&v)[1]) { *p = v[0]; }
+__device__ __forceinline__ void st_ns(__nv_bfloat16* p, const float (&v)[2]) {
+    *reinterpret_cast<uint32_t*>(p) = pack_bf16(v[0], v[1]);
+}
+__device__ __forceinline__ void st_ns(__half* p, const float (&v)[2]) { *reinterpret_cast<uint32_t*>(p) = pack_f16(v[0], v[1]); }
 __device__ __forceinline__ void lds_ns(const float* p, float (&v)[2]) {
     const float2 q = *reinterpret_cast<const float2*>(p);
     v[0] = q.x; v[1] = q.y;
@@ -283,8 +298,8 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
         }
         const size_t o = (size_t)row * ld + b0 + bl;
         if (SAVE_DRIVE) {
-#pragma unroll
-            for (int i = 0; i < NS; i += 2) *reinterpret_cast<float2*>(drive + o + i) = make_float2(a[i], a[i + 1]);
+            if constexpr (NS == 1) drive[o] = a[0];
+            else *reinterpret_cast<float2*>(drive + o) = make_float2(a[0], a[1]);
         }
         const float g = __ldg(&rgain[row]), th = __ldg(&rthr[row]);
         float hv[NS];
@@ -333,38 +348,63 @@ __device__ __forceinline__ void st16(TO* o, const float* hv) {
     }
 }
 
-template <class TI, class TO>
-__global__ void __launch_bounds__(kThreads, 6) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
-                                                         const int2* __restrict__ pairs, const TI* __restrict__ hp,
-                                                         const float* __restrict__ rgain, const float* __restrict__ rthr,
-                                                         const int* __restrict__ drow, const float* __restrict__ drive,
-                                                         TO* __restrict__ h, int n_rows, int ld) {
+// FULL: the warp's whole chunk lies inside the batch (ld a multiple of 64 V): no per-pair validity tests.
+template <class TI, class TO, bool FULL>
+__global__ void __launch_bounds__(kThreads) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
+                                                      const int2* __restrict__ pairs, const TI* __restrict__ hp,
+                                                      const float* __restrict__ rgain, const float* __restrict__ rthr,
+                                                      const int* __restrict__ drow, const float* __restrict__ drive,
+                                                      TO* __restrict__ h, int n_rows, int ld) {
     constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H;
     const int slot = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (slot >= n_rows) return;
     const int t = __ldg(&sched[slot]);
     const int c0 = blockIdx.y * 64 * V + lane * V, c1 = c0 + 32 * V;     // the lane's two groups
-    if (c0 >= ld) return;
-    const bool g1 = c1 < ld;
+    if (!FULL && c0 >= ld) return;
+    const bool g1 = FULL || c1 < ld;
     float2 a0[H], a1[H];
 #pragma unroll
     for (int i = 0; i < H; ++i) { a0[i] = make_float2(0.f, 0.f); a1[i] = make_float2(0.f, 0.f); }
     const int e0 = __ldg(&pptr[t]), e1 = __ldg(&pptr[t + 1]);
-    const unsigned row_elems = (unsigned)ld;
-    const TI* b0 = hp + c0;
-    const TI* b1 = hp + (g1 ? c1 : c0);
-    for (int e = e0; e < e1; ++e) {
-        const int2 p = __ldg(&pairs[e]);
-        const size_t ro = (size_t)((unsigned)p.x * row_elems);
-        float2 v0[H], v1[H];
-        ld16<TI>(b0 + ro, v0);
-        if (g1) ld16<TI>(b1 + ro, v1);
-        const float2 w = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+    const size_t row_bytes = (size_t)ld * sizeof(TI);
+    const char* base = reinterpret_cast<const char*>(hp + c0);
+    constexpr int G1 = 32 * 16;                          // byte offset of the lane's second group
+    int e = e0;
+    if (g1) {
+        for (; e + 2 <= e1; e += 2) {
+            const int2 p = __ldg(&pairs[e]), q = __ldg(&pairs[e + 1]);
+            const char* ap = base + (unsigned)p.x * row_bytes;
+            const char* aq = base + (unsigned)q.x * row_bytes;
+            float2 v0[H], v1[H], u0[H], u1[H];
+            ld16<TI>(reinterpret_cast<const TI*>(ap), v0);
+            ld16<TI>(reinterpret_cast<const TI*>(ap + G1), v1);
+            ld16<TI>(reinterpret_cast<const TI*>(aq), u0);
+            ld16<TI>(reinterpret_cast<const TI*>(aq + G1), u1);
+            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+            const float2 wq = make_float2(__int_as_float(q.y), __int_as_float(q.y));
 #pragma unroll
-        for (int i = 0; i < H; ++i) a0[i] = __ffma2_rn(w, v0[i], a0[i]);
-        if (g1) {
+            for (int i = 0; i < H; ++i) { a0[i] = __ffma2_rn(wp, v0[i], a0[i]); a1[i] = __ffma2_rn(wp, v1[i], a1[i]); }
 #pragma unroll
-            for (int i = 0; i < H; ++i) a1[i] = __ffma2_rn(w, v1[i], a1[i]);
+            for (int i = 0; i < H; ++i) { a0[i] = __ffma2_rn(wq, u0[i], a0[i]); a1[i] = __ffma2_rn(wq, u1[i], a1[i]); }
+        }
+        if (e < e1) {
+            const int2 p = __ldg(&pairs[e]);
+            const char* ap = base + (unsigned)p.x * row_bytes;
+            float2 v0[H], v1[H];
+            ld16<TI>(reinterpret_cast<const TI*>(ap), v0);
+            ld16<TI>(reinterpret_cast<const TI*>(ap + G1), v1);
+            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+#pragma unroll
+            for (int i = 0; i < H; ++i) { a0[i] = __ffma2_rn(wp, v0[i], a0[i]); a1[i] = __ffma2_rn(wp, v1[i], a1[i]); }
+        }
+    } else {                                              // only the first group is inside the batch
+        for (; e < e1; ++e) {
+            const int2 p = __ldg(&pairs[e]);
+            float2 v0[H];
+            ld16<TI>(reinterpret_cast<const TI*>(base + (unsigned)p.x * row_bytes), v0);
+            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+#pragma unroll
+            for (int i = 0; i < H; ++i) a0[i] = __ffma2_rn(wp, v0[i], a0[i]);
         }
     }
     if (drow) {
@@ -706,11 +746,11 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ pptr
 
 // transposed hop: gh[s, b] = sum over merged pairs (dst, w) of source row s of w * gz[dst, b]. The source rows are
 // cut into segments of at most a fixed number of pairs (hub sources have tens of thousands); a segment of a row that
-// has one finishes the row, the others write a partial row that k_seg_reduce adds up in slot order.
+// has one finishes the row, the others write partial rows that the last of them to finish adds up in slot order.
 // One warp per (segment, 256-sample chunk); each lane owns two 4-sample groups 128 samples apart (every warp load is
 // one contiguous 512-byte run); packed fp32x2 FMAs; segments longest first. seg = {row, first pair, end, slot or -1}.
-// The host launches it over groups of chunks (chunk0 = the group's first) small enough that the gz columns a launch
-// gathers from stay in L2: hub rows reach every destination row, so each chunk reads its whole gz column slab.
+// Chunk-major launch order and hub rows cut into short segments keep the few chunks in flight inside L2 (a hub row
+// reaches every destination row, so each chunk reads its whole gz column slab).
 // Finishing a row (EPI): the source layer's neuron backward is fused in - g = gh * [h > 0]; gz = g * gain is written
 // (not gh), gdrive[drow] += gz, and the row's per-chunk sums of g*z (z = (h + thr) / gain where h > 0), of g and of
 // [g != 0] go to nsum[row][chunk][3] for k_neuron_reduce. Without EPI (the sensory layer) gh itself is written.
@@ -777,71 +817,98 @@ __device__ __forceinline__ void finish_row(int s, int chunk, int c0, int c1, boo
     }
 }
 
-template <bool EPI>
-__global__ void __launch_bounds__(kThreads, 6) k_hop_bwd_t(const int4* __restrict__ segs,
-                                                           const int2* __restrict__ tpairs,
-                                                           const float* __restrict__ gz, float* __restrict__ out,
-                                                           float* __restrict__ part, int n_segs, int ld, int chunk0,
-                                                           NeuronEpi ep) {
+// A segment of a split row writes its partial row to part[slot], then counts itself in done[red][chunk]; the last of
+// the row's segments to arrive (no waiting: the others just leave) adds all the row's partials in slot order through
+// L2 and finishes the row, then resets the counter for the next call. Deterministic: the sum order is fixed.
+template <bool EPI, bool FULL>
+__global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__ segs, const int* __restrict__ seg_red,
+                                                        const int4* __restrict__ reds, int* __restrict__ done,
+                                                        const int2* __restrict__ tpairs, const float* __restrict__ gz,
+                                                        float* __restrict__ out, float* __restrict__ part, int n_segs,
+                                                        int ld, NeuronEpi ep) {
     const int sidx = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (sidx >= n_segs) return;
     const int4 sg = __ldg(&segs[sidx]);
-    const int chunk = chunk0 + blockIdx.y;
+    const int chunk = blockIdx.y;
     const int c0 = chunk * 256 + lane * 4, c1 = c0 + 128;
     // lanes past the batch stay to the end (the epilogue reduces over the warp) but load and store nothing
-    const bool v0 = c0 < ld, v1 = c1 < ld;
+    const bool v0 = FULL || c0 < ld, v1 = FULL || c1 < ld;
     float2 a0[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)}, a1[2] = {a0[0], a0[1]};
-    const unsigned row_elems = (unsigned)ld;
-    const float* b0 = gz + (v0 ? c0 : 0);
-    const float* b1 = gz + (v1 ? c1 : 0);
-    if (v0) {
+    const size_t row_bytes = (size_t)ld * 4;
+    const char* base = reinterpret_cast<const char*>(gz + (v0 ? c0 : 0));
+    if (v0 && v1) {
+        int e = sg.y;
+        for (; e + 2 <= sg.z; e += 2) {
+            const int2 p = __ldg(&tpairs[e]), q = __ldg(&tpairs[e + 1]);
+            const char* ap = base + (unsigned)p.x * row_bytes;
+            const char* aq = base + (unsigned)q.x * row_bytes;
+            float2 x0[2], x1[2], y0[2], y1[2];
+            ld16<float>(reinterpret_cast<const float*>(ap), x0);
+            ld16<float>(reinterpret_cast<const float*>(ap + 512), x1);
+            ld16<float>(reinterpret_cast<const float*>(aq), y0);
+            ld16<float>(reinterpret_cast<const float*>(aq + 512), y1);
+            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+            const float2 wq = make_float2(__int_as_float(q.y), __int_as_float(q.y));
+            a0[0] = __ffma2_rn(wp, x0[0], a0[0]); a0[1] = __ffma2_rn(wp, x0[1], a0[1]);
+            a1[0] = __ffma2_rn(wp, x1[0], a1[0]); a1[1] = __ffma2_rn(wp, x1[1], a1[1]);
+            a0[0] = __ffma2_rn(wq, y0[0], a0[0]); a0[1] = __ffma2_rn(wq, y0[1], a0[1]);
+            a1[0] = __ffma2_rn(wq, y1[0], a1[0]); a1[1] = __ffma2_rn(wq, y1[1], a1[1]);
+        }
+        if (e < sg.z) {
+            const int2 p = __ldg(&tpairs[e]);
+            const char* ap = base + (unsigned)p.x * row_bytes;
+            float2 x0[2], x1[2];
+            ld16<float>(reinterpret_cast<const float*>(ap), x0);
+            ld16<float>(reinterpret_cast<const float*>(ap + 512), x1);
+            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+            a0[0] = __ffma2_rn(wp, x0[0], a0[0]); a0[1] = __ffma2_rn(wp, x0[1], a0[1]);
+            a1[0] = __ffma2_rn(wp, x1[0], a1[0]); a1[1] = __ffma2_rn(wp, x1[1], a1[1]);
+        }
+    } else if (v0) {
         for (int e = sg.y; e < sg.z; ++e) {
             const int2 p = __ldg(&tpairs[e]);
-            const size_t ro = (size_t)((unsigned)p.x * row_elems);
-            float2 x0[2], x1[2];
-            ld16<float>(b0 + ro, x0);
-            if (v1) ld16<float>(b1 + ro, x1);
-            const float2 w = make_float2(__int_as_float(p.y), __int_as_float(p.y));
-            a0[0] = __ffma2_rn(w, x0[0], a0[0]);
-            a0[1] = __ffma2_rn(w, x0[1], a0[1]);
-            if (v1) {
-                a1[0] = __ffma2_rn(w, x1[0], a1[0]);
-                a1[1] = __ffma2_rn(w, x1[1], a1[1]);
-            }
+            float2 x0[2];
+            ld16<float>(reinterpret_cast<const float*>(base + (unsigned)p.x * row_bytes), x0);
+            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+            a0[0] = __ffma2_rn(wp, x0[0], a0[0]); a0[1] = __ffma2_rn(wp, x0[1], a0[1]);
         }
     }
-    const float r0[4] = {a0[0].x, a0[0].y, a0[1].x, a0[1].y}, r1[4] = {a1[0].x, a1[0].y, a1[1].x, a1[1].y};
-    if (sg.w >= 0) {
+    float r0[4] = {a0[0].x, a0[0].y, a0[1].x, a0[1].y}, r1[4] = {a1[0].x, a1[0].y, a1[1].x, a1[1].y};
+    if (sg.w < 0) {
+        finish_row<EPI>(sg.x, chunk, c0, c1, v0, v1, ld, r0, r1, out, ep);
+        return;
+    }
+    {                                                      // a segment of a split row
         float* o = part + (size_t)sg.w * ld;
         if (v0) *reinterpret_cast<float4*>(o + c0) = make_float4(r0[0], r0[1], r0[2], r0[3]);
         if (v1) *reinterpret_cast<float4*>(o + c1) = make_float4(r1[0], r1[1], r1[2], r1[3]);
-        return;
     }
-    finish_row<EPI>(sg.x, chunk, c0, c1, v0, v1, ld, r0, r1, out, ep);
-}
-// red = {row, first slot, slot count, -}: the row = the sum of its partial rows in slot order, then finished as above
-template <bool EPI>
-__global__ void __launch_bounds__(kThreads) k_seg_reduce(const int4* __restrict__ red, const float* __restrict__ part,
-                                                         float* __restrict__ out, int n_red, int ld, NeuronEpi ep) {
-    const int ridx = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (ridx >= n_red) return;
-    const int4 r = __ldg(&red[ridx]);
-    const int c0 = blockIdx.y * 256 + lane * 4, c1 = c0 + 128;
-    const bool v0 = c0 < ld, v1 = c1 < ld;
-    float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int i = 0; i < r.z; ++i) {
-        const float* q = part + (size_t)(r.y + i) * ld;
+    const int ri = __ldg(&seg_red[sidx]);
+    const int4 rd = __ldg(&reds[ri]);
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&done[(size_t)ri * gridDim.y + chunk], 1) == rd.z - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { r0[i] = 0.f; r1[i] = 0.f; }
+    for (int i = 0; i < rd.z; ++i) {
+        const float* q = part + (size_t)(rd.y + i) * ld;
         if (v0) {
-            const float4 u = __ldg(reinterpret_cast<const float4*>(q + c0));
-            a0[0] += u.x; a0[1] += u.y; a0[2] += u.z; a0[3] += u.w;
+            const float4 u = __ldcg(reinterpret_cast<const float4*>(q + c0));
+            r0[0] += u.x; r0[1] += u.y; r0[2] += u.z; r0[3] += u.w;
         }
         if (v1) {
-            const float4 u = __ldg(reinterpret_cast<const float4*>(q + c1));
-            a1[0] += u.x; a1[1] += u.y; a1[2] += u.z; a1[3] += u.w;
+            const float4 u = __ldcg(reinterpret_cast<const float4*>(q + c1));
+            r1[0] += u.x; r1[1] += u.y; r1[2] += u.z; r1[3] += u.w;
         }
     }
-    finish_row<EPI>(r.x, blockIdx.y, c0, c1, v0, v1, ld, a0, a1, out, ep);
+    finish_row<EPI>(sg.x, chunk, c0, c1, v0, v1, ld, r0, r1, out, ep);
+    if (lane == 0) done[(size_t)ri * gridDim.y + chunk] = 0;
 }
+
 // per row of a layer: gain grad += sum over chunks of g*z, theta grad += -(sum of g) * sigmoid(theta); live = any g
 __global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __restrict__ nid,
                                 const float* __restrict__ rsig, float* __restrict__ ggain, float* __restrict__ gtheta,
