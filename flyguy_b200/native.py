@@ -47,6 +47,8 @@ SIGNATURES = {
     "fg_launches": (_cll, [_vp]),
     "fg_timing": (_ci, [_vp, _ci]),
     "fg_timing_read": (_ci, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_cll), _ci]),
+    "fg_kl_loss_noalloc": (_ci, [_vp, _vp, _ci, _ci, _cf, _vp, _vp, _vp]),
+    "fg_noalloc_last_error": (ctypes.c_char_p, []),
 }
 KERNEL_CLASSES = ("layout", "fold", "plug_fwd", "hop_fwd", "out_fwd", "loss", "out_bwd", "act_bwd", "sddmm",
                   "hop_bwd_t", "plug_bwd", "adam", "norm")
@@ -256,6 +258,18 @@ def _wrap(ptr: int, n: int, device):
     import torch
     with torch.cuda.device(device):
         return torch.as_tensor(_CudaArray(ptr, n), device=device)
+
+
+def kl_loss_noalloc(logits, teacher, inv_temp: float, dlogits, stats, stream=None) -> None:
+    """KL loss and its gradient without any device allocation (fg_kl_loss_noalloc): logits, teacher, dlogits [B, n_act]
+    and stats [2] are caller-owned CUDA fp32 tensors; the work is queued on `stream` (default: torch's current)."""
+    import torch
+    L = lib()
+    st = (stream or torch.cuda.current_stream(logits.device)).cuda_stream
+    rc = L.fg_kl_loss_noalloc(logits.data_ptr(), teacher.data_ptr(), logits.shape[0], logits.shape[1],
+                              float(inv_temp), dlogits.data_ptr(), stats.data_ptr(), st)
+    if rc:
+        raise FlyguyError(L.fg_noalloc_last_error().decode())
 
 
 def exported_symbols() -> list[str]:

@@ -117,6 +117,18 @@ int fg_timing(void* h, int on);
  * 11 Adam, 12 gradient norm. Returns the number of classes. */
 int fg_timing_read(void* h, double* ms, long long* count, int n);
 
+/* No counterpart in the reference. KL(softmax(teacher * inv_temp) || softmax(logits)) over a batch and its gradient
+ * for callers that cannot allocate device memory (for example a trainer embedded in a host application that only
+ * hands over pointers into memory it reserved up front). logits, teacher, dlogits: [B, n_act] device, fp32;
+ * dlogits = (softmax(logits) - p_teacher) / B; stats: device float[2] = sum of KL over the batch, number of argmax
+ * agreements. Allocates nothing: its scratch is a fixed 512 KiB array inside the library, so B is at most 65,536
+ * (larger batches are refused with -1). The first call on a device looks up that array and should come before any
+ * stream capture; calls that overlap on the GPU share the array and race. Queued on `stream`; returns 0 or -1
+ * (fg_noalloc_last_error says why). */
+int fg_kl_loss_noalloc(const float* logits, const float* teacher, int B, int n_act, float inv_temp, float* dlogits,
+                       float* stats, void* stream);
+const char* fg_noalloc_last_error(void);
+
 #ifdef __cplusplus
 }
 #endif
