@@ -80,7 +80,7 @@ struct Core {
     float *x = nullptr, *drive = nullptr, *lg = nullptr, *dl = nullptr;
     void* h0 = nullptr;
     float *gz_a = nullptr, *gz_b = nullptr, *gdrive = nullptr, *part = nullptr;
-    float *nsum = nullptr, *plug_part = nullptr;
+    float* nsum = nullptr;
     float *kl_s = nullptr, *ag_s = nullptr, *stats = nullptr, *norm_part = nullptr, *norm = nullptr;
     int* live = nullptr;
     int out_splits = 1;
@@ -391,7 +391,6 @@ void alloc_all(Core& c) {
         c.gdrive = dalloc<float>(c, (size_t)c.n_s * B);
         c.live = dalloc<int>(c, max_rows);
         c.nsum = dalloc<float>(c, (size_t)max_rows * ((B + 255) / 256) * 3);
-        c.plug_part = dalloc<float>(c, (size_t)c.n_s * kPlugSplits * (c.fan + 3));
         c.out_splits = std::max(1, std::min(64, (int)((B + 1023) / 1024)));
         c.part = dalloc<float>(c, (size_t)c.out_splits * c.n_act * (c.n_dn + 1));
         c.kl_s = dalloc<float>(c, B);
@@ -408,12 +407,17 @@ void alloc_all(Core& c) {
 }
 
 template <class T>
-int plug_smem(const Core& c) { return c.obs_dim * PlugCfg<T>::cols * (int)sizeof(T); }
+int plug_smem(const Core& c) {
+    const int f = (c.fan % 4 == 0 && c.fan > 0 && c.fan <= 16) ? c.fan : 1;
+    return (c.obs_dim * PlugCfg<T>::cols * (int)sizeof(T) + 15) / 16 * 16 + (kPlugThreads / 32) * 32 * f * 8;
+}
 
 template <class T, bool SAVE>
 void plug_limit(const Core& c) {
     const int smem = plug_smem<T>(c);
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 12>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
 }
@@ -461,6 +465,12 @@ void plug_launch(Core& c, const float* Pw, int B) {
                 c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
         else if (c.fan == 16)
             k_plug_fwd<T, SAVE, 16><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+                c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
+        else if (c.fan == 4)
+            k_plug_fwd<T, SAVE, 4><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+                c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
+        else if (c.fan == 12)
+            k_plug_fwd<T, SAVE, 12><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
                 c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
         else
             k_plug_fwd<T, SAVE, 0><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
@@ -603,14 +613,19 @@ void backward(Core& c, int B) {
     }
     // gz now holds gh0 (the sensory layer's incoming gradient)
     launch(c, K_PLUG_BWD, [&]() {
-        k_plug_bwd<<<dim3(c.n_s, kPlugSplits), kThreads, 0, c.st>>>(gz, (const float*)c.h0, c.drive, c.gdrive,
-                                                                    c.d_in_crow, c.d_in_col, c.x, c.d_rgain,
-                                                                    c.plug_part, c.fan, B, B);
-    });
-    launch(c, K_PLUG_BWD, [&]() {
-        k_plug_reduce<<<blocks((long long)c.n_s * (c.fan + 3)), 256, 0, c.st>>>(
-            c.plug_part, c.d_n0, c.d_rsig, c.G + c.off[1], c.G + c.off[2], c.G + c.off[3], c.G + c.off[4], c.n_s,
-            c.fan);
+        const dim3 g((c.n_s + kWarps - 1) / kWarps);
+        if (c.fan == 8)
+            k_plug_bwd<8><<<g, kThreads, 0, c.st>>>(gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
+                                                    c.x, c.d_rgain, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
+                                                    c.G + c.off[3], c.G + c.off[4], c.n_s, c.fan, B, B);
+        else if (c.fan == 16)
+            k_plug_bwd<16><<<g, kThreads, 0, c.st>>>(gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
+                                                     c.x, c.d_rgain, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
+                                                     c.G + c.off[3], c.G + c.off[4], c.n_s, c.fan, B, B);
+        else
+            k_plug_bwd<0><<<g, kThreads, 0, c.st>>>(gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
+                                                    c.x, c.d_rgain, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
+                                                    c.G + c.off[3], c.G + c.off[4], c.n_s, c.fan, B, B);
     });
 }
 

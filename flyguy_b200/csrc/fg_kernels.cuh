@@ -225,26 +225,10 @@ __device__ __forceinline__ void st_ns(__half* p, const float (&v)[4]) {
     *reinterpret_cast<uint2*>(p) = make_uint2(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]));
 }
 
-// the row's plug columns and weights, FAN at a time (FAN % 4 == 0) or one by one (FAN == 0: any fan)
-template <int FAN>
-struct PlugRow {
-    int c[FAN > 0 ? FAN : 1];
-    float w[FAN > 0 ? FAN : 1];
-    __device__ __forceinline__ void load(const int* col, const float* wt, size_t e) {
-        if constexpr (FAN > 0) {
-#pragma unroll
-            for (int j = 0; j < FAN; j += 4) {
-                const int4 q = __ldg(reinterpret_cast<const int4*>(col + e + j));
-                const float4 r = __ldg(reinterpret_cast<const float4*>(wt + e + j));
-                c[j] = q.x; c[j + 1] = q.y; c[j + 2] = q.z; c[j + 3] = q.w;
-                w[j] = r.x; w[j + 1] = r.y; w[j + 2] = r.z; w[j + 3] = r.w;
-            }
-        }
-    }
-};
-
-// A CTA owns one chunk of C samples and a block of rows: x for the chunk is staged once, then each warp walks rows
-// (its next row's columns and weights loaded ahead, in registers) gathering from shared memory.
+// A CTA owns one chunk of C samples and a block of rows: x for the chunk is staged once (as the state type for
+// 16-bit states), then each warp takes 32 consecutive rows at a time, stages their plug columns and weights in its own
+// slice of shared memory with one coalesced load, and walks them with broadcast reads - no global-memory latency
+// inside the row loop. FAN: the plug's fan-in (a multiple of 4 up to 16) or 0 for any fan (slower path).
 template <class T, bool SAVE_DRIVE, int FAN>
 __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict__ in_col,
                                                            const float* __restrict__ in_w,
@@ -254,8 +238,14 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
                                                            float* __restrict__ drive, T* __restrict__ h0, int n_s,
                                                            int fan, int rows_per_cta, int obs_dim, int ld) {
     constexpr int C = PlugCfg<T>::cols, NS = C / 32;
+    constexpr int F = FAN > 0 ? FAN : 1;
+    constexpr int kWarpsP = kPlugThreads / 32;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    T* xs = reinterpret_cast<T*>(smem_raw);                                   // [obs_dim][C]
+    T* xs = reinterpret_cast<T*>(smem_raw);                                               // [obs_dim][C]
+    int* rc_all = reinterpret_cast<int*>(smem_raw + ((size_t)obs_dim * C * sizeof(T) + 15) / 16 * 16);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int* rc = rc_all + warp * 32 * F * 2;                                                // [32][F] cols
+    float* rw = reinterpret_cast<float*>(rc + 32 * F);                                   // [32][F] weights
     const int b0 = blockIdx.y * C;
     const int r_lo = blockIdx.x * rows_per_cta, r_hi = min(n_s, r_lo + rows_per_cta);
     for (int i = threadIdx.x; i < obs_dim * (C / 4); i += blockDim.x) {
@@ -265,48 +255,65 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
         cvt_store4(xs + f * C + q, v);
     }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bl = NS * lane;
-    if (b0 + bl >= ld) return;
-    constexpr int STEP = kPlugThreads / 32;
-    PlugRow<FAN> cur, nxt;
-    int row = r_lo + warp;
-    if (FAN > 0 && row < r_hi) cur.load(in_col, in_w, (size_t)row * FAN);
-    for (; row < r_hi; row += STEP) {
-        if (FAN > 0 && row + STEP < r_hi) nxt.load(in_col, in_w, (size_t)(row + STEP) * FAN);
-        float a[NS];
-        const float bias = __ldg(&in_b[row]);
-#pragma unroll
-        for (int i = 0; i < NS; ++i) a[i] = bias;
+    const bool on = b0 + bl < ld;
+    for (int r0 = r_lo + warp * 32; r0 < r_hi; r0 += kWarpsP * 32) {
+        const int nrows = min(32, r_hi - r0);
         if constexpr (FAN > 0) {
+            __syncwarp();
+            if (lane < nrows) {
+                const size_t e = (size_t)(r0 + lane) * FAN;
 #pragma unroll
-            for (int j = 0; j < FAN; ++j) {
-                float v[NS];
-                lds_ns(xs + cur.c[j] * C + bl, v);
-#pragma unroll
-                for (int i = 0; i < NS; ++i) a[i] = fmaf(cur.w[j], v[i], a[i]);
+                for (int j = 0; j < FAN; j += 4) {
+                    *reinterpret_cast<int4*>(rc + lane * F + j) = __ldg(reinterpret_cast<const int4*>(in_col + e + j));
+                    *reinterpret_cast<float4*>(rw + lane * F + j) = __ldg(reinterpret_cast<const float4*>(in_w + e + j));
+                }
             }
-        } else {
-            const size_t e0 = (size_t)row * fan;
-            for (int j = 0; j < fan; ++j) {
-                float v[NS];
-                lds_ns(xs + __ldg(&in_col[e0 + j]) * C + bl, v);
-                const float w = __ldg(&in_w[e0 + j]);
+            __syncwarp();
+        }
+        if (!on) continue;
+        for (int i = 0; i < nrows; ++i) {
+            const int row = r0 + i;
+            float a[NS];
+            const float bias = __ldg(&in_b[row]);
 #pragma unroll
-                for (int i = 0; i < NS; ++i) a[i] = fmaf(w, v[i], a[i]);
+            for (int k = 0; k < NS; ++k) a[k] = bias;
+            if constexpr (FAN > 0) {
+#pragma unroll
+                for (int j = 0; j < FAN; j += 4) {
+                    const int4 cc = *reinterpret_cast<const int4*>(rc + i * F + j);
+                    const float4 ww = *reinterpret_cast<const float4*>(rw + i * F + j);
+                    const int cs[4] = {cc.x, cc.y, cc.z, cc.w};
+                    const float ws[4] = {ww.x, ww.y, ww.z, ww.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        float v[NS];
+                        lds_ns(xs + cs[u] * C + bl, v);
+#pragma unroll
+                        for (int k = 0; k < NS; ++k) a[k] = fmaf(ws[u], v[k], a[k]);
+                    }
+                }
+            } else {
+                const size_t e0 = (size_t)row * fan;
+                for (int j = 0; j < fan; ++j) {
+                    float v[NS];
+                    lds_ns(xs + __ldg(&in_col[e0 + j]) * C + bl, v);
+                    const float w = __ldg(&in_w[e0 + j]);
+#pragma unroll
+                    for (int k = 0; k < NS; ++k) a[k] = fmaf(w, v[k], a[k]);
+                }
             }
-        }
-        const size_t o = (size_t)row * ld + b0 + bl;
-        if (SAVE_DRIVE) {
-            if constexpr (NS == 1) drive[o] = a[0];
-            else *reinterpret_cast<float2*>(drive + o) = make_float2(a[0], a[1]);
-        }
-        const float g = __ldg(&rgain[row]), th = __ldg(&rthr[row]);
-        float hv[NS];
+            const size_t o = (size_t)row * ld + b0 + bl;
+            if (SAVE_DRIVE) {
+                if constexpr (NS == 1) drive[o] = a[0];
+                else *reinterpret_cast<float2*>(drive + o) = make_float2(a[0], a[1]);
+            }
+            const float g = __ldg(&rgain[row]), th = __ldg(&rthr[row]);
+            float hv[NS];
 #pragma unroll
-        for (int i = 0; i < NS; ++i) hv[i] = fmaxf(fmaf(g, a[i], -th), 0.f);
-        st_ns(h0 + o, hv);
-        if constexpr (FAN > 0) cur = nxt;
+            for (int k = 0; k < NS; ++k) hv[k] = fmaxf(fmaf(g, a[k], -th), 0.f);
+            st_ns(h0 + o, hv);
+        }
     }
 }
 
@@ -924,36 +931,35 @@ __global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __res
     live[s] = n > 0.f;
 }
 
-// sensory layer and plug, one CTA per (sensory row s, batch split): g0 = gh0 * [h0 > 0]; sums over the split of
-// g0 * drive, g0, gd = gdrive (re-drive from later hops) + g0 * gain, and gd * x[col_e] for the row's fan edges
-// (kPlugFan at a time) go to part[s][split][fan + 3]; k_plug_reduce adds the splits in order into the gradients of
-// gain, theta, in_b and in_w. Four samples per thread per step.
-constexpr int kPlugFan = 16, kPlugSplits = 4;
+// sensory layer and plug, one warp per sensory row s over the whole batch (4 samples per lane per step):
+// g0 = gh0 * [h0 > 0]; gd = gdrive (re-drive from later hops) + g0 * gain; sums over the batch of g0 * drive, g0, gd and
+// gd * x[col_e] for the row's fan edges (FAN of them, FAN <= 16; FAN 0: up to 16 in steps), reduced over the warp in
+// a fixed order and added to the gradients of gain, theta, in_b and in_w.
+constexpr int kPlugFan = 16;
+template <int FAN>
 __global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__ gh0, const float* __restrict__ h0,
                                                        const float* __restrict__ drive, const float* __restrict__ gdrive,
-                                                       const int* __restrict__ in_crow, const int* __restrict__ in_col,
+                                                       const int* __restrict__ n0, const int* __restrict__ in_col,
                                                        const float* __restrict__ x, const float* __restrict__ rgain,
-                                                       float* __restrict__ part, int fan, int B, int ld) {
-    constexpr int F = kPlugFan;
-    __shared__ float red[(F + 3) * kWarps];
-    const int s = blockIdx.x, split = blockIdx.y;
-    const int span = (B / 4 + kPlugSplits - 1) / kPlugSplits * 4;
-    const int b_lo = split * span, b_hi = min(B, b_lo + span);
-    const float gn = rgain[s];
+                                                       const float* __restrict__ rsig, float* __restrict__ ggain,
+                                                       float* __restrict__ gtheta, float* __restrict__ gin_w,
+                                                       float* __restrict__ gin_b, int n_s, int fan, int B, int ld) {
+    constexpr int F = FAN > 0 ? FAN : kPlugFan;
+    const int s = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (s >= n_s) return;
+    const float gn = __ldg(&rgain[s]);
     const size_t o = (size_t)s * ld;
-    const int e0 = in_crow[s], e1 = in_crow[s + 1];
-    float* out = part + ((size_t)s * kPlugSplits + split) * (fan + 3);
-    int f0 = e0;
-    do {
-        const int nf = max(0, min(F, e1 - f0));
-        const bool first = f0 == e0;
-        int col[F];
+    const size_t e0 = (size_t)s * fan;
+    for (int f0 = 0; f0 < fan || f0 == 0; f0 += F) {
+        const int nf = min(F, fan - f0);
+        const bool first = f0 == 0;
+        const float* xr[F];
 #pragma unroll
-        for (int u = 0; u < F; ++u) col[u] = u < nf ? in_col[f0 + u] : 0;
+        for (int u = 0; u < F; ++u) xr[u] = x + (size_t)(u < nf ? __ldg(&in_col[e0 + f0 + u]) : 0) * ld;
         float v[F + 3];
 #pragma unroll
         for (int u = 0; u < F + 3; ++u) v[u] = 0.f;
-        for (int b = b_lo + threadIdx.x * 4; b < b_hi; b += kThreads * 4) {
+        for (int b = lane * 4; b < B; b += 128) {
             const float4 gh = __ldg(reinterpret_cast<const float4*>(gh0 + o + b));
             const float4 hh = __ldg(reinterpret_cast<const float4*>(h0 + o + b));
             const float4 gr = __ldg(reinterpret_cast<const float4*>(gdrive + o + b));
@@ -969,33 +975,25 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__
             }
 #pragma unroll
             for (int u = 0; u < F; ++u) {
-                if (u < nf) {
-                    const float4 xv = __ldg(reinterpret_cast<const float4*>(x + (size_t)col[u] * ld + b));
+                if (FAN > 0 || u < nf) {
+                    const float4 xv = __ldg(reinterpret_cast<const float4*>(xr[u] + b));
                     v[u] += gd[0] * xv.x + gd[1] * xv.y + gd[2] * xv.z + gd[3] * xv.w;
                 }
             }
         }
-        block_sum<F + 3>(v, red);
-        if (threadIdx.x == 0) {
-            if (first) { out[fan] = v[F]; out[fan + 1] = v[F + 1]; out[fan + 2] = v[F + 2]; }
-            for (int u = 0; u < nf; ++u) out[f0 - e0 + u] = v[u];
+#pragma unroll
+        for (int u = 0; u < F + 3; ++u) v[u] = warp_sum(v[u]);
+        if (lane == 0) {
+            if (first) {
+                const int id = __ldg(&n0[s]);
+                ggain[id] += v[F];
+                gtheta[id] += -v[F + 1] * __ldg(&rsig[s]);
+                gin_b[s] += v[F + 2];
+            }
+            for (int u = 0; u < nf; ++u) gin_w[e0 + f0 + u] += v[u];
         }
-        f0 += F;
-    } while (f0 < e1);
-}
-__global__ void k_plug_reduce(const float* __restrict__ part, const int* __restrict__ n0,
-                              const float* __restrict__ rsig, float* __restrict__ ggain, float* __restrict__ gtheta,
-                              float* __restrict__ gin_w, float* __restrict__ gin_b, int n_s, int fan) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;      // one thread per (row, fan + 3 values)
-    const int per = fan + 3;
-    if (i >= n_s * per) return;
-    const int s = i / per, j = i - s * per;
-    float v = 0.f;
-    for (int k = 0; k < kPlugSplits; ++k) v += part[((size_t)s * kPlugSplits + k) * per + j];
-    if (j < fan) gin_w[(size_t)s * fan + j] += v;
-    else if (j == fan) ggain[n0[s]] += v;
-    else if (j == fan + 1) gtheta[n0[s]] += -v * rsig[s];
-    else gin_b[s] += v;
+        if (fan == 0) break;
+    }
 }
 
 // ---------------------------------------------------------------- optimiser
