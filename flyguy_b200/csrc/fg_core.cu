@@ -44,7 +44,7 @@ struct Hop {
     bool out_f32 = false;                    // this hop's layer is stored in fp32 (the last layer always is)
 };
 
-constexpr int kSegLen = 256;                 // pairs per transposed segment
+constexpr int kSegLen = 64;                  // pairs per transposed segment (short: hub CTAs retire fast)
 
 // kernel classes timed by fg_timing (CUDA events around every launch of the class, on the handle's stream)
 enum KClass { K_TRANSPOSE, K_FOLD, K_PLUG_FWD, K_HOP_FWD, K_OUT_FWD, K_LOSS, K_OUT_BWD, K_ACT_BWD, K_SDDMM, K_HOP_BWD,

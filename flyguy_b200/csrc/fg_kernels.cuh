@@ -727,6 +727,7 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ pptr
         float acc[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+#pragma unroll 2
         for (int b = threadIdx.x * 4; b < B; b += kThreads * 4) {
             const float4 q = __ldg(reinterpret_cast<const float4*>(g + b));
             if (q.x == 0.f && q.y == 0.f && q.z == 0.f && q.w == 0.f) continue;     // silent samples: nothing to add
