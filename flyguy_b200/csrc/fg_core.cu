@@ -36,7 +36,11 @@ struct Hop {
     long long rbase = 0;                     // first row of this hop's layer in the per-row arrays
     bool widx_unique = true, redrive = false;
     int *d_nid = nullptr, *d_drow = nullptr, *d_sched = nullptr, *d_pptr = nullptr;
-    int *d_tsched = nullptr, *d_tptr = nullptr;
+    std::vector<int> h_psrc, h_pptr;             // host copies of the forward pairs (for the backward plan)
+    long long tbase = 0;                         // first transposed pair of this hop in the concatenated arrays
+    int T = 0;                                   // transposed pairs kept for the backward
+    int *d_live_dst = nullptr, n_live_dst = 0;   // rows of this hop's layer whose gradient can be non-zero
+    int *d_live_src = nullptr, n_live_src = 0;   // rows of the layer below that this hop's backward writes
     int4 *d_segs = nullptr, *d_reds = nullptr;   // transposed product: segments of source rows, split-row reductions
     int* d_seg_red = nullptr;                    // per segment: its split row's reduction index, or -1
     int n_segs = 0, n_reds = 0, n_slots = 0;
@@ -68,7 +72,10 @@ struct Core {
     int* seg_done = nullptr;                             // arrival counters of split rows' segments [red][chunk]
     int *d_in_crow = nullptr, *d_in_col = nullptr, *d_n0 = nullptr, *d_dn = nullptr;
     std::vector<Hop> hop;
-    long long R = 0, Ptot = 0, Etot = 0;
+    long long R = 0, Ptot = 0, Etot = 0, Ttot = 0;
+    int* d_plug_live = nullptr;                         // sensory rows the plug backward visits
+    int* d_gh0_valid = nullptr;                         // per sensory row: 1 if the backward writes its gh0
+    int n_plug_live = 0;
     int* d_row_nid = nullptr;
     float *d_rgain = nullptr, *d_rthr = nullptr, *d_rsig = nullptr;
     int2 *d_pairs = nullptr, *d_tpairs = nullptr;
@@ -161,7 +168,7 @@ void check_ptr(const std::vector<int>& p, long long n, const char* what) {
 // merged pairs of one hop: pair = the edges of one (row, source); returns host arrays appended to the global ones
 void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::vector<int>& col,
                     const std::vector<int>& widx, std::vector<int2>& pairs, std::vector<int>& gptr,
-                    std::vector<int>& gw, std::vector<int2>& tpairs, std::vector<int>& tpi, std::vector<char>& mark) {
+                    std::vector<int>& gw, std::vector<char>& mark) {
     const int rows = h.rows;
     std::vector<int> pptr(rows + 1, 0), order;
     const long long pbase = (long long)pairs.size();
@@ -186,63 +193,108 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
     for (int w : widx) mark[w] = 0;
     h.P = (int)psrc.size();
     for (int p = 0; p < h.P; ++p) pairs.push_back(make_int2(psrc[p], 0));
-    // transposed: by source, destinations ascending
-    std::vector<int> tptr(h.n_src + 1, 0);
-    for (int s : psrc) ++tptr[s + 1];
-    for (int s = 0; s < h.n_src; ++s) tptr[s + 1] += tptr[s];
-    std::vector<int> fill(tptr.begin(), tptr.end() - 1);
-    std::vector<int2> tp(h.P);
-    std::vector<int> ti(h.P);
-    for (int t = 0; t < rows; ++t)
-        for (int p = pptr[t]; p < pptr[t + 1]; ++p) {
-            const int q = fill[psrc[p]]++;
-            tp[q] = make_int2(t, 0);
-            ti[q] = (int)(pbase + p);
-        }
-    tpairs.insert(tpairs.end(), tp.begin(), tp.end());
-    tpi.insert(tpi.end(), ti.begin(), ti.end());
-    // schedules: rows (sources) with most pairs first, so the long ones start early
-    std::vector<int> sched(rows), tsched(h.n_src);
+    // schedule: rows with most pairs first, so the long ones start early
+    std::vector<int> sched(rows);
     std::iota(sched.begin(), sched.end(), 0);
     std::stable_sort(sched.begin(), sched.end(),
                      [&](int a, int b) { return pptr[a + 1] - pptr[a] > pptr[b + 1] - pptr[b]; });
-    std::iota(tsched.begin(), tsched.end(), 0);
-    std::stable_sort(tsched.begin(), tsched.end(),
-                     [&](int a, int b) { return tptr[a + 1] - tptr[a] > tptr[b + 1] - tptr[b]; });
-    std::vector<int4> segs, reds;
-    std::vector<int> seg_red;
-    for (int s = 0; s < h.n_src; ++s) {
-        const int n = tptr[s + 1] - tptr[s];
-        if (n <= kSegLen) {
-            segs.push_back(make_int4(s, tptr[s], tptr[s + 1], -1));
-            seg_red.push_back(-1);
-            continue;
-        }
-        const int nseg = (n + kSegLen - 1) / kSegLen;
-        for (int i = 0; i < nseg; ++i) {
-            segs.push_back(make_int4(s, tptr[s] + i * kSegLen, std::min(tptr[s + 1], tptr[s] + (i + 1) * kSegLen),
-                                     h.n_slots + i));
-            seg_red.push_back((int)reds.size());
-        }
-        reds.push_back(make_int4(s, h.n_slots, nseg, 0));
-        h.n_slots += nseg;
-    }
-    std::vector<int> by_len(segs.size());
-    std::iota(by_len.begin(), by_len.end(), 0);
-    std::stable_sort(by_len.begin(), by_len.end(),
-                     [&](int a, int b) { return segs[a].z - segs[a].y > segs[b].z - segs[b].y; });
-    std::vector<int4> segs_s(segs.size());
-    std::vector<int> red_s(segs.size());
-    for (size_t i = 0; i < by_len.size(); ++i) { segs_s[i] = segs[by_len[i]]; red_s[i] = seg_red[by_len[i]]; }
-    h.n_segs = (int)segs.size();
-    h.n_reds = (int)reds.size();
-    h.d_segs = upload(c, segs_s);
-    h.d_seg_red = upload(c, red_s);
-    h.d_reds = upload(c, reds);
+    h.h_psrc = std::move(psrc);
+    h.h_pptr = pptr;
     h.d_pptr = upload(c, pptr);
     h.d_sched = upload(c, sched);
-    h.d_tptr = upload(c, tptr);
-    h.d_tsched = upload(c, tsched);
+}
+
+// The backward plan. A row's gradient can be non-zero only if the row feeds a row whose gradient can be non-zero
+// (the descending rows of the last layer start it): rows of the synthetic graph that no later row reads from get an
+// exactly zero gradient, so the backward skips them - no transposed pairs into them, no weight gradients from them,
+// nothing written for them (the reference skips zero gradients at run time, warp by warp). Then per hop: the
+// transposed pairs into live rows, by source and destination, cut into segments of at most kSegLen pairs.
+void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, const std::vector<int>& dn,
+                          std::vector<int2>& tpairs, std::vector<int>& tpi) {
+    const int K = c.hops;
+    std::vector<std::vector<char>> live(K + 1);
+    live[K].assign(c.sizes[K], 0);
+    for (int d : dn) live[K][d] = 1;
+    for (int k = K; k >= 1; --k) {
+        const Hop& h = c.hop[k - 1];
+        live[k - 1].assign(c.sizes[k - 1], 0);
+        for (int t = 0; t < h.rows; ++t)
+            if (live[k][t])
+                for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; ++p) live[k - 1][h.h_psrc[p]] = 1;
+    }
+    // sensory rows: live through hop 1, or re-driven into a live row of a later layer
+    std::vector<char> plug_live(live[0]);
+    for (int k = 1; k <= K; ++k)
+        for (int t = 0; t < c.sizes[k]; ++t)
+            if (live[k][t] && drows[k - 1][t] >= 0) plug_live[drows[k - 1][t]] = 1;
+    std::vector<int> pl;
+    for (int s = 0; s < c.n_s; ++s) if (plug_live[s]) pl.push_back(s);
+    c.n_plug_live = (int)pl.size();
+    c.d_plug_live = upload(c, pl);
+    c.d_gh0_valid = upload(c, std::vector<int>(live[0].begin(), live[0].end()));
+    for (int k = 1; k <= K; ++k) {
+        Hop& h = c.hop[k - 1];
+        std::vector<int> ld, ls;
+        for (int t = 0; t < h.rows; ++t) if (live[k][t]) ld.push_back(t);
+        for (int s = 0; s < h.n_src; ++s) if (live[k - 1][s]) ls.push_back(s);
+        h.n_live_dst = (int)ld.size();
+        h.n_live_src = (int)ls.size();
+        h.d_live_dst = upload(c, ld);
+        h.d_live_src = upload(c, ls);
+        // transposed pairs into live rows: by source, destinations ascending
+        std::vector<int> tptr(h.n_src + 1, 0);
+        for (int t = 0; t < h.rows; ++t)
+            if (live[k][t])
+                for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; ++p) ++tptr[h.h_psrc[p] + 1];
+        for (int s = 0; s < h.n_src; ++s) tptr[s + 1] += tptr[s];
+        h.T = tptr[h.n_src];
+        h.tbase = (long long)tpairs.size();
+        std::vector<int> fill(tptr.begin(), tptr.end() - 1);
+        std::vector<int2> tp(h.T);
+        std::vector<int> ti(h.T);
+        for (int t = 0; t < h.rows; ++t) {
+            if (!live[k][t]) continue;
+            for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; ++p) {
+                const int q = fill[h.h_psrc[p]]++;
+                tp[q] = make_int2(t, 0);
+                ti[q] = (int)(h.pbase + p);
+            }
+        }
+        tpairs.insert(tpairs.end(), tp.begin(), tp.end());
+        tpi.insert(tpi.end(), ti.begin(), ti.end());
+        std::vector<int4> segs, reds;
+        std::vector<int> seg_red;
+        for (int s : ls) {
+            const int n = tptr[s + 1] - tptr[s];
+            if (n <= kSegLen) {
+                segs.push_back(make_int4(s, tptr[s], tptr[s + 1], -1));
+                seg_red.push_back(-1);
+                continue;
+            }
+            const int nseg = (n + kSegLen - 1) / kSegLen;
+            for (int i = 0; i < nseg; ++i) {
+                segs.push_back(make_int4(s, tptr[s] + i * kSegLen,
+                                         std::min(tptr[s + 1], tptr[s] + (i + 1) * kSegLen), h.n_slots + i));
+                seg_red.push_back((int)reds.size());
+            }
+            reds.push_back(make_int4(s, h.n_slots, nseg, 0));
+            h.n_slots += nseg;
+        }
+        std::vector<int> by_len(segs.size());
+        std::iota(by_len.begin(), by_len.end(), 0);
+        std::stable_sort(by_len.begin(), by_len.end(),
+                         [&](int a, int b) { return segs[a].z - segs[a].y > segs[b].z - segs[b].y; });
+        std::vector<int4> segs_s(segs.size());
+        std::vector<int> red_s(segs.size());
+        for (size_t i = 0; i < by_len.size(); ++i) { segs_s[i] = segs[by_len[i]]; red_s[i] = seg_red[by_len[i]]; }
+        h.n_segs = (int)segs.size();
+        h.n_reds = (int)reds.size();
+        h.d_segs = upload(c, segs_s);
+        h.d_seg_red = upload(c, red_s);
+        h.d_reds = upload(c, reds);
+        std::vector<int>().swap(h.h_psrc);
+        std::vector<int>().swap(h.h_pptr);
+    }
 }
 
 // the file's arrays, read and checked on the host before anything touches the GPU
@@ -330,10 +382,16 @@ void upload_net(Core& c, NetHost& n) {
         h.d_nid = upload(c, src.nid);
         h.d_drow = h.redrive ? upload(c, src.drow) : nullptr;
         row_nid.insert(row_nid.end(), src.nid.begin(), src.nid.end());
-        build_hop_plan(c, h, src.crow, src.col, src.widx, pairs, gptr, gw, tpairs, tpi, mark);
+        build_hop_plan(c, h, src.crow, src.col, src.widx, pairs, gptr, gw, mark);
         rbase += h.rows;
     }
     c.d_dn = upload(c, n.dn);
+    {
+        std::vector<std::vector<int>> drows;
+        for (auto& hh : n.hop) drows.push_back(hh.drow);
+        build_backward_plans(c, drows, n.dn, tpairs, tpi);
+    }
+    c.Ttot = (long long)tpairs.size();
     gptr.push_back((int)gw.size());
     c.R = (long long)row_nid.size();
     c.Ptot = (long long)pairs.size();
@@ -438,7 +496,8 @@ void fold(Core& c, int which) {
                                                   c.d_rsig, (int)c.R); });
     if (c.Ptot) {
         launch(c, K_FOLD, [&]() { k_fold_pairs<<<blocks(c.Ptot), 256, 0, c.st>>>(c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, (int)c.Ptot); });
-        launch(c, K_FOLD, [&]() { k_fold_tpairs<<<blocks(c.Ptot), 256, 0, c.st>>>(c.d_tpi, c.d_pairs, c.d_tpairs, (int)c.Ptot); });
+        if (c.Ttot)
+            launch(c, K_FOLD, [&]() { k_fold_tpairs<<<blocks(c.Ttot), 256, 0, c.st>>>(c.d_tpi, c.d_pairs, c.d_tpairs, (int)c.Ttot); });
     }
     launch(c, K_FOLD, [&]() { k_fold_owT<<<blocks((long long)c.n_dn * kOutA), 256, 0, c.st>>>(src + c.off[5], c.owT,
                                                                                          c.n_act, c.n_dn); });
@@ -570,29 +629,32 @@ void backward(Core& c, int B) {
     for (int k = c.hops - 1; k >= 0; --k) {
         const Hop& h = c.hop[k];
         const float* hprev = k ? (const float*)c.hop[k - 1].d_h : (const float*)c.h0;
-        if (h.widx_unique)
+        if (h.n_live_dst == 0) {}
+        else if (h.widx_unique)
             launch(c, K_SDDMM, [&]() {
-                k_sddmm<float, false><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase,
+                k_sddmm<float, false><<<h.n_live_dst, kThreads, 0, c.st>>>(h.d_live_dst, h.d_pptr, c.d_pairs + h.pbase,
                                                                      c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live,
                                                                      c.G + c.off[0], B, B);
             });
         else
             launch(c, K_SDDMM, [&]() {
-                k_sddmm<float, true><<<h.rows, kThreads, 0, c.st>>>(h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase,
+                k_sddmm<float, true><<<h.n_live_dst, kThreads, 0, c.st>>>(h.d_live_dst, h.d_pptr, c.d_pairs + h.pbase,
+                                                                    c.d_gptr + h.pbase,
                                                                     c.d_gw, gz, hprev, c.live, c.G + c.off[0], B, B);
             });
         const bool full = B % 256 == 0;
         auto transposed = [&](auto epi, const NeuronEpi& ep) {
             constexpr bool EPI = decltype(epi)::value;
             const dim3 gs((h.n_segs + kWarps - 1) / kWarps, chunks);
+            if (h.n_segs == 0) return;
             launch(c, K_HOP_BWD, [&]() {
                 if (full)
                     k_hop_bwd_t<EPI, true><<<gs, kThreads, 0, c.st>>>(h.d_segs, h.d_seg_red, h.d_reds, c.seg_done,
-                                                                      c.d_tpairs + h.pbase, gz, nxt, c.seg_part,
+                                                                      c.d_tpairs + h.tbase, gz, nxt, c.seg_part,
                                                                       h.n_segs, B, ep);
                 else
                     k_hop_bwd_t<EPI, false><<<gs, kThreads, 0, c.st>>>(h.d_segs, h.d_seg_red, h.d_reds, c.seg_done,
-                                                                       c.d_tpairs + h.pbase, gz, nxt, c.seg_part,
+                                                                       c.d_tpairs + h.tbase, gz, nxt, c.seg_part,
                                                                        h.n_segs, B, ep);
             });
         };
@@ -600,10 +662,11 @@ void backward(Core& c, int B) {
             const Hop& lo = c.hop[k - 1];
             NeuronEpi ep{hprev, c.d_rgain + lo.rbase, c.d_rthr + lo.rbase, lo.d_drow, c.gdrive, c.nsum, chunks};
             transposed(std::true_type{}, ep);
+            if (h.n_live_src)
             launch(c, K_ACT_BWD, [&]() {
-                k_neuron_reduce<<<blocks(lo.rows), 256, 0, c.st>>>(c.nsum, lo.d_nid, c.d_rsig + lo.rbase,
-                                                                  c.G + c.off[1], c.G + c.off[2], c.live, lo.rows,
-                                                                  chunks);
+                k_neuron_reduce<<<blocks(h.n_live_src), 256, 0, c.st>>>(c.nsum, h.d_live_src, lo.d_nid,
+                                                                       c.d_rsig + lo.rbase, c.G + c.off[1],
+                                                                       c.G + c.off[2], c.live, h.n_live_src, chunks);
             });
         } else {
             NeuronEpi ep{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, chunks};
@@ -612,20 +675,21 @@ void backward(Core& c, int B) {
         std::swap(gz, nxt);
     }
     // gz now holds gh0 (the sensory layer's incoming gradient)
+    if (c.n_plug_live)
     launch(c, K_PLUG_BWD, [&]() {
-        const dim3 g((c.n_s + kWarps - 1) / kWarps);
+        const dim3 g((c.n_plug_live + kWarps - 1) / kWarps);
         if (c.fan == 8)
-            k_plug_bwd<8><<<g, kThreads, 0, c.st>>>(gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
+            k_plug_bwd<8><<<g, kThreads, 0, c.st>>>(c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
                                                     c.x, c.d_rgain, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
-                                                    c.G + c.off[3], c.G + c.off[4], c.n_s, c.fan, B, B);
+                                                    c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
         else if (c.fan == 16)
-            k_plug_bwd<16><<<g, kThreads, 0, c.st>>>(gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
+            k_plug_bwd<16><<<g, kThreads, 0, c.st>>>(c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
                                                      c.x, c.d_rgain, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
-                                                     c.G + c.off[3], c.G + c.off[4], c.n_s, c.fan, B, B);
+                                                     c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
         else
-            k_plug_bwd<0><<<g, kThreads, 0, c.st>>>(gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
+            k_plug_bwd<0><<<g, kThreads, 0, c.st>>>(c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
                                                     c.x, c.d_rgain, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
-                                                    c.G + c.off[3], c.G + c.off[4], c.n_s, c.fan, B, B);
+                                                    c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
     });
 }
 

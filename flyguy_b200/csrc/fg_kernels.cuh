@@ -707,15 +707,16 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
 }
 
 // per merged pair p of row t: gp = sum_b gz[t,b] * hp[src_p, b], added to the gradient of every edge weight of the
-// pair. One CTA per row, the row's pairs 8 at a time.
+// pair. One CTA per row of `rows` (the rows whose gradient can be non-zero), the row's pairs 8 at a time.
 template <class T, bool ATOMIC>
-__global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ pptr, const int2* __restrict__ pairs,
+__global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ rows, const int* __restrict__ pptr,
+                                                    const int2* __restrict__ pairs,
                                                     const int* __restrict__ gptr, const int* __restrict__ gw,
                                                     const float* __restrict__ gz, const float* __restrict__ hp,
                                                     const int* __restrict__ live, float* __restrict__ gW, int B,
                                                     int ld) {
     __shared__ float red[8 * kWarps];
-    const int t = blockIdx.x;
+    const int t = __ldg(&rows[blockIdx.x]);
     if (!live[t]) return;
     const int e0 = pptr[t], e1 = pptr[t + 1];
     const float* g = gz + (size_t)t * ld;
@@ -917,37 +918,44 @@ __global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__
     if (lane == 0) done[(size_t)ri * gridDim.y + chunk] = 0;
 }
 
-// per row of a layer: gain grad += sum over chunks of g*z, theta grad += -(sum of g) * sigmoid(theta); live = any g
-__global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __restrict__ nid,
-                                const float* __restrict__ rsig, float* __restrict__ ggain, float* __restrict__ gtheta,
-                                int* __restrict__ live, int rows, int chunks) {
-    const int s = blockIdx.x * blockDim.x + threadIdx.x;
-    if (s >= rows) return;
-    float a = 0.f, b = 0.f, n = 0.f;
+// per listed row of a layer (the rows the transposed hop finished): gain grad += sum over chunks of g*z, theta grad +=
+// -(sum of g) * sigmoid(theta); live = any g
+__global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __restrict__ list,
+                                const int* __restrict__ nid, const float* __restrict__ rsig,
+                                float* __restrict__ ggain, float* __restrict__ gtheta, int* __restrict__ live, int n,
+                                int chunks) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int s = __ldg(&list[i]);
+    float a = 0.f, b = 0.f, nz = 0.f;
     const float* p = nsum + (size_t)s * chunks * 3;
-    for (int k = 0; k < chunks; ++k) { a += p[3 * k]; b += p[3 * k + 1]; n += p[3 * k + 2]; }
+    for (int k = 0; k < chunks; ++k) { a += p[3 * k]; b += p[3 * k + 1]; nz += p[3 * k + 2]; }
     const int id = nid[s];
     ggain[id] += a;
     gtheta[id] += -b * rsig[s];
-    live[s] = n > 0.f;
+    live[s] = nz > 0.f;
 }
 
-// sensory layer and plug, one warp per sensory row s over the whole batch (4 samples per lane per step):
+// sensory layer and plug, one warp per listed sensory row s (the rows with a possibly non-zero gradient) over the
+// whole batch (4 samples per lane per step):
 // g0 = gh0 * [h0 > 0]; gd = gdrive (re-drive from later hops) + g0 * gain; sums over the batch of g0 * drive, g0, gd and
 // gd * x[col_e] for the row's fan edges (FAN of them, FAN <= 16; FAN 0: up to 16 in steps), reduced over the warp in
 // a fixed order and added to the gradients of gain, theta, in_b and in_w.
 constexpr int kPlugFan = 16;
 template <int FAN>
-__global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__ gh0, const float* __restrict__ h0,
+__global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ list, const int* __restrict__ gh_valid,
+                                                       const float* __restrict__ gh0, const float* __restrict__ h0,
                                                        const float* __restrict__ drive, const float* __restrict__ gdrive,
                                                        const int* __restrict__ n0, const int* __restrict__ in_col,
                                                        const float* __restrict__ x, const float* __restrict__ rgain,
                                                        const float* __restrict__ rsig, float* __restrict__ ggain,
                                                        float* __restrict__ gtheta, float* __restrict__ gin_w,
-                                                       float* __restrict__ gin_b, int n_s, int fan, int B, int ld) {
+                                                       float* __restrict__ gin_b, int n_list, int fan, int B, int ld) {
     constexpr int F = FAN > 0 ? FAN : kPlugFan;
-    const int s = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (s >= n_s) return;
+    const int i = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (i >= n_list) return;
+    const int s = __ldg(&list[i]);
+    const bool ghv = __ldg(&gh_valid[s]) != 0;      // rows the transposed hop did not write have gh0 = 0
     const float gn = __ldg(&rgain[s]);
     const size_t o = (size_t)s * ld;
     const size_t e0 = (size_t)s * fan;
@@ -961,7 +969,7 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const float* __restrict__
 #pragma unroll
         for (int u = 0; u < F + 3; ++u) v[u] = 0.f;
         for (int b = lane * 4; b < B; b += 128) {
-            const float4 gh = __ldg(reinterpret_cast<const float4*>(gh0 + o + b));
+            const float4 gh = ghv ? __ldg(reinterpret_cast<const float4*>(gh0 + o + b)) : make_float4(0.f, 0.f, 0.f, 0.f);
             const float4 hh = __ldg(reinterpret_cast<const float4*>(h0 + o + b));
             const float4 gr = __ldg(reinterpret_cast<const float4*>(gdrive + o + b));
             const float g[4] = {hh.x > 0.f ? gh.x : 0.f, hh.y > 0.f ? gh.y : 0.f, hh.z > 0.f ? gh.z : 0.f,
