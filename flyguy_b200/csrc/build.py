@@ -34,12 +34,12 @@ def stale() -> bool:
     return not LIB.exists() or any(d.stat().st_mtime > LIB.stat().st_mtime for d in DEPS)
 
 
-def build(force: bool = False, ptxas_v: bool = False, out: Path = LIB) -> Path:
+def build(force: bool = False, ptxas_v: bool = False, out: Path = LIB, defines: tuple[str, ...] = ()) -> Path:
     if not force and out == LIB and not stale():
         return out
     tmp = out.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "-I", str(REPO / "include"), "-o", str(tmp), *map(str, SOURCES)]
+           "-I", str(REPO / "include"), *[f"-D{d}" for d in defines], "-o", str(tmp), *map(str, SOURCES)]
     if ptxas_v:
         cmd += ["-Xptxas", "-v"]
     r = subprocess.run(cmd, capture_output=True, text=True)

@@ -15,7 +15,7 @@ import numpy as np
 from .netfile import Structure, read_net, write_net
 
 PKG = Path(__file__).resolve().parent
-LIB_PATH = PKG / "libflyguy_b200.so"
+LIB_PATH = Path(os.environ.get("FLYGUY_B200_LIB", PKG / "libflyguy_b200.so"))   # (override: a variant build)
 FG_ACT_BF16, FG_INFER_ONLY, FG_ACT_F16 = 1, 2, 4
 _lib = None
 
