@@ -49,7 +49,13 @@ WORKLOADS = {
     "train": dict(cfg=3, batch=16384, per_gpu=False, flags="train", metric="train samples/sec", unit="samples/s",
                   dtype="f32", desc="config 3: distillation step (forward, KL loss, backward, Adam) fp32, global "
                                     "batch 16,384 data-parallel, one NCCL all-reduce of the flat gradient per step"),
+    "full": dict(cfg=4, batch=32768, per_gpu=False, flags="train", graph="full", metric="train samples/sec",
+                 unit="samples/s", dtype="f32",
+                 desc="config 4: the untrimmed graph (166,700 neurons, 15,283,167 edges, every hop past the first over "
+                      "all edges with shared weights, sensory drive at every hop): forward + backward + Adam fp32, "
+                      "global batch 32,768 data-parallel (pieces of at most 16,384 per GPU, one all-reduce per step)"),
 }
+PIECE = 16384          # largest batch one handle runs at once (config 4: memory for the 166,700-row layers)
 LR = 3e-4
 FALLBACK_HBM_GBS = 6650.0
 
@@ -153,15 +159,21 @@ def algo_bytes(cls: str, s, B: int, act: int) -> float:
 
 
 # ------------------------------------------------------------------ our arm
+def make_graph(W):
+    from flyguy_b200 import synth
+    return synth.make_full_graph() if W.get("graph") == "full" else synth.make_synthetic()
+
+
 def run_ours(a, W, rank, world, dev, torch, dist):
     from flyguy_b200 import native, synth
-    s, P = synth.make_synthetic()
+    s, P = make_graph(W)
     Bg = (a.batch or W["batch"]) * (world if W["per_gpu"] else 1)
     B = Bg // world
     assert B % 32 == 0 and B * world == Bg, "the batch must split into multiples of 32"
     flags = {"bf16": native.FG_ACT_BF16, "f16": native.FG_ACT_F16, "fp32": native.FG_INFER_ONLY,
              "train": 0}[W["flags"]]
-    h = native.Handle(s, B, flags, device=dev)
+    piece = min(B, PIECE) if W.get("graph") == "full" else B
+    h = native.Handle(s, piece, flags, device=dev)
     h.set_params(P, 0)
     h.set_params(P, 1)
     obs_np, teacher_np = synth.make_batch(B, seed=1000 + rank)
@@ -175,7 +187,8 @@ def run_ours(a, W, rank, world, dev, torch, dist):
     def step():
         if train:
             h.zero_grad()
-            h.teach(obs, teacher, 1.0, logits=None, stats=False)
+            for lo in range(0, B, piece):
+                h.teach(obs[lo:lo + piece], teacher[lo:lo + piece], 1.0, logits=None, stats=False, loss_norm=B)
             if world > 1:
                 dist.all_reduce(grad, op=dist.ReduceOp.AVG)
             h.step(LR, 0.3 * LR, LR, 0.0, 0.999)
@@ -238,7 +251,7 @@ def run_ours(a, W, rank, world, dev, torch, dist):
                  "frac": round(per_unit * value / world / 1e9 / peak, 4)}
     # ---- e2e through the host-buffer entry points
     e2e = None if a.no_e2e else run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier,
-                                          max_over_ranks, grad)
+                                          max_over_ranks, grad, piece)
     # ---- CPU baseline (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -246,12 +259,16 @@ def run_ours(a, W, rank, world, dev, torch, dist):
     out = {"metric": W["metric"], "value": round(value, 1), "unit": W["unit"], "n_gpus": world, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": round(t_max / a.steps * 1e3, 4), "higher_is_better": True,
            "scaling": "weak" if W["per_gpu"] else "strong", "vs_baseline": None, "dtype": W["dtype"],
-           "data": "synthetic: seeded 3-hop graph (16,894/46,393/37,748/1,332 neurons, 2,992,734 edges, lognormal "
-                   "in-degree mean 35, Zipf(1.5) sources), obs ~ N(0,1), teacher ~ N(0,4)",
+           "data": ("synthetic: seeded untrimmed graph (166,700 neurons, 15,283,167 edges, lognormal in-degree mean 92, "
+                    "Zipf(1.5) sources), obs ~ N(0,1), teacher ~ N(0,4)" if W.get("graph") == "full" else
+                    "synthetic: seeded 3-hop graph (16,894/46,393/37,748/1,332 neurons, 2,992,734 edges, lognormal "
+                    "in-degree mean 35, Zipf(1.5) sources), obs ~ N(0,1), teacher ~ N(0,4)"),
            "config": {"workload": W["desc"], "baseline_config": W["cfg"], "global_batch": Bg, "per_gpu_batch": B,
                       "parallelism": (f"dp{world}" if train else f"batch-sharded x{world}, no collective"),
                       "l2": "flushed between timed steps (256 MiB write, outside the step events)",
-                      "graph": "synthetic flyguy-sized 3-hop", "edges": E},
+                      "graph": ("synthetic untrimmed 166,700-neuron graph" if W.get("graph") == "full"
+                                else "synthetic flyguy-sized 3-hop"), "edges": s["n_w"], "edge_steps": E,
+                      "pieces_per_step": (B + piece - 1) // piece},
            "roofline": roof, "step_roofline": step_roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
            "gpu_launches": int(launches),
            "kernels_ms_per_step": {k: round(v[0], 4) for k, v in kern_step.items()}}
@@ -268,7 +285,7 @@ def traffic_of(cls: str, W) -> float | None:
     return float(v) if v is not None else None
 
 
-def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier, max_over_ranks, grad):
+def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier, max_over_ranks, grad, piece):
     train = W["flags"] == "train"
     obs_h = torch.from_numpy(obs_np).pin_memory()
     out_h = torch.empty(B, s["n_act"]).pin_memory()
@@ -281,7 +298,10 @@ def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barr
             obs_d.copy_(obs_h, non_blocking=True)
             teach_d.copy_(teach_h, non_blocking=True)
             h.zero_grad()
-            st = h.teach(obs_d, teach_d, 1.0, logits=None, stats=world == 1)
+            st = None
+            for lo in range(0, B, piece):
+                st = h.teach(obs_d[lo:lo + piece], teach_d[lo:lo + piece], 1.0, logits=None, stats=world == 1,
+                             loss_norm=B)
             if world > 1:
                 dist.all_reduce(grad, op=dist.ReduceOp.AVG)
                 h.step(LR, 0.3 * LR, LR, 0.0, 0.999)
@@ -324,6 +344,11 @@ def _ref_forward(s, P, threads):
 
 
 def cpu_baseline(W, s, P, budget: float):
+    """The reference's CPU path timed on this host's cores on a bounded sample sized to ~`budget` seconds."""
+    return _cpu_baseline(W, s, P, budget)
+
+
+def _cpu_baseline(W, s, P, budget: float):
     """The reference's CPU path timed on this host's cores on a bounded sample sized to ~`budget` seconds."""
     from flyguy_b200 import synth
     threads = os.cpu_count() or 1
@@ -391,7 +416,7 @@ def _cpu_model() -> str:
 def run_reference(a, W):
     """The reference's CPU implementation of the path, W warm-up + K timed steps of a bounded sample each."""
     from flyguy_b200 import synth
-    s, P = synth.make_synthetic()
+    s, P = make_graph(W)
     threads = os.cpu_count() or 1
     Bg = W["batch"]
     if W["flags"] == "train":

@@ -40,6 +40,8 @@ struct Hop {
     long long tbase = 0;                         // first transposed pair of this hop in the concatenated arrays
     int T = 0;                                   // transposed pairs kept for the backward
     int *d_live_dst = nullptr, n_live_dst = 0;   // rows of this hop's layer whose gradient can be non-zero
+    int2* d_sd_items = nullptr;                  // weight-gradient work items {row, first of up to 4 pairs}
+    int n_sd_items = 0;
     int *d_live_src = nullptr, n_live_src = 0;   // rows of the layer below that this hop's backward writes
     int4 *d_segs = nullptr, *d_reds = nullptr;   // transposed product: segments of source rows, split-row reductions
     int* d_seg_red = nullptr;                    // per segment: its split row's reduction index, or -1
@@ -68,6 +70,7 @@ struct Core {
     int maxB = 0, flags = 0;
     bool bf16 = false, f16 = false, train = true, redrive = false;
     float* owT = nullptr;                                // out_w transposed, padded to kOutA actions
+    float* out_part = nullptr;                           // the output plug's per-slice partial logits
     float* seg_part = nullptr;                           // partial rows of split transposed segments
     int* seg_done = nullptr;                             // arrival counters of split rows' segments [red][chunk]
     int *d_in_crow = nullptr, *d_in_col = nullptr, *d_n0 = nullptr, *d_dn = nullptr;
@@ -239,6 +242,11 @@ void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, c
         for (int s = 0; s < h.n_src; ++s) if (live[k - 1][s]) ls.push_back(s);
         h.n_live_dst = (int)ld.size();
         h.n_live_src = (int)ls.size();
+        std::vector<int2> items;
+        for (int t : ld)
+            for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; p += 4) items.push_back(make_int2(t, p));
+        h.n_sd_items = (int)items.size();
+        h.d_sd_items = upload(c, items);
         h.d_live_dst = upload(c, ld);
         h.d_live_src = upload(c, ls);
         // transposed pairs into live rows: by source, destinations ascending
@@ -438,6 +446,13 @@ void alloc_all(Core& c) {
         h.d_h = dalloc<char>(c, (size_t)h.rows * B * (h.out_f32 ? 4 : act_bytes(c)));
     }
     c.owT = dalloc<float>(c, (size_t)c.n_dn * kOutA);
+    {
+        const int tiles = (int)((B + kOutB - 1) / kOutB);
+        const int slices = std::max(1, std::min(8, (2 * 148 + tiles - 1) / tiles));
+        // sized for the largest slice count any batch up to max_batch can take
+        c.out_part = dalloc<float>(c, (size_t)8 * kOutA * std::min<size_t>(B, (size_t)2 * 148 * kOutB));
+        (void)slices;
+    }
     c.lg = dalloc<float>(c, (size_t)c.n_act * B);
     c.norm_part = dalloc<float>(c, 1024);
     c.norm = dalloc<float>(c, 4);
@@ -576,11 +591,19 @@ void forward_t(Core& c, const float* obs, int B, float* logits, int ema, bool ke
         hp = h.d_h;
         hp_f32 = h.out_f32;
     }
+    // enough CTAs for ~2 waves: split the dn columns when the batch alone gives too few sample tiles
+    const int tiles = (B + kOutB - 1) / kOutB;
+    const int slices = std::max(1, std::min(8, (2 * 148 + tiles - 1) / tiles));
     launch(c, K_OUT_FWD, [&]() {
-        k_out_fwd<float><<<(B + kOutB - 1) / kOutB, 256, 0, c.st>>>(c.owT, Pw + c.off[6], c.d_dn, (const float*)hp,
-                                                                  keep_lg ? c.lg : nullptr, logits, c.n_act, c.n_dn, B,
-                                                                  B);
+        k_out_fwd<float><<<dim3(tiles, slices), 256, 0, c.st>>>(c.owT, Pw + c.off[6], c.d_dn, (const float*)hp,
+                                                                keep_lg ? c.lg : nullptr, logits, c.out_part, c.n_act,
+                                                                c.n_dn, B, B);
     });
+    if (slices > 1)
+        launch(c, K_OUT_FWD, [&]() {
+            k_out_reduce<<<(B + 31) / 32, 256, 0, c.st>>>(c.out_part, Pw + c.off[6], keep_lg ? c.lg : nullptr, logits,
+                                                          slices, c.n_act, B, B);
+        });
     c.lastB = B;
 }
 
@@ -629,19 +652,21 @@ void backward(Core& c, int B) {
     for (int k = c.hops - 1; k >= 0; --k) {
         const Hop& h = c.hop[k];
         const float* hprev = k ? (const float*)c.hop[k - 1].d_h : (const float*)c.h0;
-        if (h.n_live_dst == 0) {}
-        else if (h.widx_unique)
-            launch(c, K_SDDMM, [&]() {
-                k_sddmm<float, false><<<h.n_live_dst, kThreads, 0, c.st>>>(h.d_live_dst, h.d_pptr, c.d_pairs + h.pbase,
-                                                                     c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live,
-                                                                     c.G + c.off[0], B, B);
-            });
-        else
-            launch(c, K_SDDMM, [&]() {
-                k_sddmm<float, true><<<h.n_live_dst, kThreads, 0, c.st>>>(h.d_live_dst, h.d_pptr, c.d_pairs + h.pbase,
-                                                                    c.d_gptr + h.pbase,
-                                                                    c.d_gw, gz, hprev, c.live, c.G + c.off[0], B, B);
-            });
+        if (h.n_sd_items) {
+            const unsigned g = (unsigned)((h.n_sd_items + kWarps - 1) / kWarps);
+            if (h.widx_unique)
+                launch(c, K_SDDMM, [&]() {
+                    k_sddmm<false><<<g, kThreads, 0, c.st>>>(h.d_sd_items, h.d_pptr, c.d_pairs + h.pbase,
+                                                             c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live,
+                                                             c.G + c.off[0], h.n_sd_items, B, B);
+                });
+            else
+                launch(c, K_SDDMM, [&]() {
+                    k_sddmm<true><<<g, kThreads, 0, c.st>>>(h.d_sd_items, h.d_pptr, c.d_pairs + h.pbase,
+                                                            c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live,
+                                                            c.G + c.off[0], h.n_sd_items, B, B);
+                });
+        }
         const bool full = B % 256 == 0;
         auto transposed = [&](auto epi, const NeuronEpi& ep) {
             constexpr bool EPI = decltype(epi)::value;
@@ -909,13 +934,19 @@ void fc_sync(void* h) {
 }
 
 int fg_teach(void* h, const float* obs, const float* teacher, int B, float inv_temp, float* logits, double* stats) {
+    return fg_teach_ex(h, obs, teacher, B, inv_temp, (float)B, logits, stats);
+}
+
+int fg_teach_ex(void* h, const float* obs, const float* teacher, int B, float inv_temp, float loss_norm, float* logits,
+                double* stats) {
     return guarded(h, [&]() {
+        if (!(loss_norm > 0.f)) throw Err("fg_teach_ex: loss_norm must be positive");
         Core& c = *as_core(h);
         check_batch(c, B);
         if (!c.train) throw Err("this handle was created for inference only");
         forward(c, obs, B, logits, 0, true);
         CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
-        launch(c, K_LOSS, [&]() { k_loss<<<blocks(B), 256, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp); });
+        launch(c, K_LOSS, [&]() { k_loss<<<blocks(B), 256, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp, 1.f / loss_norm); });
         launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
         backward(c, B);
         if (stats) {

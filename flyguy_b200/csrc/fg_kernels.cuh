@@ -452,27 +452,30 @@ __global__ void __launch_bounds__(kThreads, HopOcc<TI>::min_blocks) k_hop_fwd(co
 }
 
 // output plug: logits[a,b] = out_b[a] + sum_j out_w[a,j] * hK[dn[j], b], a register-blocked product: a CTA owns
-// 96 actions x 128 samples, each thread 6 actions x 8 samples; owT is out_w transposed and padded to 96 actions
-// ([n_dn][96], refreshed with the weights), staged with hK 32 columns at a time. Writes the neuron-major copy
-// lg [n_act, ld] (for the loss) and/or the caller's rows out [B, n_act].
-constexpr int kOutA = 96, kOutB = 128, kOutK = 32;
+// 96 actions x 64 samples and one slice of the dn columns (split K: blockIdx.y of gridDim.y), each thread 6 actions x
+// 4 samples; owT is out_w transposed and padded to 96 actions ([n_dn][96], refreshed with the weights), staged with hK
+// 32 columns at a time. With one slice it finishes the logits itself; with several, each writes its partial
+// [96][ld] slab and k_out_reduce adds the slices in order.
+constexpr int kOutA = 96, kOutB = 64, kOutK = 32;
 template <class T>
 __global__ void __launch_bounds__(256) k_out_fwd(const float* __restrict__ owT, const float* __restrict__ ob,
                                                  const int* __restrict__ dn, const T* __restrict__ hK,
-                                                 float* __restrict__ lg, float* __restrict__ out, int n_act, int n_dn,
-                                                 int B, int ld) {
-    __shared__ __align__(16) float sm[kOutK * kOutA + kOutK * kOutB];   // 28 KB; reused for the output rows
+                                                 float* __restrict__ lg, float* __restrict__ out,
+                                                 float* __restrict__ part, int n_act, int n_dn, int B, int ld) {
+    __shared__ __align__(16) float sm[kOutK * kOutA + kOutK * kOutB];   // 20 KB; reused for the output rows
     float* Ws = sm;
     float* Hs = sm + kOutK * kOutA;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int b0 = blockIdx.x * kOutB;
-    float acc[6][8];
+    const int slices = gridDim.y, per = (n_dn + slices - 1) / slices;
+    const int k_lo = blockIdx.y * per, k_hi = min(n_dn, k_lo + per);
+    float acc[6][4];
 #pragma unroll
     for (int i = 0; i < 6; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
-    for (int k0 = 0; k0 < n_dn; k0 += kOutK) {
-        const int nk = min(kOutK, n_dn - k0);
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int k0 = k_lo; k0 < k_hi; k0 += kOutK) {
+        const int nk = min(kOutK, k_hi - k0);
         __syncthreads();
         for (int i = threadIdx.x; i < kOutK * kOutA / 4; i += 256) {
             const int k = i / (kOutA / 4);
@@ -485,71 +488,96 @@ __global__ void __launch_bounds__(256) k_out_fwd(const float* __restrict__ owT, 
             Hs[i] = (k < nk && b0 + b < B) ? ld1(hK + (size_t)__ldg(&dn[k0 + k]) * ld + b0 + b) : 0.f;
         }
         __syncthreads();
-#pragma unroll 4
+#pragma unroll 8
         for (int k = 0; k < kOutK; ++k) {
-            const float4 h0 = *reinterpret_cast<const float4*>(Hs + k * kOutB + tx * 8);
-            const float4 h1 = *reinterpret_cast<const float4*>(Hs + k * kOutB + tx * 8 + 4);
+            const float4 h = *reinterpret_cast<const float4*>(Hs + k * kOutB + tx * 4);
             const float2 w01 = *reinterpret_cast<const float2*>(Ws + k * kOutA + ty * 6);
             const float2 w23 = *reinterpret_cast<const float2*>(Ws + k * kOutA + ty * 6 + 2);
             const float2 w45 = *reinterpret_cast<const float2*>(Ws + k * kOutA + ty * 6 + 4);
-            const float hv[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            const float hv[4] = {h.x, h.y, h.z, h.w};
             const float wv[6] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y};
 #pragma unroll
             for (int i = 0; i < 6; ++i)
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(wv[i], hv[j], acc[i][j]);
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wv[i], hv[j], acc[i][j]);
         }
+    }
+    if (slices > 1) {                                      // partial slab of this slice: part[slice][a][ld]
+        float* pp = part + (size_t)blockIdx.y * kOutA * ld;
+#pragma unroll
+        for (int i = 0; i < 6; ++i) {
+            const int a = ty * 6 + i;
+            const int b = b0 + tx * 4;
+            if (b + 4 <= B) *reinterpret_cast<float4*>(pp + (size_t)a * ld + b) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            else for (int j = 0; j < 4; ++j) if (b + j < B) pp[(size_t)a * ld + b + j] = acc[i][j];
+        }
+        return;
     }
 #pragma unroll
     for (int i = 0; i < 6; ++i) {
         const int a = ty * 6 + i;
         const float bias = a < n_act ? __ldg(&ob[a]) : 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] += bias;
+        for (int j = 0; j < 4; ++j) acc[i][j] += bias;
     }
     if (lg) {
 #pragma unroll
         for (int i = 0; i < 6; ++i) {
             const int a = ty * 6 + i;
             if (a >= n_act) continue;
-            float* row = lg + (size_t)a * ld + b0 + tx * 8;
-            if (b0 + tx * 8 + 8 <= B) {
-                *reinterpret_cast<float4*>(row) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-                *reinterpret_cast<float4*>(row + 4) = make_float4(acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
-            } else {
-                for (int j = 0; j < 8; ++j) if (b0 + tx * 8 + j < B) row[j] = acc[i][j];
-            }
+            float* row = lg + (size_t)a * ld + b0 + tx * 4;
+            if (b0 + tx * 4 + 4 <= B) *reinterpret_cast<float4*>(row) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            else for (int j = 0; j < 4; ++j) if (b0 + tx * 4 + j < B) row[j] = acc[i][j];
         }
     }
-    if (out) {                                            // [128 samples][n_act] rows, staged for coalesced stores
+    if (out) {                                            // [64 samples][n_act] rows, staged for coalesced stores
         __syncthreads();
-        float* st = sm;                                   // needs kOutB * (kOutA + 1) floats: reuse + spill below
+        float* st = sm;                                   // 64 x 97 floats fit the 20 KB buffer
         const int stride = kOutA + 1;
-        for (int half = 0; half < 2; ++half) {            // 64 samples at a time fit the 28 KB buffer
-            __syncthreads();
-            if ((tx >> 3) == half) {
 #pragma unroll
-                for (int i = 0; i < 6; ++i)
+        for (int i = 0; i < 6; ++i)
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) st[((tx & 7) * 8 + j) * stride + ty * 6 + i] = acc[i][j];
-            }
-            __syncthreads();
-            const int sb = b0 + half * 64;
-            const int nbb = max(0, min(64, B - sb));
-            float* o = out + (size_t)sb * n_act;
-            for (int i = threadIdx.x; i < nbb * n_act; i += 256) {
-                const int bb = i / n_act, a = i - bb * n_act;
-                o[i] = st[bb * stride + a];
-            }
+            for (int j = 0; j < 4; ++j) st[(tx * 4 + j) * stride + ty * 6 + i] = acc[i][j];
+        __syncthreads();
+        const int nbb = max(0, min(kOutB, B - b0));
+        float* o = out + (size_t)b0 * n_act;
+        for (int i = threadIdx.x; i < nbb * n_act; i += 256) {
+            const int bb = i / n_act, a = i - bb * n_act;
+            o[i] = st[bb * stride + a];
         }
+    }
+}
+// the slices' partial logits added in slice order + bias -> lg [n_act, ld] and/or out [B, n_act]; a CTA per 32 samples
+__global__ void __launch_bounds__(256) k_out_reduce(const float* __restrict__ part, const float* __restrict__ ob,
+                                                    float* __restrict__ lg, float* __restrict__ out, int slices,
+                                                    int n_act, int B, int ld) {
+    __shared__ float st[32][kOutA + 1];
+    const int b0 = blockIdx.x * 32;
+    for (int i = threadIdx.x; i < n_act * 32; i += 256) {
+        const int a = i >> 5, bb = i & 31, b = b0 + bb;
+        if (b >= B) continue;
+        float v = __ldg(&ob[a]);
+        for (int s = 0; s < slices; ++s) v += __ldg(&part[((size_t)s * kOutA + a) * ld + b]);
+        if (lg) lg[(size_t)a * ld + b] = v;
+        st[bb][a] = v;
+    }
+    if (!out) return;
+    __syncthreads();
+    const int nbb = max(0, min(32, B - b0));
+    float* o = out + (size_t)b0 * n_act;
+    for (int i = threadIdx.x; i < nbb * n_act; i += 256) {
+        const int bb = i / n_act, a = i - bb * n_act;
+        o[i] = st[bb][a];
     }
 }
 
 // ---------------------------------------------------------------- loss
-// per sample: p_t = softmax(teacher * it); kl = sum p_t (log p_t - log softmax(s)); dl = (softmax(s) - p_t) / B;
+// per sample: p_t = softmax(teacher * it); kl = sum p_t (log p_t - log softmax(s)); dl = (softmax(s) - p_t) * inv_norm
+// (inv_norm = 1 / the number of samples the loss averages over: the batch, or more when a batch comes in pieces);
 // argmax agreement. teacher is the caller's [B, n_act]; lg and dl are neuron-major.
 __global__ void k_loss(const float* __restrict__ lg, const float* __restrict__ teacher, float* __restrict__ dl,
-                       float* __restrict__ kl_s, float* __restrict__ ag_s, int n_act, int B, int ld, float it) {
+                       float* __restrict__ kl_s, float* __restrict__ ag_s, int n_act, int B, int ld, float it,
+                       float inv_norm) {
     int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     const float* t = teacher + (size_t)b * n_act;
@@ -562,12 +590,12 @@ __global__ void k_loss(const float* __restrict__ lg, const float* __restrict__ t
     }
     float zs = 0.f, zt = 0.f;
     for (int a = 0; a < n_act; ++a) { zs += expf(lg[(size_t)a * ld + b] - ms); zt += expf(t[a] * it - mt); }
-    const float ls = ms + logf(zs), lt = mt + logf(zt), inv_b = 1.f / (float)B;
+    const float ls = ms + logf(zs), lt = mt + logf(zt);
     float kl = 0.f;
     for (int a = 0; a < n_act; ++a) {
         float lps = lg[(size_t)a * ld + b] - ls, lpt = t[a] * it - lt, pt = expf(lpt);
         kl += pt * (lpt - lps);
-        dl[(size_t)a * ld + b] = (expf(lps) - pt) * inv_b;
+        dl[(size_t)a * ld + b] = (expf(lps) - pt) * inv_norm;
     }
     kl_s[b] = kl;
     ag_s[b] = as == at ? 1.f : 0.f;
@@ -710,48 +738,45 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
 }
 
 // per merged pair p of row t: gp = sum_b gz[t,b] * hp[src_p, b], added to the gradient of every edge weight of the
-// pair. One CTA per row of `rows` (the rows whose gradient can be non-zero), the row's pairs 8 at a time.
-template <class T, bool ATOMIC>
-__global__ void __launch_bounds__(kThreads) k_sddmm(const int* __restrict__ rows, const int* __restrict__ pptr,
-                                                    const int2* __restrict__ pairs,
-                                                    const int* __restrict__ gptr, const int* __restrict__ gw,
-                                                    const float* __restrict__ gz, const float* __restrict__ hp,
-                                                    const int* __restrict__ live, float* __restrict__ gW, int B,
-                                                    int ld) {
-    __shared__ float red[8 * kWarps];
-    const int t = __ldg(&rows[blockIdx.x]);
-    if (!live[t]) return;
-    const int e0 = pptr[t], e1 = pptr[t + 1];
+// pair. One warp per work item {row, first pair} - up to 4 consecutive pairs of one row whose gradient can be
+// non-zero - over the whole batch, 4 samples per lane per step; a warp-shuffle reduction in a fixed order (no block
+// barriers, no atomics for weights used once per hop).
+template <bool ATOMIC>
+__global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ items, const int* __restrict__ pptr,
+                                                    const int2* __restrict__ pairs, const int* __restrict__ gptr,
+                                                    const int* __restrict__ gw, const float* __restrict__ gz,
+                                                    const float* __restrict__ hp, const int* __restrict__ live,
+                                                    float* __restrict__ gW, int n_items, int B, int ld) {
+    const int wi = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (wi >= n_items) return;
+    const int2 it = __ldg(&items[wi]);
+    const int t = it.x, p0 = it.y;
+    if (!__ldg(&live[t])) return;
+    const int np = min(4, __ldg(&pptr[t + 1]) - p0);
+    const float* hs[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) hs[u] = hp + (size_t)(u < np ? __ldg(&pairs[p0 + u].x) : 0) * ld;
     const float* g = gz + (size_t)t * ld;
-    for (int p0 = e0; p0 < e1; p0 += 8) {
-        const int np = min(8, e1 - p0);
-        int src[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) src[u] = u < np ? __ldg(&pairs[p0 + u].x) : 0;
-        float acc[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 2
-        for (int b = threadIdx.x * 4; b < B; b += kThreads * 4) {
-            const float4 q = __ldg(reinterpret_cast<const float4*>(g + b));
-            if (q.x == 0.f && q.y == 0.f && q.z == 0.f && q.w == 0.f) continue;     // silent samples: nothing to add
+    for (int b = lane * 4; b < B; b += 128) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(g + b));
+        if (q.x == 0.f && q.y == 0.f && q.z == 0.f && q.w == 0.f) continue;       // silent samples: nothing to add
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                if (u < np) {
-                    const float4 hq = __ldg(reinterpret_cast<const float4*>(hp + (size_t)src[u] * ld + b));
-                    acc[u] = fmaf(q.x, hq.x, fmaf(q.y, hq.y, fmaf(q.z, hq.z, fmaf(q.w, hq.w, acc[u]))));
-                }
+        for (int u = 0; u < 4; ++u) {
+            if (u < np) {
+                const float4 hq = __ldg(reinterpret_cast<const float4*>(hs[u] + b));
+                acc[u] = fmaf(q.x, hq.x, fmaf(q.y, hq.y, fmaf(q.z, hq.z, fmaf(q.w, hq.w, acc[u]))));
             }
         }
-        block_sum<8>(acc, red);
-        if (threadIdx.x < np) {
-            const int p = p0 + threadIdx.x;
-            float v = 0.f;
+    }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) if (u == (int)threadIdx.x) v = acc[u];
-            for (int j = gptr[p]; j < gptr[p + 1]; ++j) {
-                if (ATOMIC) atomicAdd(&gW[gw[j]], v); else gW[gw[j]] += v;
-            }
+    for (int u = 0; u < 4; ++u) acc[u] = warp_sum(acc[u]);
+    if (lane < np) {
+        const int p = p0 + lane;
+        const float v = lane == 0 ? acc[0] : lane == 1 ? acc[1] : lane == 2 ? acc[2] : acc[3];
+        for (int j = __ldg(&gptr[p]); j < __ldg(&gptr[p + 1]); ++j) {
+            if (ATOMIC) atomicAdd(&gW[gw[j]], v); else gW[gw[j]] += v;
         }
     }
 }

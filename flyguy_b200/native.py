@@ -42,6 +42,7 @@ SIGNATURES = {
     "fg_offsets": (None, [_vp, ctypes.POINTER(_cll)]),
     "fg_layout": (_ci, [_vp, ctypes.POINTER(_ci), ctypes.POINTER(_cll)]),
     "fg_teach": (_ci, [_vp, _vp, _vp, _ci, _cf, _vp, ctypes.POINTER(ctypes.c_double)]),
+    "fg_teach_ex": (_ci, [_vp, _vp, _vp, _ci, _cf, _cf, _vp, ctypes.POINTER(ctypes.c_double)]),
     "fg_forward_host": (_ci, [_vp, _vp, _ci, _vp, _ci]),
     "fg_layer": (_ci, [_vp, _ci, _vp, _ci]),
     "fg_launches": (_cll, [_vp]),
@@ -205,10 +206,12 @@ class Handle:
         self.check()
         return int(v)
 
-    def teach(self, obs, teacher, inv_temp: float = 1.0, logits=None, stats: bool = True):
+    def teach(self, obs, teacher, inv_temp: float = 1.0, logits=None, stats: bool = True, loss_norm: float = 0.0):
+        """Fused forward + KL loss + backward (gradient ADDED); loss_norm: samples the loss averages over (0: B)."""
         self.bind_stream()
         st = (ctypes.c_double * 2)() if stats else None
-        rc = self.L.fg_teach(self.h, _ptr(obs), _ptr(teacher), obs.shape[0], float(inv_temp), _ptr(logits), st)
+        rc = self.L.fg_teach_ex(self.h, _ptr(obs), _ptr(teacher), obs.shape[0], float(inv_temp),
+                                float(loss_norm or obs.shape[0]), _ptr(logits), st)
         if rc:
             self.check()
         return (float(st[0]), float(st[1])) if stats else None

@@ -98,6 +98,10 @@ int fg_layout(void* h, int* sizes, long long* pairs);
  * obs [B, obs_dim], teacher [B, n_act] device; logits [B, n_act] device or NULL. stats: host double[2] (sum of KL over
  * the batch, number of argmax agreements), or NULL to not wait for the GPU. Returns 0 or -1 (see fg_last_error). */
 int fg_teach(void* h, const float* obs, const float* teacher, int B, float inv_temp, float* logits, double* stats);
+/* fg_teach with the loss averaged over loss_norm samples instead of B: a batch larger than max_batch goes through in
+ * pieces (each adds its share of the gradient of the mean over all loss_norm samples). fg_teach = loss_norm B. */
+int fg_teach_ex(void* h, const float* obs, const float* teacher, int B, float inv_temp, float loss_norm, float* logits,
+                double* stats);
 
 /* Forward from HOST memory: obs_host [B, obs_dim] -> logits_host [B, n_act], host<->device copies overlapped with the
  * compute in chunks (pinned host memory makes the copies asynchronous). Waits for the result. Returns 0 or -1. */

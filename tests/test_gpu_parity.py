@@ -304,3 +304,31 @@ def test_stream_binding_and_zero_copy_gradient(cuda):
     G = [g.cpu().numpy() for g in h.get(4)]
     for i in range(7):
         assert rel(G[i], 2 * d[f"G{i}"]) < TOL_GRAD, i
+
+
+def test_untrimmed_graph_config4_matches_oracle(cuda):
+    """Config 4's graph (166,700 neurons, 15,283,167 edges, hops 2-3 over all edges with shared weights, sensory
+    drive re-added at every hop): logits and all gradients of a 64-sample teaching step against the oracle, and a batch
+    in two pieces (fg_teach_ex with the loss over both) equal to one piece."""
+    import torch
+    from oracle.oracle import loss
+    s, P = synth.make_full_graph()
+    obs, teacher = synth.make_batch(64, seed=21)
+    h = _handle(s, P, 64)
+    lg = torch.empty(64, s["n_act"], device="cuda")
+    h.zero_grad()
+    h.teach(_t(obs), _t(teacher), 1.0, logits=lg)
+    G = [g.cpu().numpy() for g in h.get(4)]
+    o = Oracle(s)
+    want_lg = o.forward(P, obs)
+    _, _, dl = loss(want_lg, teacher, 1.0)
+    want = o.backward(P, obs, dl)
+    assert rel(lg.cpu().numpy(), want_lg) < TOL_FP32
+    for i in range(7):
+        assert rel(G[i], want[i]) < TOL_GRAD, i
+    h.zero_grad()
+    for lo in (0, 32):
+        h.teach(_t(obs[lo:lo + 32]), _t(teacher[lo:lo + 32]), 1.0, loss_norm=64)
+    G2 = [g.cpu().numpy() for g in h.get(4)]
+    for i in range(7):
+        assert rel(G2[i], G[i]) < TOL_GRAD, i
