@@ -462,7 +462,9 @@ __global__ void __launch_bounds__(256) k_out_fwd(const float* __restrict__ owT, 
                                                  const int* __restrict__ dn, const T* __restrict__ hK,
                                                  float* __restrict__ lg, float* __restrict__ out,
                                                  float* __restrict__ part, int n_act, int n_dn, int B, int ld) {
-    __shared__ __align__(16) float sm[kOutK * kOutA + kOutK * kOutB];   // 20 KB; reused for the output rows
+    // operand tiles (32 x 96 + 32 x 64 floats), reused afterwards for the 64 x 97 output rows: the larger of the two
+    constexpr int kOperands = kOutK * kOutA + kOutK * kOutB, kRows = kOutB * (kOutA + 1);
+    __shared__ __align__(16) float sm[kOperands > kRows ? kOperands : kRows];
     float* Ws = sm;
     float* Hs = sm + kOutK * kOutA;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -532,7 +534,7 @@ __global__ void __launch_bounds__(256) k_out_fwd(const float* __restrict__ owT, 
     }
     if (out) {                                            // [64 samples][n_act] rows, staged for coalesced stores
         __syncthreads();
-        float* st = sm;                                   // 64 x 97 floats fit the 20 KB buffer
+        float* st = sm;                                   // 64 x 97 floats (the buffer is sized for them)
         const int stride = kOutA + 1;
 #pragma unroll
         for (int i = 0; i < 6; ++i)
