@@ -71,6 +71,7 @@ struct Core {
     bool bf16 = false, f16 = false, train = true, redrive = false;
     float* owT = nullptr;                                // out_w transposed, padded to kOutA actions
     float* out_part = nullptr;                           // the output plug's per-slice partial logits
+    int out_slices = 1;                                  // split-K slices of the dn columns (fixed by the graph)
     float* seg_part = nullptr;                           // partial rows of split transposed segments
     int* seg_done = nullptr;                             // arrival counters of split rows' segments [red][chunk]
     int *d_in_crow = nullptr, *d_in_col = nullptr, *d_n0 = nullptr, *d_dn = nullptr;
@@ -446,13 +447,10 @@ void alloc_all(Core& c) {
         h.d_h = dalloc<char>(c, (size_t)h.rows * B * (h.out_f32 ? 4 : act_bytes(c)));
     }
     c.owT = dalloc<float>(c, (size_t)c.n_dn * kOutA);
-    {
-        const int tiles = (int)((B + kOutB - 1) / kOutB);
-        const int slices = std::max(1, std::min(8, (2 * 148 + tiles - 1) / tiles));
-        // sized for the largest slice count any batch up to max_batch can take
-        c.out_part = dalloc<float>(c, (size_t)8 * kOutA * std::min<size_t>(B, (size_t)2 * 148 * kOutB));
-        (void)slices;
-    }
+    // The slice count depends on the graph only, never on the batch, so a sample's logits are the same bits whatever
+    // batch (or piece of one) it is computed in: one slice per ~320 dn columns, at most 8.
+    c.out_slices = std::max(1, std::min(8, (c.n_dn + 319) / 320));
+    if (c.out_slices > 1) c.out_part = dalloc<float>(c, (size_t)c.out_slices * kOutA * B);
     c.lg = dalloc<float>(c, (size_t)c.n_act * B);
     c.norm_part = dalloc<float>(c, 1024);
     c.norm = dalloc<float>(c, 4);
@@ -591,9 +589,9 @@ void forward_t(Core& c, const float* obs, int B, float* logits, int ema, bool ke
         hp = h.d_h;
         hp_f32 = h.out_f32;
     }
-    // enough CTAs for ~2 waves: split the dn columns when the batch alone gives too few sample tiles
+    // sample tiles x split-K slices of the dn columns (k_out_reduce adds the slices in order, then the bias)
     const int tiles = (B + kOutB - 1) / kOutB;
-    const int slices = std::max(1, std::min(8, (2 * 148 + tiles - 1) / tiles));
+    const int slices = c.out_slices;
     launch(c, K_OUT_FWD, [&]() {
         k_out_fwd<float><<<dim3(tiles, slices), 256, 0, c.st>>>(c.owT, Pw + c.off[6], c.d_dn, (const float*)hp,
                                                                 keep_lg ? c.lg : nullptr, logits, c.out_part, c.n_act,
