@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the connectome hop path on B200: one JSON line (rank 0).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload infer|infer32|train] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload infer|infer16|infer32|train|full] [--sources zipf|uniform] [--impl ours|reference]
   (N > 1: python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N)
 
 Workloads (the reference's BASELINE configs, synthetic inputs: the seeded 2,992,734-edge 3-hop graph of
@@ -71,6 +71,11 @@ def args_():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling of a small case only)")
+    ap.add_argument("--hub-tc", action="store_true",
+                    help="16-bit workloads: hops with hub sources on the tensor-core hop (FG_HUB_TC, opt-in)")
+    ap.add_argument("--sources", choices=["zipf", "uniform"], default="zipf",
+                    help="source distribution of the 3-hop synthetic graph (configs 1-3): Zipf(1.5) ranks, or uniform "
+                         "(no L2 locality from hub sources, and every row of every layer feeds the output)")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -159,19 +164,23 @@ def algo_bytes(cls: str, s, B: int, act: int) -> float:
 
 
 # ------------------------------------------------------------------ our arm
-def make_graph(W):
+def make_graph(W, sources="zipf"):
     from flyguy_b200 import synth
-    return synth.make_full_graph() if W.get("graph") == "full" else synth.make_synthetic()
+    if W.get("graph") == "full":
+        return synth.make_full_graph()
+    return synth.make_synthetic(uniform=sources == "uniform")
 
 
 def run_ours(a, W, rank, world, dev, torch, dist):
     from flyguy_b200 import native, synth
-    s, P = make_graph(W)
+    s, P = make_graph(W, a.sources)
     Bg = (a.batch or W["batch"]) * (world if W["per_gpu"] else 1)
     B = Bg // world
     assert B % 32 == 0 and B * world == Bg, "the batch must split into multiples of 32"
     flags = {"bf16": native.FG_ACT_BF16, "f16": native.FG_ACT_F16, "fp32": native.FG_INFER_ONLY,
              "train": 0}[W["flags"]]
+    if a.hub_tc and W["flags"] in ("bf16", "f16"):
+        flags |= native.FG_HUB_TC
     piece = min(B, PIECE) if W.get("graph") == "full" else B
     h = native.Handle(s, piece, flags, device=dev)
     h.set_params(P, 0)
@@ -238,7 +247,7 @@ def run_ours(a, W, rank, world, dev, torch, dist):
     peak, peak_src = peaks()
     achieved = byts / (kern_step[dom][0] / 1e3) / 1e9 if byts else None
     roof = {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1) if achieved else None, "peak": peak,
-            "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None, "traffic": traffic_of(dom, W),
+            "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None, "traffic": traffic_of(dom, W, a.sources),
             "algorithmic_bytes_per_step": byts, "launches_per_step": kern_step[dom][1],
             "ms_per_step": round(kern_step[dom][0], 4), "peak_source": peak_src}
     # whole-step view: the path's algorithmic bytes per unit (SURVEY formula) x rate
@@ -262,26 +271,30 @@ def run_ours(a, W, rank, world, dev, torch, dist):
            "data": ("synthetic: seeded untrimmed graph (166,700 neurons, 15,283,167 edges, lognormal in-degree mean 92, "
                     "Zipf(1.5) sources), obs ~ N(0,1), teacher ~ N(0,4)" if W.get("graph") == "full" else
                     "synthetic: seeded 3-hop graph (16,894/46,393/37,748/1,332 neurons, 2,992,734 edges, lognormal "
-                    "in-degree mean 35, Zipf(1.5) sources), obs ~ N(0,1), teacher ~ N(0,4)"),
+                    f"in-degree mean 35, {'Zipf(1.5)' if a.sources == 'zipf' else 'uniform'} sources), obs ~ N(0,1), "
+                    "teacher ~ N(0,4)"),
            "config": {"workload": W["desc"], "baseline_config": W["cfg"], "global_batch": Bg, "per_gpu_batch": B,
                       "parallelism": (f"dp{world}" if train else f"batch-sharded x{world}, no collective"),
                       "l2": "flushed between timed steps (256 MiB write, outside the step events)",
                       "graph": ("synthetic untrimmed 166,700-neuron graph" if W.get("graph") == "full"
-                                else "synthetic flyguy-sized 3-hop"), "edges": s["n_w"], "edge_steps": E,
-                      "pieces_per_step": (B + piece - 1) // piece},
+                                else f"synthetic flyguy-sized 3-hop, {a.sources} sources"), "edges": s["n_w"],
+                      "edge_steps": E,
+                      "pieces_per_step": (B + piece - 1) // piece,
+                      "hop_kernel": ("tensor-core hub product + CUDA-core tail (FG_HUB_TC)"
+                                     if a.hub_tc and W["flags"] in ("bf16", "f16") else "CUDA cores")},
            "roofline": roof, "step_roofline": step_roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
            "gpu_launches": int(launches),
            "kernels_ms_per_step": {k: round(v[0], 4) for k, v in kern_step.items()}}
     return out
 
 
-def traffic_of(cls: str, W) -> float | None:
+def traffic_of(cls: str, W, sources: str = "zipf") -> float | None:
     """Per-step DRAM bytes of the kernel class from the committed ncu summary (profiles/traffic.json), if any."""
     p = REPO / "profiles" / "traffic.json"
-    if not p.exists():
+    if not p.exists() or W.get("graph") == "full":
         return None
     d = json.loads(p.read_text())
-    v = d.get(W["flags"], {}).get(cls)
+    v = d.get(W["flags"] + ("" if sources == "zipf" else "/" + sources), {}).get(cls)
     return float(v) if v is not None else None
 
 
@@ -416,7 +429,7 @@ def _cpu_model() -> str:
 def run_reference(a, W):
     """The reference's CPU implementation of the path, W warm-up + K timed steps of a bounded sample each."""
     from flyguy_b200 import synth
-    s, P = make_graph(W)
+    s, P = make_graph(W, a.sources)
     threads = os.cpu_count() or 1
     Bg = W["batch"]
     if W["flags"] == "train":

@@ -178,7 +178,8 @@ __global__ void k_to_neuron_major(const float* __restrict__ in, float* __restric
 // states - 128 samples - or fp32 - 64 samples) and its rows' plug columns and weights in shared memory, then every warp
 // computes rows from there: lane l owns the chunk's samples [NS*l, NS*l + NS).
 constexpr int kPlugThreads = 512;
-template <class T> struct PlugCfg { static constexpr int cols = sizeof(T) == 4 ? 32 : 64; };   // 66 KB staged
+// samples per CTA chunk: 2 per lane for fp32 states, 4 for 16-bit states (517 obs rows x 64 or 128 = 132 KB staged)
+template <class T> struct PlugCfg { static constexpr int cols = sizeof(T) == 4 ? 64 : 128; };
 __device__ __forceinline__ void cvt_store4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 __device__ __forceinline__ void cvt_store4(__nv_bfloat16* p, float4 v) {
     *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
@@ -279,6 +280,10 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
 #pragma unroll
             for (int k = 0; k < NS; ++k) a[k] = bias;
             if constexpr (FAN > 0) {
+                static_assert(NS % 2 == 0, "packed fp32x2 products need an even number of samples per lane");
+                float2 a2[NS / 2];
+#pragma unroll
+                for (int k = 0; k < NS / 2; ++k) a2[k] = make_float2(bias, bias);
 #pragma unroll
                 for (int j = 0; j < FAN; j += 4) {
                     const int4 cc = *reinterpret_cast<const int4*>(rc + i * F + j);
@@ -289,10 +294,14 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
                     for (int u = 0; u < 4; ++u) {
                         float v[NS];
                         lds_ns(xs + cs[u] * C + bl, v);
+                        const float2 w2 = make_float2(ws[u], ws[u]);
 #pragma unroll
-                        for (int k = 0; k < NS; ++k) a[k] = fmaf(ws[u], v[k], a[k]);
+                        for (int k = 0; k < NS / 2; ++k)      // the same fp32 FMA per sample, two per instruction
+                            a2[k] = __ffma2_rn(w2, make_float2(v[2 * k], v[2 * k + 1]), a2[k]);
                     }
                 }
+#pragma unroll
+                for (int k = 0; k < NS / 2; ++k) { a[2 * k] = a2[k].x; a[2 * k + 1] = a2[k].y; }
             } else {
                 const size_t e0 = (size_t)row * fan;
                 for (int j = 0; j < fan; ++j) {
@@ -305,8 +314,8 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
             }
             const size_t o = (size_t)row * ld + b0 + bl;
             if (SAVE_DRIVE) {
-                if constexpr (NS == 1) drive[o] = a[0];
-                else *reinterpret_cast<float2*>(drive + o) = make_float2(a[0], a[1]);
+                if constexpr (NS == 2) *reinterpret_cast<float2*>(drive + o) = make_float2(a[0], a[1]);
+                else *reinterpret_cast<float4*>(drive + o) = make_float4(a[0], a[1], a[2], a[3]);
             }
             const float g = __ldg(&rgain[row]), th = __ldg(&rthr[row]);
             float hv[NS];
@@ -356,16 +365,46 @@ __device__ __forceinline__ void st16(TO* o, const float* hv) {
 }
 
 // FULL: the warp's whole chunk lies inside the batch (ld a multiple of 64 V): no per-pair validity tests.
-// Resident CTAs per SM the register allocation is sized for: 6 (40 registers) for 16-bit sources, where more warps
-// in flight hide the gathers' latency (measured 7.9 vs 9.0 ms at batch 65,536); 4 for fp32 sources (no gain there).
-template <class TI> struct HopOcc { static constexpr int min_blocks = sizeof(TI) == 2 ? 6 : 4; };
+// UNR pairs per step: their records and 2 UNR 16-byte gathers are issued before any of their products, so each warp
+// keeps 2 UNR loads in flight (the gathers are L2-latency bound when sources are spread out). Resident CTAs per SM the
+// register allocation is sized for: HopOcc (more warps in flight also hide the gathers' latency).
+#ifndef FG_HOP_UNR
+#define FG_HOP_UNR 2
+#endif
+#ifndef FG_HOP_MINB16
+#define FG_HOP_MINB16 6
+#endif
+#ifndef FG_HOP_MINB32
+#define FG_HOP_MINB32 4
+#endif
+template <class TI> struct HopOcc { static constexpr int min_blocks = sizeof(TI) == 2 ? FG_HOP_MINB16 : FG_HOP_MINB32; };
+// the 16 raw bytes of a gather, unpacked to fp32 and multiplied into a (same FMA per sample as one at a time)
+template <class TI>
+__device__ __forceinline__ void fma16(const uint4& r, float2 w, float2 (&a)[Vec16<TI>::H]) {
+    if constexpr (sizeof(TI) == 4) {
+        a[0] = __ffma2_rn(w, make_float2(__uint_as_float(r.x), __uint_as_float(r.y)), a[0]);
+        a[1] = __ffma2_rn(w, make_float2(__uint_as_float(r.z), __uint_as_float(r.w)), a[1]);
+    } else {
+        const TI* tag = nullptr;
+        float2 v[4];
+        unpack2(tag, r.x, v[0]); unpack2(tag, r.y, v[1]); unpack2(tag, r.z, v[2]); unpack2(tag, r.w, v[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = __ffma2_rn(w, v[i], a[i]);
+    }
+}
+__device__ __forceinline__ uint4 ldg16(const char* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+// byte offset of row r of a [rows][ld] array: a 32 x 32 -> 64-bit product (row_bytes = ld * element size < 2^32), so the
+// address is one widening multiply-add instead of a 64-bit product
+__device__ __forceinline__ const char* row_at(const char* base, int r, unsigned row_bytes) {
+    return base + (unsigned long long)(unsigned)r * row_bytes;
+}
 template <class TI, class TO, bool FULL>
 __global__ void __launch_bounds__(kThreads, HopOcc<TI>::min_blocks) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
                                                       const int2* __restrict__ pairs, const TI* __restrict__ hp,
                                                       const float* __restrict__ rgain, const float* __restrict__ rthr,
                                                       const int* __restrict__ drow, const float* __restrict__ drive,
                                                       TO* __restrict__ h, int n_rows, int ld) {
-    constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H;
+    constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H, U = FG_HOP_UNR;
     const int slot = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (slot >= n_rows) return;
     const int t = __ldg(&sched[slot]);
@@ -376,45 +415,42 @@ __global__ void __launch_bounds__(kThreads, HopOcc<TI>::min_blocks) k_hop_fwd(co
 #pragma unroll
     for (int i = 0; i < H; ++i) { a0[i] = make_float2(0.f, 0.f); a1[i] = make_float2(0.f, 0.f); }
     const int e0 = __ldg(&pptr[t]), e1 = __ldg(&pptr[t + 1]);
-    const size_t row_bytes = (size_t)ld * sizeof(TI);
+    const unsigned row_bytes = (unsigned)ld * (unsigned)sizeof(TI);
     const char* base = reinterpret_cast<const char*>(hp + c0);
     constexpr int G1 = 32 * 16;                          // byte offset of the lane's second group
     int e = e0;
     if (g1) {
-        for (; e + 2 <= e1; e += 2) {
-            const int2 p = __ldg(&pairs[e]), q = __ldg(&pairs[e + 1]);
-            const char* ap = base + (unsigned)p.x * row_bytes;
-            const char* aq = base + (unsigned)q.x * row_bytes;
-            float2 v0[H], v1[H], u0[H], u1[H];
-            ld16<TI>(reinterpret_cast<const TI*>(ap), v0);
-            ld16<TI>(reinterpret_cast<const TI*>(ap + G1), v1);
-            ld16<TI>(reinterpret_cast<const TI*>(aq), u0);
-            ld16<TI>(reinterpret_cast<const TI*>(aq + G1), u1);
-            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
-            const float2 wq = make_float2(__int_as_float(q.y), __int_as_float(q.y));
+        for (; e + U <= e1; e += U) {
+            int2 p[U];
+            uint4 r0[U], r1[U];
 #pragma unroll
-            for (int i = 0; i < H; ++i) { a0[i] = __ffma2_rn(wp, v0[i], a0[i]); a1[i] = __ffma2_rn(wp, v1[i], a1[i]); }
+            for (int u = 0; u < U; ++u) p[u] = __ldg(&pairs[e + u]);
 #pragma unroll
-            for (int i = 0; i < H; ++i) { a0[i] = __ffma2_rn(wq, u0[i], a0[i]); a1[i] = __ffma2_rn(wq, u1[i], a1[i]); }
+            for (int u = 0; u < U; ++u) {
+                const char* ap = row_at(base, p[u].x, row_bytes);
+                r0[u] = ldg16(ap);
+                r1[u] = ldg16(ap + G1);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const float2 w = make_float2(__int_as_float(p[u].y), __int_as_float(p[u].y));
+                fma16<TI>(r0[u], w, a0);
+                fma16<TI>(r1[u], w, a1);
+            }
         }
-        if (e < e1) {
+        for (; e < e1; ++e) {
             const int2 p = __ldg(&pairs[e]);
-            const char* ap = base + (unsigned)p.x * row_bytes;
-            float2 v0[H], v1[H];
-            ld16<TI>(reinterpret_cast<const TI*>(ap), v0);
-            ld16<TI>(reinterpret_cast<const TI*>(ap + G1), v1);
-            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
-#pragma unroll
-            for (int i = 0; i < H; ++i) { a0[i] = __ffma2_rn(wp, v0[i], a0[i]); a1[i] = __ffma2_rn(wp, v1[i], a1[i]); }
+            const char* ap = row_at(base, p.x, row_bytes);
+            const uint4 r0 = ldg16(ap), r1 = ldg16(ap + G1);
+            const float2 w = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+            fma16<TI>(r0, w, a0);
+            fma16<TI>(r1, w, a1);
         }
     } else {                                              // only the first group is inside the batch
         for (; e < e1; ++e) {
             const int2 p = __ldg(&pairs[e]);
-            float2 v0[H];
-            ld16<TI>(reinterpret_cast<const TI*>(base + (unsigned)p.x * row_bytes), v0);
-            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
-#pragma unroll
-            for (int i = 0; i < H; ++i) a0[i] = __ffma2_rn(wp, v0[i], a0[i]);
+            const uint4 r0 = ldg16(row_at(base, p.x, row_bytes));
+            fma16<TI>(r0, make_float2(__int_as_float(p.y), __int_as_float(p.y)), a0);
         }
     }
     if (drow) {
@@ -691,7 +727,7 @@ __global__ void __launch_bounds__(128) k_out_bwd_h(const float* __restrict__ ow,
 }
 
 // ---------------------------------------------------------------- backward: through the neurons
-// one CTA per row: g = gh * [h > 0]; gz = g * gain -> gz; gain grad += sum g*z with z = (h + thr) / gain (exact where
+// one CTA per listed row of the top layer: g = gh * [h > 0]; gz = g * gain -> gz; gain grad += sum g*z with z = (h + thr) / gain (exact where
 // h > 0, the only place it counts); theta grad += sum -g * sigmoid(theta); gdrive[drow] += gz. Returns through
 // `live[row]` whether any g was non-zero (rows that never fire are skipped by the weight gradient).
 template <class T>
@@ -700,10 +736,10 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
                                                       const float* __restrict__ rgain, const float* __restrict__ rthr,
                                                       const float* __restrict__ rsig, float* __restrict__ gz,
                                                       float* __restrict__ ggain, float* __restrict__ gtheta,
-                                                      float* __restrict__ gdrive, int* __restrict__ live, int B,
-                                                      int ld) {
+                                                      float* __restrict__ gdrive, int* __restrict__ live,
+                                                      const int* __restrict__ rows, int B, int ld) {
     __shared__ float red[3 * kWarps];
-    const int t = blockIdx.x;
+    const int t = __ldg(&rows[blockIdx.x]);             // a row whose gradient can be non-zero (an output-plug column)
     const float gn = rgain[t], th = rthr[t];
     const float inv_g = gn != 0.f ? 1.f / gn : 0.f;
     const int d = drow ? drow[t] : -1;
@@ -873,14 +909,14 @@ __global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__
     // lanes past the batch stay to the end (the epilogue reduces over the warp) but load and store nothing
     const bool v0 = FULL || c0 < ld, v1 = FULL || c1 < ld;
     float2 a0[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)}, a1[2] = {a0[0], a0[1]};
-    const size_t row_bytes = (size_t)ld * 4;
+    const unsigned row_bytes = (unsigned)ld * 4u;
     const char* base = reinterpret_cast<const char*>(gz + (v0 ? c0 : 0));
     if (v0 && v1) {
         int e = sg.y;
         for (; e + 2 <= sg.z; e += 2) {
             const int2 p = __ldg(&tpairs[e]), q = __ldg(&tpairs[e + 1]);
-            const char* ap = base + (unsigned)p.x * row_bytes;
-            const char* aq = base + (unsigned)q.x * row_bytes;
+            const char* ap = row_at(base, p.x, row_bytes);
+            const char* aq = row_at(base, q.x, row_bytes);
             float2 x0[2], x1[2], y0[2], y1[2];
             ld16<float>(reinterpret_cast<const float*>(ap), x0);
             ld16<float>(reinterpret_cast<const float*>(ap + 512), x1);
@@ -895,7 +931,7 @@ __global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__
         }
         if (e < sg.z) {
             const int2 p = __ldg(&tpairs[e]);
-            const char* ap = base + (unsigned)p.x * row_bytes;
+            const char* ap = row_at(base, p.x, row_bytes);
             float2 x0[2], x1[2];
             ld16<float>(reinterpret_cast<const float*>(ap), x0);
             ld16<float>(reinterpret_cast<const float*>(ap + 512), x1);
@@ -907,7 +943,7 @@ __global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__
         for (int e = sg.y; e < sg.z; ++e) {
             const int2 p = __ldg(&tpairs[e]);
             float2 x0[2];
-            ld16<float>(reinterpret_cast<const float*>(base + (unsigned)p.x * row_bytes), x0);
+            ld16<float>(reinterpret_cast<const float*>(row_at(base, p.x, row_bytes)), x0);
             const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
             a0[0] = __ffma2_rn(wp, x0[0], a0[0]); a0[1] = __ffma2_rn(wp, x0[1], a0[1]);
         }

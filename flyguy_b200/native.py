@@ -16,7 +16,7 @@ from .netfile import Structure, read_net, write_net
 
 PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("FLYGUY_B200_LIB", PKG / "libflyguy_b200.so"))   # (override: a variant build)
-FG_ACT_BF16, FG_INFER_ONLY, FG_ACT_F16 = 1, 2, 4
+FG_ACT_BF16, FG_INFER_ONLY, FG_ACT_F16, FG_HUB_TC = 1, 2, 4, 8
 _lib = None
 
 # the exported symbols and their ctypes signatures: (restype, argtypes)

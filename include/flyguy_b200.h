@@ -71,7 +71,11 @@ void fc_sync(void* h);
 #define FG_ACT_BF16 1     /* states stored as bf16 (fp32 accumulation, fp32 weights); forward only */
 #define FG_INFER_ONLY 2   /* no gradient / optimiser buffers: fc_backward and fc_step fail */
 #define FG_ACT_F16 4      /* states stored as IEEE fp16 (the reference's 16-bit "cuda16" states); forward only */
-/* In both 16-bit modes the last layer (the descending neurons the output plug reads) stays fp32. */
+#define FG_HUB_TC 8       /* 16-bit states: hops with hub sources use the tensor-core hop (opt-in, see below) */
+/* In both 16-bit modes the last layer (the descending neurons the output plug reads) stays fp32. With FG_HUB_TC, 16-bit
+   states and a batch that is a multiple of 256, a hop whose sources include hubs (rows read by many of the hop's rows)
+   sums the hub pairs with tensor cores (weights as 16-bit hi + lo terms, fp32 accumulation) and the rest on CUDA
+   cores. Without it every hop runs on CUDA cores, which is faster on the graphs measured so far. */
 
 /* fc_create with flags (FG_ACT_BF16 and FG_ACT_F16 imply FG_INFER_ONLY). */
 void* fg_create(const char* net_path, int max_batch, int flags);

@@ -215,6 +215,45 @@ def test_synthetic_16bit_batch65536(flygraph, cuda):
     assert agree["bf16"] >= 0.99
 
 
+@pytest.mark.parametrize("flag", ["bf16", "f16"])
+def test_tensor_core_hops_match_cuda_core_hops(flygraph, flag, cuda):
+    """FG_HUB_TC, 16-bit states, a batch that is a multiple of 256: a hop whose sources include hubs sums the hub pairs
+    with tensor cores (tcgen05, weights as hi + lo 16-bit terms, fp32 accumulation in TMEM) and its other pairs on CUDA
+    cores; the default handle sums every pair on CUDA cores. Every layer agrees within a few 16-bit roundings, the
+    logits within the 16-bit tolerance and against the oracle, and no bounded wait expired."""
+    s, P = flygraph
+    B = 8192
+    f = native.FG_ACT_BF16 if flag == "bf16" else native.FG_ACT_F16
+    obs, _ = synth.make_batch(B, seed=21)
+    x = _t(obs)
+    h_tc = _handle(s, P, B, f | native.FG_HUB_TC)
+    h_sm = _handle(s, P, B, f)
+    h_tc.forward(x[:256])                         # the weight folds run once, at the first forward
+    h_sm.forward(x[:256])
+    n0 = h_tc.launches()
+    got_tc = h_tc.forward(x).cpu().numpy()
+    n_tc = h_tc.launches() - n0
+    h_tc.sync()                                   # raises if a wait of the tensor-core hop expired
+    n0 = h_sm.launches()
+    got_sm = h_sm.forward(x).cpu().numpy()
+    n_sm = h_sm.launches() - n0
+    assert n_tc > n_sm                            # the hub gathers ran: the tensor-core path was taken
+    for k in range(1, len(s["sizes"])):
+        a, b = h_tc.layer(k, B).cpu().numpy(), h_sm.layer(k, B).cpu().numpy()
+        assert rel(a, b) < (1e-2 if flag == "bf16" else 3e-3), k
+    assert rel(got_tc, got_sm) < TOL_BF16
+    idx = _spread(B, 48)
+    want = Oracle(s).forward(P, obs[idx])
+    assert rel(got_tc[idx], want) < TOL_BF16
+    assert np.mean(got_tc.argmax(1) == got_sm.argmax(1)) >= 0.99
+    # a batch that is not a multiple of 256 runs every hop on CUDA cores (the hub handle's pairs in its own order)
+    Bs = B - 32
+    n0 = h_tc.launches()
+    a = h_tc.forward(x[:Bs]).cpu().numpy()
+    assert h_tc.launches() - n0 == n_sm
+    assert rel(a, h_sm.forward(x[:Bs]).cpu().numpy()) < TOL_BF16
+
+
 @pytest.mark.parametrize("case", CASES)
 def test_forward_f16_matches_reference(case, cuda):
     s, P, d = load_case(case)
