@@ -559,6 +559,9 @@ int plug_smem(const Core& c) {
 template <class T, bool SAVE>
 void plug_limit(const Core& c) {
     const int smem = plug_smem<T>(c);
+    if (smem > 232448)
+        throw Err("input plug: obs_dim " + std::to_string(c.obs_dim) + " with fan " + std::to_string(c.fan) +
+                  " needs " + std::to_string(smem) + " bytes of shared memory per CTA (at most 232448)");
     CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 12>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
