@@ -748,11 +748,13 @@ void backward(Core& c, int B) {
     CK(cudaMemsetAsync(c.gdrive, 0, (size_t)c.n_s * B * 4, c.st));
     const Hop& top = c.hop.back();
     const float* hK = (const float*)top.d_h;
-    const int splits = std::max(1, std::min(c.out_splits, (B + 1023) / 1024));
+    // weight gradient: 64-column tiles x batch slices, about two waves of CTAs (slices of at least 512 samples)
+    const int wtiles = (c.n_dn + 1 + kOutB - 1) / kOutB;
+    const int splits = std::max(1, std::min({c.out_splits, (2 * c.n_sm + wtiles - 1) / wtiles, B / 512}));
     const int split_len = ((B + splits - 1) / splits + 31) / 32 * 32;
     launch(c, K_OUT_BWD, [&]() {
-        k_out_bwd_w<float><<<dim3((c.n_dn + 1 + 31) / 32, (c.n_act + 31) / 32, splits), 256, 0, c.st>>>(
-            c.dl, hK, c.d_dn, c.part, c.n_act, c.n_dn, B, B, split_len);
+        k_out_bwd_wt<float><<<dim3(wtiles, splits), 256, 0, c.st>>>(c.dl, hK, c.d_dn, c.part, c.n_act, c.n_dn, B,
+                                                                    split_len, B);
     });
     launch(c, K_OUT_BWD, [&]() {
         k_out_bwd_reduce<<<blocks((long long)c.n_act * (c.n_dn + 1)), 256, 0, c.st>>>(c.part, c.G + c.off[5],
@@ -762,10 +764,9 @@ void backward(Core& c, int B) {
     float* gz = c.gz_a;                      // gz of the layer being processed
     float* nxt = c.gz_b;                     // gz (or gh0) of the layer below
     // only the output plug's columns of the top layer get a gradient; the other rows of gh / gz are never read
-    const int jper = 64;
     launch(c, K_OUT_BWD, [&]() {
-        k_out_bwd_h<<<dim3((B + 127) / 128, (c.n_dn + jper - 1) / jper), 128, jper * c.n_act * 4, c.st>>>(
-            W + c.off[5], c.dl, c.d_dn, nxt, c.n_act, c.n_dn, B, B, jper);
+        k_out_bwd_ht<<<dim3((B + kOutB - 1) / kOutB, (c.n_dn + kOutA - 1) / kOutA), 256, 0, c.st>>>(
+            W + c.off[5], c.dl, c.d_dn, nxt, c.n_act, c.n_dn, B, B);
     });
     if (top.n_live_dst)
     launch(c, K_ACT_BWD, [&]() {

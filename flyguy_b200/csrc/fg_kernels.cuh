@@ -652,44 +652,112 @@ __global__ void k_loss_stats(const float* __restrict__ kl_s, const float* __rest
 }
 
 // ---------------------------------------------------------------- backward: output plug
-// split-K partial sums over the batch: part[s][a][j] = sum_{b in split s} dl[a,b] * hK[dn[j], b] for j < n_dn and
-// sum_b dl[a,b] for j == n_dn. A CTA owns a 32x32 (action, column) tile and one batch split.
+// Output-plug weight gradient as a register-blocked product: part[s][a][j] = sum over slice s of the batch of
+// dl[a, b] * hK[dn[j], b] (column j = n_dn is the bias: hK = 1). A CTA owns all 96 (padded) actions x 64 columns and one
+// batch slice (blockIdx.y); each thread 6 actions x 4 columns. Both operands are read along the batch (a warp reads
+// 32 consecutive samples of one row) and stored transposed, 32 samples at a time ([sample][action],
+// [sample][column]); the padded row strides (98, 68 floats) keep the transposing stores at 2- and 4-way bank conflicts
+// and the products' float2 / float4 reads aligned.
+constexpr int kSA = 98, kSH = 68;
 template <class T>
-__global__ void __launch_bounds__(256) k_out_bwd_w(const float* __restrict__ dl, const T* __restrict__ hK,
-                                                   const int* __restrict__ dn, float* __restrict__ part, int n_act,
-                                                   int n_dn, int B, int ld, int split_len) {
-    __shared__ float sd[32][33], sh[32][33];
-    const int a0 = blockIdx.y * 32, j0 = blockIdx.x * 32, s = blockIdx.z;
+__global__ void __launch_bounds__(256) k_out_bwd_wt(const float* __restrict__ dl, const T* __restrict__ hK,
+                                                    const int* __restrict__ dn, float* __restrict__ part, int n_act,
+                                                    int n_dn, int ld, int split_len, int B) {
+    __shared__ __align__(16) float As[kOutK * kSA];
+    __shared__ __align__(16) float Hs[kOutK * kSH];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4, lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    const int j0 = blockIdx.x * kOutB, s = blockIdx.y;
     const int b_lo = s * split_len, b_hi = min(B, b_lo + split_len);
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 8 rows of threads, each does 4 actions
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int b0 = b_lo; b0 < b_hi; b0 += 32) {
+    const int n_col = n_dn + 1;
+    float acc[6][4];
+#pragma unroll
+    for (int i = 0; i < 6; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int b0 = b_lo; b0 < b_hi; b0 += kOutK) {
         __syncthreads();
-        for (int r = ty; r < 32; r += 8) {
-            int a = a0 + r, j = j0 + r, b = b0 + tx;
-            sd[r][tx] = (a < n_act && b < b_hi) ? dl[(size_t)a * ld + b] : 0.f;
-            float hv = 0.f;
-            if (b < b_hi) {
-                if (j < n_dn) hv = ld1(hK + (size_t)__ldg(&dn[j]) * ld + b);
-                else if (j == n_dn) hv = 1.f;
-            }
-            sh[r][tx] = hv;
+        for (int a = wp; a < kOutA; a += 8)                 // warp per action row, lane per sample
+            As[lane * kSA + a] = a < n_act ? __ldg(&dl[(size_t)a * ld + b0 + lane]) : 0.f;
+        for (int jj = wp; jj < kOutB; jj += 8) {             // warp per column, lane per sample
+            const int j = j0 + jj;
+            float v = 0.f;
+            if (j < n_dn) v = ld1(hK + (size_t)__ldg(&dn[j]) * ld + b0 + lane);
+            else if (j == n_dn) v = 1.f;
+            Hs[lane * kSH + jj] = v;
         }
         __syncthreads();
 #pragma unroll 8
-        for (int k = 0; k < 32; ++k) {
-            const float hv = sh[tx][k];
+        for (int k = 0; k < kOutK; ++k) {
+            const float4 h = *reinterpret_cast<const float4*>(&Hs[k * kSH + tx * 4]);
+            const float2 w01 = *reinterpret_cast<const float2*>(&As[k * kSA + ty * 6]);
+            const float2 w23 = *reinterpret_cast<const float2*>(&As[k * kSA + ty * 6 + 2]);
+            const float2 w45 = *reinterpret_cast<const float2*>(&As[k * kSA + ty * 6 + 4]);
+            const float hv[4] = {h.x, h.y, h.z, h.w};
+            const float wv[6] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc[i] = fmaf(sd[ty + 8 * i][k], hv, acc[i]);
+            for (int i = 0; i < 6; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wv[i], hv[j], acc[i][j]);
         }
     }
-    const int j = j0 + tx, n_col = n_dn + 1;
-    if (j < n_col) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            int a = a0 + ty + 8 * i;
-            if (a < n_act) part[((size_t)s * n_act + a) * n_col + j] = acc[i];
+    for (int i = 0; i < 6; ++i) {
+        const int a = ty * 6 + i;
+        if (a >= n_act) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int c = j0 + tx * 4 + j;
+            if (c < n_col) part[((size_t)s * n_act + a) * n_col + c] = acc[i][j];
         }
+    }
+}
+// gh[dn[j], b] = sum_a out_w[a, j] * dl[a, b] as a register-blocked product: a CTA owns 96 output-plug columns x 64
+// samples, each thread 6 columns x 4 samples; out_w rows and dl rows are staged 32 actions at a time.
+__global__ void __launch_bounds__(256) k_out_bwd_ht(const float* __restrict__ ow, const float* __restrict__ dl,
+                                                    const int* __restrict__ dn, float* __restrict__ gh, int n_act,
+                                                    int n_dn, int B, int ld) {
+    __shared__ __align__(16) float As[kOutK][kOutA];      // [action][column]
+    __shared__ __align__(16) float Bs[kOutK][kOutB];      // [action][sample]
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int b0 = blockIdx.x * kOutB, j0 = blockIdx.y * kOutA;
+    float acc[6][4];
+#pragma unroll
+    for (int i = 0; i < 6; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int a0 = 0; a0 < n_act; a0 += kOutK) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < kOutK * kOutA; i += 256) {
+            const int k = i / kOutA, m = i - k * kOutA, a = a0 + k, j = j0 + m;
+            As[k][m] = (a < n_act && j < n_dn) ? __ldg(&ow[(size_t)a * n_dn + j]) : 0.f;
+        }
+        for (int i = threadIdx.x; i < kOutK * kOutB; i += 256) {
+            const int k = i / kOutB, n = i - k * kOutB, a = a0 + k, b = b0 + n;
+            Bs[k][n] = (a < n_act && b < B) ? __ldg(&dl[(size_t)a * ld + b]) : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < kOutK; ++k) {
+            const float4 d = *reinterpret_cast<const float4*>(&Bs[k][tx * 4]);
+            const float2 w01 = *reinterpret_cast<const float2*>(&As[k][ty * 6]);
+            const float2 w23 = *reinterpret_cast<const float2*>(&As[k][ty * 6 + 2]);
+            const float2 w45 = *reinterpret_cast<const float2*>(&As[k][ty * 6 + 4]);
+            const float dv[4] = {d.x, d.y, d.z, d.w};
+            const float wv[6] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y};
+#pragma unroll
+            for (int i = 0; i < 6; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wv[i], dv[j], acc[i][j]);
+        }
+    }
+    const int b = b0 + tx * 4;
+    if (b >= B) return;
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+        const int j = j0 + ty * 6 + i;
+        if (j < n_dn)
+            *reinterpret_cast<float4*>(gh + (size_t)__ldg(&dn[j]) * ld + b) =
+                make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
     }
 }
 // G_out_w[a*n_dn + j] += sum_s part[s][a][j]; G_out_b[a] += sum_s part[s][a][n_dn]
@@ -703,31 +771,7 @@ __global__ void k_out_bwd_reduce(const float* __restrict__ part, float* __restri
     int a = i / n_col, j = i - a * n_col;
     if (j < n_dn) gow[(size_t)a * n_dn + j] += s; else gob[a] += s;
 }
-// gh[dn[j], b] = sum_a out_w[a, j] * dl[a, b]: a thread per sample holds dl[., b] in registers (n_act <= 96)
-constexpr int kMaxAct = 96;
-__global__ void __launch_bounds__(128) k_out_bwd_h(const float* __restrict__ ow, const float* __restrict__ dl,
-                                                   const int* __restrict__ dn, float* __restrict__ gh, int n_act,
-                                                   int n_dn, int B, int ld, int j_per_cta) {
-    extern __shared__ float w_s[];                        // [j_per_cta][n_act]
-    const int b = blockIdx.x * 128 + threadIdx.x, jb = blockIdx.y * j_per_cta;
-    const int nj = min(j_per_cta, n_dn - jb);
-    for (int i = threadIdx.x; i < nj * n_act; i += blockDim.x) {
-        int jj = i / n_act, a = i - jj * n_act;
-        w_s[i] = __ldg(&ow[(size_t)a * n_dn + jb + jj]);
-    }
-    __syncthreads();
-    if (b >= B) return;
-    float d[kMaxAct];
-#pragma unroll
-    for (int a = 0; a < kMaxAct; ++a) d[a] = a < n_act ? dl[(size_t)a * ld + b] : 0.f;
-    for (int jj = 0; jj < nj; ++jj) {
-        const float* w = w_s + jj * n_act;
-        float s = 0.f;
-#pragma unroll
-        for (int a = 0; a < kMaxAct; ++a) if (a < n_act) s = fmaf(w[a], d[a], s);
-        gh[(size_t)__ldg(&dn[jb + jj]) * ld + b] = s;
-    }
-}
+constexpr int kMaxAct = 96;                // actions at most (the output plug's tiles pad to 96)
 
 // ---------------------------------------------------------------- backward: through the neurons
 // one CTA per listed row of the top layer: g = gh * [h > 0]; gz = g * gain -> gz; gain grad += sum g*z with z = (h + thr) / gain (exact where
