@@ -401,17 +401,18 @@ __device__ __forceinline__ uint4 ldg16(const char* p) { return __ldg(reinterpret
 __device__ __forceinline__ const char* row_at(const char* base, int r, unsigned row_bytes) {
     return base + (unsigned long long)(unsigned)r * row_bytes;
 }
+// one warp's work: row `slot` of the schedule x sample chunk `chunk`
 template <class TI, class TO, bool FULL>
-__global__ void __launch_bounds__(kThreads, HopOcc<TI>::min_blocks) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
-                                                      const int2* __restrict__ pairs, const TI* __restrict__ hp,
-                                                      const float* __restrict__ rgain, const float* __restrict__ rthr,
-                                                      const int* __restrict__ drow, const float* __restrict__ drive,
-                                                      TO* __restrict__ h, int n_rows, int ld) {
+__device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restrict__ sched,
+                                        const int* __restrict__ pptr, const int2* __restrict__ pairs,
+                                        const TI* __restrict__ hp, const float* __restrict__ rgain,
+                                        const float* __restrict__ rthr, const int* __restrict__ drow,
+                                        const float* __restrict__ drive, TO* __restrict__ h, int n_rows, int ld) {
     constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H, U = FG_HOP_UNR;
-    const int slot = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31;
     if (slot >= n_rows) return;
     const int t = __ldg(&sched[slot]);
-    const int c0 = blockIdx.y * 64 * V + lane * V, c1 = c0 + 32 * V;     // the lane's two groups
+    const int c0 = chunk * 64 * V + lane * V, c1 = c0 + 32 * V;         // the lane's two groups
     if (!FULL && c0 >= ld) return;
     const bool g1 = FULL || c1 < ld;
     float2 a0[H], a1[H];
@@ -490,6 +491,15 @@ __global__ void __launch_bounds__(kThreads, HopOcc<TI>::min_blocks) k_hop_fwd(co
     }
 }
 
+template <class TI, class TO, bool FULL>
+__global__ void __launch_bounds__(kThreads, HopOcc<TI>::min_blocks) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
+                                                      const int2* __restrict__ pairs, const TI* __restrict__ hp,
+                                                      const float* __restrict__ rgain, const float* __restrict__ rthr,
+                                                      const int* __restrict__ drow, const float* __restrict__ drive,
+                                                      TO* __restrict__ h, int n_rows, int ld) {
+    hop_row<TI, TO, FULL>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, sched, pptr, pairs, hp, rgain, rthr,
+                          drow, drive, h, n_rows, ld);
+}
 // output plug: logits[a,b] = out_b[a] + sum_j out_w[a,j] * hK[dn[j], b], a register-blocked product: a CTA owns
 // 96 actions x 64 samples and one slice of the dn columns (split K: blockIdx.y of gridDim.y), each thread 6 actions x
 // 4 samples; owT is out_w transposed and padded to 96 actions ([n_dn][96], refreshed with the weights), staged with hK
