@@ -1110,8 +1110,16 @@ int fg_forward_host(void* h, const float* obs_host, int B, float* logits_host, i
             CK(cudaStreamCreateWithFlags(&c.h2d, cudaStreamNonBlocking));
             CK(cudaStreamCreateWithFlags(&c.d2h, cudaStreamNonBlocking));
         }
-        const int nch = B >= 4 * 256 ? 4 : 1;
-        const int chunk = ((B + nch - 1) / nch + 255) / 256 * 256;
+        // Pieces of about 16,384 samples (multiples of 256, so every sample's logits are the bits the device forward
+        // gives); the first piece's upload and the last piece's read-back are the only copies not hidden behind compute.
+        // Measured at batch 65,536: pieces of 16,384 beat pieces of 2,048 / 4,096 / 8,192 and small edge pieces (the
+        // forward's kernels lose more at small batches than the shorter exposed copies save); batch 4,096: one piece.
+        std::vector<std::pair<int, int>> pieces;           // (first sample, count)
+        {
+            const int n = std::max(1, B / 16384);
+            const int step = ((B + n - 1) / n + 255) / 256 * 256;
+            for (int b0 = 0; b0 < B; b0 += step) pieces.emplace_back(b0, std::min(step, B - b0));
+        }
         std::vector<cudaEvent_t> ev;
         auto event = [&]() {
             cudaEvent_t e;
@@ -1124,17 +1132,16 @@ int fg_forward_host(void* h, const float* obs_host, int B, float* logits_host, i
             CK(cudaEventRecord(start, c.st));          // the copies start after the handle's earlier work
             CK(cudaStreamWaitEvent(c.h2d, start, 0));
             std::vector<cudaEvent_t> in_done, out_done;
-            for (int b0 = 0; b0 < B; b0 += chunk) {
-                const int n = std::min(chunk, B - b0);
+            for (const auto& pc : pieces) {
+                const int b0 = pc.first, n = pc.second;
                 CK(cudaMemcpyAsync(c.obs_dev + (size_t)b0 * c.obs_dim, obs_host + (size_t)b0 * c.obs_dim,
                                    (size_t)n * c.obs_dim * 4, cudaMemcpyHostToDevice, c.h2d));
                 cudaEvent_t e = event();
                 CK(cudaEventRecord(e, c.h2d));
                 in_done.push_back(e);
             }
-            int i = 0;
-            for (int b0 = 0; b0 < B; b0 += chunk, ++i) {
-                const int n = std::min(chunk, B - b0);
+            for (size_t i = 0; i < pieces.size(); ++i) {
+                const int b0 = pieces[i].first, n = pieces[i].second;
                 CK(cudaStreamWaitEvent(c.st, in_done[i], 0));
                 forward(c, c.obs_dev + (size_t)b0 * c.obs_dim, n, c.logits_dev + (size_t)b0 * c.n_act, ema, false);
                 cudaEvent_t e = event();

@@ -548,9 +548,12 @@ __global__ void __launch_bounds__(256) k_out_fwd(const float* __restrict__ owT, 
             const float hv[4] = {h.x, h.y, h.z, h.w};
             const float wv[6] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y};
 #pragma unroll
-            for (int i = 0; i < 6; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wv[i], hv[j], acc[i][j]);
+            for (int i = 0; i < 6; ++i) {                         // two packed fp32x2 FMAs (same rounding)
+                const float2 w2 = make_float2(wv[i], wv[i]);
+                const float2 p0 = __ffma2_rn(w2, make_float2(hv[0], hv[1]), make_float2(acc[i][0], acc[i][1]));
+                const float2 p1 = __ffma2_rn(w2, make_float2(hv[2], hv[3]), make_float2(acc[i][2], acc[i][3]));
+                acc[i][0] = p0.x; acc[i][1] = p0.y; acc[i][2] = p1.x; acc[i][3] = p1.y;
+            }
         }
     }
     if (slices > 1) {                                      // partial slab of this slice: part[slice][a][ld]
@@ -705,9 +708,12 @@ __global__ void __launch_bounds__(256) k_out_bwd_wt(const float* __restrict__ dl
             const float hv[4] = {h.x, h.y, h.z, h.w};
             const float wv[6] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y};
 #pragma unroll
-            for (int i = 0; i < 6; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wv[i], hv[j], acc[i][j]);
+            for (int i = 0; i < 6; ++i) {                         // two packed fp32x2 FMAs (same rounding)
+                const float2 w2 = make_float2(wv[i], wv[i]);
+                const float2 p0 = __ffma2_rn(w2, make_float2(hv[0], hv[1]), make_float2(acc[i][0], acc[i][1]));
+                const float2 p1 = __ffma2_rn(w2, make_float2(hv[2], hv[3]), make_float2(acc[i][2], acc[i][3]));
+                acc[i][0] = p0.x; acc[i][1] = p0.y; acc[i][2] = p1.x; acc[i][3] = p1.y;
+            }
         }
     }
 #pragma unroll
@@ -755,9 +761,12 @@ __global__ void __launch_bounds__(256) k_out_bwd_ht(const float* __restrict__ ow
             const float dv[4] = {d.x, d.y, d.z, d.w};
             const float wv[6] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y};
 #pragma unroll
-            for (int i = 0; i < 6; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(wv[i], dv[j], acc[i][j]);
+            for (int i = 0; i < 6; ++i) {                         // two packed fp32x2 FMAs (same rounding)
+                const float2 w2 = make_float2(wv[i], wv[i]);
+                const float2 p0 = __ffma2_rn(w2, make_float2(dv[0], dv[1]), make_float2(acc[i][0], acc[i][1]));
+                const float2 p1 = __ffma2_rn(w2, make_float2(dv[2], dv[3]), make_float2(acc[i][2], acc[i][3]));
+                acc[i][0] = p0.x; acc[i][1] = p0.y; acc[i][2] = p1.x; acc[i][3] = p1.y;
+            }
         }
     }
     const int b = b0 + tx * 4;

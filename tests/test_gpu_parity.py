@@ -314,10 +314,12 @@ def test_errors_leave_the_handle_usable(cuda):
         hi.backward(_t(d["dlogits"]))
 
 
-def test_host_buffer_forward_matches_device_forward(flygraph, cuda):
+@pytest.mark.parametrize("B", [8192, 33024])
+def test_host_buffer_forward_matches_device_forward(flygraph, B, cuda):
+    """fg_forward_host (pinned host buffers, copies overlapped with compute; 33,024 runs as two pieces of 16,640 and
+    16,384 samples) gives the device forward's logits bit for bit."""
     import torch
     s, P = flygraph
-    B = 8192
     obs, _ = synth.make_batch(B, seed=14)
     h = _handle(s, P, B, native.FG_ACT_BF16)
     dev = h.forward(_t(obs)).cpu()
