@@ -18,8 +18,8 @@ HERE = Path(__file__).resolve().parent
 PKG = HERE.parent
 REPO = PKG.parent
 LIB = PKG / "libflyguy_b200.so"
-SOURCES = [HERE / "fg_core.cu", HERE / "fg_noalloc.cu"]
-DEPS = SOURCES + [HERE / "fg_kernels.cuh", REPO / "include" / "flyguy_b200.h"]
+SOURCES = [HERE / "fg_core.cu", HERE / "fg_noalloc.cu", HERE / "fg_hopop.cu"]
+DEPS = SOURCES + [HERE / "fg_kernels.cuh", HERE / "fg_tc.cuh", REPO / "include" / "flyguy_b200.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -50,6 +50,9 @@ SIGNATURES = {
     "fg_timing_read": (_ci, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_cll), _ci]),
     "fg_kl_loss_noalloc": (_ci, [_vp, _vp, _ci, _ci, _cf, _vp, _vp, _vp]),
     "fg_noalloc_last_error": (ctypes.c_char_p, []),
+    "fg_hop_fwd": (_ci, [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _vp, _vp]),
+    "fg_hop_bwd": (_ci, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _vp, _vp, _vp]),
+    "fg_hop_last_error": (ctypes.c_char_p, []),
 }
 KERNEL_CLASSES = ("layout", "fold", "plug_fwd", "hop_fwd", "out_fwd", "loss", "out_bwd", "act_bwd", "sddmm",
                   "hop_bwd_t", "plug_bwd", "adam", "norm")

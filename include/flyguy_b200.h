@@ -137,6 +137,24 @@ int fg_kl_loss_noalloc(const float* logits, const float* teacher, int B, int n_a
                        float* stats, void* stream);
 const char* fg_noalloc_last_error(void);
 
+/* ---- the per-hop operator (replaces the reference's HopCuda, flyguy/fly_cuda.py:78-115) ------------------------
+ * Handle-free, on the caller's device buffers and stream (NULL = the legacy default stream); states are
+ * [neurons, batch] fp32, 16-byte aligned, batch a multiple of 32; CSR index arrays as the reference's FlyActor buffers
+ * (crow/tcrow/tperm int64, col/tcol int32). Return 0, or -1 with the reason in fg_hop_last_error(). */
+
+/* HopCuda.forward (fly_cuda.py:83-92, kernels spmm_f / spmm_h at 25-39): out[t, b] = sum over the edges e of row t of
+ * w[e] * h[col[e], b]. half != 0: h read rounded to fp16 (h.half()), sums in fp32. */
+int fg_hop_fwd(const float* w, const float* h, const long long* crow, const int* col, int n_rows, int n_src, int B,
+               int half, float* out, void* stream);
+/* HopCuda.backward (fly_cuda.py:94-115, kernels sddmm_f / sddmm_h at 44-54): gw[e] = sum_b gz[t(e), b] * h[col[e], b]
+ * (gw NULL: skipped); gh[s, b] = sum over the by-source edges i of s of w[tperm[i]] * gz[tcol[i], b] (gh NULL:
+ * skipped). half != 0: gz / max|gz| and h read rounded to fp16, sums in fp32, results times max|gz| (fly_cuda.py:100-113). */
+int fg_hop_bwd(const float* w, const float* h, const float* gz, const long long* crow, const int* col,
+               const long long* tcrow, const int* tcol, const long long* tperm, int n_rows, int n_src, int B,
+               int half, float* gw, float* gh, void* stream);
+/* Why the calling thread's last fg_hop_* call failed ("" after a success). */
+const char* fg_hop_last_error(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -72,3 +72,15 @@ def test_null_handle_calls_do_not_crash():
     L = native.lib()
     L.fc_zero_grad(None)
     assert L.fg_teach(None, None, None, 32, 1.0, None, None) == -1
+
+
+def test_hop_operator_argument_errors_are_statuses():
+    """fg_hop_fwd / fg_hop_bwd check their arguments before any GPU work: a bad batch or a missing buffer is -1 and a
+    message, never a crash."""
+    L = native.lib()
+    assert L.fg_hop_fwd(None, None, None, None, 10, 10, 33, 0, None, None) == -1
+    assert "multiple of 32" in L.fg_hop_last_error().decode()
+    assert L.fg_hop_fwd(None, None, None, None, 10, 10, 64, 0, None, None) == -1
+    assert "null pointer" in L.fg_hop_last_error().decode()
+    assert L.fg_hop_bwd(None, None, None, None, None, None, None, None, -1, 10, 64, 0, None, None, None) == -1
+    assert "negative" in L.fg_hop_last_error().decode()
