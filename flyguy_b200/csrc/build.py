@@ -18,7 +18,8 @@ HERE = Path(__file__).resolve().parent
 PKG = HERE.parent
 REPO = PKG.parent
 LIB = PKG / "libflyguy_b200.so"
-SOURCES = [HERE / "fg_core.cu", HERE / "fg_noalloc.cu", HERE / "fg_hopop.cu"]
+TRAIN = PKG / "fg_train"                             # the trainer executable (a main() over fg_train_main)
+SOURCES = [HERE / "fg_core.cu", HERE / "fg_noalloc.cu", HERE / "fg_hopop.cu", HERE / "fg_train.cu"]
 DEPS = SOURCES + [HERE / "fg_kernels.cuh", HERE / "fg_tc.cuh", REPO / "include" / "flyguy_b200.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -31,7 +32,8 @@ def nvcc() -> str:
 
 
 def stale() -> bool:
-    return not LIB.exists() or any(d.stat().st_mtime > LIB.stat().st_mtime for d in DEPS)
+    return (not LIB.exists() or not TRAIN.exists() or
+            any(d.stat().st_mtime > LIB.stat().st_mtime for d in DEPS + [HERE / "fg_train_main.c"]))
 
 
 def build(force: bool = False, ptxas_v: bool = False, out: Path = LIB, defines: tuple[str, ...] = ()) -> Path:
@@ -48,7 +50,20 @@ def build(force: bool = False, ptxas_v: bool = False, out: Path = LIB, defines: 
     if ptxas_v:
         sys.stderr.write(r.stderr)
     os.replace(tmp, out)
+    if out == LIB:
+        build_trainer()
     return out
+
+
+def build_trainer() -> Path:
+    """fg_train: gcc on the three-line main, linked to the library next to it (rpath $ORIGIN)."""
+    cc = shutil.which("gcc") or "cc"
+    cmd = [cc, "-O2", "-I", str(REPO / "include"), "-o", str(TRAIN), str(HERE / "fg_train_main.c"), "-L", str(PKG),
+           "-lflyguy_b200", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode:
+        raise RuntimeError(f"building fg_train failed ({r.returncode}):\n{r.stdout}\n{r.stderr}")
+    return TRAIN
 
 
 if __name__ == "__main__":

@@ -53,6 +53,7 @@ SIGNATURES = {
     "fg_hop_fwd": (_ci, [_vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _vp, _vp]),
     "fg_hop_bwd": (_ci, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _vp, _vp, _vp]),
     "fg_hop_last_error": (ctypes.c_char_p, []),
+    "fg_train_main": (_ci, [_ci, ctypes.POINTER(ctypes.c_char_p)]),
 }
 KERNEL_CLASSES = ("layout", "fold", "plug_fwd", "hop_fwd", "out_fwd", "loss", "out_bwd", "act_bwd", "sddmm",
                   "hop_bwd_t", "plug_bwd", "adam", "norm")

@@ -138,6 +138,45 @@ def read_params(path: str | Path, s: Structure) -> tuple[int, list[np.ndarray]]:
     return step, out
 
 
+def write_chunk(obs: np.ndarray, teacher: np.ndarray, path: str | Path) -> None:
+    """A FLYD chunk of recorded teacher data (flyguy/native/flyguy_train.cu:13-14, 374-386): "FLYD", n (int64),
+    obs_dim, n_act (int32), then the n observations and the n teacher-logit rows as IEEE fp16."""
+    obs = np.ascontiguousarray(obs, dtype=np.float16)
+    teacher = np.ascontiguousarray(teacher, dtype=np.float16)
+    if obs.ndim != 2 or teacher.ndim != 2 or len(obs) != len(teacher) or not len(obs):
+        raise ValueError("write_chunk: obs [n, obs_dim] and teacher [n, n_act] with n > 0")
+    with open(path, "wb") as fh:
+        fh.write(b"FLYD")
+        fh.write(struct.pack("<qii", len(obs), obs.shape[1], teacher.shape[1]))
+        fh.write(obs.tobytes())
+        fh.write(teacher.tobytes())
+
+
+def read_chunk(path: str | Path) -> tuple[np.ndarray, np.ndarray]:
+    raw = Path(path).read_bytes()
+    if raw[:4] != b"FLYD":
+        raise ValueError(f"{path}: not a FLYD chunk")
+    n, od, na = struct.unpack("<qii", raw[4:20])
+    obs = np.frombuffer(raw, np.float16, n * od, 20).reshape(n, od)
+    teacher = np.frombuffer(raw, np.float16, n * na, 20 + 2 * n * od).reshape(n, na)
+    return obs, teacher
+
+
+def read_opt(path: str | Path, s: Structure) -> tuple[int, int, list[np.ndarray], list[np.ndarray]]:
+    """A FLYO optimiser state (flyguy/native/flyguy_train.cu:288-293): "FLYO", step, adam_t (int64), then M and V of
+    each of the seven arrays in turn. Returns (step, adam_t, M, V)."""
+    raw = Path(path).read_bytes()
+    if raw[:4] != b"FLYO":
+        raise ValueError(f"{path}: not a FLYO optimiser file")
+    step, adam_t = struct.unpack("<qq", raw[4:20])
+    M, V, off = [], [], 20
+    for n in s.param_sizes():
+        M.append(np.frombuffer(raw, np.float32, n, off).copy())
+        V.append(np.frombuffer(raw, np.float32, n, off + 4 * n).copy())
+        off += 8 * n
+    return step, adam_t, M, V
+
+
 def structure_of_actor(f) -> Structure:
     """The structure of a FlyActor (this package's or the reference's: the same buffer names), with only the
     connections in play as weights (flyguy/native/export.py:32-49)."""

@@ -155,6 +155,11 @@ int fg_hop_bwd(const float* w, const float* h, const float* gz, const long long*
 /* Why the calling thread's last fg_hop_* call failed ("" after a success). */
 const char* fg_hop_last_error(void);
 
+/* ---- the standalone teaching trainer (replaces the reference's flyguy_train executable, flyguy/native/
+ * flyguy_train.cu main() at 631-788): argv as the command line "fg_train NET.bin PARAMS.bin DATA_DIR OUT_PREFIX
+ * [options]" (options and file formats in csrc/fg_train.cu). Returns the process exit status (0: done or stopped). */
+int fg_train_main(int argc, const char* const* argv);
+
 #ifdef __cplusplus
 }
 #endif

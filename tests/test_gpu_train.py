@@ -1,0 +1,102 @@
+"""The standalone teaching trainer (fg_train; the reference's flyguy_train main loop, flyguy/native/flyguy_train.cu:
+631-788) on a small synthetic network: it learns, writes FLYP / FLYO in the reference's formats, is deterministic,
+matches the same steps driven from Python through the library bit for bit, restarts from its own save with the
+optimiser state, and stops on a STOP file."""
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+from flyguy_b200 import native, netfile, synth
+
+pytestmark = pytest.mark.gpu
+TRAIN = REPO / "flyguy_b200" / "fg_train"
+M64 = (1 << 64) - 1
+
+
+def _setup(tmp_path):
+    s, P = synth.make_synthetic(sizes=(300, 600, 500, 120), total_edges=20000, seed=3)
+    netfile.write_net(s, tmp_path / "NET.bin")
+    netfile.write_params(P, tmp_path / "P0.bin", step=0)
+    data = tmp_path / "data"
+    data.mkdir()
+    for i, (n, seed) in enumerate(((700, 31), (500, 32))):
+        obs, teacher = synth.make_batch(n, seed=seed)
+        netfile.write_chunk(obs, teacher, data / f"chunk_{i:03d}.bin")
+        os.utime(data / f"chunk_{i:03d}.bin", (1_000_000 + i, 1_000_000 + i))     # chunk_000 is the older one
+    return s, P, data
+
+
+def _run(tmp_path, params, out, *opts):
+    cmd = [str(TRAIN), str(tmp_path / "NET.bin"), str(params), str(tmp_path / "data"), str(out), "--batch", "64",
+           "--log", "10", "--eval-batches", "2", "--save-sec", "1e9", "--lr", "1e-3", *map(str, opts)]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    return r.stdout
+
+
+def _splitmix64(x):
+    x = (x + 0x9E3779B97F4A7C15) & M64
+    x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & M64
+    x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & M64
+    return x ^ (x >> 31)
+
+
+def test_trainer_learns_and_writes_the_reference_formats(tmp_path, cuda):
+    s, P, data = _setup(tmp_path)
+    log = _run(tmp_path, tmp_path / "P0.bin", tmp_path / "out", "--steps", 40)
+    kls = [float(m) for m in re.findall(r"^step \d+ \| \d+ samples/s \| kl ([0-9.]+)", log, re.M)]
+    assert len(kls) == 4 and kls[-1] < kls[0], log
+    assert "eval step 0" in log
+    step, W = netfile.read_params(tmp_path / "out.bin", s)
+    assert step == 40 and all(np.isfinite(a).all() for a in W)
+    assert netfile.read_params(tmp_path / "out.ema.bin", s)[0] == 40
+    st, adam_t, M, V = netfile.read_opt(tmp_path / "out.opt.bin", s)
+    assert (st, adam_t) == (40, 40) and any(np.abs(m).max() > 0 for m in M)
+    # deterministic: the same run again writes the same bytes
+    _run(tmp_path, tmp_path / "P0.bin", tmp_path / "again", "--steps", 40)
+    assert (tmp_path / "out.bin").read_bytes() == (tmp_path / "again.bin").read_bytes()
+    # a restart from its own save goes on with the running average and the optimiser state
+    log2 = _run(tmp_path, tmp_path / "out.bin", tmp_path / "out", "--steps", 10)
+    assert "start step 40, optimiser state restored" in log2
+    assert netfile.read_params(tmp_path / "out.bin", s)[0] == 50
+    assert netfile.read_opt(tmp_path / "out.opt.bin", s)[1] == 50
+
+
+def test_trainer_steps_equal_the_library_driven_from_python(tmp_path, cuda):
+    """Three trainer steps = the same draws (counter-based), the same fused step and the same schedule through
+    flyguy_b200.native from Python: identical weights."""
+    import torch
+    s, P, data = _setup(tmp_path)
+    _run(tmp_path, tmp_path / "P0.bin", tmp_path / "t3", "--steps", 3, "--eval-batches", 0)
+    chunks = [netfile.read_chunk(data / f"chunk_{i:03d}.bin") for i in range(2)]
+    obs_all = np.concatenate([c[0] for c in chunks]).astype(np.float32)
+    tl_all = np.concatenate([c[1] for c in chunks]).astype(np.float32)
+    total, B, seed = len(obs_all), 64, 12345
+    h = native.Handle(s, B)
+    h.set_params(P, 0)
+    h.set_params(P, 1)
+    f32 = np.float32
+    lr, lr_n, lr_p, lr_min = f32(1e-3), f32(1e-4), f32(3e-4), f32(3e-5)
+    for step in range(3):
+        sel = [_splitmix64(seed ^ ((step << 32) | b)) % total for b in range(B)]
+        h.zero_grad()
+        h.teach(torch.as_tensor(obs_all[sel]).cuda(), torch.as_tensor(tl_all[sel]).cuda(), 1.0, loss_norm=B)
+        sched = f32(0.5 ** ((step + 1) / 20000.0))
+        rate = lambda base: float(max(lr_min * base / lr, base * sched))
+        h.step(rate(lr), rate(lr_n), rate(lr_p), 0.0, 0.999)
+    want = [a.cpu().numpy() for a in h.get(0)]
+    got = netfile.read_params(tmp_path / "t3.bin", s)[1]
+    for i in range(7):
+        assert np.array_equal(got[i], want[i]), i
+
+
+def test_trainer_stops_on_request(tmp_path, cuda):
+    s, P, data = _setup(tmp_path)
+    (tmp_path / "st.STOP").write_text("")
+    log = _run(tmp_path, tmp_path / "P0.bin", tmp_path / "st", "--eval-batches", 0)
+    assert "stopped on request at step 1" in log
+    assert (tmp_path / "st.STOP.done").exists() and netfile.read_params(tmp_path / "st.bin", s)[0] == 1

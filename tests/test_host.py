@@ -15,7 +15,7 @@ from conftest import GOLDEN, REPO
 sys.path.insert(0, str(GOLDEN))
 from make_golden import toy_connectome  # noqa: E402  (the fixture script's own made-up connectome)
 
-from flyguy_b200 import netfile  # noqa: E402
+from flyguy_b200 import netfile, synth  # noqa: E402
 from flyguy_b200.fly import FlyActor  # noqa: E402
 
 
@@ -120,3 +120,20 @@ def test_missing_rank_is_detected_on_the_host(tmp_path):
     import torch.multiprocessing as mp
     mp.start_processes(_lonely_worker, args=(1, _free_port(), str(tmp_path)), nprocs=1, start_method="spawn")
     assert (tmp_path / "error").exists() and not (tmp_path / "joined").exists()
+
+
+def test_flyd_chunk_round_trip(tmp_path):
+    obs, teacher = synth.make_batch(50, seed=8)
+    netfile.write_chunk(obs, teacher, tmp_path / "chunk_000.bin")
+    o2, t2 = netfile.read_chunk(tmp_path / "chunk_000.bin")
+    assert np.array_equal(o2, obs.astype(np.float16)) and np.array_equal(t2, teacher.astype(np.float16))
+    raw = (tmp_path / "chunk_000.bin").read_bytes()
+    assert raw[:4] == b"FLYD" and len(raw) == 20 + 2 * 50 * (517 + 90)
+
+
+def test_trainer_argument_errors_exit_without_a_gpu():
+    """fg_train_main reads its command line before touching the GPU: usage and bad options are exit status 1."""
+    from flyguy_b200 import train
+    assert train.main([]) == 1
+    assert train.main(["a", "b", "c", "d", "--batch", "33"]) == 1
+    assert train.main(["a", "b", "c", "d", "--bogus", "1"]) == 1
