@@ -49,6 +49,14 @@ WORKLOADS = {
     "train": dict(cfg=3, batch=16384, per_gpu=False, flags="train", metric="train samples/sec", unit="samples/s",
                   dtype="f32", desc="config 3: distillation step (forward, KL loss, backward, Adam) fp32, global "
                                     "batch 16,384 data-parallel, one NCCL all-reduce of the flat gradient per step"),
+    "infer4": dict(cfg="4-hop", batch=65536, per_gpu=False, flags="bf16", graph="h4", metric="decisions/sec",
+                   unit="decisions/s", dtype="bf16",
+                   desc="4-hop network (145,113 neurons, 8.4M connections; docs/HOW_IT_WORKS.md:57-59): bf16-state "
+                        "forward, global batch 65,536 batch-sharded, no collective"),
+    "train4": dict(cfg="4-hop", batch=16384, per_gpu=False, flags="train", graph="h4", metric="train samples/sec",
+                   unit="samples/s", dtype="f32",
+                   desc="4-hop network: distillation step (forward, KL loss, backward, Adam) fp32, global batch "
+                        "16,384 data-parallel, one NCCL all-reduce of the flat gradient per step"),
     "full": dict(cfg=4, batch=32768, per_gpu=False, flags="train", graph="full", metric="train samples/sec",
                  unit="samples/s", dtype="f32",
                  desc="config 4: the untrimmed graph (166,700 neurons, 15,283,167 edges, every hop past the first over "
@@ -168,6 +176,8 @@ def make_graph(W, sources="zipf"):
     from flyguy_b200 import synth
     if W.get("graph") == "full":
         return synth.make_full_graph()
+    if W.get("graph") == "h4":
+        return synth.make_synthetic4(uniform=sources == "uniform")
     return synth.make_synthetic(uniform=sources == "uniform")
 
 
@@ -270,14 +280,16 @@ def run_ours(a, W, rank, world, dev, torch, dist):
            "scaling": "weak" if W["per_gpu"] else "strong", "vs_baseline": None, "dtype": W["dtype"],
            "data": ("synthetic: seeded untrimmed graph (166,700 neurons, 15,283,167 edges, lognormal in-degree mean 92, "
                     "Zipf(1.5) sources), obs ~ N(0,1), teacher ~ N(0,4)" if W.get("graph") == "full" else
-                    "synthetic: seeded 3-hop graph (16,894/46,393/37,748/1,332 neurons, 2,992,734 edges, lognormal "
+                    f"synthetic: seeded {len(s['sizes']) - 1}-hop graph "
+                    f"({'/'.join(f'{v:,}' for v in s['sizes'])} neurons, {s['n_w']:,} edges, lognormal "
                     f"in-degree mean 35, {'Zipf(1.5)' if a.sources == 'zipf' else 'uniform'} sources), obs ~ N(0,1), "
                     "teacher ~ N(0,4)"),
            "config": {"workload": W["desc"], "baseline_config": W["cfg"], "global_batch": Bg, "per_gpu_batch": B,
                       "parallelism": (f"dp{world}" if train else f"batch-sharded x{world}, no collective"),
                       "l2": "flushed between timed steps (256 MiB write, outside the step events)",
                       "graph": ("synthetic untrimmed 166,700-neuron graph" if W.get("graph") == "full"
-                                else f"synthetic flyguy-sized 3-hop, {a.sources} sources"), "edges": s["n_w"],
+                                else f"synthetic flyguy-sized {len(s['sizes']) - 1}-hop, {a.sources} sources"),
+                      "edges": s["n_w"],
                       "edge_steps": E,
                       "pieces_per_step": (B + piece - 1) // piece,
                       "hop_kernel": ("tensor-core hub product + CUDA-core tail (FG_HUB_TC)"

@@ -124,6 +124,17 @@ def make_synthetic(sizes=FLYGUY_SIZES, total_edges: int = FLYGUY_EDGES, fan: int
     return s, params
 
 
+# the 4-hop variant (docs/HOW_IT_WORKS.md:57-59: 145,113 neurons, 8.4 million connections): the 3-hop layers with a
+# second 46,393-neuron layer and a 34,101-neuron fourth, as distinct neuron sets
+FLYGUY4_SIZES = (16894, 46393, 46393, 34101, 1332)
+FLYGUY4_EDGES = 8_400_000
+
+
+def make_synthetic4(uniform: bool = False, seed: int = 0) -> tuple[Structure, list[np.ndarray]]:
+    """The seeded synthetic 4-hop graph (same generator as make_synthetic)."""
+    return make_synthetic(sizes=FLYGUY4_SIZES, total_edges=FLYGUY4_EDGES, uniform=uniform, seed=seed)
+
+
 def make_full_graph(n_neurons: int = 166_700, n_edges: int = 15_283_167, n_sens: int = 16_894, n_dn: int = 1_332,
                     hops: int = 3, fan: int = 8, obs_dim: int = OBS_DIM, n_act: int = N_ACT, mean_deg: float = 92.0,
                     sigma: float = 1.2, zipf: float = 1.5, seed: int = 0) -> tuple[Structure, list[np.ndarray]]:

@@ -265,6 +265,33 @@ def test_forward_f16_matches_reference(case, cuda):
     assert np.mean(got.argmax(1) == d["logits"].argmax(1)) >= 0.97
 
 
+def test_synthetic_4hop_forward_and_gradients(cuda):
+    """The 4-hop network (145,113 neurons, 8.4M connections): fp32 logits and a 32-sample batch's gradients against
+    the oracle, bf16 logits within the 16-bit tolerance - the same kernels, one more hop."""
+    import torch
+    from oracle.oracle import loss
+    s, P = synth.make_synthetic4()
+    obs, teacher = synth.make_batch(1024, seed=16)
+    h = _handle(s, P, 1024)
+    got = h.forward(_t(obs)).cpu().numpy()
+    idx = _spread(1024, 32)
+    want = Oracle(s).forward(P, obs[idx])
+    assert rel(got[idx], want) < TOL_FP32
+    assert (got[idx].argmax(1) == want.argmax(1)).all()
+    small = 32
+    h.zero_grad()
+    lg = torch.empty(small, s["n_act"], device="cuda")
+    h.teach(_t(obs[:small]), _t(teacher[:small]), 1.0, logits=lg)
+    G = [g.cpu().numpy() for g in h.get(4)]
+    want_lg = Oracle(s).forward(P, obs[:small])
+    _, _, dl = loss(want_lg, teacher[:small], 1.0)
+    want_g = Oracle(s).backward(P, obs[:small], dl)
+    for i in range(7):
+        assert rel(G[i], want_g[i]) < TOL_GRAD, i
+    hb = _handle(s, P, 1024, native.FG_ACT_BF16)
+    assert rel(hb.forward(_t(obs)).cpu().numpy()[idx], want) < TOL_BF16
+
+
 def test_synthetic_training_gradients(flygraph, cuda):
     """Config 3's step on the benchmark graph: gradients of a 64-sample batch against the oracle; at batch 16,384 the
     gradient is the sum of its halves' (linearity over samples)."""
