@@ -110,6 +110,8 @@ struct Core {
     std::vector<void*> allocs;
     int device = 0, n_sm = 148;
     int* d_err = nullptr;                               // device error word of the tensor-core hop (0: none)
+    int* sv_fired = nullptr;                            // during fg_survey: per-row firing counts and
+    float* sv_sq = nullptr;                             //   sums of squared pre-activations (all layers' rows)
     long long launches = 0;
     Timer timer;
 };
@@ -672,6 +674,21 @@ void tc_hop(Core& c, const Hop& h, const void* hp, int B) {
 
 template <class TI, class TO>
 void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
+    if (c.sv_fired) {                                     // the firing survey: CUDA-core hop with per-row counters
+        constexpr int N = Lane32<TI>::N;
+        const dim3 g((h.rows + kWarps - 1) / kWarps, (unsigned)((B + 32 * N - 1) / (32 * N)));
+        launch(c, K_HOP_FWD, [&]() {
+            if (B % (32 * N) == 0)
+                k_hop_fwd_surv<TI, TO, true><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase,
+                    (const TI*)hp, c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive, (TO*)h.d_h, h.rows, B,
+                    c.sv_fired + h.rbase, c.sv_sq + h.rbase);
+            else
+                k_hop_fwd_surv<TI, TO, false><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase,
+                    (const TI*)hp, c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive, (TO*)h.d_h, h.rows, B,
+                    c.sv_fired + h.rbase, c.sv_sq + h.rbase);
+        });
+        return;
+    }
     if constexpr (sizeof(TI) == 2) {
         if (h.K && B % kTcCols == 0) {
             tc_hop<TI, TO>(c, h, hp, B);
@@ -1090,6 +1107,44 @@ int fg_teach_ex(void* h, const float* obs, const float* teacher, int B, float in
         launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
         backward(c, B);
         if (stats) {
+            float s[2];
+            CK(cudaMemcpyAsync(s, c.stats, 8, cudaMemcpyDeviceToHost, c.st));
+            CK(cudaStreamSynchronize(c.st));
+            stats[0] = s[0];
+            stats[1] = s[1];
+        }
+        return 0;
+    }, -1);
+}
+
+int fg_survey(void* h, const float* obs, const float* teacher, int B, int ema, int* fired, float* sq, double* stats) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        check_batch(c, B);
+        if (!obs || !fired || !sq) throw Err("fg_survey: obs, fired and sq are required");
+        const bool loss = teacher && stats;
+        if (loss && !c.train) throw Err("fg_survey: the loss needs a handle made for training");
+        c.sv_fired = fired;
+        c.sv_sq = sq;
+        try {
+            forward(c, obs, B, nullptr, ema, loss);
+        } catch (...) {
+            c.sv_fired = nullptr;
+            c.sv_sq = nullptr;
+            throw;
+        }
+        c.sv_fired = nullptr;
+        c.sv_sq = nullptr;
+        launch(c, K_HOP_FWD, [&]() {
+            const unsigned g = (unsigned)((c.n_s + kWarps - 1) / kWarps);
+            if (c.bf16) k_count_fired<__nv_bfloat16><<<g, kThreads, 0, c.st>>>((const __nv_bfloat16*)c.h0, fired, c.n_s, B, B);
+            else if (c.f16) k_count_fired<__half><<<g, kThreads, 0, c.st>>>((const __half*)c.h0, fired, c.n_s, B, B);
+            else k_count_fired<float><<<g, kThreads, 0, c.st>>>((const float*)c.h0, fired, c.n_s, B, B);
+        });
+        if (loss) {
+            CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
+            launch(c, K_LOSS, [&]() { k_loss<<<blocks(B), 256, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, 1.f, 1.f / B); });
+            launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
             float s[2];
             CK(cudaMemcpyAsync(s, c.stats, 8, cudaMemcpyDeviceToHost, c.st));
             CK(cudaStreamSynchronize(c.st));

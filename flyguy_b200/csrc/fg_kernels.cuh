@@ -401,13 +401,16 @@ __device__ __forceinline__ uint4 ldg16(const char* p) { return __ldg(reinterpret
 __device__ __forceinline__ const char* row_at(const char* base, int r, unsigned row_bytes) {
     return base + (unsigned long long)(unsigned)r * row_bytes;
 }
-// one warp's work: row `slot` of the schedule x sample chunk `chunk`
-template <class TI, class TO, bool FULL>
+// one warp's work: row `slot` of the schedule x sample chunk `chunk`. SURV (the firing survey): also adds, per row,
+// the number of samples whose state is positive to fired[t] and the sum of the squared pre-activations to sq[t]
+// (per-lane atomics: lanes past the batch have already returned).
+template <class TI, class TO, bool FULL, bool SURV = false>
 __device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restrict__ sched,
                                         const int* __restrict__ pptr, const int2* __restrict__ pairs,
                                         const TI* __restrict__ hp, const float* __restrict__ rgain,
                                         const float* __restrict__ rthr, const int* __restrict__ drow,
-                                        const float* __restrict__ drive, TO* __restrict__ h, int n_rows, int ld) {
+                                        const float* __restrict__ drive, TO* __restrict__ h, int n_rows, int ld,
+                                        int* __restrict__ fired = nullptr, float* __restrict__ sq = nullptr) {
     constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H, U = FG_HOP_UNR;
     const int lane = threadIdx.x & 31;
     if (slot >= n_rows) return;
@@ -475,10 +478,16 @@ __device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restri
     }
     const float g = __ldg(&rgain[t]), th = __ldg(&rthr[t]);
     float hv[V];
+    int n_on = 0;
+    float s2 = 0.f;
 #pragma unroll
     for (int i = 0; i < H; ++i) {
         hv[2 * i] = fmaxf(fmaf(g, a0[i].x, -th), 0.f);
         hv[2 * i + 1] = fmaxf(fmaf(g, a0[i].y, -th), 0.f);
+        if (SURV) {
+            n_on += (hv[2 * i] > 0.f) + (hv[2 * i + 1] > 0.f);
+            s2 = fmaf(a0[i].x, a0[i].x, fmaf(a0[i].y, a0[i].y, s2));
+        }
     }
     st16<TO, V>(h + (size_t)t * ld + c0, hv);
     if (g1) {
@@ -486,8 +495,16 @@ __device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restri
         for (int i = 0; i < H; ++i) {
             hv[2 * i] = fmaxf(fmaf(g, a1[i].x, -th), 0.f);
             hv[2 * i + 1] = fmaxf(fmaf(g, a1[i].y, -th), 0.f);
+            if (SURV) {
+                n_on += (hv[2 * i] > 0.f) + (hv[2 * i + 1] > 0.f);
+                s2 = fmaf(a1[i].x, a1[i].x, fmaf(a1[i].y, a1[i].y, s2));
+            }
         }
         st16<TO, V>(h + (size_t)t * ld + c1, hv);
+    }
+    if (SURV) {
+        atomicAdd(&fired[t], n_on);
+        atomicAdd(&sq[t], s2);
     }
 }
 
@@ -500,6 +517,32 @@ __global__ void __launch_bounds__(kThreads, HopOcc<TI>::min_blocks) k_hop_fwd(co
     hop_row<TI, TO, FULL>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, sched, pptr, pairs, hp, rgain, rthr,
                           drow, drive, h, n_rows, ld);
 }
+// the same forward hop for the firing survey (fired / sq: this hop's rows)
+template <class TI, class TO, bool FULL>
+__global__ void __launch_bounds__(kThreads) k_hop_fwd_surv(const int* __restrict__ sched, const int* __restrict__ pptr,
+                                                           const int2* __restrict__ pairs, const TI* __restrict__ hp,
+                                                           const float* __restrict__ rgain,
+                                                           const float* __restrict__ rthr,
+                                                           const int* __restrict__ drow,
+                                                           const float* __restrict__ drive, TO* __restrict__ h,
+                                                           int n_rows, int ld, int* __restrict__ fired,
+                                                           float* __restrict__ sq) {
+    hop_row<TI, TO, FULL, true>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, sched, pptr, pairs, hp, rgain,
+                                rthr, drow, drive, h, n_rows, ld, fired, sq);
+}
+// the firing survey of the sensory layer: samples with a positive state per row (a warp per row)
+template <class T>
+__global__ void __launch_bounds__(kThreads) k_count_fired(const T* __restrict__ h0, int* __restrict__ fired, int n_s,
+                                                          int B, int ld) {
+    const int r = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= n_s) return;
+    int c = 0;
+    for (int b = lane; b < B; b += 32) c += ld1(h0 + (size_t)r * ld + b) > 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    if (lane == 0) fired[r] += c;
+}
+
 // output plug: logits[a,b] = out_b[a] + sum_j out_w[a,j] * hK[dn[j], b], a register-blocked product: a CTA owns
 // 96 actions x 64 samples and one slice of the dn columns (split K: blockIdx.y of gridDim.y), each thread 6 actions x
 // 4 samples; owT is out_w transposed and padded to 96 actions ([n_dn][96], refreshed with the weights), staged with hK

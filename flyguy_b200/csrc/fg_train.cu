@@ -6,7 +6,8 @@
 //
 //   fg_train NET.bin PARAMS.bin DATA_DIR OUT_PREFIX [--batch 512] [--lr 3e-4] [--lr-neuron 1e-4] [--lr-plug 3e-4]
 //            [--lr-min 3e-5] [--half-life 20000] [--ema 0.999] [--log 100] [--save-sec 120] [--steps 0] [--clip 0]
-//            [--temp 1] [--ring 3] [--max-reuse -1] [--eval-batches 16] [--seed 12345]
+//            [--temp 1] [--ring 3] [--max-reuse -1] [--eval-batches 16] [--seed 12345] [--revive-every 0]
+//            [--revive-batches 4] [--revive-target 0.4] [--revive-first 0]
 //
 // Data (flyguy/native/flyguy_train.cu:13-14, 366-417): DATA_DIR/chunk_*.bin = "FLYD", n (int64), obs_dim, n_act
 // (int32), then n x obs_dim observations and n x n_act teacher logits as IEEE fp16. The newest --ring chunks form the
@@ -16,8 +17,11 @@
 // argmax agreement of the running average at temperature 1, --eval-batches batches) before it joins the ring.
 // Saves OUT.bin and OUT.ema.bin (FLYP: "FLYP", step int64, the seven float32 arrays) and OUT.opt.bin (FLYO: "FLYO",
 // step, adam_t, then M and V of each array) - export.py's formats; started from OUT.bin the run goes on from there with
-// its running average and optimiser state. Not here: the firing survey and dead-neuron revival of the reference
-// (survey() / revive(), flyguy_train.cu:437-551).
+// its running average and optimiser state. Eval lines (a new chunk, before it joins the ring) carry the running
+// average's and the raw weights' KL and agreement, each layer's firing share and the silent neurons (fg_survey; the
+// reference's survey() / firing_line(), flyguy_train.cu:437-471). --revive-every N [--revive-batches 4]
+// [--revive-target 0.4] [--revive-first 0]: every N steps the neurons past the sensory layer that fire for none of
+// the surveyed samples are brought back with the network's output unchanged (the reference's revive(), 486-551).
 //
 // Sample draws: sample i of step s is splitmix64(seed ^ (s * 2^32 + i)) modulo the ring's sample count (counter-based,
 // so a Python re-run draws the same samples; the reference uses a sequential mt19937_64 stream).
@@ -33,6 +37,7 @@
 #include <filesystem>
 #include <map>
 #include <memory>
+#include <random>
 #include <string>
 #include <thread>
 #include <vector>
@@ -124,8 +129,9 @@ ChunkP read_chunk(const fs::path& p, int obs_dim, int n_act) {
 
 struct Args {
     std::string net, params, data, out;
-    int B = 512, log_every = 100, ring = 3, eval_batches = 16;
-    long long max_steps = 0;
+    int B = 512, log_every = 100, ring = 3, eval_batches = 16, revive_batches = 4, revive_first = 0;
+    long long max_steps = 0, revive_every = 0;
+    float revive_target = 0.4f;
     double save_sec = 120, half_life = 20000, max_reuse = -1;
     float lr = 3e-4f, lr_neuron = 1e-4f, lr_plug = 3e-4f, lr_min = 3e-5f, ema = 0.999f, clip = 0.f, temp = 1.f;
     uint64_t seed = 12345;
@@ -155,6 +161,10 @@ Args parse(int argc, const char* const* argv) {
         else if (k == "--max-reuse") a.max_reuse = v;
         else if (k == "--eval-batches") a.eval_batches = (int)v;
         else if (k == "--seed") a.seed = (uint64_t)strtoull(argv[i + 1], nullptr, 10);
+        else if (k == "--revive-every") a.revive_every = (long long)v;
+        else if (k == "--revive-batches") a.revive_batches = std::max(1, (int)v);
+        else if (k == "--revive-target") a.revive_target = (float)v;
+        else if (k == "--revive-first") a.revive_first = (int)v;
         else throw TrainErr{"unknown option " + k};
     }
     if (a.B <= 0 || a.B % 32) throw TrainErr{"--batch must be a positive multiple of 32"};
@@ -276,21 +286,80 @@ bool read_flyo(const std::string& path, const Sizes& z, long long step, long lon
 
 double now() { return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count(); }
 
+// what revival needs of NET.bin (export.py:9-16): per hop the rows' neuron ids and the connections (CSR by target,
+// weight index per connection), the sensory neuron ids, the descending rows of the last layer
+struct NetInfo {
+    int obs_dim = 0, n_act = 0, hops = 0, n_neurons = 0, n_w = 0, n_s = 0, fan = 0, n_dn = 0;
+    std::vector<int> sizes, n0, dn;
+    struct H { std::vector<int> nid, crow, col, widx; };
+    std::vector<H> hop;
+};
+NetInfo read_netinfo(const std::string& path) {
+    FILE* f = fopen(path.c_str(), "rb");
+    if (!f) throw TrainErr{"cannot open " + path};
+    auto ints = [&](size_t n) {
+        std::vector<int> v(n);
+        if (n && fread(v.data(), 4, n, f) != n) { fclose(f); throw TrainErr{"short NET.bin " + path}; }
+        return v;
+    };
+    char magic[4];
+    if (fread(magic, 1, 4, f) != 4 || memcmp(magic, "FLY1", 4)) { fclose(f); throw TrainErr{"not a NET.bin: " + path}; }
+    NetInfo n;
+    auto hd = ints(8);
+    n.obs_dim = hd[0]; n.n_act = hd[1]; n.hops = hd[2]; n.n_neurons = hd[3]; n.n_w = hd[4]; n.n_s = hd[5];
+    n.fan = hd[6]; n.n_dn = hd[7];
+    n.sizes = ints(n.hops + 1);
+    auto E = ints(n.hops);
+    auto in_crow = ints(n.n_s + 1);
+    const int e_in = in_crow.back();
+    ints(e_in); ints(n.obs_dim + 1); ints(e_in); ints(e_in);     // plug: in_col, in_tcrow, in_tcol, in_tperm
+    n.n0 = ints(n.n_s);
+    for (int k = 0; k < n.hops; ++k) {
+        NetInfo::H h;
+        h.nid = ints(n.sizes[k + 1]);
+        h.crow = ints(n.sizes[k + 1] + 1);
+        h.col = ints(E[k]);
+        h.widx = ints(E[k]);
+        ints(n.sizes[k] + 1); ints(E[k]); ints(E[k]); ints(n.sizes[k + 1]);   // tcrow, tcol, twidx, drow
+        n.hop.push_back(std::move(h));
+    }
+    n.dn = ints(n.n_dn);
+    fclose(f);
+    return n;
+}
+
+float median_positive(const std::vector<float>& v) {
+    std::vector<float> p;
+    for (float x : v) if (x > 0.f) p.push_back(x);
+    if (p.empty()) return 0.f;
+    std::nth_element(p.begin(), p.begin() + p.size() / 2, p.end());
+    return p[p.size() / 2];
+}
+
+struct Surv {                   // a survey: per row of every layer, samples fired and summed squared input
+    std::vector<int> cnt;
+    std::vector<float> sq;
+    double kl = 0, agree = 0, samples = 0;
+};
+
 struct Trainer {
     Args a;
     void* h = nullptr;
     Sizes z{};
+    NetInfo net;
+    int R = 0;                                          // rows of all layers
+    int* d_fired = nullptr;
+    float* d_sq = nullptr;
     std::vector<ChunkP> ring;
     std::map<std::string, fs::file_time_type> known;
-    float *obs = nullptr, *teacher = nullptr, *logits = nullptr, *dlogits = nullptr, *dstats = nullptr;
+    float *obs = nullptr, *teacher = nullptr;
     long long step = 0, ran = 0;
 
     ~Trainer() {
         if (obs) cudaFree(obs);
         if (teacher) cudaFree(teacher);
-        if (logits) cudaFree(logits);
-        if (dlogits) cudaFree(dlogits);
-        if (dstats) cudaFree(dstats);
+        if (d_fired) cudaFree(d_fired);
+        if (d_sq) cudaFree(d_sq);
         ring.clear();
         if (h) fg_destroy(h);
     }
@@ -342,25 +411,174 @@ struct Trainer {
         k_draw_gather<<<(a.B + 7) / 8, 256>>>(r, seed, s, a.B, z.obs_dim, z.n_act, obs, teacher);
         TCK(cudaGetLastError());
     }
-    // KL and argmax agreement of the running average on --eval-batches batches of one chunk, temperature 1
-    void eval(const ChunkP& c, const char* what) {
-        if (a.eval_batches <= 0) return;
+    static RingDev ring_of(const std::vector<ChunkP>& src) {
         RingDev r{};
-        r.obs[0] = c->obs; r.lg[0] = c->lg; r.n[0] = c->n; r.count = 1; r.total = c->n;
-        double kl = 0, ag = 0;
-        for (int i = 0; i < a.eval_batches; ++i) {
-            draw(r, a.seed ^ 0xE7A1ull, (long long)i);       // (the handle works on the same, default stream)
-            fc_forward(h, obs, a.B, logits, 1);
-            check(h);
-            if (fg_kl_loss_noalloc(logits, teacher, a.B, z.n_act, 1.f, dlogits, dstats, nullptr))
-                throw TrainErr{fg_noalloc_last_error()};
-            float st[2];
-            TCK(cudaMemcpy(st, dstats, 8, cudaMemcpyDeviceToHost));
-            kl += st[0];
-            ag += st[1];
+        r.count = (int)src.size();
+        for (size_t i = 0; i < src.size(); ++i) {
+            r.obs[i] = src[i]->obs; r.lg[i] = src[i]->lg; r.n[i] = src[i]->n; r.total += src[i]->n;
         }
-        const double n = (double)a.B * a.eval_batches;
-        printf("eval step %lld | kl %.4f agree %.4f | %s %s\n", step, kl / n, ag / n, c->name.c_str(), what);
+        return r;
+    }
+    // `batches` batches from src (the same samples for the same seed) through the weights (ema 0) or their running
+    // average (ema 1), no learning: loss and agreement at temperature 1, per row the samples fired and summed z^2
+    Surv survey(int ema, const std::vector<ChunkP>& src, int batches, uint64_t seed) {
+        TCK(cudaMemset(d_fired, 0, (size_t)R * 4));
+        TCK(cudaMemset(d_sq, 0, (size_t)R * 4));
+        Surv s;
+        const RingDev r = ring_of(src);
+        for (int i = 0; i < batches; ++i) {
+            draw(r, seed, (long long)i);
+            double st[2];
+            if (fg_survey(h, obs, teacher, a.B, ema, d_fired, d_sq, st)) check(h);
+            s.kl += st[0];
+            s.agree += st[1];
+        }
+        s.cnt.resize(R);
+        s.sq.resize(R);
+        TCK(cudaMemcpy(s.cnt.data(), d_fired, (size_t)R * 4, cudaMemcpyDeviceToHost));
+        TCK(cudaMemcpy(s.sq.data(), d_sq, (size_t)R * 4, cudaMemcpyDeviceToHost));
+        s.samples = (double)a.B * batches;
+        s.kl /= s.samples;
+        s.agree /= s.samples;
+        return s;
+    }
+    // per neuron (it can sit in several hops): how many times it fired; play = in a hop past the sensory layer
+    void per_neuron(const Surv& s, std::vector<long long>& fired, std::vector<char>& play, std::vector<char>& sens) {
+        fired.assign(net.n_neurons, 0);
+        play.assign(net.n_neurons, 0);
+        sens.assign(net.n_neurons, 0);
+        for (int g : net.n0) sens[g] = 1;
+        size_t off = net.n_s;
+        for (auto& hh : net.hop) {
+            for (size_t t = 0; t < hh.nid.size(); ++t) { play[hh.nid[t]] = 1; fired[hh.nid[t]] += s.cnt[off + t]; }
+            off += hh.nid.size();
+        }
+    }
+    std::string firing_line(const Surv& s, int& silent, int& in_play) {
+        std::vector<long long> fired;
+        std::vector<char> play, sens;
+        per_neuron(s, fired, play, sens);
+        silent = in_play = 0;
+        for (int g = 0; g < net.n_neurons; ++g)
+            if (play[g] && !sens[g]) { ++in_play; if (!fired[g]) ++silent; }
+        std::string out;
+        size_t off = 0;
+        char buf[32];
+        for (int k = 0; k <= net.hops; ++k) {
+            const int rows = net.sizes[k];
+            double c = 0;
+            for (int t = 0; t < rows; ++t) c += s.cnt[off + t];
+            snprintf(buf, sizeof buf, " %.3f", c / (rows * s.samples));
+            out += buf;
+            off += rows;
+        }
+        return out;
+    }
+    // the running average (what would be installed) and the raw weights on --eval-batches batches of one chunk
+    void eval(const ChunkP& c, uint64_t seed, const char* what) {
+        if (a.eval_batches <= 0) return;
+        const std::vector<ChunkP> one{c};
+        const Surv ev = survey(1, one, a.eval_batches, seed), raw = survey(0, one, a.eval_batches, seed);
+        int silent = 0, in_play = 0;
+        const std::string fl = firing_line(ev, silent, in_play);
+        printf("eval step %lld | kl %.4f agree %.4f | raw kl %.4f agree %.4f | firing%s | silent %d of %d | %s %s\n",
+               step, ev.kl, ev.agree, raw.kl, raw.agree, fl.c_str(), silent, in_play, c->name.c_str(), what);
+        fflush(stdout);
+    }
+    // Silent neurons back to work with the network's output unchanged (the reference's revive(), flyguy_train.cu:
+    // 479-551): every neuron past the sensory layer that fired for none of the surveyed samples gets its incoming
+    // strengths' sizes with a random sign and one common factor that brings its input to `target` (rms, three
+    // passes); gain 1 and threshold -4; its strengths onto live neurons and onto the actions become 0 - it sent
+    // nothing before and sends nothing now, but it fires, so those can learn. The running average takes the new
+    // values; Adam restarts for them at a typical scale.
+    void revive(const std::vector<ChunkP>& src, uint64_t seed) {
+        const Surv s0 = survey(0, src, a.revive_batches, seed);
+        const int N = net.n_neurons, K = net.hops;
+        std::vector<long long> fired;
+        std::vector<char> play, sens, dead(N, 0);
+        per_neuron(s0, fired, play, sens);
+        int n_dead = 0, n_play = 0;
+        for (int g = 0; g < N; ++g)
+            if (play[g] && !sens[g]) { ++n_play; if (!fired[g]) { dead[g] = 1; ++n_dead; } }
+        if (!n_dead) {
+            printf("revive step %lld | no silent neuron among %d over %.0f samples\n", step, n_play, s0.samples);
+            fflush(stdout);
+            return;
+        }
+        auto P = from_core(h, 0, z);
+        std::vector<float>&W = P[0], &gain = P[1], &theta = P[2], &ow = P[5];
+        std::vector<char> mark(net.n_w, 0);            // 1: into a silent neuron (new sign); 2: from one into a live one
+        std::mt19937_64 r(seed * 7919ULL + 17);
+        long long n_in = 0, n_out = 0;
+        for (int k = 0; k < K; ++k) {
+            const auto& hh = net.hop[k];
+            const std::vector<int>& below = k ? net.hop[k - 1].nid : net.n0;
+            for (size_t t = 0; t < hh.nid.size(); ++t) {
+                const bool dpost = dead[hh.nid[t]];
+                for (int e = hh.crow[t]; e < hh.crow[t + 1]; ++e) {
+                    const int wi = hh.widx[e];
+                    if (mark[wi]) continue;
+                    if (dpost) { W[wi] = std::max(fabsf(W[wi]), 1e-4f) * ((r() & 1) ? 1.f : -1.f); mark[wi] = 1; ++n_in; }
+                    else if (dead[below[hh.col[e]]]) { W[wi] = 0.f; mark[wi] = 2; ++n_out; }
+                }
+            }
+        }
+        for (int g = 0; g < N; ++g) if (dead[g]) { gain[g] = 1.f; theta[g] = -4.f; }
+        const auto& top = net.hop[K - 1];
+        std::vector<char> dcol(net.n_dn, 0);
+        int n_dn_dead = 0;
+        for (int j = 0; j < net.n_dn; ++j)
+            if (dead[top.nid[net.dn[j]]]) {
+                dcol[j] = 1;
+                ++n_dn_dead;
+                for (int k2 = 0; k2 < net.n_act; ++k2) ow[(size_t)k2 * net.n_dn + j] = 0.f;
+            }
+        to_core(h, 0, P, z);
+        for (int pass = 0; pass < 3; ++pass) {          // hop after hop the revived neurons' inputs come to the target
+            const Surv s = survey(0, src, a.revive_batches, seed);
+            std::vector<float> rms(N, 0.f);
+            size_t off = net.n_s;
+            for (auto& hh : net.hop) {
+                for (size_t t = 0; t < hh.nid.size(); ++t)
+                    rms[hh.nid[t]] = std::max(rms[hh.nid[t]], (float)std::sqrt(s.sq[off + t] / s.samples));
+                off += hh.nid.size();
+            }
+            std::vector<char> done(net.n_w, 0);
+            for (auto& hh : net.hop)
+                for (size_t t = 0; t < hh.nid.size(); ++t) {
+                    const int g = hh.nid[t];
+                    if (!dead[g] || rms[g] <= 0.f) continue;
+                    const float sc = std::min(200.f, std::max(0.02f, a.revive_target / rms[g]));
+                    for (int e = hh.crow[t]; e < hh.crow[t + 1]; ++e) {
+                        const int wi = hh.widx[e];
+                        if (!done[wi]) { W[wi] *= sc; done[wi] = 1; }
+                    }
+                }
+            to_core(h, 0, P, z);
+        }
+        const Surv s1 = survey(0, src, a.revive_batches, seed);
+        per_neuron(s1, fired, play, sens);
+        int still = 0;
+        for (int g = 0; g < N; ++g) if (dead[g] && !fired[g]) ++still;
+        {   // the running average and Adam follow
+            auto E = from_core(h, 1, z), M = from_core(h, 2, z), V = from_core(h, 3, z);
+            const float fill = median_positive(V[0]);
+            for (int i = 0; i < net.n_w; ++i) if (mark[i]) { E[0][i] = W[i]; M[0][i] = 0.f; V[0][i] = fill; }
+            for (int p = 1; p <= 2; ++p) {
+                const float f2 = median_positive(V[p]);
+                for (int g = 0; g < N; ++g) if (dead[g]) { E[p][g] = p == 1 ? 1.f : -4.f; M[p][g] = 0.f; V[p][g] = f2; }
+            }
+            for (int j = 0; j < net.n_dn; ++j)
+                if (dcol[j])
+                    for (int k2 = 0; k2 < net.n_act; ++k2) { E[5][(size_t)k2 * net.n_dn + j] = 0.f; M[5][(size_t)k2 * net.n_dn + j] = 0.f; }
+            to_core(h, 1, E, z);
+            to_core(h, 2, M, z);
+            to_core(h, 3, V, z);
+        }
+        printf("revive step %lld | %d of %d neurons past the sensory layer silent over %.0f samples | new sign for %lld "
+               "incoming strengths, zero for %lld outgoing and for %d descending neurons' action weights | %d still "
+               "silent | kl %.5f -> %.5f (must be equal)\n",
+               step, n_dead, n_play, s0.samples, n_in, n_out, n_dn_dead, still, s0.kl, s1.kl);
         fflush(stdout);
     }
     void save() {
@@ -396,9 +614,11 @@ struct Trainer {
         check(h);
         TCK(cudaMalloc(&obs, (size_t)a.B * z.obs_dim * 4));
         TCK(cudaMalloc(&teacher, (size_t)a.B * z.n_act * 4));
-        TCK(cudaMalloc(&logits, (size_t)a.B * z.n_act * 4));
-        TCK(cudaMalloc(&dlogits, (size_t)a.B * z.n_act * 4));
-        TCK(cudaMalloc(&dstats, 8));
+        net = read_netinfo(a.net);
+        R = 0;
+        for (int v : net.sizes) R += v;
+        TCK(cudaMalloc(&d_fired, (size_t)R * 4));
+        TCK(cudaMalloc(&d_sq, (size_t)R * 4));
         printf("flyguy_b200 trainer: batch %d, lr %g (neurons %g, plugs %g), teacher temperature %g, ring of %d "
                "chunks, start step %lld%s\n",
                a.B, a.lr, a.lr_neuron, a.lr_plug, a.temp, a.ring, step, opt ? ", optimiser state restored" : "");
@@ -411,18 +631,19 @@ struct Trainer {
             fflush(stdout);
             std::this_thread::sleep_for(std::chrono::seconds(5));
         }
-        eval(ring.back(), "at the start");
+        eval(ring.back(), 4242, "at the start");
         const double max_reuse = a.max_reuse < 0 ? (a.max_steps ? 0 : 4) : a.max_reuse;
         auto ring_total = [&]() { double s = 0; for (auto& c : ring) s += (double)c->n; return s; };
         double allow = max_reuse * ring_total();
         double t_log = now(), t_save = now(), kl = 0, ag = 0;
+        long long last_revive = a.revive_first ? step - a.revive_every : step;
         long long since = 0;
         const float it = 1.f / a.temp;
         const std::string stop = a.out + ".STOP";
         while (!a.max_steps || ran < a.max_steps) {
             if (since == 0 || ran % a.log_every == 0) {
                 for (auto& c : scan()) {                      // a new chunk: scored, then into the ring
-                    eval(c, "unseen");
+                    eval(c, 1000003ULL * (uint64_t)step + 7, "unseen");
                     into_ring(c);
                     allow = std::min(allow + max_reuse * (double)c->n, max_reuse * ring_total());
                 }
@@ -437,6 +658,10 @@ struct Trainer {
                 continue;
             }
             allow -= a.B;
+            if (a.revive_every > 0 && step - last_revive >= a.revive_every) {
+                revive(ring, 99991ULL * (uint64_t)step + 3);
+                last_revive = step;
+            }
             draw(ring_dev(), a.seed, step);                   // queued before the step on the same stream
             fc_zero_grad(h);                                  // each step's gradient is its batch's alone
             double s[2];

@@ -54,6 +54,7 @@ SIGNATURES = {
     "fg_hop_bwd": (_ci, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _ci, _ci, _ci, _ci, _vp, _vp, _vp]),
     "fg_hop_last_error": (ctypes.c_char_p, []),
     "fg_train_main": (_ci, [_ci, ctypes.POINTER(ctypes.c_char_p)]),
+    "fg_survey": (_ci, [_vp, _vp, _vp, _ci, _ci, _vp, _vp, ctypes.POINTER(ctypes.c_double)]),
 }
 KERNEL_CLASSES = ("layout", "fold", "plug_fwd", "hop_fwd", "out_fwd", "loss", "out_bwd", "act_bwd", "sddmm",
                   "hop_bwd_t", "plug_bwd", "adam", "norm")
@@ -226,6 +227,21 @@ class Handle:
         rc = self.L.fg_forward_host(self.h, obs_host.data_ptr(), obs_host.shape[0], logits_host.data_ptr(), ema)
         if rc:
             self.check()
+
+    def survey(self, obs, teacher=None, ema: int = 0, fired=None, sq=None):
+        """The firing survey of one batch (fg_survey): per row of every layer the samples whose state is positive and
+        the sum of the squared pre-activations, ADDED to fired / sq (int32 / float32 [sum of layer sizes], made when
+        None); with teacher, (KL sum, agreements) at temperature 1 as the third result."""
+        R = int(sum(self.s["sizes"]))
+        if fired is None:
+            fired = self.torch.zeros(R, dtype=self.torch.int32, device=self.device)
+        if sq is None:
+            sq = self.torch.zeros(R, dtype=self.torch.float32, device=self.device)
+        st = (ctypes.c_double * 2)() if teacher is not None else None
+        self.bind_stream()
+        if self.L.fg_survey(self.h, _ptr(obs), _ptr(teacher), obs.shape[0], ema, _ptr(fired), _ptr(sq), st):
+            self.check()
+        return fired, sq, ((float(st[0]), float(st[1])) if st is not None else None)
 
     def layer(self, k: int, B: int):
         rows = self.s["sizes"][k]

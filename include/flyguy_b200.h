@@ -137,6 +137,14 @@ int fg_kl_loss_noalloc(const float* logits, const float* teacher, int B, int n_a
                        float* stats, void* stream);
 const char* fg_noalloc_last_error(void);
 
+/* The firing survey (the reference trainer's survey(), flyguy_train.cu:437-454, kernel k_fired at 180-187): one
+ * forward of obs [B, obs_dim] (device) with the weights (ema 0) or their running average (ema 1) that ADDS, for every
+ * row of every layer (the sensory rows, then each hop's rows in order: fg_layout), the number of samples whose state
+ * is positive to fired[row] and the sum of the squared pre-activations (sensory rows: 0) to sq[row] (device arrays).
+ * teacher [B, n_act] and stats non-NULL (training handles): stats[0] = sum of KL at temperature 1 over the batch,
+ * stats[1] = argmax agreements (waits for the GPU). Returns 0 or -1. */
+int fg_survey(void* h, const float* obs, const float* teacher, int B, int ema, int* fired, float* sq, double* stats);
+
 /* ---- the per-hop operator (replaces the reference's HopCuda, flyguy/fly_cuda.py:78-115) ------------------------
  * Handle-free, on the caller's device buffers and stream (NULL = the legacy default stream); states are
  * [neurons, batch] fp32, 16-byte aligned, batch a multiple of 32; CSR index arrays as the reference's FlyActor buffers

@@ -100,3 +100,52 @@ def test_trainer_stops_on_request(tmp_path, cuda):
     log = _run(tmp_path, tmp_path / "P0.bin", tmp_path / "st", "--eval-batches", 0)
     assert "stopped on request at step 1" in log
     assert (tmp_path / "st.STOP.done").exists() and netfile.read_params(tmp_path / "st.bin", s)[0] == 1
+
+
+def test_survey_counts_and_squared_inputs(tmp_path, cuda):
+    """fg_survey: per row, the samples whose state is positive (= the layers the forward leaves) and the summed squared
+    pre-activations (= float64 recomputation from the layer below), and the loss at temperature 1 (= the oracle)."""
+    import torch
+    from conftest import rel
+    from oracle.oracle import Oracle, loss
+    s, P, data = _setup(tmp_path)
+    B = 256
+    obs, teacher = synth.make_batch(B, seed=44)
+    h = native.Handle(s, B)
+    h.set_params(P, 0)
+    h.set_params(P, 1)
+    fired, sq, st = h.survey(torch.as_tensor(obs).cuda(), torch.as_tensor(teacher).cuda())
+    fired, sq = fired.cpu().numpy(), sq.cpu().numpy()
+    layers = [h.layer(k, B).cpu().numpy().astype(np.float64) for k in range(len(s["sizes"]))]
+    off = 0
+    W = P[0].astype(np.float64)
+    for k, L in enumerate(layers):
+        rows = L.shape[0]
+        assert np.array_equal(fired[off:off + rows], (L > 0).sum(1)), k
+        if k:
+            hop = s["hop"][k - 1]
+            z = np.zeros_like(L)
+            r = np.repeat(np.arange(rows), np.diff(hop["crow"]))
+            np.add.at(z, r, W[hop["widx"]][:, None] * layers[k - 1][hop["col"]])
+            assert rel(sq[off:off + rows], (z * z).sum(1)) < 1e-4, k
+        off += rows
+    kl_sum, agreements, _ = loss(Oracle(s).forward(P, obs), teacher, 1.0)
+    assert abs(st[0] - kl_sum) < 1e-4 * abs(kl_sum)
+    assert abs(st[1] - agreements) <= 1
+
+
+def test_revive_brings_silent_neurons_back_with_the_output_unchanged(tmp_path, cuda):
+    s, P, data = _setup(tmp_path)
+    n_s = s["sizes"][0]
+    P = [a.copy() for a in P]
+    P[2][n_s:n_s + 60] = 20.0                     # 60 layer-1 neurons whose threshold no input reaches: silent
+    netfile.write_params(P, tmp_path / "Ps.bin", step=0)
+    log = _run(tmp_path, tmp_path / "Ps.bin", tmp_path / "rv", "--steps", 2, "--revive-every", 1,
+               "--revive-batches", 2, "--eval-batches", 1)
+    m = re.search(r"revive step 1 \| (\d+) of \d+ neurons .* \| (\d+) still silent \| kl ([0-9.]+) -> ([0-9.]+) "
+                  r"\(must be equal\)", log)
+    assert m, log
+    n_dead, still, kl0, kl1 = int(m.group(1)), int(m.group(2)), m.group(3), m.group(4)
+    assert n_dead >= 60 and still < n_dead and kl0 == kl1, log
+    assert re.search(r"^eval step 0 \| kl [0-9.]+ agree [0-9.]+ \| raw kl .* \| firing( [0-9.]+){4} \| silent \d+ of",
+                     log, re.M), log
