@@ -57,6 +57,10 @@ WORKLOADS = {
                    unit="samples/s", dtype="f32",
                    desc="4-hop network: distillation step (forward, KL loss, backward, Adam) fp32, global batch "
                         "16,384 data-parallel, one NCCL all-reduce of the flat gradient per step"),
+    "play": dict(cfg="play", batch=8, per_gpu=False, flags="play", metric="decisions/sec", unit="decisions/s",
+                 dtype="f32", desc="playing: one decision for 8 cars per call through the reference's fly_* "
+                                   "interface (fly_forward: host observations in, host logits and the first car's "
+                                   "firing bytes out), fp32, the config-2 graph; latency-bound"),
     "full": dict(cfg=4, batch=32768, per_gpu=False, flags="train", graph="full", metric="train samples/sec",
                  unit="samples/s", dtype="f32",
                  desc="config 4: the untrimmed graph (166,700 neurons, 15,283,167 edges, every hop past the first over "
@@ -490,11 +494,78 @@ def run_reference(a, W):
             "e2e": {"value": round(value, 1), "unit": W["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def _play_calls(fwd, obs_pool, n):
+    """n calls of fwd on the pool's observation batches in turn; seconds per call (host wall clock)."""
+    t0 = time.perf_counter()
+    for i in range(n):
+        fwd(obs_pool[i % len(obs_pool)])
+    return (time.perf_counter() - t0) / n
+
+
+def run_play(a, W, reference: bool):
+    """The playing path: fly_forward for 8 cars per call, host buffers in and out, timed per call on the host clock
+    (a decision is latency); K steps of CALLS calls after W warm-up steps. Ours: the GPU library; the reference: its
+    CPU library (oracle/_ref/libfly_infer.so, one thread, as the bot calls it)."""
+    import ctypes
+    from flyguy_b200 import synth
+    from flyguy_b200.play import Player
+    s, P = make_graph(W, a.sources)
+    ref = REPO / "oracle" / "_ref" / "libfly_infer.so"
+    pool = [synth.make_batch(W["batch"], seed=700 + i)[0] for i in range(16)]
+    CALLS = 50 if reference else 200                   # (the CPU library takes milliseconds a call)
+    players = {}
+    if not reference:
+        players["gpu"] = Player(s, P)
+    if ref.exists() and (reference or not a.no_cpu_baseline):
+        players["cpu"] = Player(s, P, lib=ctypes.CDLL(str(ref)))
+    key = "cpu" if reference else "gpu"
+    if key not in players:
+        return {"impl": "reference" if reference else "ours", "unavailable": f"{ref} is not built"}
+    fwd = lambda o, p=players[key]: p.forward(o, tap=True)
+    _play_calls(fwd, pool, CALLS * a.warmup)
+    clk = None
+    if reference:
+        per = [_play_calls(fwd, pool, CALLS) for _ in range(a.steps)]
+    else:
+        import torch
+        with Clocks(torch.cuda.current_device()) as clk:
+            per = [_play_calls(fwd, pool, CALLS) for _ in range(a.steps)]
+    dt = sum(per) / len(per)
+    value = W["batch"] / dt
+    out = {"metric": W["metric"], "value": round(value, 1), "unit": W["unit"], "n_gpus": 0 if reference else 1,
+           "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt * CALLS * 1e3, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic: the config-2 graph, obs ~ N(0,1)",
+           "config": {"workload": W["desc"], "baseline_config": W["cfg"], "cars_per_call": W["batch"],
+                      "calls_per_step": CALLS, "timing": "host wall clock per fly_forward call",
+                      "latency_ms_per_call": round(dt * 1e3, 4)},
+           "roofline": None,
+           "e2e": {"value": round(value, 1), "unit": W["unit"], "h2d_bytes_per_step": CALLS * W["batch"] * s["obs_dim"] * 4,
+                   "d2h_bytes_per_step": CALLS * (W["batch"] * s["n_act"] * 4 + int(sum(s["sizes"])))}}
+    if reference:
+        out.update(impl="reference", cpu_baseline={"value": round(value, 1), "unit": W["unit"], "cores": 1,
+                                                   "kind": "reference", "sample": f"{CALLS} calls per step; "
+                                                   "flyguy/native/fly_infer.cpp fly_forward", "cpu": _cpu_model()})
+    else:
+        cpu = None
+        if "cpu" in players:
+            dc = _play_calls(lambda o, p=players["cpu"]: p.forward(o, tap=True), pool, 50)
+            cpu = {"value": round(W["batch"] / dc, 1), "unit": W["unit"], "cores": 1, "kind": "reference",
+                   "sample": f"50 calls of 8 cars, {dc * 1e3:.3f} ms per call; flyguy/native/fly_infer.cpp "
+                             "fly_forward (oracle/_ref), one thread", "cpu": _cpu_model()}
+        out.update(cpu_baseline=cpu, clocks=clk.summary(), gpu_launches=int((len(s["hop"]) + 2) * CALLS * a.steps))
+    return out
+
+
 def main():
     a = args_()
     W = WORKLOADS[a.workload]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if W["flags"] == "play":                    # one process plays; under torchrun the other ranks have nothing to do
+        if rank == 0:
+            print(json.dumps(run_play(a, W, a.impl == "reference")), flush=True)
+        return
     if a.impl == "reference":
         if rank == 0:
             print(json.dumps(run_reference(a, W)), flush=True)

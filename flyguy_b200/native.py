@@ -55,6 +55,13 @@ SIGNATURES = {
     "fg_hop_last_error": (ctypes.c_char_p, []),
     "fg_train_main": (_ci, [_ci, ctypes.POINTER(ctypes.c_char_p)]),
     "fg_survey": (_ci, [_vp, _vp, _vp, _ci, _ci, _vp, _vp, ctypes.POINTER(ctypes.c_double)]),
+    "fly_create": (_vp, [_ci, _ci, _ci]),
+    "fly_set_plug": (None, [_vp, _ci, _ci] + [_vp] * 6),
+    "fly_set_hop": (None, [_vp, _ci, _ci, _ci, _ci] + [_vp] * 6),
+    "fly_set_out": (None, [_vp, _ci, _vp, _vp, _vp]),
+    "fly_forward": (None, [_vp, _vp, _ci, _vp, _vp]),
+    "fly_free": (None, [_vp]),
+    "fg_fly_last_error": (ctypes.c_char_p, []),
 }
 KERNEL_CLASSES = ("layout", "fold", "plug_fwd", "hop_fwd", "out_fwd", "loss", "out_bwd", "act_bwd", "sddmm",
                   "hop_bwd_t", "plug_bwd", "adam", "norm")
@@ -304,7 +311,7 @@ def header_symbols(path: Path | None = None) -> list[str]:
     import re
     path = path or PKG.parent / "include" / "flyguy_b200.h"
     text = Path(path).read_text()
-    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b((?:fc|fg)_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b((?:fc|fg|fly)_\w+)\s*\(", text, re.M)))
 
 
 def default_threads() -> int:

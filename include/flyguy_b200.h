@@ -163,6 +163,29 @@ int fg_hop_bwd(const float* w, const float* h, const float* gz, const long long*
 /* Why the calling thread's last fg_hop_* call failed ("" after a success). */
 const char* fg_hop_last_error(void);
 
+/* ---- the playing network's interface (replaces the reference's CPU library flyguy/native/fly_infer.cpp, loaded by
+ * FlyActor._native, flyguy/fly.py:187-241): the same names, arguments and HOST buffers; the forward runs on the GPU.
+ * Errors: fg_fly_last_error() (the interface itself has no status; a failed fly_forward answers NaN logits). */
+
+/* fly_infer.cpp:33-36. */
+void* fly_create(int obs_dim, int n_act, int hops);
+/* fly_infer.cpp:37-42: the plug, CSR by sensory row; gain g0 and threshold t0 (softplus(theta)) per sensory row. */
+void fly_set_plug(void* p, int n_s, int E, const int* crow, const int* col, const float* w, const float* b,
+                  const float* g0, const float* t0);
+/* fly_infer.cpp:43-47: hop k's connections by SOURCE neuron (tcrow[src + 1], tcol = target row, w in that order),
+ * gain g and threshold t per target row, drow = the sensory row re-driven into a target row or -1. */
+void fly_set_hop(void* p, int k, int rows, int src, int E, const int* tcrow, const int* tcol, const float* w,
+                 const float* g, const float* t, const int* drow);
+/* fly_infer.cpp:48-54: the output plug, w [n_act, n_dn] row = action. */
+void fly_set_out(void* p, int n_dn, const int* dn, const float* w, const float* b);
+/* fly_infer.cpp:55-97: obs [batch, obs_dim] -> logits [batch, n_act] (host); tap (or NULL): one byte per neuron
+ * state of the first car, layer after layer, 255 * tanh(1.5 * state). */
+void fly_forward(void* p, const float* obs, int batch, float* logits, unsigned char* tap);
+/* fly_infer.cpp:98. */
+void fly_free(void* p);
+/* Why the calling thread's last fly_* call failed ("" after a success). */
+const char* fg_fly_last_error(void);
+
 /* ---- the standalone teaching trainer (replaces the reference's flyguy_train executable, flyguy/native/
  * flyguy_train.cu main() at 631-788): argv as the command line "fg_train NET.bin PARAMS.bin DATA_DIR OUT_PREFIX
  * [options]" (options and file formats in csrc/fg_train.cu). Returns the process exit status (0: done or stopped). */
