@@ -103,28 +103,37 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampled every 200 ms while the timed region runs."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """nvidia-smi sampled every 50 ms (with timestamps) from before the warm-up; mark_start / mark_end bracket the
+    timed region and the summary keeps the samples taken inside it (within 0.1 s). A region shorter than the sampling
+    interval falls back to the sample nearest its middle (and says so)."""
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index, self.proc, self.path = index, None, None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-f", self.path], stdout=subprocess.DEVNULL,
+                                          "-lms", "50", "-f", self.path], stdout=subprocess.DEVNULL,
                                          stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.proc = None
         return self
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def __exit__(self, *exc):
         if self.proc:
-            time.sleep(0.25)
+            time.sleep(0.15)
             self.proc.terminate()
             try:
                 self.proc.wait(5)
@@ -132,26 +141,39 @@ class Clocks:
                 self.proc.kill()
 
     def summary(self):
+        import datetime
         if not self.path or not os.path.exists(self.path):
             return None
         rows = []
         for line in Path(self.path).read_text().splitlines():
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9 or not f[0].isdigit() or int(f[0]) != self.index:
+            if len(f) < 10 or not f[1].isdigit() or int(f[1]) != self.index:
                 continue
             try:
-                rows.append((float(f[1]), float(f[2]), float(f[3]), f[5:9]))
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(f[2]), float(f[3]), float(f[4]), f[6:10]))
             except ValueError:
                 continue
         os.unlink(self.path)
         if not rows:
             return None
+        t0 = self.t0 if self.t0 is not None else rows[0][0]
+        t1 = self.t1 if self.t1 is not None else rows[-1][0]
+        inside = [r for r in rows if t0 - 0.1 <= r[0] <= t1 + 0.1]
+        nearest = not inside
+        if nearest:
+            mid = 0.5 * (t0 + t1)
+            inside = [min(rows, key=lambda r: abs(r[0] - mid))]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower().startswith("active")})
-        load = [r for r in rows if r[2] > 300.0] or rows
-        return {"sm_mhz": statistics.median(r[0] for r in load), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows), "samples_under_load": len(load),
-                "power_w_max": max(r[2] for r in rows), "gpu_index": self.index}
+        reasons = sorted({names[i] for r in inside for i, v in enumerate(r[4]) if v.lower().startswith("active")})
+        load = [r for r in inside if r[3] > 300.0] or inside
+        out = {"sm_mhz": statistics.median(r[1] for r in load), "sm_max_mhz": max(r[2] for r in rows),
+               "reasons": reasons, "samples": len(inside), "samples_under_load": len([r for r in inside if r[3] > 300.0]),
+               "power_w_max": max(r[3] for r in inside), "gpu_index": self.index,
+               "timed_region_s": round(t1 - t0, 4), "sampling_ms": 50}
+        if nearest:
+            out["nearest_sample"] = True
+        return out
 
 
 def algo_bytes(cls: str, s, B: int, act: int) -> float:
@@ -229,22 +251,24 @@ def run_ours(a, W, rank, world, dev, torch, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(a.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    # ---- timed region (device time, per-step CUDA events; L2 flushed between steps outside the events)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
-    h.timing(True)
-    launches0 = h.launches()
     with Clocks(int(os.environ.get("LOCAL_RANK", dev.index or 0))) as clk:
+        for _ in range(a.warmup):
+            step()
+        torch.cuda.synchronize(dev)
+        # ---- timed region (device time, per-step CUDA events; L2 flushed between steps outside the events)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+        h.timing(True)
+        launches0 = h.launches()
         barrier()
         torch.cuda.synchronize(dev)
+        clk.mark_start()
         for e0, e1 in evs:
             flush.zero_()
             e0.record()
             step()
             e1.record()
         torch.cuda.synchronize(dev)
+        clk.mark_end()
         barrier()
     launches = h.launches() - launches0
     kern = h.timing_read()
@@ -529,7 +553,9 @@ def run_play(a, W, reference: bool):
     else:
         import torch
         with Clocks(torch.cuda.current_device()) as clk:
+            clk.mark_start()
             per = [_play_calls(fwd, pool, CALLS) for _ in range(a.steps)]
+            clk.mark_end()
     dt = sum(per) / len(per)
     value = W["batch"] / dt
     out = {"metric": W["metric"], "value": round(value, 1), "unit": W["unit"], "n_gpus": 0 if reference else 1,
