@@ -537,7 +537,7 @@ void alloc_all(Core& c) {
         c.gdrive = dalloc<float>(c, (size_t)c.n_s * B);
         c.live = dalloc<int>(c, max_rows);
         c.nsum = dalloc<float>(c, (size_t)max_rows * ((B + 255) / 256) * 3);
-        c.out_splits = std::max(1, std::min(64, (int)((B + 1023) / 1024)));
+        c.out_splits = std::max(1, std::min(64, (int)(B / 128)));     // batch slices of the output-plug backward
         c.part = dalloc<float>(c, (size_t)c.out_splits * c.n_act * (c.n_dn + 1));
         c.kl_s = dalloc<float>(c, B);
         int slots = 0;
@@ -765,9 +765,9 @@ void backward(Core& c, int B) {
     CK(cudaMemsetAsync(c.gdrive, 0, (size_t)c.n_s * B * 4, c.st));
     const Hop& top = c.hop.back();
     const float* hK = (const float*)top.d_h;
-    // weight gradient: 64-column tiles x batch slices, about two waves of CTAs (slices of at least 512 samples)
+    // weight gradient: 64-column tiles x batch slices, about two waves of CTAs (slices of at least 128 samples)
     const int wtiles = (c.n_dn + 1 + kOutB - 1) / kOutB;
-    const int splits = std::max(1, std::min({c.out_splits, (2 * c.n_sm + wtiles - 1) / wtiles, B / 512}));
+    const int splits = std::max(1, std::min({c.out_splits, (2 * c.n_sm + wtiles - 1) / wtiles, B / 128}));
     const int split_len = ((B + splits - 1) / splits + 31) / 32 * 32;
     launch(c, K_OUT_BWD, [&]() {
         k_out_bwd_wt<float><<<dim3(wtiles, splits), 256, 0, c.st>>>(c.dl, hK, c.d_dn, c.part, c.n_act, c.n_dn, B,
@@ -1103,7 +1103,7 @@ int fg_teach_ex(void* h, const float* obs, const float* teacher, int B, float in
         if (!c.train) throw Err("this handle was created for inference only");
         forward(c, obs, B, logits, 0, true);
         CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
-        launch(c, K_LOSS, [&]() { k_loss<<<blocks(B), 256, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp, 1.f / loss_norm); });
+        launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, 64), 64, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp, 1.f / loss_norm); });
         launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
         backward(c, B);
         if (stats) {
@@ -1143,7 +1143,7 @@ int fg_survey(void* h, const float* obs, const float* teacher, int B, int ema, i
         });
         if (loss) {
             CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
-            launch(c, K_LOSS, [&]() { k_loss<<<blocks(B), 256, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, 1.f, 1.f / B); });
+            launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, 64), 64, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, 1.f, 1.f / B); });
             launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
             float s[2];
             CK(cudaMemcpyAsync(s, c.stats, 8, cudaMemcpyDeviceToHost, c.st));

@@ -17,10 +17,6 @@ namespace fg {
 constexpr int kWarps = 8;                 // warps per CTA of the row kernels
 constexpr int kThreads = 32 * kWarps;
 
-template <class T> struct Act;
-template <> struct Act<float> { static constexpr int V = 4; };
-template <> struct Act<__nv_bfloat16> { static constexpr int V = 8; };
-template <> struct Act<__half> { static constexpr int V = 8; };
 
 // ---- 16-byte vector loads / stores of V activations as fp32
 __device__ __forceinline__ void ld_act(const float* p, float (&v)[4]) {
@@ -190,22 +186,7 @@ __device__ __forceinline__ void cvt_store4(__nv_bfloat16* p, float4 v) {
 __device__ __forceinline__ void cvt_store4(__half* p, float4 v) {
     *reinterpret_cast<uint2*>(p) = make_uint2(pack_f16(v.x, v.y), pack_f16(v.z, v.w));
 }
-// NS consecutive staged values as fp32 (NS = 1 for fp32, 2 for 16-bit types)
-__device__ __forceinline__ void lds_ns(const float* p, float (&v)[1]) { v[0] = *p; }
-__device__ __forceinline__ void lds_ns(const __nv_bfloat16* p, float (&v)[2]) {
-    const uint32_t q = *reinterpret_cast<const uint32_t*>(p);
-    v[0] = __uint_as_float(q << 16); v[1] = __uint_as_float(q & 0xffff0000u);
-}
-__device__ __forceinline__ void lds_ns(const __half* p, float (&v)[2]) {
-    const uint32_t q = *reinterpret_cast<const uint32_t*>(p);
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&q));
-    v[0] = a.x; v[1] = a.y;
-}
-__device__ __forceinline__ void st_ns(float* p, const float (&v)[1]) { *p = v[0]; }
-__device__ __forceinline__ void st_ns(__nv_bfloat16* p, const float (&v)[2]) {
-    *reinterpret_cast<uint32_t*>(p) = pack_bf16(v[0], v[1]);
-}
-__device__ __forceinline__ void st_ns(__half* p, const float (&v)[2]) { *reinterpret_cast<uint32_t*>(p) = pack_f16(v[0], v[1]); }
+// NS consecutive staged values as fp32 (NS = 2 for fp32, 4 for 16-bit types)
 __device__ __forceinline__ void lds_ns(const float* p, float (&v)[2]) {
     const float2 q = *reinterpret_cast<const float2*>(p);
     v[0] = q.x; v[1] = q.y;
