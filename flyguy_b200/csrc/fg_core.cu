@@ -594,7 +594,7 @@ void fold(Core& c, int which) {
     launch(c, K_FOLD, [&]() { k_fold_neurons<<<blocks(c.R), 256, 0, c.st>>>(c.d_row_nid, src + c.off[1], src + c.off[2], c.d_rgain, c.d_rthr,
                                                   c.d_rsig, (int)c.R); });
     if (c.Ptot) {
-        launch(c, K_FOLD, [&]() { k_fold_pairs<<<blocks(c.Ptot), 256, 0, c.st>>>(c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, (int)c.Ptot); });
+        launch(c, K_FOLD, [&]() { k_fold_pairs<<<blocks(c.Ptot, kThreads), kThreads, 0, c.st>>>(c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, (int)c.Ptot); });
         if (c.Ttot)
             launch(c, K_FOLD, [&]() { k_fold_tpairs<<<blocks(c.Ttot), 256, 0, c.st>>>(c.d_tpi, c.d_pairs, c.d_tpairs, (int)c.Ttot); });
         for (auto& h : c.hop) {
@@ -863,15 +863,22 @@ void backward(Core& c, int B) {
     });
 }
 
-float grad_norm(Core& c, float max_norm) {
+// the gradient norm and the clipping scale into c.norm (device)
+void grad_norm_launch(Core& c, float max_norm) {
     const long long n = c.off[7];
     const int nb = (int)std::min<long long>(1024, std::max<long long>(1, blocks(n)));
     launch(c, K_NORM, [&]() { k_sumsq<<<nb, 256, 0, c.st>>>(c.G, n, c.norm_part); });
     launch(c, K_NORM, [&]() { k_norm_final<<<1, 256, 0, c.st>>>(c.norm_part, nb, max_norm, c.norm); });
+}
+float read_norm(Core& c) {
     float g = 0.f;
     CK(cudaMemcpyAsync(&g, c.norm, 4, cudaMemcpyDeviceToHost, c.st));
     CK(cudaStreamSynchronize(c.st));
     return g;
+}
+float grad_norm(Core& c, float max_norm) {
+    grad_norm_launch(c, max_norm);
+    return read_norm(c);
 }
 
 float* flat(Core& c, int which) {
@@ -1054,17 +1061,17 @@ float fc_step(void* h, float lr, float lr_neuron, float lr_plug, float max_norm,
     return guarded(h, [&]() {
         Core& c = *as_core(h);
         if (!c.train) throw Err("this handle was created for inference only");
-        float g = 0.f;
         const float* scale = nullptr;
-        if (max_norm > 0) { g = grad_norm(c, max_norm); scale = c.norm; }
+        if (max_norm > 0) { grad_norm_launch(c, max_norm); scale = c.norm; }
         ++c.adam_t;
         const long long tc = std::min<long long>(c.adam_t, 100000);
         const float c1 = 1.f - (float)pow(0.9, (double)tc), c2 = 1.f - (float)pow(0.999, (double)tc);
         const long long n = c.off[7];
-        launch(c, K_ADAM, [&]() { k_adam<<<(unsigned)std::min<long long>(blocks(n), 148 * 16), 256, 0, c.st>>>(
+        launch(c, K_ADAM, [&]() { k_adam<<<(unsigned)std::min<long long>(blocks((n + 3) / 4), 148 * 8), 256, 0, c.st>>>(
             c.P, c.G, c.M, c.V, c.EMA, n, c.off[1], c.off[3], lr, lr_neuron, lr_plug, c1, c2, scale, ema); });
         c.folded = -1;
-        return g;
+        // the update is queued behind the norm on the device; the host reads the norm afterwards
+        return max_norm > 0 ? read_norm(c) : 0.f;
     }, 0.f);
 }
 
@@ -1103,7 +1110,7 @@ int fg_teach_ex(void* h, const float* obs, const float* teacher, int B, float in
         if (!c.train) throw Err("this handle was created for inference only");
         forward(c, obs, B, logits, 0, true);
         CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
-        launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, 64), 64, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp, 1.f / loss_norm); });
+        launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, kLossS), kLossS, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp, 1.f / loss_norm); });
         launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
         backward(c, B);
         if (stats) {
@@ -1143,7 +1150,7 @@ int fg_survey(void* h, const float* obs, const float* teacher, int B, int ema, i
         });
         if (loss) {
             CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
-            launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, 64), 64, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, 1.f, 1.f / B); });
+            launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, kLossS), kLossS, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, 1.f, 1.f / B); });
             launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
             float s[2];
             CK(cudaMemcpyAsync(s, c.stats, 8, cudaMemcpyDeviceToHost, c.st));

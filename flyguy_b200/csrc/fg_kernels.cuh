@@ -16,6 +16,7 @@ namespace fg {
 
 constexpr int kWarps = 8;                 // warps per CTA of the row kernels
 constexpr int kThreads = 32 * kWarps;
+constexpr int kMaxAct = 96;                // actions at most (the output plug's tiles pad to 96)
 
 
 // ---- 16-byte vector loads / stores of V activations as fp32
@@ -129,13 +130,31 @@ __global__ void k_fold_neurons(const int* __restrict__ nid, const float* __restr
     rsig[i] = sigmoid_f(th);
 }
 // merged pair weight = sum of the weights of its edges (edges of one (row, source) pair are contiguous)
-__global__ void k_fold_pairs(const int* __restrict__ gptr, const int* __restrict__ gw, const float* __restrict__ W,
-                             int2* __restrict__ pairs, int n) {
-    int p = blockIdx.x * blockDim.x + threadIdx.x;
-    if (p >= n) return;
+// A warp owns 32 consecutive pairs: it gathers the weights of their edges (a contiguous range of gw) into shared memory
+// with all lanes, 256 at a time, then each lane adds its own pair's edges from there in edge order
+constexpr int kFoldBuf = 256;
+__global__ void __launch_bounds__(kThreads) k_fold_pairs(const int* __restrict__ gptr, const int* __restrict__ gw,
+                                                         const float* __restrict__ W, int2* __restrict__ pairs, int n) {
+    __shared__ float buf[kWarps][kFoldBuf];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int p0 = (blockIdx.x * kWarps + warp) * 32;
+    if (p0 >= n) return;
+    const int p = p0 + lane, pend = min(p0 + 32, n);
+    const int e_lo = __ldg(&gptr[p0]), e_hi = __ldg(&gptr[pend]);
+    const int my_lo = p < n ? __ldg(&gptr[p]) : e_hi, my_hi = p < n ? __ldg(&gptr[p + 1]) : e_hi;
+    float* sb = buf[warp];
     float s = 0.f;
-    for (int j = gptr[p]; j < gptr[p + 1]; ++j) s += __ldg(&W[gw[j]]);
-    pairs[p].y = __float_as_int(s);
+    for (int base = e_lo; base < e_hi; base += kFoldBuf) {
+        const int cnt = min(kFoldBuf, e_hi - base);
+#pragma unroll 8
+        for (int i = lane; i < kFoldBuf; i += 32)
+            if (i < cnt) sb[i] = __ldg(&W[__ldg(&gw[base + i])]);
+        __syncwarp();
+        const int lo = max(my_lo, base), hi = min(my_hi, base + cnt);
+        for (int e = lo; e < hi; ++e) s += sb[e - base];
+        __syncwarp();
+    }
+    if (p < n) pairs[p].y = __float_as_int(s);
 }
 __global__ void k_fold_tpairs(const int* __restrict__ tpi, const int2* __restrict__ pairs, int2* __restrict__ tpairs,
                               int n) {
@@ -653,30 +672,54 @@ __global__ void __launch_bounds__(256) k_out_reduce(const float* __restrict__ pa
 // per sample: p_t = softmax(teacher * it); kl = sum p_t (log p_t - log softmax(s)); dl = (softmax(s) - p_t) * inv_norm
 // (inv_norm = 1 / the number of samples the loss averages over: the batch, or more when a batch comes in pieces);
 // argmax agreement. teacher is the caller's [B, n_act]; lg and dl are neuron-major.
-__global__ void k_loss(const float* __restrict__ lg, const float* __restrict__ teacher, float* __restrict__ dl,
-                       float* __restrict__ kl_s, float* __restrict__ ag_s, int n_act, int B, int ld, float it,
-                       float inv_norm) {
-    int b = blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= B) return;
-    const float* t = teacher + (size_t)b * n_act;
-    float ms = -INFINITY, mt = -INFINITY;
-    int as = 0, at = 0;
-    for (int a = 0; a < n_act; ++a) {
-        float s = lg[(size_t)a * ld + b], tv = t[a] * it;
-        if (s > ms) { ms = s; as = a; }
-        if (tv > mt) { mt = tv; at = a; }
+// A CTA owns kLossS samples: their logit rows ([a][b], coalesced) and teacher rows ([b][a], contiguous) are staged in
+// shared memory (teacher row stride n_act + 1 words: odd for n_act = 90, so the per-sample reads do not conflict), then
+// one thread per sample runs the three passes over its actions in order, writes dl into the staged logits, and the
+// CTA stores dl back row by row.
+constexpr int kLossS = 32;
+__global__ void __launch_bounds__(kLossS) k_loss(const float* __restrict__ lg, const float* __restrict__ teacher,
+                                                 float* __restrict__ dl, float* __restrict__ kl_s,
+                                                 float* __restrict__ ag_s, int n_act, int B, int ld, float it,
+                                                 float inv_norm) {
+    __shared__ float sl[kMaxAct * kLossS];
+    __shared__ float stt[kLossS * (kMaxAct + 1)];
+    const int b0 = blockIdx.x * kLossS, nb = min(kLossS, B - b0), j = threadIdx.x, tw = n_act + 1;
+#pragma unroll 8
+    for (int a = 0; a < n_act; ++a)
+        if (j < nb) sl[a * kLossS + j] = __ldg(&lg[(size_t)a * ld + b0 + j]);
+    const float* tb = teacher + (size_t)b0 * n_act;
+#pragma unroll 8
+    for (int i = j; i < nb * n_act; i += kLossS) {
+        const int r = i / n_act;
+        stt[r * tw + (i - r * n_act)] = __ldg(&tb[i]);
     }
-    float zs = 0.f, zt = 0.f;
-    for (int a = 0; a < n_act; ++a) { zs += expf(lg[(size_t)a * ld + b] - ms); zt += expf(t[a] * it - mt); }
-    const float ls = ms + logf(zs), lt = mt + logf(zt);
-    float kl = 0.f;
-    for (int a = 0; a < n_act; ++a) {
-        float lps = lg[(size_t)a * ld + b] - ls, lpt = t[a] * it - lt, pt = expf(lpt);
-        kl += pt * (lpt - lps);
-        dl[(size_t)a * ld + b] = (expf(lps) - pt) * inv_norm;
+    __syncthreads();
+    if (j < nb) {
+        const float* t = stt + j * tw;
+        float* s_ = sl + j;
+        float ms = -INFINITY, mt = -INFINITY;
+        int as = 0, at = 0;
+        for (int a = 0; a < n_act; ++a) {
+            float s = s_[a * kLossS], tv = t[a] * it;
+            if (s > ms) { ms = s; as = a; }
+            if (tv > mt) { mt = tv; at = a; }
+        }
+        float zs = 0.f, zt = 0.f;
+        for (int a = 0; a < n_act; ++a) { zs += expf(s_[a * kLossS] - ms); zt += expf(t[a] * it - mt); }
+        const float ls = ms + logf(zs), lt = mt + logf(zt);
+        float kl = 0.f;
+        for (int a = 0; a < n_act; ++a) {
+            float lps = s_[a * kLossS] - ls, lpt = t[a] * it - lt, pt = expf(lpt);
+            kl += pt * (lpt - lps);
+            s_[a * kLossS] = (expf(lps) - pt) * inv_norm;
+        }
+        kl_s[b0 + j] = kl;
+        ag_s[b0 + j] = as == at ? 1.f : 0.f;
     }
-    kl_s[b] = kl;
-    ag_s[b] = as == at ? 1.f : 0.f;
+    __syncthreads();
+#pragma unroll 8
+    for (int a = 0; a < n_act; ++a)
+        if (j < nb) dl[(size_t)a * ld + b0 + j] = sl[a * kLossS + j];
 }
 // stats[0] = sum kl, stats[1] = sum agree (one CTA, fixed order)
 __global__ void k_loss_stats(const float* __restrict__ kl_s, const float* __restrict__ ag_s, float* __restrict__ stats,
@@ -814,7 +857,6 @@ __global__ void k_out_bwd_reduce(const float* __restrict__ part, float* __restri
     int a = i / n_col, j = i - a * n_col;
     if (j < n_dn) gow[(size_t)a * n_dn + j] += s; else gob[a] += s;
 }
-constexpr int kMaxAct = 96;                // actions at most (the output plug's tiles pad to 96)
 
 // ---------------------------------------------------------------- backward: through the neurons
 // one CTA per listed row of the top layer: g = gh * [h > 0]; gz = g * gain -> gz; gain grad += sum g*z with z = (h + thr) / gain (exact where
@@ -1184,20 +1226,36 @@ __global__ void k_norm_final(const float* __restrict__ part, int n, float max_no
     }
 }
 // Adam over the flat parameter buffer: segments [0, seg1) at lr0 (strengths), [seg1, seg2) at lr1 (gain, theta),
-// the rest at lr2 (plugs). Gradient scale from norm[1] when `scale` is given.
+// the rest at lr2 (plugs). Gradient scale from norm[1] when `scale` is given. Four elements per thread step (the
+// buffers are separate 256-byte aligned allocations); each element's arithmetic is the scalar update.
+__device__ __forceinline__ void adam1(float& p, float g, float& m, float& v, float& e, float lr, float c1, float c2,
+                                      float decay) {
+    const float mi = 0.9f * m + 0.1f * g, vi = 0.999f * v + 0.001f * g * g;
+    m = mi; v = vi;
+    p = p - lr * (mi / c1) / (sqrtf(vi / c2) + 1e-8f);
+    e = decay * e + (1.f - decay) * p;
+}
 __global__ void k_adam(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
                        float* __restrict__ ema, long long n, long long seg1, long long seg2, float lr0, float lr1,
                        float lr2, float c1, float c2, const float* __restrict__ scale, float decay) {
     const float gs = scale ? scale[1] : 1.f;
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        const float lr = i < seg1 ? lr0 : (i < seg2 ? lr1 : lr2);
-        const float gr = g[i] * gs;
-        const float mi = 0.9f * m[i] + 0.1f * gr, vi = 0.999f * v[i] + 0.001f * gr * gr;
-        m[i] = mi; v[i] = vi;
-        const float pi = p[i] - lr * (mi / c1) / (sqrtf(vi / c2) + 1e-8f);
-        p[i] = pi;
-        ema[i] = decay * ema[i] + (1.f - decay) * pi;
+    const long long n4 = n >> 2, stride = (long long)gridDim.x * blockDim.x;
+    for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < n4; q += stride) {
+        float4 P = reinterpret_cast<float4*>(p)[q], M = reinterpret_cast<float4*>(m)[q];
+        float4 V = reinterpret_cast<float4*>(v)[q], E = reinterpret_cast<float4*>(ema)[q];
+        const float4 G = __ldg(reinterpret_cast<const float4*>(g) + q);
+        float* pp = &P.x; float* mm = &M.x; float* vv = &V.x; float* ee = &E.x;
+        const float gg[4] = {G.x, G.y, G.z, G.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const long long i = 4 * q + k;
+            adam1(pp[k], gg[k] * gs, mm[k], vv[k], ee[k], i < seg1 ? lr0 : (i < seg2 ? lr1 : lr2), c1, c2, decay);
+        }
+        reinterpret_cast<float4*>(p)[q] = P; reinterpret_cast<float4*>(m)[q] = M;
+        reinterpret_cast<float4*>(v)[q] = V; reinterpret_cast<float4*>(ema)[q] = E;
     }
+    for (long long i = 4 * n4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        adam1(p[i], g[i] * gs, m[i], v[i], ema[i], i < seg1 ? lr0 : (i < seg2 ? lr1 : lr2), c1, c2, decay);
 }
 
 }  // namespace fg
