@@ -63,7 +63,7 @@ enum KClass { K_TRANSPOSE, K_FOLD, K_PLUG_FWD, K_HOP_FWD, K_OUT_FWD, K_LOSS, K_O
               K_PLUG_BWD, K_ADAM, K_NORM, K_NCLASS };
 
 struct Timer {
-    bool on = false;
+    unsigned mask = 0;                         // classes being timed (bit = KClass)
     std::vector<cudaEvent_t> pool;
     size_t used = 0;
     struct Rec { int cls; cudaEvent_t a, b; };
@@ -89,7 +89,7 @@ struct Core {
     int* d_row_nid = nullptr;
     float *d_rgain = nullptr, *d_rthr = nullptr, *d_rsig = nullptr;
     int2 *d_pairs = nullptr, *d_tpairs = nullptr;
-    int *d_gptr = nullptr, *d_gw = nullptr, *d_tpi = nullptr;
+    int *d_gptr = nullptr, *d_gw = nullptr, *d_tpos = nullptr;   // d_tpos: pair -> transposed pair, or -1
     long long off[8] = {0};                             // segment starts in the flat arrays (256-byte aligned)
     long long psize[7] = {0};                           // the seven arrays' true lengths
     float *P = nullptr, *G = nullptr, *M = nullptr, *V = nullptr, *EMA = nullptr;
@@ -128,7 +128,8 @@ cudaEvent_t pool_event(Core& c) {
 template <class F>
 void launch(Core& c, int cls, F&& f) {
     cudaEvent_t a = nullptr, b = nullptr;
-    if (c.timer.on) {
+    const bool timed = (c.timer.mask >> cls) & 1u;
+    if (timed) {
         a = pool_event(c);
         b = pool_event(c);
         CK(cudaEventRecord(a, c.st));
@@ -136,7 +137,7 @@ void launch(Core& c, int cls, F&& f) {
     f();
     CK(cudaGetLastError());
     ++c.launches;
-    if (c.timer.on) {
+    if (timed) {
         CK(cudaEventRecord(b, c.st));
         c.timer.recs.push_back({cls, a, b});
     }
@@ -478,7 +479,11 @@ void upload_net(Core& c, NetHost& n) {
     c.d_tpairs = upload(c, tpairs);
     c.d_gptr = upload(c, gptr);
     c.d_gw = upload(c, gw);
-    c.d_tpi = upload(c, tpi);
+    if (c.Ttot) {
+        std::vector<int> tpos(c.Ptot, -1);
+        for (long long q = 0; q < c.Ttot; ++q) tpos[tpi[q]] = (int)q;
+        c.d_tpos = upload(c, tpos);
+    }
 }
 
 size_t act_bytes(const Core& c) { return (c.bf16 || c.f16) ? 2 : 4; }
@@ -594,9 +599,7 @@ void fold(Core& c, int which) {
     launch(c, K_FOLD, [&]() { k_fold_neurons<<<blocks(c.R), 256, 0, c.st>>>(c.d_row_nid, src + c.off[1], src + c.off[2], c.d_rgain, c.d_rthr,
                                                   c.d_rsig, (int)c.R); });
     if (c.Ptot) {
-        launch(c, K_FOLD, [&]() { k_fold_pairs<<<blocks(c.Ptot, kThreads), kThreads, 0, c.st>>>(c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, (int)c.Ptot); });
-        if (c.Ttot)
-            launch(c, K_FOLD, [&]() { k_fold_tpairs<<<blocks(c.Ttot), 256, 0, c.st>>>(c.d_tpi, c.d_pairs, c.d_tpairs, (int)c.Ttot); });
+        launch(c, K_FOLD, [&]() { k_fold_pairs<<<blocks(c.Ptot, kThreads), kThreads, 0, c.st>>>(c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, c.d_tpos, c.d_tpairs, (int)c.Ptot); });
         for (auto& h : c.hop) {
             if (!h.n_hub_pairs) continue;
             launch(c, K_FOLD, [&]() {
@@ -1110,7 +1113,7 @@ int fg_teach_ex(void* h, const float* obs, const float* teacher, int B, float in
         if (!c.train) throw Err("this handle was created for inference only");
         forward(c, obs, B, logits, 0, true);
         CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
-        launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, kLossS), kLossS, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp, 1.f / loss_norm); });
+        launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, kLossS), kLossT, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp, 1.f / loss_norm); });
         launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
         backward(c, B);
         if (stats) {
@@ -1150,7 +1153,7 @@ int fg_survey(void* h, const float* obs, const float* teacher, int B, int ema, i
         });
         if (loss) {
             CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
-            launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, kLossS), kLossS, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, 1.f, 1.f / B); });
+            launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, kLossS), kLossT, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, 1.f, 1.f / B); });
             launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
             float s[2];
             CK(cudaMemcpyAsync(s, c.stats, 8, cudaMemcpyDeviceToHost, c.st));
@@ -1230,14 +1233,16 @@ long long fg_launches(void* h) {
     return guarded(h, [&]() { return as_core(h)->launches; }, (long long)-1);
 }
 
-int fg_timing(void* h, int on) {
+int fg_timing_classes(void* h, unsigned mask) {
     return guarded(h, [&]() {
         Core& c = *as_core(h);
-        if (!on && !c.timer.recs.empty()) throw Err("fg_timing: read the recorded times (fg_timing_read) first");
-        c.timer.on = on != 0;
+        if (!mask && !c.timer.recs.empty()) throw Err("fg_timing: read the recorded times (fg_timing_read) first");
+        c.timer.mask = mask & ((1u << K_NCLASS) - 1u);
         return 0;
     }, -1);
 }
+
+int fg_timing(void* h, int on) { return fg_timing_classes(h, on ? ~0u : 0u); }
 
 int fg_timing_read(void* h, double* ms, long long* count, int n) {
     return guarded(h, [&]() {

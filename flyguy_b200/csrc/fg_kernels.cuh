@@ -131,10 +131,13 @@ __global__ void k_fold_neurons(const int* __restrict__ nid, const float* __restr
 }
 // merged pair weight = sum of the weights of its edges (edges of one (row, source) pair are contiguous)
 // A warp owns 32 consecutive pairs: it gathers the weights of their edges (a contiguous range of gw) into shared memory
-// with all lanes, 256 at a time, then each lane adds its own pair's edges from there in edge order
+// with all lanes, 256 at a time, then each lane adds its own pair's edges from there in edge order. The sum is also
+// written to the pair's place among the transposed pairs (tpos[p] >= 0) when there are any.
 constexpr int kFoldBuf = 256;
 __global__ void __launch_bounds__(kThreads) k_fold_pairs(const int* __restrict__ gptr, const int* __restrict__ gw,
-                                                         const float* __restrict__ W, int2* __restrict__ pairs, int n) {
+                                                         const float* __restrict__ W, int2* __restrict__ pairs,
+                                                         const int* __restrict__ tpos, int2* __restrict__ tpairs,
+                                                         int n) {
     __shared__ float buf[kWarps][kFoldBuf];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int p0 = (blockIdx.x * kWarps + warp) * 32;
@@ -154,13 +157,11 @@ __global__ void __launch_bounds__(kThreads) k_fold_pairs(const int* __restrict__
         for (int e = lo; e < hi; ++e) s += sb[e - base];
         __syncwarp();
     }
-    if (p < n) pairs[p].y = __float_as_int(s);
-}
-__global__ void k_fold_tpairs(const int* __restrict__ tpi, const int2* __restrict__ pairs, int2* __restrict__ tpairs,
-                              int n) {
-    int q = blockIdx.x * blockDim.x + threadIdx.x;
-    if (q >= n) return;
-    tpairs[q].y = pairs[tpi[q]].y;
+    if (p < n) {
+        pairs[p].y = __float_as_int(s);
+        const int q = tpos ? __ldg(&tpos[p]) : -1;
+        if (q >= 0) tpairs[q].y = __float_as_int(s);
+    }
 }
 
 // out_w [n_act][n_dn] -> owT [n_dn][kOutA] (actions padded with zeros), the output plug's operand layout
@@ -672,29 +673,30 @@ __global__ void __launch_bounds__(256) k_out_reduce(const float* __restrict__ pa
 // per sample: p_t = softmax(teacher * it); kl = sum p_t (log p_t - log softmax(s)); dl = (softmax(s) - p_t) * inv_norm
 // (inv_norm = 1 / the number of samples the loss averages over: the batch, or more when a batch comes in pieces);
 // argmax agreement. teacher is the caller's [B, n_act]; lg and dl are neuron-major.
-// A CTA owns kLossS samples: their logit rows ([a][b], coalesced) and teacher rows ([b][a], contiguous) are staged in
-// shared memory (teacher row stride n_act + 1 words: odd for n_act = 90, so the per-sample reads do not conflict), then
-// one thread per sample runs the three passes over its actions in order, writes dl into the staged logits, and the
-// CTA stores dl back row by row.
-constexpr int kLossS = 32;
-__global__ void __launch_bounds__(kLossS) k_loss(const float* __restrict__ lg, const float* __restrict__ teacher,
+// A CTA owns kLossS samples: all its threads stage their logit rows ([a][b], coalesced) and teacher rows ([b][a],
+// contiguous) in shared memory (teacher row stride n_act + 1 words: odd for n_act = 90, so the per-sample reads do not
+// conflict), then one thread per sample runs the three passes over its actions in order, writes dl into the staged
+// logits, and the CTA stores dl back row by row.
+constexpr int kLossS = 32, kLossT = 256;
+__global__ void __launch_bounds__(kLossT) k_loss(const float* __restrict__ lg, const float* __restrict__ teacher,
                                                  float* __restrict__ dl, float* __restrict__ kl_s,
                                                  float* __restrict__ ag_s, int n_act, int B, int ld, float it,
                                                  float inv_norm) {
     __shared__ float sl[kMaxAct * kLossS];
     __shared__ float stt[kLossS * (kMaxAct + 1)];
-    const int b0 = blockIdx.x * kLossS, nb = min(kLossS, B - b0), j = threadIdx.x, tw = n_act + 1;
-#pragma unroll 8
-    for (int a = 0; a < n_act; ++a)
+    const int b0 = blockIdx.x * kLossS, nb = min(kLossS, B - b0), tw = n_act + 1;
+    const int j = threadIdx.x & (kLossS - 1), a0 = threadIdx.x / kLossS;
+#pragma unroll 4
+    for (int a = a0; a < n_act; a += kLossT / kLossS)
         if (j < nb) sl[a * kLossS + j] = __ldg(&lg[(size_t)a * ld + b0 + j]);
     const float* tb = teacher + (size_t)b0 * n_act;
-#pragma unroll 8
-    for (int i = j; i < nb * n_act; i += kLossS) {
+#pragma unroll 4
+    for (int i = threadIdx.x; i < nb * n_act; i += kLossT) {
         const int r = i / n_act;
         stt[r * tw + (i - r * n_act)] = __ldg(&tb[i]);
     }
     __syncthreads();
-    if (j < nb) {
+    if (threadIdx.x < nb) {
         const float* t = stt + j * tw;
         float* s_ = sl + j;
         float ms = -INFINITY, mt = -INFINITY;
@@ -717,8 +719,8 @@ __global__ void __launch_bounds__(kLossS) k_loss(const float* __restrict__ lg, c
         ag_s[b0 + j] = as == at ? 1.f : 0.f;
     }
     __syncthreads();
-#pragma unroll 8
-    for (int a = 0; a < n_act; ++a)
+#pragma unroll 4
+    for (int a = a0; a < n_act; a += kLossT / kLossS)
         if (j < nb) dl[(size_t)a * ld + b0 + j] = sl[a * kLossS + j];
 }
 // stats[0] = sum kl, stats[1] = sum agree (one CTA, fixed order)

@@ -47,6 +47,7 @@ SIGNATURES = {
     "fg_layer": (_ci, [_vp, _ci, _vp, _ci]),
     "fg_launches": (_cll, [_vp]),
     "fg_timing": (_ci, [_vp, _ci]),
+    "fg_timing_classes": (_ci, [_vp, ctypes.c_uint]),
     "fg_timing_read": (_ci, [_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_cll), _ci]),
     "fg_kl_loss_noalloc": (_ci, [_vp, _vp, _ci, _ci, _cf, _vp, _vp, _vp]),
     "fg_noalloc_last_error": (ctypes.c_char_p, []),
@@ -261,8 +262,16 @@ class Handle:
     def launches(self) -> int:
         return int(self.L.fg_launches(self.h))
 
-    def timing(self, on: bool) -> None:
-        if self.L.fg_timing(self.h, int(on)):
+    def timing(self, on: bool, classes=None) -> None:
+        """Per-launch CUDA-event timing: of every kernel class, or of the named ones (KERNEL_CLASSES) only."""
+        if on and classes is not None:
+            mask = 0
+            for k in classes:
+                mask |= 1 << KERNEL_CLASSES.index(k)
+            rc = self.L.fg_timing_classes(self.h, mask)
+        else:
+            rc = self.L.fg_timing(self.h, int(on))
+        if rc:
             self.check()
 
     def timing_read(self) -> dict:

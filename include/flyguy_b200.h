@@ -119,6 +119,9 @@ long long fg_launches(void* h);
 /* on 1: every later kernel launch is bracketed by CUDA events on the handle's stream (for live per-kernel timing);
  * on 0: stop (after reading). */
 int fg_timing(void* h, int on);
+/* Like fg_timing, for the classes whose bit (1 << class, classes as for fg_timing_read) is set in mask only; the other
+ * launches run without events. mask 0: stop (after reading). */
+int fg_timing_classes(void* h, unsigned mask);
 /* Waits for the stream; sums the recorded times per kernel class into ms[0..n-1] (milliseconds) and count[0..n-1]
  * (launches), then forgets them. Classes: 0 layout change, 1 weight folds, 2 input plug, 3 hop forward, 4 output
  * plug, 5 loss, 6 output-plug backward, 7 neuron backward, 8 weight gradient, 9 transposed hop, 10 plug backward,
