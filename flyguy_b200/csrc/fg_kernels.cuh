@@ -912,7 +912,7 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
 // per merged pair p of row t: gp = sum_b gz[t,b] * hp[src_p, b], added to the gradient of every edge weight of the
 // pair. One warp per work item {row, first pair} - up to 4 consecutive pairs of one row whose gradient can be
 // non-zero - over the whole batch, 4 samples per lane per step; a warp-shuffle reduction in a fixed order (no block
-// barriers, no atomics for weights used once per hop).
+// barriers, no atomics for weights used once per hop); the edge weights' gradients are then updated by all lanes.
 template <bool ATOMIC>
 __global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ items, const int* __restrict__ pptr,
                                                     const int2* __restrict__ pairs, const int* __restrict__ gptr,
@@ -944,12 +944,15 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ ite
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) acc[u] = warp_sum(acc[u]);
-    if (lane < np) {
-        const int p = p0 + lane;
-        const float v = lane == 0 ? acc[0] : lane == 1 ? acc[1] : lane == 2 ? acc[2] : acc[3];
-        for (int j = __ldg(&gptr[p]); j < __ldg(&gptr[p + 1]); ++j) {
-            if (ATOMIC) atomicAdd(&gW[gw[j]], v); else gW[gw[j]] += v;
-        }
+    // the item's edges are one contiguous range of gw (pair after pair): every lane adds a pair's sum into the
+    // gradient of one edge weight at a time; each weight is used once per hop unless ATOMIC
+    const int e0 = __ldg(&gptr[p0]), e1 = __ldg(&gptr[p0 + np]);
+    const int m1 = np > 1 ? __ldg(&gptr[p0 + 1]) : e1, m2 = np > 2 ? __ldg(&gptr[p0 + 2]) : e1,
+              m3 = np > 3 ? __ldg(&gptr[p0 + 3]) : e1;
+    for (int j = e0 + lane; j < e1; j += 32) {
+        const float v = j < m1 ? acc[0] : j < m2 ? acc[1] : j < m3 ? acc[2] : acc[3];
+        const int w = __ldg(&gw[j]);
+        if (ATOMIC) atomicAdd(&gW[w], v); else gW[w] += v;
     }
 }
 
