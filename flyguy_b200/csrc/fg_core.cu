@@ -13,6 +13,7 @@
 
 #include "fg_kernels.cuh"
 #include "fg_tc.cuh"
+#include "fg_outtc.cuh"
 #include "flyguy_b200.h"
 
 using namespace fg;
@@ -78,6 +79,8 @@ struct Core {
     float* owT = nullptr;                                // out_w transposed, padded to kOutA actions
     float* out_part = nullptr;                           // the output plug's per-slice partial logits
     int out_slices = 1;                                  // split-K slices of the dn columns (fixed by the graph)
+    float* ow_tc = nullptr;                              // out_w in the tensor-core operand layout (hi, lo terms)
+    int out_chunks = 0, out_cps = 0;                     // 32-column chunks of the dn columns; chunks per slice
     float* seg_part = nullptr;                           // partial rows of split transposed segments
     int* seg_done = nullptr;                             // arrival counters of split rows' segments [red][chunk]
     int *d_in_crow = nullptr, *d_in_col = nullptr, *d_n0 = nullptr, *d_dn = nullptr;
@@ -529,8 +532,14 @@ void alloc_all(Core& c) {
     }
     // The slice count depends on the graph only, never on the batch, so a sample's logits are the same bits whatever
     // batch (or piece of one) it is computed in: one slice per ~320 dn columns, at most 8.
-    c.out_slices = std::max(1, std::min(8, (c.n_dn + 319) / 320));
-    if (c.out_slices > 1) c.out_part = dalloc<float>(c, (size_t)c.out_slices * kOutA * B);
+    c.out_chunks = (c.n_dn + kOtKC - 1) / kOtKC;
+    {
+        const int want = std::max(1, std::min(8, (c.n_dn + 319) / 320));
+        c.out_cps = (c.out_chunks + want - 1) / want;
+        c.out_slices = (c.out_chunks + c.out_cps - 1) / c.out_cps;
+    }
+    c.out_part = dalloc<float>(c, (size_t)c.out_slices * kOutA * B);
+    c.ow_tc = dalloc<float>(c, (size_t)c.out_chunks * 2 * kOtN * kOtKC);
     c.lg = dalloc<float>(c, (size_t)c.n_act * B);
     c.norm_part = dalloc<float>(c, 1024);
     c.norm = dalloc<float>(c, 4);
@@ -585,12 +594,14 @@ void set_smem_limits(const Core& c) {
                             tc_smem(kHubMax)));
     CK(cudaFuncSetAttribute(k_hop_tc<__half, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(kHubMax)));
     CK(cudaFuncSetAttribute(k_hop_tc<__half, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(kHubMax)));
+    CK(cudaFuncSetAttribute(k_out_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kOtSmem));
     plug_limit<float, true>(c); plug_limit<float, false>(c);
     plug_limit<__nv_bfloat16, true>(c); plug_limit<__nv_bfloat16, false>(c);
     plug_limit<__half, true>(c); plug_limit<__half, false>(c);
 }
 
 inline unsigned blocks(long long n, int t = 256) { return (unsigned)((n + t - 1) / t); }
+static_assert(kOtN == kOutA, "the tensor-core output plug writes the partial slabs k_out_reduce reads");
 
 // derived per-version arrays: per-row gain / threshold / sigmoid, merged pair weights (forward and transposed)
 void fold(Core& c, int which) {
@@ -613,6 +624,8 @@ void fold(Core& c, int which) {
             });
         }
     }
+    launch(c, K_FOLD, [&]() { k_fold_ow_tc<<<blocks((long long)c.out_chunks * kOtN * kOtKC), 256, 0, c.st>>>(
+                                  src + c.off[5], c.ow_tc, c.n_act, c.n_dn, c.out_chunks); });
     launch(c, K_FOLD, [&]() { k_fold_owT<<<blocks((long long)c.n_dn * kOutA), 256, 0, c.st>>>(src + c.off[5], c.owT,
                                                                                          c.n_act, c.n_dn); });
     c.folded = which;
@@ -735,19 +748,18 @@ void forward_t(Core& c, const float* obs, int B, float* logits, int ema, bool ke
         hp = h.d_h;
         hp_f32 = h.out_f32;
     }
-    // sample tiles x split-K slices of the dn columns (k_out_reduce adds the slices in order, then the bias)
-    const int tiles = (B + kOutB - 1) / kOutB;
-    const int slices = c.out_slices;
+    // tensor-core tiles of 128 samples x split-K slices of the dn columns, then k_out_reduce adds the bias and the
+    // slices in order
+    OutTc ot;
+    ot.wt = c.ow_tc; ot.dn = c.d_dn; ot.hK = (const float*)hp; ot.part = c.out_part; ot.err = c.d_err;
+    ot.n_dn = c.n_dn; ot.B = B; ot.ld = B; ot.chunks = c.out_chunks; ot.cps = c.out_cps;
     launch(c, K_OUT_FWD, [&]() {
-        k_out_fwd<float><<<dim3(tiles, slices), 256, 0, c.st>>>(c.owT, Pw + c.off[6], c.d_dn, (const float*)hp,
-                                                                keep_lg ? c.lg : nullptr, logits, c.out_part, c.n_act,
-                                                                c.n_dn, B, B);
+        k_out_tc<<<dim3((B + kOtM - 1) / kOtM, c.out_slices), kOtThreads, kOtSmem, c.st>>>(ot);
     });
-    if (slices > 1)
-        launch(c, K_OUT_FWD, [&]() {
-            k_out_reduce<<<(B + 31) / 32, 256, 0, c.st>>>(c.out_part, Pw + c.off[6], keep_lg ? c.lg : nullptr, logits,
-                                                          slices, c.n_act, B, B);
-        });
+    launch(c, K_OUT_FWD, [&]() {
+        k_out_reduce<<<(B + 31) / 32, 256, 0, c.st>>>(c.out_part, Pw + c.off[6], keep_lg ? c.lg : nullptr, logits,
+                                                      c.out_slices, c.n_act, B, B);
+    });
     c.lastB = B;
 }
 
@@ -1094,7 +1106,7 @@ void fc_sync(void* h) {
         CK(cudaMemcpy(&e, c.d_err, sizeof(int), cudaMemcpyDeviceToHost));
         if (e) {
             CK(cudaMemset(c.d_err, 0, sizeof(int)));
-            throw Err("tensor-core hop: a wait expired (code " + std::to_string(e) + "); its states are not valid");
+            throw Err("tensor-core kernel: a wait expired (code " + std::to_string(e) + "); its results are not valid");
         }
         return 0;
     }, 0);

@@ -544,107 +544,10 @@ __global__ void __launch_bounds__(kThreads) k_count_fired(const T* __restrict__ 
     if (lane == 0) fired[r] += c;
 }
 
-// output plug: logits[a,b] = out_b[a] + sum_j out_w[a,j] * hK[dn[j], b], a register-blocked product: a CTA owns
-// 96 actions x 64 samples and one slice of the dn columns (split K: blockIdx.y of gridDim.y), each thread 6 actions x
-// 4 samples; owT is out_w transposed and padded to 96 actions ([n_dn][96], refreshed with the weights), staged with hK
-// 32 columns at a time. With one slice it finishes the logits itself; with several, each writes its partial
-// [96][ld] slab and k_out_reduce adds the slices in order.
+// output plug: the forward product is the tensor-core kernel k_out_tc (fg_outtc.cuh); kOutA is the padded action
+// count of its partial slabs and of the backward's operand layouts, kOutB / kOutK the backward's sample tile and
+// staging depth
 constexpr int kOutA = 96, kOutB = 64, kOutK = 32;
-template <class T>
-__global__ void __launch_bounds__(256) k_out_fwd(const float* __restrict__ owT, const float* __restrict__ ob,
-                                                 const int* __restrict__ dn, const T* __restrict__ hK,
-                                                 float* __restrict__ lg, float* __restrict__ out,
-                                                 float* __restrict__ part, int n_act, int n_dn, int B, int ld) {
-    // operand tiles (32 x 96 + 32 x 64 floats), reused afterwards for the 64 x 97 output rows: the larger of the two
-    constexpr int kOperands = kOutK * kOutA + kOutK * kOutB, kRows = kOutB * (kOutA + 1);
-    __shared__ __align__(16) float sm[kOperands > kRows ? kOperands : kRows];
-    float* Ws = sm;
-    float* Hs = sm + kOutK * kOutA;
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    const int b0 = blockIdx.x * kOutB;
-    const int slices = gridDim.y, per = (n_dn + slices - 1) / slices;
-    const int k_lo = blockIdx.y * per, k_hi = min(n_dn, k_lo + per);
-    float acc[6][4];
-#pragma unroll
-    for (int i = 0; i < 6; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-    for (int k0 = k_lo; k0 < k_hi; k0 += kOutK) {
-        const int nk = min(kOutK, k_hi - k0);
-        __syncthreads();
-        for (int i = threadIdx.x; i < kOutK * kOutA / 4; i += 256) {
-            const int k = i / (kOutA / 4);
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (k < nk) v = __ldg(reinterpret_cast<const float4*>(owT + (size_t)(k0 + k) * kOutA) + (i - k * (kOutA / 4)));
-            reinterpret_cast<float4*>(Ws)[i] = v;
-        }
-        for (int i = threadIdx.x; i < kOutK * kOutB; i += 256) {
-            const int k = i / kOutB, b = i - k * kOutB;
-            Hs[i] = (k < nk && b0 + b < B) ? ld1(hK + (size_t)__ldg(&dn[k0 + k]) * ld + b0 + b) : 0.f;
-        }
-        __syncthreads();
-#pragma unroll 8
-        for (int k = 0; k < kOutK; ++k) {
-            const float4 h = *reinterpret_cast<const float4*>(Hs + k * kOutB + tx * 4);
-            const float2 w01 = *reinterpret_cast<const float2*>(Ws + k * kOutA + ty * 6);
-            const float2 w23 = *reinterpret_cast<const float2*>(Ws + k * kOutA + ty * 6 + 2);
-            const float2 w45 = *reinterpret_cast<const float2*>(Ws + k * kOutA + ty * 6 + 4);
-            const float hv[4] = {h.x, h.y, h.z, h.w};
-            const float wv[6] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y};
-#pragma unroll
-            for (int i = 0; i < 6; ++i) {                         // two packed fp32x2 FMAs (same rounding)
-                const float2 w2 = make_float2(wv[i], wv[i]);
-                const float2 p0 = __ffma2_rn(w2, make_float2(hv[0], hv[1]), make_float2(acc[i][0], acc[i][1]));
-                const float2 p1 = __ffma2_rn(w2, make_float2(hv[2], hv[3]), make_float2(acc[i][2], acc[i][3]));
-                acc[i][0] = p0.x; acc[i][1] = p0.y; acc[i][2] = p1.x; acc[i][3] = p1.y;
-            }
-        }
-    }
-    if (slices > 1) {                                      // partial slab of this slice: part[slice][a][ld]
-        float* pp = part + (size_t)blockIdx.y * kOutA * ld;
-#pragma unroll
-        for (int i = 0; i < 6; ++i) {
-            const int a = ty * 6 + i;
-            const int b = b0 + tx * 4;
-            if (b + 4 <= B) *reinterpret_cast<float4*>(pp + (size_t)a * ld + b) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-            else for (int j = 0; j < 4; ++j) if (b + j < B) pp[(size_t)a * ld + b + j] = acc[i][j];
-        }
-        return;
-    }
-#pragma unroll
-    for (int i = 0; i < 6; ++i) {
-        const int a = ty * 6 + i;
-        const float bias = a < n_act ? __ldg(&ob[a]) : 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] += bias;
-    }
-    if (lg) {
-#pragma unroll
-        for (int i = 0; i < 6; ++i) {
-            const int a = ty * 6 + i;
-            if (a >= n_act) continue;
-            float* row = lg + (size_t)a * ld + b0 + tx * 4;
-            if (b0 + tx * 4 + 4 <= B) *reinterpret_cast<float4*>(row) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-            else for (int j = 0; j < 4; ++j) if (b0 + tx * 4 + j < B) row[j] = acc[i][j];
-        }
-    }
-    if (out) {                                            // [64 samples][n_act] rows, staged for coalesced stores
-        __syncthreads();
-        float* st = sm;                                   // 64 x 97 floats (the buffer is sized for them)
-        const int stride = kOutA + 1;
-#pragma unroll
-        for (int i = 0; i < 6; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) st[(tx * 4 + j) * stride + ty * 6 + i] = acc[i][j];
-        __syncthreads();
-        const int nbb = max(0, min(kOutB, B - b0));
-        float* o = out + (size_t)b0 * n_act;
-        for (int i = threadIdx.x; i < nbb * n_act; i += 256) {
-            const int bb = i / n_act, a = i - bb * n_act;
-            o[i] = st[bb * stride + a];
-        }
-    }
-}
 // the slices' partial logits added in slice order + bias -> lg [n_act, ld] and/or out [B, n_act]; a CTA per 32 samples
 __global__ void __launch_bounds__(256) k_out_reduce(const float* __restrict__ part, const float* __restrict__ ob,
                                                     float* __restrict__ lg, float* __restrict__ out, int slices,

@@ -1,0 +1,206 @@
+// Output plug forward on the tensor cores (sm_100a: tcgen05 kind::tf32 MMA, TMEM accumulator, bulk async copies,
+// mbarriers): part[slice][a][b] = sum over the slice's dn columns j of out_w[a, j] * hK[dn[j], b] for one tile of 128
+// samples x 96 actions (90 used, padded with zero weights), the slices' partials then added in order with the bias by
+// k_out_reduce (the slice count is fixed by the graph, so a sample's logits do not depend on the batch it is in).
+//
+// fp32 accuracy from tf32 operands (3 x TF32): each fp32 operand x is split into hi = tf32(x) and lo = tf32(x - hi),
+// and the product is accumulated as hi*hi + hi*lo + lo*hi (the dropped lo*lo term is ~2^-22 of the product); the
+// tensor cores multiply tf32 values exactly and accumulate in fp32.
+//
+// MMA shape M = 128 samples, N = 96 actions, K = 8 columns per instruction, 32 columns (one chunk) per pipeline stage.
+// Both operands are K-major in the canonical no-swizzle core-matrix layout: an operand of R rows x 32 tf32 columns is
+// R/8 x 8 core matrices of 8 rows x 16 bytes (4 columns), core matrix (i, kk) at byte (i * 8 + kk) * 128, row r of it
+// at + r * 16, so LBO (K direction) = 128 B and SBO (8-row groups) = 1024 B.
+//   - out_w is folded into that layout once per weight version (k_fold_ow_tc: [chunk][hi, lo][96 x 32]) and arrives
+//     in shared memory with one bulk copy per stage;
+//   - hK's dn rows are gathered by 8 producer warps: warp w loads columns 4w .. 4w + 3 of the chunk (coalesced 128-byte
+//     rows of 32 samples), splits them and writes each sample's 4 columns as one 16-byte core-matrix row (conflict-free
+//     per quarter warp), then fences the writes for the tensor cores' (async proxy) reads.
+// Warp 8, lane 0 issues the copies and the MMAs; the producer warps then read the accumulator out of TMEM (warp w:
+// lanes 32 (w % 4) .., columns 48 (w / 4) ..) into the partial slab. Every wait is bounded (about 2 s): on expiry the
+// CTA records an error code and stops.
+#pragma once
+#include "fg_tc.cuh"
+
+namespace fg {
+
+constexpr int kOtM = 128, kOtN = 96, kOtKC = 32, kOtStages = 3, kOtProd = 8;
+constexpr int kOtThreads = 32 * (kOtProd + 1);
+constexpr uint32_t kOtA = kOtM * kOtKC * 4;            // one term of a chunk of hK (16 KB)
+constexpr uint32_t kOtB = kOtN * kOtKC * 4;            // one term of a chunk of out_w (12 KB)
+constexpr uint32_t kOtStage = 2 * kOtA + 2 * kOtB;     // A hi, A lo, B hi, B lo
+constexpr int kOtSmem = kOtStages * kOtStage + 128;
+constexpr int kTcErrOutFull = 11, kTcErrOutEmpty = 12, kTcErrOutAcc = 13;
+
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+// kind::tf32 instruction descriptor: fp32 accumulator, A and B tf32 (format 2), both K-major, N = 96, M = 128
+__device__ __forceinline__ constexpr uint32_t out_idesc() {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kOtN >> 3) << 17) | ((uint32_t)(kOtM >> 4) << 24);
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+// out_w [n_act][n_dn] -> wt [chunk][hi, lo][96 x 32] in the operand layout (zero past n_act actions and n_dn columns)
+__global__ void k_fold_ow_tc(const float* __restrict__ ow, float* __restrict__ wt, int n_act, int n_dn, int chunks) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= chunks * kOtN * kOtKC) return;
+    const int c = i / (kOtN * kOtKC), r = i - c * (kOtN * kOtKC), a = r / kOtKC, k = r - a * kOtKC;
+    const int j = c * kOtKC + k;
+    const float w = (a < n_act && j < n_dn) ? __ldg(&ow[(size_t)a * n_dn + j]) : 0.f;
+    const uint32_t hi = to_tf32(w), lo = to_tf32(w - __uint_as_float(hi));
+    const int off = ((a >> 3) * (kOtKC / 4) + (k >> 2)) * 32 + (a & 7) * 4 + (k & 3);
+    float* base = wt + (size_t)c * 2 * kOtN * kOtKC;
+    base[off] = __uint_as_float(hi);
+    base[kOtN * kOtKC + off] = __uint_as_float(lo);
+}
+
+struct OutTc {
+    const float* wt;         // folded out_w, [chunks][hi, lo][96 x 32]
+    const int* dn;           // [n_dn] rows of hK read by the plug
+    const float* hK;         // the top layer [rows][ld], fp32
+    float* part;             // [slices][96][ld]
+    int* err;
+    int n_dn, B, ld, chunks, cps;    // cps: chunks per slice
+};
+
+__global__ void __launch_bounds__(kOtThreads, 1) k_out_tc(const OutTc a) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOtStages * kOtStage);
+    // bars: 0..2 stage full, 3..5 stage empty, 6 accumulator complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b0 = blockIdx.x * kOtM, slice = blockIdx.y;
+    const int c0 = slice * a.cps, n = max(0, min(a.chunks, c0 + a.cps) - c0);
+    const uint32_t bb = smem_u32(bars);
+    auto bar = [&](int i) { return bb + 8u * (uint32_t)i; };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kOtStages; ++s) {
+            mbar_init(bar(s), kOtProd + 1);
+            mbar_init(bar(kOtStages + s), 1);
+        }
+        mbar_init(bar(2 * kOtStages), 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kOtProd) {                                  // the control warp owns the TMEM allocation
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(128)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kOtProd) {
+        if (lane == 0 && n > 0) {
+            constexpr uint32_t idesc = out_idesc();
+            bool ok = true;
+            for (int i = 0; i < n; ++i) {
+                const int s = i % kOtStages, u = i / kOtStages;
+                if (i >= kOtStages && !mbar_wait(bar(kOtStages + s), (u - 1) & 1, abort, a.err, kTcErrOutEmpty)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t ah = smem_u32(smem + (size_t)s * kOtStage), al = ah + kOtA, bh = ah + 2 * kOtA,
+                               bl = bh + kOtB;
+                mbar_expect_tx(bar(s), 2 * kOtB);
+                bulk_g2s(bh, a.wt + (size_t)(c0 + i) * 2 * kOtN * kOtKC, 2 * kOtB, bar(s));
+                if (!mbar_wait(bar(s), u & 1, abort, a.err, kTcErrOutFull)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int ks = 0; ks < kOtKC / 8; ++ks) {
+                    const uint32_t o = (uint32_t)ks * 256u;
+                    mma_tf32(tmem, smem_desc(ah + o, 128u, 1024u), smem_desc(bh + o, 128u, 1024u), idesc,
+                             (i > 0 || ks > 0) ? 1u : 0u);
+                    mma_tf32(tmem, smem_desc(ah + o, 128u, 1024u), smem_desc(bl + o, 128u, 1024u), idesc, 1u);
+                    mma_tf32(tmem, smem_desc(al + o, 128u, 1024u), smem_desc(bh + o, 128u, 1024u), idesc, 1u);
+                }
+                mma_commit(bar(kOtStages + s));
+            }
+            if (ok) mma_commit(bar(2 * kOtStages));
+        }
+        __syncwarp();
+    } else {
+        bool ok = true;
+        for (int i = 0; i < n; ++i) {
+            const int s = i % kOtStages, u = i / kOtStages;
+            if (i >= kOtStages) {
+                const bool w_ok = mbar_wait(bar(kOtStages + s), (u - 1) & 1, abort, a.err, kTcErrOutEmpty);
+                if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
+            }
+            unsigned char* st = smem + (size_t)s * kOtStage;
+            const int j0 = (c0 + i) * kOtKC + 4 * warp;
+            const float* rows[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                rows[k] = j0 + k < a.n_dn ? a.hK + (size_t)__ldg(&a.dn[j0 + k]) * a.ld : nullptr;
+            float v[4][4];
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int b = b0 + lane + 32 * m;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) v[m][k] = (rows[k] && b < a.B) ? __ldg(rows[k] + b) : 0.f;
+            }
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const int sb = lane + 32 * m;
+                uint4 hi, lo;
+                hi.x = to_tf32(v[m][0]); lo.x = to_tf32(v[m][0] - __uint_as_float(hi.x));
+                hi.y = to_tf32(v[m][1]); lo.y = to_tf32(v[m][1] - __uint_as_float(hi.y));
+                hi.z = to_tf32(v[m][2]); lo.z = to_tf32(v[m][2] - __uint_as_float(hi.z));
+                hi.w = to_tf32(v[m][3]); lo.w = to_tf32(v[m][3] - __uint_as_float(hi.w));
+                const uint32_t off = ((uint32_t)(sb >> 3) * (kOtKC / 4) + (uint32_t)warp) * 128u + (uint32_t)(sb & 7) * 16u;
+                *reinterpret_cast<uint4*>(st + off) = hi;
+                *reinterpret_cast<uint4*>(st + kOtA + off) = lo;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> tensor-core reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(s));
+        }
+        // the accumulator into this slice's partial slab: thread = sample 32 (w % 4) + lane, 48 actions
+        const int q = warp & 3, ch = warp >> 2;
+        const int b = b0 + 32 * q + lane;
+        float* pp = a.part + (size_t)slice * kOtN * a.ld + b;
+        if (n == 0) {
+            if (b < a.B)
+                for (int c = 0; c < 48; ++c) pp[(size_t)(48 * ch + c) * a.ld] = 0.f;
+        } else if (ok) {
+            const bool full = mbar_wait(bar(2 * kOtStages), 0, abort, a.err, kTcErrOutAcc);
+            if (__all_sync(0xffffffffu, full)) {
+                tc_fence_after();
+#pragma unroll
+                for (int g = 0; g < 3; ++g) {
+                    uint32_t r[16];
+                    tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(48 * ch + 16 * g), r);
+                    tmem_wait_ld();
+                    if (b < a.B) {
+#pragma unroll
+                        for (int c = 0; c < 16; ++c) pp[(size_t)(48 * ch + 16 * g + c) * a.ld] = __uint_as_float(r[c]);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kOtProd) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128) : "memory");
+    }
+}
+
+}  // namespace fg
