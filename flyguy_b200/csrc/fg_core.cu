@@ -80,6 +80,8 @@ struct Core {
     float* out_part = nullptr;                           // the output plug's per-slice partial logits
     int out_slices = 1;                                  // split-K slices of the dn columns (fixed by the graph)
     float* ow_tc = nullptr;                              // out_w in the tensor-core operand layout (hi, lo terms)
+    float* ow_bt = nullptr;                              // out_w^T in the backward's operand layout (training)
+    int ob_tiles = 0;                                    // 128-column tiles of the dn columns
     int out_chunks = 0, out_cps = 0;                     // 32-column chunks of the dn columns; chunks per slice
     float* seg_part = nullptr;                           // partial rows of split transposed segments
     int* seg_done = nullptr;                             // arrival counters of split rows' segments [red][chunk]
@@ -540,6 +542,8 @@ void alloc_all(Core& c) {
     }
     c.out_part = dalloc<float>(c, (size_t)c.out_slices * kOutA * B);
     c.ow_tc = dalloc<float>(c, (size_t)c.out_chunks * 2 * kOtN * kOtKC);
+    c.ob_tiles = (c.n_dn + kObN - 1) / kObN;
+    if (c.train) c.ow_bt = dalloc<float>(c, (size_t)c.ob_tiles * kObChunks * 2 * kObN * kOtKC);
     c.lg = dalloc<float>(c, (size_t)c.n_act * B);
     c.norm_part = dalloc<float>(c, 1024);
     c.norm = dalloc<float>(c, 4);
@@ -595,6 +599,7 @@ void set_smem_limits(const Core& c) {
     CK(cudaFuncSetAttribute(k_hop_tc<__half, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(kHubMax)));
     CK(cudaFuncSetAttribute(k_hop_tc<__half, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(kHubMax)));
     CK(cudaFuncSetAttribute(k_out_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kOtSmem));
+    CK(cudaFuncSetAttribute(k_out_bwd_h_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kObSmem));
     plug_limit<float, true>(c); plug_limit<float, false>(c);
     plug_limit<__nv_bfloat16, true>(c); plug_limit<__nv_bfloat16, false>(c);
     plug_limit<__half, true>(c); plug_limit<__half, false>(c);
@@ -626,6 +631,9 @@ void fold(Core& c, int which) {
     }
     launch(c, K_FOLD, [&]() { k_fold_ow_tc<<<blocks((long long)c.out_chunks * kOtN * kOtKC), 256, 0, c.st>>>(
                                   src + c.off[5], c.ow_tc, c.n_act, c.n_dn, c.out_chunks); });
+    if (c.ow_bt)
+        launch(c, K_FOLD, [&]() { k_fold_owbt<<<blocks((long long)c.ob_tiles * kObChunks * kObN * kOtKC), 256, 0,
+                                                   c.st>>>(src + c.off[5], c.ow_bt, c.n_act, c.n_dn, c.ob_tiles); });
     launch(c, K_FOLD, [&]() { k_fold_owT<<<blocks((long long)c.n_dn * kOutA), 256, 0, c.st>>>(src + c.off[5], c.owT,
                                                                                          c.n_act, c.n_dn); });
     c.folded = which;
@@ -776,7 +784,6 @@ void backward(Core& c, int B) {
     if (!c.train) throw Err("this handle was created for inference only");
     if (B != c.lastB) throw Err("fc_backward batch differs from the last forward's");
     fold(c, 0);
-    const float* W = c.P;
     CK(cudaMemsetAsync(c.gdrive, 0, (size_t)c.n_s * B * 4, c.st));
     const Hop& top = c.hop.back();
     const float* hK = (const float*)top.d_h;
@@ -796,10 +803,17 @@ void backward(Core& c, int B) {
     float* gz = c.gz_a;                      // gz of the layer being processed
     float* nxt = c.gz_b;                     // gz (or gh0) of the layer below
     // only the output plug's columns of the top layer get a gradient; the other rows of gh / gz are never read
-    launch(c, K_OUT_BWD, [&]() {
-        k_out_bwd_ht<<<dim3((B + kOutB - 1) / kOutB, (c.n_dn + kOutA - 1) / kOutA), 256, 0, c.st>>>(
-            W + c.off[5], c.dl, c.d_dn, nxt, c.n_act, c.n_dn, B, B);
-    });
+    {
+        // gh = out_w^T dl on the tensor cores: 128-sample tiles x runs of 128-column tiles, about one CTA per SM
+        OutBh ob;
+        ob.wt = c.ow_bt; ob.dl = c.dl; ob.dn = c.d_dn; ob.gh = nxt; ob.err = c.d_err;
+        ob.n_act = c.n_act; ob.n_dn = c.n_dn; ob.B = B; ob.ld = B; ob.n_tiles = c.ob_tiles;
+        const int st = (B + 127) / 128;
+        const int groups = std::max(1, std::min(c.ob_tiles, c.n_sm / st));
+        ob.tpg = (c.ob_tiles + groups - 1) / groups;
+        const int ng = (c.ob_tiles + ob.tpg - 1) / ob.tpg;
+        launch(c, K_OUT_BWD, [&]() { k_out_bwd_h_tc<<<dim3(st, ng), kOtThreads, kObSmem, c.st>>>(ob); });
+    }
     if (top.n_live_dst)
     launch(c, K_ACT_BWD, [&]() {
         k_act_bwd<float><<<top.n_live_dst, kThreads, 0, c.st>>>(nxt, hK, top.d_nid, top.d_drow,

@@ -699,58 +699,6 @@ __global__ void __launch_bounds__(256) k_out_bwd_wt(const float* __restrict__ dl
         }
     }
 }
-// gh[dn[j], b] = sum_a out_w[a, j] * dl[a, b] as a register-blocked product: a CTA owns 96 output-plug columns x 64
-// samples, each thread 6 columns x 4 samples; out_w rows and dl rows are staged 32 actions at a time.
-__global__ void __launch_bounds__(256) k_out_bwd_ht(const float* __restrict__ ow, const float* __restrict__ dl,
-                                                    const int* __restrict__ dn, float* __restrict__ gh, int n_act,
-                                                    int n_dn, int B, int ld) {
-    __shared__ __align__(16) float As[kOutK][kOutA];      // [action][column]
-    __shared__ __align__(16) float Bs[kOutK][kOutB];      // [action][sample]
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    const int b0 = blockIdx.x * kOutB, j0 = blockIdx.y * kOutA;
-    float acc[6][4];
-#pragma unroll
-    for (int i = 0; i < 6; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-    for (int a0 = 0; a0 < n_act; a0 += kOutK) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < kOutK * kOutA; i += 256) {
-            const int k = i / kOutA, m = i - k * kOutA, a = a0 + k, j = j0 + m;
-            As[k][m] = (a < n_act && j < n_dn) ? __ldg(&ow[(size_t)a * n_dn + j]) : 0.f;
-        }
-        for (int i = threadIdx.x; i < kOutK * kOutB; i += 256) {
-            const int k = i / kOutB, n = i - k * kOutB, a = a0 + k, b = b0 + n;
-            Bs[k][n] = (a < n_act && b < B) ? __ldg(&dl[(size_t)a * ld + b]) : 0.f;
-        }
-        __syncthreads();
-#pragma unroll 8
-        for (int k = 0; k < kOutK; ++k) {
-            const float4 d = *reinterpret_cast<const float4*>(&Bs[k][tx * 4]);
-            const float2 w01 = *reinterpret_cast<const float2*>(&As[k][ty * 6]);
-            const float2 w23 = *reinterpret_cast<const float2*>(&As[k][ty * 6 + 2]);
-            const float2 w45 = *reinterpret_cast<const float2*>(&As[k][ty * 6 + 4]);
-            const float dv[4] = {d.x, d.y, d.z, d.w};
-            const float wv[6] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y};
-#pragma unroll
-            for (int i = 0; i < 6; ++i) {                         // two packed fp32x2 FMAs (same rounding)
-                const float2 w2 = make_float2(wv[i], wv[i]);
-                const float2 p0 = __ffma2_rn(w2, make_float2(dv[0], dv[1]), make_float2(acc[i][0], acc[i][1]));
-                const float2 p1 = __ffma2_rn(w2, make_float2(dv[2], dv[3]), make_float2(acc[i][2], acc[i][3]));
-                acc[i][0] = p0.x; acc[i][1] = p0.y; acc[i][2] = p1.x; acc[i][3] = p1.y;
-            }
-        }
-    }
-    const int b = b0 + tx * 4;
-    if (b >= B) return;
-#pragma unroll
-    for (int i = 0; i < 6; ++i) {
-        const int j = j0 + ty * 6 + i;
-        if (j < n_dn)
-            *reinterpret_cast<float4*>(gh + (size_t)__ldg(&dn[j]) * ld + b) =
-                make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-    }
-}
 // G_out_w[a*n_dn + j] += sum_s part[s][a][j]; G_out_b[a] += sum_s part[s][a][n_dn]
 __global__ void k_out_bwd_reduce(const float* __restrict__ part, float* __restrict__ gow, float* __restrict__ gob,
                                  int n_act, int n_dn, int splits) {

@@ -203,4 +203,201 @@ __global__ void __launch_bounds__(kOtThreads, 1) k_out_tc(const OutTc a) {
     }
 }
 
+
+// ---------------------------------------------------------------- output plug backward: gh = out_w^T dl
+// gh[dn[j], b] = sum_a out_w[a, j] * dl[a, b] on the tensor cores, the same 3 x TF32 split: M = 128 samples, N = 128 dn
+// columns per column tile, K = the 96 (padded) actions in 3 chunks of 32. A CTA owns one 128-sample tile and a run of
+// column tiles: its 8 producer warps gather and split dl's rows once (the A operand, all 3 chunks, resident in shared
+// memory; lane l loads samples 4l .. 4l + 3 of 4 action rows with 16-byte loads and writes each sample's 4 actions as
+// one core-matrix row), the control thread streams each column tile's folded out_w (k_fold_owbt:
+// [column tile][chunk][hi, lo][128 x 32]) through a 3-stage bulk-copy ring and issues the MMAs into one of two TMEM
+// accumulators, and the same 8 warps then read each finished tile out (warp w: samples 32 (w % 4) .., columns
+// 64 (w / 4) ..) and write its gh rows (a warp store = 32 consecutive samples of one row).
+constexpr int kObN = 128, kObChunks = 3;
+// dl^T's operand: 128 samples x 32 actions per chunk and term, 8-row groups 1040 B apart (one 16-byte pad each), so the
+// 16-byte rows a quarter warp writes (lane l: samples 4l .. 4l + 3) fall in 8 different bank groups
+constexpr uint32_t kObSBO = 8 * 128 + 16;
+constexpr uint32_t kObA = 128 / 8 * kObSBO;
+constexpr uint32_t kObB = kObN * kOtKC * 4;                     // one term of one chunk of out_w^T (16 KB)
+constexpr uint32_t kObStage = 2 * kObB;
+constexpr int kObSmem = kObChunks * 2 * kObA + 3 * kObStage + 128;
+constexpr int kTcErrObA = 21, kTcErrObW = 22, kTcErrObEmpty = 23, kTcErrObAccEmpty = 24, kTcErrObAccFull = 25;
+static_assert(kObChunks * kOtKC == 96, "the padded action count");
+
+__device__ __forceinline__ constexpr uint32_t ob_idesc() {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kObN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+// out_w [n_act][n_dn] -> wt [column tile][chunk][hi, lo][128 columns x 32 actions] in the K-major operand layout
+__global__ void k_fold_owbt(const float* __restrict__ ow, float* __restrict__ wt, int n_act, int n_dn, int n_tiles) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_tiles * kObChunks * kObN * kOtKC) return;
+    const int blk = i / (kObN * kOtKC), r = i - blk * (kObN * kOtKC);
+    const int t = blk / kObChunks, c = blk - t * kObChunks;
+    const int j = r / kOtKC, k = r - j * kOtKC;
+    const int col = t * kObN + j, a = c * kOtKC + k;
+    const float w = (a < n_act && col < n_dn) ? __ldg(&ow[(size_t)a * n_dn + col]) : 0.f;
+    const uint32_t hi = to_tf32(w), lo = to_tf32(w - __uint_as_float(hi));
+    const int off = ((j >> 3) * (kOtKC / 4) + (k >> 2)) * 32 + (j & 7) * 4 + (k & 3);
+    float* base = wt + (size_t)blk * 2 * kObN * kOtKC;
+    base[off] = __uint_as_float(hi);
+    base[kObN * kOtKC + off] = __uint_as_float(lo);
+}
+
+struct OutBh {
+    const float* wt;         // folded out_w^T
+    const float* dl;         // [n_act][ld]
+    const int* dn;
+    float* gh;               // the top layer's gradient rows [rows][ld]; rows dn[j] are written
+    int* err;
+    int n_act, n_dn, B, ld, n_tiles, tpg;    // column tiles; column tiles per CTA
+};
+
+__global__ void __launch_bounds__(kOtThreads, 1) k_out_bwd_h_tc(const OutBh a) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    unsigned char* sa = smem;                                      // A: [chunk][hi, lo] of kObA bytes
+    unsigned char* sw = smem + kObChunks * 2 * kObA;               // W ring: 3 stages of [hi, lo]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sw + 3 * kObStage);
+    // bars: 0 A ready, 1..3 W full, 4..6 W empty, 7..8 accumulator full, 9..10 accumulator empty
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b0 = blockIdx.x * 128, t0 = blockIdx.y * a.tpg;
+    const int nt = max(0, min(a.n_tiles, t0 + a.tpg) - t0);
+    const uint32_t bb = smem_u32(bars);
+    auto bar = [&](int i) { return bb + 8u * (uint32_t)i; };
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar(0), kOtProd);
+        for (int s = 0; s < 3; ++s) {
+            mbar_init(bar(1 + s), 1);
+            mbar_init(bar(4 + s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bar(7 + b), 1);
+            mbar_init(bar(9 + b), kOtProd);
+        }
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kOtProd) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(256)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kOtProd) {
+        if (lane == 0 && nt > 0) {
+            constexpr uint32_t idesc = ob_idesc();
+            const int n = nt * kObChunks;                          // chunks over all of this CTA's column tiles
+            auto copy_w = [&](int g) {
+                const int s = g % 3, t = t0 + g / kObChunks, c = g % kObChunks;
+                mbar_expect_tx(bar(1 + s), kObStage);
+                bulk_g2s(smem_u32(sw + (size_t)s * kObStage),
+                         a.wt + ((size_t)t * kObChunks + c) * 2 * kObN * kOtKC, kObStage, bar(1 + s));
+            };
+            bool ok = true;
+            for (int g = 0; g < min(n, 3); ++g) copy_w(g);
+            if (!mbar_wait(bar(0), 0, abort, a.err, kTcErrObA)) ok = false;
+            for (int g = 0; ok && g < n; ++g) {
+                const int s = g % 3, c = g % kObChunks, it = g / kObChunks, ab = it & 1;
+                if (c == 0 && it >= 2 &&
+                    !mbar_wait(bar(9 + ab), ((it >> 1) - 1) & 1, abort, a.err, kTcErrObAccEmpty)) { ok = false; break; }
+                if (!mbar_wait(bar(1 + s), (g / 3) & 1, abort, a.err, kTcErrObW)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t ah = smem_u32(sa + (size_t)c * 2 * kObA), al = ah + kObA;
+                const uint32_t wh = smem_u32(sw + (size_t)s * kObStage), wl = wh + kObB;
+                const uint32_t d = tmem + (uint32_t)(ab * kObN);
+#pragma unroll
+                for (int ks = 0; ks < kOtKC / 8; ++ks) {
+                    const uint32_t o = (uint32_t)ks * 256u;
+                    mma_tf32(d, smem_desc(ah + o, 128u, kObSBO), smem_desc(wh + o, 128u, 1024u), idesc,
+                             (c > 0 || ks > 0) ? 1u : 0u);
+                    mma_tf32(d, smem_desc(ah + o, 128u, kObSBO), smem_desc(wl + o, 128u, 1024u), idesc, 1u);
+                    mma_tf32(d, smem_desc(al + o, 128u, kObSBO), smem_desc(wh + o, 128u, 1024u), idesc, 1u);
+                }
+                mma_commit(bar(4 + s));
+                if (c == kObChunks - 1) mma_commit(bar(7 + ab));
+                if (g >= 1 && g + 2 < n) {                         // refill the previous chunk's stage
+                    const int sp = (g - 1) % 3;
+                    if (!mbar_wait(bar(4 + sp), ((g - 1) / 3) & 1, abort, a.err, kTcErrObEmpty)) { ok = false; break; }
+                    copy_w(g + 2);
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // A: dl's rows for this sample tile, transposed and split; warp w: actions 4w .. 4w + 3 of each chunk
+        const int bl = b0 + 4 * lane;
+        const bool in = bl < a.B;
+        for (int c = 0; c < kObChunks; ++c) {
+            float4 v[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int act = c * kOtKC + 4 * warp + k;
+                v[k] = (in && act < a.n_act) ? __ldg(reinterpret_cast<const float4*>(a.dl + (size_t)act * a.ld + bl))
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            unsigned char* st = sa + (size_t)c * 2 * kObA;
+            const float* f0 = &v[0].x;
+            const float* f1 = &v[1].x;
+            const float* f2 = &v[2].x;
+            const float* f3 = &v[3].x;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int sb = 4 * lane + q;
+                uint4 hi, lo;
+                hi.x = to_tf32(f0[q]); lo.x = to_tf32(f0[q] - __uint_as_float(hi.x));
+                hi.y = to_tf32(f1[q]); lo.y = to_tf32(f1[q] - __uint_as_float(hi.y));
+                hi.z = to_tf32(f2[q]); lo.z = to_tf32(f2[q] - __uint_as_float(hi.z));
+                hi.w = to_tf32(f3[q]); lo.w = to_tf32(f3[q] - __uint_as_float(hi.w));
+                const uint32_t off = (uint32_t)(sb >> 3) * kObSBO + (uint32_t)warp * 128u + (uint32_t)(sb & 7) * 16u;
+                *reinterpret_cast<uint4*>(st + off) = hi;
+                *reinterpret_cast<uint4*>(st + kObA + off) = lo;
+            }
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(0));
+        // epilogue: each finished column tile into gh
+        const int q = warp & 3, ch = warp >> 2;
+        const int b = b0 + 32 * q + lane;
+        for (int it = 0; it < nt; ++it) {
+            const int ab = it & 1;
+            const bool full = mbar_wait(bar(7 + ab), (it >> 1) & 1, abort, a.err, kTcErrObAccFull);
+            if (!__all_sync(0xffffffffu, full)) break;
+            tc_fence_after();
+            uint32_t r[4][16];
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * kObN + 64 * ch + 16 * g), r[g]);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(9 + ab));
+            const int j0 = (t0 + it) * kObN + 64 * ch;
+            if (b < a.B) {
+#pragma unroll
+                for (int g = 0; g < 4; ++g)
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int j = j0 + 16 * g + e;
+                        if (j < a.n_dn) a.gh[(size_t)__ldg(&a.dn[j]) * a.ld + b] = __uint_as_float(r[g][e]);
+                    }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kOtProd) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+    }
+}
+
 }  // namespace fg
