@@ -600,6 +600,7 @@ void set_smem_limits(const Core& c) {
     CK(cudaFuncSetAttribute(k_hop_tc<__half, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(kHubMax)));
     CK(cudaFuncSetAttribute(k_out_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kOtSmem));
     CK(cudaFuncSetAttribute(k_out_bwd_h_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kObSmem));
+    CK(cudaFuncSetAttribute(k_out_bwd_w_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kOwSmem));
     plug_limit<float, true>(c); plug_limit<float, false>(c);
     plug_limit<__nv_bfloat16, true>(c); plug_limit<__nv_bfloat16, false>(c);
     plug_limit<__half, true>(c); plug_limit<__half, false>(c);
@@ -787,14 +788,18 @@ void backward(Core& c, int B) {
     CK(cudaMemsetAsync(c.gdrive, 0, (size_t)c.n_s * B * 4, c.st));
     const Hop& top = c.hop.back();
     const float* hK = (const float*)top.d_h;
-    // weight gradient: 64-column tiles x batch slices, about two waves of CTAs (slices of at least 128 samples)
-    const int wtiles = (c.n_dn + 1 + kOutB - 1) / kOutB;
-    const int splits = std::max(1, std::min({c.out_splits, (2 * c.n_sm + wtiles - 1) / wtiles, B / 128}));
-    const int split_len = ((B + splits - 1) / splits + 31) / 32 * 32;
-    launch(c, K_OUT_BWD, [&]() {
-        k_out_bwd_wt<float><<<dim3(wtiles, splits), 256, 0, c.st>>>(c.dl, hK, c.d_dn, c.part, c.n_act, c.n_dn, B,
-                                                                    split_len, B);
-    });
+    // weight gradient on the tensor cores: 128-column tiles x batch slices (multiples of 32 samples), about two
+    // waves of CTAs; k_out_bwd_reduce adds the slices in order
+    const int wtiles = (c.n_dn + 1 + 127) / 128;
+    const int want = std::max(1, std::min({c.out_splits, (2 * c.n_sm + wtiles - 1) / wtiles, B / 32}));
+    const int split_len = ((B + want - 1) / want + 31) / 32 * 32;
+    const int splits = (B + split_len - 1) / split_len;
+    {
+        OutBw ow;
+        ow.dl = c.dl; ow.hK = hK; ow.dn = c.d_dn; ow.part = c.part; ow.err = c.d_err;
+        ow.n_act = c.n_act; ow.n_dn = c.n_dn; ow.B = B; ow.ld = B; ow.slice_len = split_len;
+        launch(c, K_OUT_BWD, [&]() { k_out_bwd_w_tc<<<dim3(wtiles, splits), kOtThreads, kOwSmem, c.st>>>(ow); });
+    }
     launch(c, K_OUT_BWD, [&]() {
         k_out_bwd_reduce<<<blocks((long long)c.n_act * (c.n_dn + 1)), 256, 0, c.st>>>(c.part, c.G + c.off[5],
                                                                                      c.G + c.off[6], c.n_act, c.n_dn,
@@ -1140,7 +1145,7 @@ int fg_teach_ex(void* h, const float* obs, const float* teacher, int B, float in
         forward(c, obs, B, logits, 0, true);
         CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
         launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, kLossS), kLossT, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp, 1.f / loss_norm); });
-        launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
+        launch(c, K_LOSS, [&]() { k_loss_stats<<<1, kStatsT, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
         backward(c, B);
         if (stats) {
             float s[2];
@@ -1180,7 +1185,7 @@ int fg_survey(void* h, const float* obs, const float* teacher, int B, int ema, i
         if (loss) {
             CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
             launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, kLossS), kLossT, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, 1.f, 1.f / B); });
-            launch(c, K_LOSS, [&]() { k_loss_stats<<<1, 256, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
+            launch(c, K_LOSS, [&]() { k_loss_stats<<<1, kStatsT, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
             float s[2];
             CK(cudaMemcpyAsync(s, c.stats, 8, cudaMemcpyDeviceToHost, c.st));
             CK(cudaStreamSynchronize(c.st));

@@ -626,14 +626,30 @@ __global__ void __launch_bounds__(kLossT) k_loss(const float* __restrict__ lg, c
     for (int a = a0; a < n_act; a += kLossT / kLossS)
         if (j < nb) dl[(size_t)a * ld + b0 + j] = sl[a * kLossS + j];
 }
-// stats[0] = sum kl, stats[1] = sum agree (one CTA, fixed order)
-__global__ void k_loss_stats(const float* __restrict__ kl_s, const float* __restrict__ ag_s, float* __restrict__ stats,
-                             int B) {
-    __shared__ float red[2 * kWarps];
-    float v[2] = {0.f, 0.f};
-    for (int b = threadIdx.x; b < B; b += blockDim.x) { v[0] += kl_s[b]; v[1] += ag_s[b]; }
-    block_sum<2>(v, red);
-    if (threadIdx.x == 0) { stats[0] += v[0]; stats[1] += v[1]; }
+// stats[0] += sum kl, stats[1] += sum agree: one CTA of 1,024 threads, 4 samples per thread step (B is a multiple of
+// 32), warp sums then the 32 warp sums in warp order - a fixed order for a given batch
+constexpr int kStatsT = 1024;
+__global__ void __launch_bounds__(kStatsT) k_loss_stats(const float* __restrict__ kl_s, const float* __restrict__ ag_s,
+                                                         float* __restrict__ stats, int B) {
+    __shared__ float red[2][kStatsT / 32];
+    float v0 = 0.f, v1 = 0.f;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < (B >> 2); i += kStatsT) {
+        const float4 k = __ldg(reinterpret_cast<const float4*>(kl_s) + i);
+        const float4 g = __ldg(reinterpret_cast<const float4*>(ag_s) + i);
+        v0 += (k.x + k.y) + (k.z + k.w);
+        v1 += (g.x + g.y) + (g.z + g.w);
+    }
+    v0 = warp_sum(v0);
+    v1 = warp_sum(v1);
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { red[0][w] = v0; red[1][w] = v1; }
+    __syncthreads();
+    if (w == 0) {
+        v0 = warp_sum(red[0][lane]);
+        v1 = warp_sum(red[1][lane]);
+        if (lane == 0) { stats[0] += v0; stats[1] += v1; }
+    }
 }
 
 // ---------------------------------------------------------------- backward: output plug

@@ -400,4 +400,186 @@ __global__ void __launch_bounds__(kOtThreads, 1) k_out_bwd_h_tc(const OutBh a) {
     }
 }
 
+// ---------------------------------------------------------------- output plug backward: gW = dl h^T
+// part[slice][a][j] = sum over the slice's samples b of dl[a, b] * h[dn[j], b] (column j = n_dn is the bias: h = 1) on
+// the tensor cores, the same 3 x TF32 split: M = 128 columns, N = 96 (padded) actions, K = the slice's samples in chunks
+// of 32. Both operands are K-major as they lie in memory (rows of samples), so 8 producer warps only gather, split and
+// place them: a warp load reads 4 rows x 32 samples (lane l: row l / 8, samples 4 (l % 8) ..), and each lane writes its
+// 4 samples as one 16-byte core-matrix row. The K-direction stride is padded to 144 B (LBO; 8-row groups 1152 B apart),
+// so the 8 rows a quarter warp writes (core matrices 0..7 along K) fall in 8 different bank groups. The loads of the
+// next chunk are issued before this chunk is written. The slices' partials are added in order by k_out_bwd_reduce.
+constexpr uint32_t kOwLBO = 144, kOwSBO = 8 * kOwLBO;
+constexpr uint32_t kOwA = 128 / 8 * kOwSBO, kOwB = 96 / 8 * kOwSBO;
+constexpr uint32_t kOwStage = 2 * kOwA + 2 * kOwB;
+constexpr int kOwStages = 3, kOwRowGroups = (128 + 96) / 4;       // 4-row load groups per chunk (7 per warp)
+constexpr int kOwSmem = kOwStages * kOwStage + 128;
+constexpr int kTcErrOwFull = 31, kTcErrOwEmpty = 32, kTcErrOwAcc = 33;
+static_assert(kOwRowGroups % kOtProd == 0, "row groups split evenly over the producer warps");
+
+__device__ __forceinline__ constexpr uint32_t ow_idesc() {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(96 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+struct OutBw {
+    const float* dl;         // [n_act][ld]
+    const float* hK;         // the top layer [rows][ld]
+    const int* dn;
+    float* part;             // [slices][n_act][n_dn + 1]
+    int* err;
+    int n_act, n_dn, B, ld, slice_len;      // slice_len: a multiple of 32
+};
+
+__global__ void __launch_bounds__(kOtThreads, 1) k_out_bwd_w_tc(const OutBw a) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOwStages * kOwStage);
+    // bars: 0..2 stage full, 3..5 stage empty, 6 accumulator complete
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j0 = blockIdx.x * 128, slice = blockIdx.y;
+    const int s0 = slice * a.slice_len, s1 = min(a.B, s0 + a.slice_len);
+    const int n = max(0, (s1 - s0 + kOtKC - 1) / kOtKC);
+    const uint32_t bb = smem_u32(bars);
+    auto bar = [&](int i) { return bb + 8u * (uint32_t)i; };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kOwStages; ++s) {
+            mbar_init(bar(s), kOtProd);
+            mbar_init(bar(kOwStages + s), 1);
+        }
+        mbar_init(bar(2 * kOwStages), 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kOtProd) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(128)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kOtProd) {
+        if (lane == 0 && n > 0) {
+            constexpr uint32_t idesc = ow_idesc();
+            bool ok = true;
+            for (int i = 0; i < n; ++i) {
+                const int s = i % kOwStages, u = i / kOwStages;
+                if (!mbar_wait(bar(s), u & 1, abort, a.err, kTcErrOwFull)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t ah = smem_u32(smem + (size_t)s * kOwStage), al = ah + kOwA, bh = ah + 2 * kOwA,
+                               bl = bh + kOwB;
+#pragma unroll
+                for (int ks = 0; ks < kOtKC / 8; ++ks) {
+                    const uint32_t o = (uint32_t)ks * 2u * kOwLBO;
+                    mma_tf32(tmem, smem_desc(ah + o, kOwLBO, kOwSBO), smem_desc(bh + o, kOwLBO, kOwSBO), idesc,
+                             (i > 0 || ks > 0) ? 1u : 0u);
+                    mma_tf32(tmem, smem_desc(ah + o, kOwLBO, kOwSBO), smem_desc(bl + o, kOwLBO, kOwSBO), idesc, 1u);
+                    mma_tf32(tmem, smem_desc(al + o, kOwLBO, kOwSBO), smem_desc(bh + o, kOwLBO, kOwSBO), idesc, 1u);
+                }
+                mma_commit(bar(kOwStages + s));
+            }
+            if (ok) mma_commit(bar(2 * kOwStages));
+        }
+        __syncwarp();
+    } else {
+        const int rsub = lane >> 3, kk = lane & 7;         // row within a load group, core matrix along K
+        constexpr int kG = kOwRowGroups / kOtProd;         // 7 load groups per warp
+        // this lane's rows: A rows 0..127 (columns j0 + row; dn gathered; the bias column reads ones), B rows 128..223
+        // (actions)
+        const float* src[kG];
+        bool ones[kG];
+#pragma unroll
+        for (int g = 0; g < kG; ++g) {
+            const int row = 4 * (warp + kOtProd * g) + rsub;
+            src[g] = nullptr;
+            ones[g] = false;
+            if (row < 128) {
+                const int j = j0 + row;
+                if (j < a.n_dn) src[g] = a.hK + (size_t)__ldg(&a.dn[j]) * a.ld;
+                else ones[g] = j == a.n_dn;
+            } else if (row - 128 < a.n_act) {
+                src[g] = a.dl + (size_t)(row - 128) * a.ld;
+            }
+        }
+        auto load = [&](int i, float4 (&v)[kG]) {
+            const int b = s0 + i * kOtKC + 4 * kk;
+            const bool in = b < s1;
+#pragma unroll
+            for (int g = 0; g < kG; ++g)
+                v[g] = (in && src[g]) ? __ldg(reinterpret_cast<const float4*>(src[g] + b))
+                                      : (in && ones[g] ? make_float4(1.f, 1.f, 1.f, 1.f) : make_float4(0.f, 0.f, 0.f, 0.f));
+        };
+        bool ok = true;
+        float4 cur[kG], nxt[kG];
+        if (n > 0) load(0, cur);
+        for (int i = 0; i < n; ++i) {
+            const int s = i % kOwStages, u = i / kOwStages;
+            if (i + 1 < n) load(i + 1, nxt);
+            if (i >= kOwStages) {
+                const bool w_ok = mbar_wait(bar(kOwStages + s), (u - 1) & 1, abort, a.err, kTcErrOwEmpty);
+                if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
+            }
+            unsigned char* st = smem + (size_t)s * kOwStage;
+#pragma unroll
+            for (int g = 0; g < kG; ++g) {
+                const int row = 4 * (warp + kOtProd * g) + rsub;
+                const bool is_a = row < 128;
+                const int r = is_a ? row : row - 128;
+                uint4 hi, lo;
+                hi.x = to_tf32(cur[g].x); lo.x = to_tf32(cur[g].x - __uint_as_float(hi.x));
+                hi.y = to_tf32(cur[g].y); lo.y = to_tf32(cur[g].y - __uint_as_float(hi.y));
+                hi.z = to_tf32(cur[g].z); lo.z = to_tf32(cur[g].z - __uint_as_float(hi.z));
+                hi.w = to_tf32(cur[g].w); lo.w = to_tf32(cur[g].w - __uint_as_float(hi.w));
+                const uint32_t off = (uint32_t)(r >> 3) * kOwSBO + (uint32_t)kk * kOwLBO + (uint32_t)(r & 7) * 16u;
+                unsigned char* base = st + (is_a ? 0u : 2u * kOwA);
+                const uint32_t term = is_a ? kOwA : kOwB;
+                *reinterpret_cast<uint4*>(base + off) = hi;
+                *reinterpret_cast<uint4*>(base + term + off) = lo;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(s));
+#pragma unroll
+            for (int g = 0; g < kG; ++g) cur[g] = nxt[g];
+        }
+        // the accumulator (lane = column j, TMEM column = action) into this slice's partials
+        const int q = warp & 3, ch = warp >> 2;
+        const int j = j0 + 32 * q + lane, n_col = a.n_dn + 1;
+        float* pp = a.part + (size_t)slice * a.n_act * n_col + j;
+        if (n == 0) {
+            if (j < n_col)
+                for (int c = 0; c < 48; ++c)
+                    if (48 * ch + c < a.n_act) pp[(size_t)(48 * ch + c) * n_col] = 0.f;
+        } else if (ok) {
+            const bool full = mbar_wait(bar(2 * kOwStages), 0, abort, a.err, kTcErrOwAcc);
+            if (__all_sync(0xffffffffu, full)) {
+                tc_fence_after();
+#pragma unroll
+                for (int g = 0; g < 3; ++g) {
+                    uint32_t r[16];
+                    tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(48 * ch + 16 * g), r);
+                    tmem_wait_ld();
+                    if (j < n_col) {
+#pragma unroll
+                        for (int c = 0; c < 16; ++c) {
+                            const int act = 48 * ch + 16 * g + c;
+                            if (act < a.n_act) pp[(size_t)act * n_col] = __uint_as_float(r[c]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kOtProd) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128) : "memory");
+    }
+}
+
 }  // namespace fg
