@@ -76,7 +76,6 @@ struct Core {
     std::vector<int> sizes;
     int maxB = 0, flags = 0;
     bool bf16 = false, f16 = false, train = true, redrive = false;
-    float* owT = nullptr;                                // out_w transposed, padded to kOutA actions
     float* out_part = nullptr;                           // the output plug's per-slice partial logits
     int out_slices = 1;                                  // split-K slices of the dn columns (fixed by the graph)
     float* ow_tc = nullptr;                              // out_w in the tensor-core operand layout (hi, lo terms)
@@ -480,6 +479,7 @@ void upload_net(Core& c, NetHost& n) {
     c.d_rgain = dalloc<float>(c, c.R);
     c.d_rthr = dalloc<float>(c, c.R);
     c.d_rsig = dalloc<float>(c, c.R);
+    pairs.push_back(make_int2(0, 0));       // one record past the end: the hop forward reads a pair ahead
     c.d_pairs = upload(c, pairs);
     c.d_tpairs = upload(c, tpairs);
     c.d_gptr = upload(c, gptr);
@@ -521,7 +521,6 @@ void alloc_all(Core& c) {
         h.out_f32 = act_bytes(c) == 4 || k + 1 == c.hop.size();
         h.d_h = dalloc<char>(c, (size_t)h.rows * B * (h.out_f32 ? 4 : act_bytes(c)));
     }
-    c.owT = dalloc<float>(c, (size_t)c.n_dn * kOutA);
     c.d_err = dalloc<int>(c, 1);
     CK(cudaMemset(c.d_err, 0, sizeof(int)));
     CK(cudaDeviceGetAttribute(&c.n_sm, cudaDevAttrMultiProcessorCount, c.device));
@@ -635,8 +634,6 @@ void fold(Core& c, int which) {
     if (c.ow_bt)
         launch(c, K_FOLD, [&]() { k_fold_owbt<<<blocks((long long)c.ob_tiles * kObChunks * kObN * kOtKC), 256, 0,
                                                    c.st>>>(src + c.off[5], c.ow_bt, c.n_act, c.n_dn, c.ob_tiles); });
-    launch(c, K_FOLD, [&]() { k_fold_owT<<<blocks((long long)c.n_dn * kOutA), 256, 0, c.st>>>(src + c.off[5], c.owT,
-                                                                                         c.n_act, c.n_dn); });
     c.folded = which;
 }
 
@@ -649,12 +646,20 @@ void check_batch(const Core& c, int B) {
 template <class T, bool SAVE>
 void plug_launch(Core& c, const float* Pw, int B) {
     const int chunks = (B + PlugCfg<T>::cols - 1) / PlugCfg<T>::cols;
-    // enough row blocks for ~2 waves of CTAs, each block at least 64 rows (the staged chunk is shared by its rows)
-    const int nblk = std::max(1, std::min((c.n_s + 63) / 64, (2 * 148 + chunks - 1) / chunks));
+    // row blocks per chunk: the count whose whole waves of CTAs cost least, a CTA's time taken as its rows plus the
+    // staging of its x chunk (about as long as 264 rows); at most one block per 64 rows
+    const int smem = plug_smem<T>(c);
+    const int per_sm = std::max(1, std::min(2048 / kPlugThreads, 233472 / (smem + 1024)));
+    int nblk = 1;
+    long long best = -1;
+    for (int k = 1; k <= std::max(1, std::min(64, (c.n_s + 63) / 64)); ++k) {
+        const long long waves = ((long long)chunks * k + (long long)c.n_sm * per_sm - 1) / ((long long)c.n_sm * per_sm);
+        const long long cost = waves * ((c.n_s + k - 1) / k + 264);
+        if (best < 0 || cost < best) { best = cost; nblk = k; }
+    }
     const int rows = (c.n_s + nblk - 1) / nblk;
     const dim3 g(nblk, chunks);
     launch(c, K_PLUG_FWD, [&]() {
-        const int smem = plug_smem<T>(c);
         if (c.fan == 8)
             k_plug_fwd<T, SAVE, 8><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
                 c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);

@@ -164,13 +164,6 @@ __global__ void __launch_bounds__(kThreads) k_fold_pairs(const int* __restrict__
     }
 }
 
-// out_w [n_act][n_dn] -> owT [n_dn][kOutA] (actions padded with zeros), the output plug's operand layout
-__global__ void k_fold_owT(const float* __restrict__ ow, float* __restrict__ owT, int n_act, int n_dn) {
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n_dn * 96) return;
-    int j = i / 96, a = i - j * 96;
-    owT[i] = a < n_act ? ow[(size_t)a * n_dn + j] : 0.f;
-}
 
 // ---------------------------------------------------------------- layout changes at the API boundary
 // in [B, D] (sample-major, the caller's) -> out [D, ld] (neuron-major); 32x32 tiles through shared memory
@@ -331,10 +324,10 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
 }
 
 // one hop: z[t,b] = sum over merged pairs (src, w) of row t of w * hp[src, b] (+ drive[drow[t], b]);
-// h = relu(gain*z - thr). One warp per (row, chunk of 2*32*V samples): each lane loads two 16-byte groups of the
+// h = relu(gain*z - thr). One warp per (row, chunk of NG*32*V samples): each lane loads NG 16-byte groups of the
 // source row per pair, the warp's loads of a group being one contiguous 512-byte run (group g of lane l: samples
-// chunk + g*32V + l*V ... + V-1), so the pair record and its address math are shared by 2V FMAs per lane; products use
-// packed fp32x2 FMAs (sm_100). Rows run in degree-descending schedule order.
+// chunk + g*32V + l*V ... + V-1), so the pair record and its address math are shared by NG*V FMAs per lane; products
+// use packed fp32x2 FMAs (sm_100). Rows run in degree-descending schedule order.
 // TI: the source layer's type, TO: this layer's (the last layer of a 16-bit network is fp32).
 __device__ __forceinline__ void unpack2(const __nv_bfloat16*, uint32_t x, float2& f) {
     f = make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
@@ -354,8 +347,6 @@ __device__ __forceinline__ void ld16(const T* p, float2 (&v)[16 / sizeof(T) / 2]
     }
 }
 template <class T> struct Vec16 { static constexpr int V = 16 / sizeof(T), H = V / 2; };
-template <class T> struct Lane32 { static constexpr int N = 32 / sizeof(T); };   // states per lane per pair
-                                                                                 // (warp chunk = 32 * N samples)
 
 template <class TO, int V>
 __device__ __forceinline__ void st16(TO* o, const float* hv) {
@@ -368,20 +359,41 @@ __device__ __forceinline__ void st16(TO* o, const float* hv) {
     }
 }
 
-// FULL: the warp's whole chunk lies inside the batch (ld a multiple of 64 V): no per-pair validity tests.
-// UNR pairs per step: their records and 2 UNR 16-byte gathers are issued before any of their products, so each warp
-// keeps 2 UNR loads in flight (the gathers are L2-latency bound when sources are spread out). Resident CTAs per SM the
-// register allocation is sized for: HopOcc (more warps in flight also hide the gathers' latency).
-#ifndef FG_HOP_UNR
-#define FG_HOP_UNR 2
+// Per source-state type (measured at batch 65,536 bf16 / 16,384 and 4,096 fp32 on the Zipf graph):
+//   NG  16-byte groups per lane per pair - the pair record, its address and the loop are shared by NG x V samples
+//       (16-bit: 4 -> 32 samples a lane, 1,024 a warp; fp32: 8 -> 32 samples a lane, 1,024 a warp);
+//   PF  the next pair's record is loaded before this pair's gathers (fp32 only: with 16-bit states the extra
+//       registers cost more than the shorter dependency chain saves);
+//   min_blocks  resident CTAs per SM the register allocation is sized for (16-bit: 64 registers, fp32: 80).
+// UNR (without PF): pairs per step whose records and gathers are issued before any of their products.
+#ifndef FG_HOP_NG16
+#define FG_HOP_NG16 4
+#endif
+#ifndef FG_HOP_NG32
+#define FG_HOP_NG32 8
+#endif
+#ifndef FG_HOP_PF16
+#define FG_HOP_PF16 0
+#endif
+#ifndef FG_HOP_PF32
+#define FG_HOP_PF32 1
 #endif
 #ifndef FG_HOP_MINB16
-#define FG_HOP_MINB16 6
+#define FG_HOP_MINB16 4
 #endif
 #ifndef FG_HOP_MINB32
-#define FG_HOP_MINB32 4
+#define FG_HOP_MINB32 3
 #endif
-template <class TI> struct HopOcc { static constexpr int min_blocks = sizeof(TI) == 2 ? FG_HOP_MINB16 : FG_HOP_MINB32; };
+#ifndef FG_HOP_UNR
+#define FG_HOP_UNR 1
+#endif
+template <class TI> struct HopCfg {
+    static constexpr int NG = sizeof(TI) == 2 ? FG_HOP_NG16 : FG_HOP_NG32;
+    static constexpr bool PF = sizeof(TI) == 2 ? FG_HOP_PF16 : FG_HOP_PF32;
+    static constexpr int min_blocks = sizeof(TI) == 2 ? FG_HOP_MINB16 : FG_HOP_MINB32;
+};
+// states per lane per pair (the warp's chunk is 32 N samples)
+template <class T> struct Lane32 { static constexpr int N = HopCfg<T>::NG * 16 / (int)sizeof(T); };
 // the 16 raw bytes of a gather, unpacked to fp32 and multiplied into a (same FMA per sample as one at a time)
 template <class TI>
 __device__ __forceinline__ void fma16(const uint4& r, float2 w, float2 (&a)[Vec16<TI>::H]) {
@@ -402,9 +414,10 @@ __device__ __forceinline__ uint4 ldg16(const char* p) { return __ldg(reinterpret
 __device__ __forceinline__ const char* row_at(const char* base, int r, unsigned row_bytes) {
     return base + (unsigned long long)(unsigned)r * row_bytes;
 }
-// one warp's work: row `slot` of the schedule x sample chunk `chunk`. SURV (the firing survey): also adds, per row,
-// the number of samples whose state is positive to fired[t] and the sum of the squared pre-activations to sq[t]
-// (per-lane atomics: lanes past the batch have already returned).
+// one warp's work: row `slot` of the schedule x sample chunk `chunk`. FULL: the warp's whole chunk lies inside the
+// batch (ld a multiple of 32 N): no per-group validity tests. SURV (the firing survey): also adds, per row, the number
+// of samples whose state is positive to fired[t] and the sum of the squared pre-activations to sq[t] (per-lane atomics:
+// lanes past the batch have already returned).
 template <class TI, class TO, bool FULL, bool SURV = false>
 __device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restrict__ sched,
                                         const int* __restrict__ pptr, const int2* __restrict__ pairs,
@@ -412,96 +425,104 @@ __device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restri
                                         const float* __restrict__ rthr, const int* __restrict__ drow,
                                         const float* __restrict__ drive, TO* __restrict__ h, int n_rows, int ld,
                                         int* __restrict__ fired = nullptr, float* __restrict__ sq = nullptr) {
-    constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H, U = FG_HOP_UNR;
+    constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H, U = FG_HOP_UNR, NG = HopCfg<TI>::NG;
+    constexpr bool PF = HopCfg<TI>::PF;
+    constexpr int GB = 32 * 16;                          // byte distance between a lane's groups
     const int lane = threadIdx.x & 31;
     if (slot >= n_rows) return;
     const int t = __ldg(&sched[slot]);
-    const int c0 = chunk * 64 * V + lane * V, c1 = c0 + 32 * V;         // the lane's two groups
+    const int c0 = chunk * 32 * V * NG + lane * V;      // the lane's group g: samples c0 + 32 V g ...
     if (!FULL && c0 >= ld) return;
-    const bool g1 = FULL || c1 < ld;
-    float2 a0[H], a1[H];
+    // groups inside the batch (ld is a multiple of 32, so a group is either wholly inside or wholly outside)
+    const int ng = FULL ? NG : min(NG, (ld - c0 + 32 * V - 1) / (32 * V));
+    float2 a[NG][H];
 #pragma unroll
-    for (int i = 0; i < H; ++i) { a0[i] = make_float2(0.f, 0.f); a1[i] = make_float2(0.f, 0.f); }
+    for (int g = 0; g < NG; ++g)
+#pragma unroll
+        for (int i = 0; i < H; ++i) a[g][i] = make_float2(0.f, 0.f);
     const int e0 = __ldg(&pptr[t]), e1 = __ldg(&pptr[t + 1]);
     const unsigned row_bytes = (unsigned)ld * (unsigned)sizeof(TI);
     const char* base = reinterpret_cast<const char*>(hp + c0);
-    constexpr int G1 = 32 * 16;                          // byte offset of the lane's second group
     int e = e0;
-    if (g1) {
-        for (; e + U <= e1; e += U) {
+    if (FULL || ng == NG) {
+        for (; !PF && e + U <= e1; e += U) {             // (with the look-ahead below, pairs go one at a time)
             int2 p[U];
-            uint4 r0[U], r1[U];
+            uint4 r[U][NG];
 #pragma unroll
             for (int u = 0; u < U; ++u) p[u] = __ldg(&pairs[e + u]);
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const char* ap = row_at(base, p[u].x, row_bytes);
-                r0[u] = ldg16(ap);
-                r1[u] = ldg16(ap + G1);
+#pragma unroll
+                for (int g = 0; g < NG; ++g) r[u][g] = ldg16(ap + g * GB);
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const float2 w = make_float2(__int_as_float(p[u].y), __int_as_float(p[u].y));
-                fma16<TI>(r0[u], w, a0);
-                fma16<TI>(r1[u], w, a1);
+#pragma unroll
+                for (int g = 0; g < NG; ++g) fma16<TI>(r[u][g], w, a[g]);
             }
         }
+        // PF: the next pair's record is loaded before this pair's gathers (the pair array has one record past its end)
+        int2 pn = PF && e < e1 ? __ldg(&pairs[e]) : make_int2(0, 0);
+        for (; e < e1; ++e) {
+            int2 p;
+            if constexpr (PF) {
+                p = pn;
+                pn = __ldg(&pairs[e + 1]);
+            } else {
+                p = __ldg(&pairs[e]);
+            }
+            const char* ap = row_at(base, p.x, row_bytes);
+            uint4 r[NG];
+#pragma unroll
+            for (int g = 0; g < NG; ++g) r[g] = ldg16(ap + g * GB);
+            const float2 w = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+#pragma unroll
+            for (int g = 0; g < NG; ++g) fma16<TI>(r[g], w, a[g]);
+        }
+    } else {                                              // the batch ends inside this chunk
         for (; e < e1; ++e) {
             const int2 p = __ldg(&pairs[e]);
             const char* ap = row_at(base, p.x, row_bytes);
-            const uint4 r0 = ldg16(ap), r1 = ldg16(ap + G1);
             const float2 w = make_float2(__int_as_float(p.y), __int_as_float(p.y));
-            fma16<TI>(r0, w, a0);
-            fma16<TI>(r1, w, a1);
-        }
-    } else {                                              // only the first group is inside the batch
-        for (; e < e1; ++e) {
-            const int2 p = __ldg(&pairs[e]);
-            const uint4 r0 = ldg16(row_at(base, p.x, row_bytes));
-            fma16<TI>(r0, make_float2(__int_as_float(p.y), __int_as_float(p.y)), a0);
+#pragma unroll
+            for (int g = 0; g < NG; ++g)
+                if (g < ng) fma16<TI>(ldg16(ap + g * GB), w, a[g]);
         }
     }
     if (drow) {
         const int d = __ldg(&drow[t]);
         if (d >= 0) {
 #pragma unroll
-            for (int gi = 0; gi < 2; ++gi) {
-                if (gi == 1 && !g1) break;
-                float2* a = gi ? a1 : a0;
-                const float4* dr = reinterpret_cast<const float4*>(drive + (size_t)d * ld + (gi ? c1 : c0));
+            for (int g = 0; g < NG; ++g) {
+                if (g >= ng) break;
+                const float4* dr = reinterpret_cast<const float4*>(drive + (size_t)d * ld + c0 + g * 32 * V);
 #pragma unroll
                 for (int i = 0; i < H / 2; ++i) {
                     const float4 q = __ldg(dr + i);
-                    a[2 * i].x += q.x; a[2 * i].y += q.y; a[2 * i + 1].x += q.z; a[2 * i + 1].y += q.w;
+                    a[g][2 * i].x += q.x; a[g][2 * i].y += q.y; a[g][2 * i + 1].x += q.z; a[g][2 * i + 1].y += q.w;
                 }
             }
         }
     }
-    const float g = __ldg(&rgain[t]), th = __ldg(&rthr[t]);
-    float hv[V];
+    const float gn = __ldg(&rgain[t]), th = __ldg(&rthr[t]);
     int n_on = 0;
     float s2 = 0.f;
 #pragma unroll
-    for (int i = 0; i < H; ++i) {
-        hv[2 * i] = fmaxf(fmaf(g, a0[i].x, -th), 0.f);
-        hv[2 * i + 1] = fmaxf(fmaf(g, a0[i].y, -th), 0.f);
-        if (SURV) {
-            n_on += (hv[2 * i] > 0.f) + (hv[2 * i + 1] > 0.f);
-            s2 = fmaf(a0[i].x, a0[i].x, fmaf(a0[i].y, a0[i].y, s2));
-        }
-    }
-    st16<TO, V>(h + (size_t)t * ld + c0, hv);
-    if (g1) {
+    for (int g = 0; g < NG; ++g) {
+        if (g >= ng) break;
+        float hv[V];
 #pragma unroll
         for (int i = 0; i < H; ++i) {
-            hv[2 * i] = fmaxf(fmaf(g, a1[i].x, -th), 0.f);
-            hv[2 * i + 1] = fmaxf(fmaf(g, a1[i].y, -th), 0.f);
+            hv[2 * i] = fmaxf(fmaf(gn, a[g][i].x, -th), 0.f);
+            hv[2 * i + 1] = fmaxf(fmaf(gn, a[g][i].y, -th), 0.f);
             if (SURV) {
                 n_on += (hv[2 * i] > 0.f) + (hv[2 * i + 1] > 0.f);
-                s2 = fmaf(a1[i].x, a1[i].x, fmaf(a1[i].y, a1[i].y, s2));
+                s2 = fmaf(a[g][i].x, a[g][i].x, fmaf(a[g][i].y, a[g][i].y, s2));
             }
         }
-        st16<TO, V>(h + (size_t)t * ld + c1, hv);
+        st16<TO, V>(h + (size_t)t * ld + c0 + g * 32 * V, hv);
     }
     if (SURV) {
         atomicAdd(&fired[t], n_on);
@@ -510,7 +531,7 @@ __device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restri
 }
 
 template <class TI, class TO, bool FULL>
-__global__ void __launch_bounds__(kThreads, HopOcc<TI>::min_blocks) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
+__global__ void __launch_bounds__(kThreads, HopCfg<TI>::min_blocks) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
                                                       const int2* __restrict__ pairs, const TI* __restrict__ hp,
                                                       const float* __restrict__ rgain, const float* __restrict__ rthr,
                                                       const int* __restrict__ drow, const float* __restrict__ drive,
@@ -544,10 +565,9 @@ __global__ void __launch_bounds__(kThreads) k_count_fired(const T* __restrict__ 
     if (lane == 0) fired[r] += c;
 }
 
-// output plug: the forward product is the tensor-core kernel k_out_tc (fg_outtc.cuh); kOutA is the padded action
-// count of its partial slabs and of the backward's operand layouts, kOutB / kOutK the backward's sample tile and
-// staging depth
-constexpr int kOutA = 96, kOutB = 64, kOutK = 32;
+// output plug: the forward and backward products are the tensor-core kernels of fg_outtc.cuh; kOutA is the padded
+// action count of the forward's partial slabs
+constexpr int kOutA = 96;
 // the slices' partial logits added in slice order + bias -> lg [n_act, ld] and/or out [B, n_act]; a CTA per 32 samples
 __global__ void __launch_bounds__(256) k_out_reduce(const float* __restrict__ part, const float* __restrict__ ob,
                                                     float* __restrict__ lg, float* __restrict__ out, int slices,
@@ -653,68 +673,6 @@ __global__ void __launch_bounds__(kStatsT) k_loss_stats(const float* __restrict_
 }
 
 // ---------------------------------------------------------------- backward: output plug
-// Output-plug weight gradient as a register-blocked product: part[s][a][j] = sum over slice s of the batch of
-// dl[a, b] * hK[dn[j], b] (column j = n_dn is the bias: hK = 1). A CTA owns all 96 (padded) actions x 64 columns and one
-// batch slice (blockIdx.y); each thread 6 actions x 4 columns. Both operands are read along the batch (a warp reads
-// 32 consecutive samples of one row) and stored transposed, 32 samples at a time ([sample][action],
-// [sample][column]); the padded row strides (98, 68 floats) keep the transposing stores at 2- and 4-way bank conflicts
-// and the products' float2 / float4 reads aligned.
-constexpr int kSA = 98, kSH = 68;
-template <class T>
-__global__ void __launch_bounds__(256) k_out_bwd_wt(const float* __restrict__ dl, const T* __restrict__ hK,
-                                                    const int* __restrict__ dn, float* __restrict__ part, int n_act,
-                                                    int n_dn, int ld, int split_len, int B) {
-    __shared__ __align__(16) float As[kOutK * kSA];
-    __shared__ __align__(16) float Hs[kOutK * kSH];
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4, lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
-    const int j0 = blockIdx.x * kOutB, s = blockIdx.y;
-    const int b_lo = s * split_len, b_hi = min(B, b_lo + split_len);
-    const int n_col = n_dn + 1;
-    float acc[6][4];
-#pragma unroll
-    for (int i = 0; i < 6; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-    for (int b0 = b_lo; b0 < b_hi; b0 += kOutK) {
-        __syncthreads();
-        for (int a = wp; a < kOutA; a += 8)                 // warp per action row, lane per sample
-            As[lane * kSA + a] = a < n_act ? __ldg(&dl[(size_t)a * ld + b0 + lane]) : 0.f;
-        for (int jj = wp; jj < kOutB; jj += 8) {             // warp per column, lane per sample
-            const int j = j0 + jj;
-            float v = 0.f;
-            if (j < n_dn) v = ld1(hK + (size_t)__ldg(&dn[j]) * ld + b0 + lane);
-            else if (j == n_dn) v = 1.f;
-            Hs[lane * kSH + jj] = v;
-        }
-        __syncthreads();
-#pragma unroll 8
-        for (int k = 0; k < kOutK; ++k) {
-            const float4 h = *reinterpret_cast<const float4*>(&Hs[k * kSH + tx * 4]);
-            const float2 w01 = *reinterpret_cast<const float2*>(&As[k * kSA + ty * 6]);
-            const float2 w23 = *reinterpret_cast<const float2*>(&As[k * kSA + ty * 6 + 2]);
-            const float2 w45 = *reinterpret_cast<const float2*>(&As[k * kSA + ty * 6 + 4]);
-            const float hv[4] = {h.x, h.y, h.z, h.w};
-            const float wv[6] = {w01.x, w01.y, w23.x, w23.y, w45.x, w45.y};
-#pragma unroll
-            for (int i = 0; i < 6; ++i) {                         // two packed fp32x2 FMAs (same rounding)
-                const float2 w2 = make_float2(wv[i], wv[i]);
-                const float2 p0 = __ffma2_rn(w2, make_float2(hv[0], hv[1]), make_float2(acc[i][0], acc[i][1]));
-                const float2 p1 = __ffma2_rn(w2, make_float2(hv[2], hv[3]), make_float2(acc[i][2], acc[i][3]));
-                acc[i][0] = p0.x; acc[i][1] = p0.y; acc[i][2] = p1.x; acc[i][3] = p1.y;
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 6; ++i) {
-        const int a = ty * 6 + i;
-        if (a >= n_act) continue;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int c = j0 + tx * 4 + j;
-            if (c < n_col) part[((size_t)s * n_act + a) * n_col + c] = acc[i][j];
-        }
-    }
-}
 // G_out_w[a*n_dn + j] += sum_s part[s][a][j]; G_out_b[a] += sum_s part[s][a][n_dn]
 __global__ void k_out_bwd_reduce(const float* __restrict__ part, float* __restrict__ gow, float* __restrict__ gob,
                                  int n_act, int n_dn, int splits) {
