@@ -296,7 +296,7 @@ def run_ours(a, W, rank, world, dev, torch, dist):
     peak, peak_src = peaks()
     achieved = byts / (kern_step[dom][0] / 1e3) / 1e9 if byts else None
     roof = {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1) if achieved else None, "peak": peak,
-            "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None, "traffic": traffic_of(dom, W, a.sources),
+            "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None, "traffic": None if a.hub_tc else traffic_of(dom, W, B, a.sources),
             "algorithmic_bytes_per_step": byts, "launches_per_step": kern_step[dom][1],
             "ms_per_step": round(kern_step[dom][0], 4), "peak_source": peak_src,
             "largest_class_in_breakdown": max(bd_step, key=lambda k: bd_step[k][0])}
@@ -341,14 +341,15 @@ def run_ours(a, W, rank, world, dev, torch, dist):
     return out
 
 
-def traffic_of(cls: str, W, sources: str = "zipf") -> float | None:
-    """Per-step DRAM bytes of the kernel class from the committed ncu summary (profiles/traffic.json), if any."""
+def traffic_of(cls: str, W, B: int, sources: str = "zipf") -> float | None:
+    """Per-step DRAM bytes of the kernel class from the committed ncu summary (profiles/traffic.json), if any, scaled
+    from the capture's per-GPU batch to B in proportion to the samples."""
     p = REPO / "profiles" / "traffic.json"
-    if not p.exists() or W.get("graph") == "full":
+    if not p.exists() or W.get("graph"):
         return None
-    d = json.loads(p.read_text())
-    v = d.get(W["flags"] + ("" if sources == "zipf" else "/" + sources), {}).get(cls)
-    return float(v) if v is not None else None
+    d = json.loads(p.read_text()).get(W["flags"] + ("" if sources == "zipf" else "/" + sources), {})
+    v = d.get(cls)
+    return round(float(v) * B / d["batch"]) if v is not None else None
 
 
 def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier, max_over_ranks, grad, piece):
