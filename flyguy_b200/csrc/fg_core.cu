@@ -42,7 +42,7 @@ struct Hop {
     long long tbase = 0;                         // first transposed pair of this hop in the concatenated arrays
     int T = 0;                                   // transposed pairs kept for the backward
     int *d_live_dst = nullptr, n_live_dst = 0;   // rows of this hop's layer whose gradient can be non-zero
-    int2* d_sd_items = nullptr;                  // weight-gradient work items {row, first of up to 4 pairs}
+    int2* d_sd_items = nullptr;                  // weight-gradient work items {row, first of up to kSdP pairs}
     int n_sd_items = 0;
     int *d_live_src = nullptr, n_live_src = 0;   // rows of the layer below that this hop's backward writes
     int4 *d_segs = nullptr, *d_reds = nullptr;   // transposed product: segments of source rows, split-row reductions
@@ -315,7 +315,7 @@ void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, c
         h.n_live_src = (int)ls.size();
         std::vector<int2> items;
         for (int t : ld)
-            for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; p += 4) items.push_back(make_int2(t, p));
+            for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; p += kSdP) items.push_back(make_int2(t, p));
         h.n_sd_items = (int)items.size();
         h.d_sd_items = upload(c, items);
         h.d_live_dst = upload(c, ld);
@@ -514,7 +514,7 @@ void alloc_all(Core& c) {
     int max_rows = c.n_s;
     for (auto& h : c.hop) max_rows = std::max(max_rows, h.rows);
     c.x = dalloc<float>(c, (size_t)c.obs_dim * B);
-    if (c.train || c.redrive) c.drive = dalloc<float>(c, (size_t)c.n_s * B);
+    if (c.redrive) c.drive = dalloc<float>(c, (size_t)c.n_s * B);   // the plug's pre-activation, for re-driven rows
     c.h0 = dalloc<char>(c, (size_t)c.n_s * B * act_bytes(c));
     for (size_t k = 0; k < c.hop.size(); ++k) {
         Hop& h = c.hop[k];
@@ -889,15 +889,15 @@ void backward(Core& c, int B) {
         const dim3 g((c.n_plug_live + kWarps - 1) / kWarps);
         if (c.fan == 8)
             k_plug_bwd<8><<<g, kThreads, 0, c.st>>>(c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
-                                                    c.x, c.d_rgain, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
+                                                    c.x, c.d_rgain, c.d_rthr, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
                                                     c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
         else if (c.fan == 16)
             k_plug_bwd<16><<<g, kThreads, 0, c.st>>>(c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
-                                                     c.x, c.d_rgain, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
+                                                     c.x, c.d_rgain, c.d_rthr, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
                                                      c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
         else
             k_plug_bwd<0><<<g, kThreads, 0, c.st>>>(c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
-                                                    c.x, c.d_rgain, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
+                                                    c.x, c.d_rgain, c.d_rthr, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
                                                     c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
     });
 }

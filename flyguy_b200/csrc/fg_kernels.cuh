@@ -735,9 +735,14 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
 }
 
 // per merged pair p of row t: gp = sum_b gz[t,b] * hp[src_p, b], added to the gradient of every edge weight of the
-// pair. One warp per work item {row, first pair} - up to 4 consecutive pairs of one row whose gradient can be
-// non-zero - over the whole batch, 4 samples per lane per step; a warp-shuffle reduction in a fixed order (no block
-// barriers, no atomics for weights used once per hop); the edge weights' gradients are then updated by all lanes.
+// pair. One warp per work item {row, first pair} - up to kSdP consecutive pairs of one row whose gradient can be
+// non-zero (the gz row is read once for all of them) - over the whole batch, 4 samples per lane per step; a
+// warp-shuffle reduction in a fixed order (no block barriers, no atomics for weights used once per hop); the edge
+// weights' gradients are then updated by all lanes. A pair's sum does not depend on kSdP.
+#ifndef FG_SDDMM_P
+#define FG_SDDMM_P 4
+#endif
+constexpr int kSdP = FG_SDDMM_P;
 template <bool ATOMIC>
 __global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ items, const int* __restrict__ pptr,
                                                     const int2* __restrict__ pairs, const int* __restrict__ gptr,
@@ -749,18 +754,20 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ ite
     const int2 it = __ldg(&items[wi]);
     const int t = it.x, p0 = it.y;
     if (!__ldg(&live[t])) return;
-    const int np = min(4, __ldg(&pptr[t + 1]) - p0);
-    const float* hs[4];
+    const int np = min(kSdP, __ldg(&pptr[t + 1]) - p0);
+    const float* hs[kSdP];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) hs[u] = hp + (size_t)(u < np ? __ldg(&pairs[p0 + u].x) : 0) * ld;
+    for (int u = 0; u < kSdP; ++u) hs[u] = hp + (size_t)(u < np ? __ldg(&pairs[p0 + u].x) : 0) * ld;
     const float* g = gz + (size_t)t * ld;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float acc[kSdP];
+#pragma unroll
+    for (int u = 0; u < kSdP; ++u) acc[u] = 0.f;
 #pragma unroll 2
     for (int b = lane * 4; b < B; b += 128) {
         const float4 q = __ldg(reinterpret_cast<const float4*>(g + b));
         if (q.x == 0.f && q.y == 0.f && q.z == 0.f && q.w == 0.f) continue;       // silent samples: nothing to add
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kSdP; ++u) {
             if (u < np) {
                 const float4 hq = __ldg(reinterpret_cast<const float4*>(hs[u] + b));
                 acc[u] = fmaf(q.x, hq.x, fmaf(q.y, hq.y, fmaf(q.z, hq.z, fmaf(q.w, hq.w, acc[u]))));
@@ -768,14 +775,17 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ ite
         }
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) acc[u] = warp_sum(acc[u]);
+    for (int u = 0; u < kSdP; ++u) acc[u] = warp_sum(acc[u]);
     // the item's edges are one contiguous range of gw (pair after pair): every lane adds a pair's sum into the
     // gradient of one edge weight at a time; each weight is used once per hop unless ATOMIC
     const int e0 = __ldg(&gptr[p0]), e1 = __ldg(&gptr[p0 + np]);
-    const int m1 = np > 1 ? __ldg(&gptr[p0 + 1]) : e1, m2 = np > 2 ? __ldg(&gptr[p0 + 2]) : e1,
-              m3 = np > 3 ? __ldg(&gptr[p0 + 3]) : e1;
+    int m[kSdP];                                         // m[u]: the first edge of pair u (u >= 1)
+#pragma unroll
+    for (int u = 1; u < kSdP; ++u) m[u] = u < np ? __ldg(&gptr[p0 + u]) : e1;
     for (int j = e0 + lane; j < e1; j += 32) {
-        const float v = j < m1 ? acc[0] : j < m2 ? acc[1] : j < m3 ? acc[2] : acc[3];
+        float v = acc[0];
+#pragma unroll
+        for (int u = 1; u < kSdP; ++u) v = j >= m[u] ? acc[u] : v;
         const int w = __ldg(&gw[j]);
         if (ATOMIC) atomicAdd(&gW[w], v); else gW[w] += v;
     }
@@ -968,7 +978,8 @@ __global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __res
 // whole batch (4 samples per lane per step):
 // g0 = gh0 * [h0 > 0]; gd = gdrive (re-drive from later hops) + g0 * gain; sums over the batch of g0 * drive, g0, gd and
 // gd * x[col_e] for the row's fan edges (FAN of them, FAN <= 16; FAN 0: up to 16 in steps), reduced over the warp in
-// a fixed order and added to the gradients of gain, theta, in_b and in_w.
+// a fixed order and added to the gradients of gain, theta, in_b and in_w. Without a saved drive (a network with no
+// sensory re-drive keeps none) the pre-activation is recovered where it counts, h0 > 0: drive = (h0 + thr) / gain.
 constexpr int kPlugFan = 16;
 template <int FAN>
 __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ list, const int* __restrict__ gh_valid,
@@ -976,6 +987,7 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ l
                                                        const float* __restrict__ drive, const float* __restrict__ gdrive,
                                                        const int* __restrict__ n0, const int* __restrict__ in_col,
                                                        const float* __restrict__ x, const float* __restrict__ rgain,
+                                                       const float* __restrict__ rthr,
                                                        const float* __restrict__ rsig, float* __restrict__ ggain,
                                                        float* __restrict__ gtheta, float* __restrict__ gin_w,
                                                        float* __restrict__ gin_b, int n_list, int fan, int B, int ld) {
@@ -984,7 +996,7 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ l
     if (i >= n_list) return;
     const int s = __ldg(&list[i]);
     const bool ghv = __ldg(&gh_valid[s]) != 0;      // rows the transposed hop did not write have gh0 = 0
-    const float gn = __ldg(&rgain[s]);
+    const float gn = __ldg(&rgain[s]), th = __ldg(&rthr[s]), inv_g = gn != 0.f ? 1.f / gn : 0.f;
     const size_t o = (size_t)s * ld;
     const size_t e0 = (size_t)s * fan;
     for (int f0 = 0; f0 < fan || f0 == 0; f0 += F) {
@@ -1005,7 +1017,9 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ l
             const float gd[4] = {fmaf(g[0], gn, gr.x), fmaf(g[1], gn, gr.y), fmaf(g[2], gn, gr.z),
                                  fmaf(g[3], gn, gr.w)};
             if (first) {
-                const float4 dr = __ldg(reinterpret_cast<const float4*>(drive + o + b));
+                const float4 dr = drive ? __ldg(reinterpret_cast<const float4*>(drive + o + b))
+                                        : make_float4((hh.x + th) * inv_g, (hh.y + th) * inv_g, (hh.z + th) * inv_g,
+                                                      (hh.w + th) * inv_g);
                 v[F] += g[0] * dr.x + g[1] * dr.y + g[2] * dr.z + g[3] * dr.w;
                 v[F + 1] += g[0] + g[1] + g[2] + g[3];
                 v[F + 2] += gd[0] + gd[1] + gd[2] + gd[3];
