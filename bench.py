@@ -300,7 +300,8 @@ def run_ours(a, W, rank, world, dev, torch, dist):
             "algorithmic_bytes_per_step": byts, "launches_per_step": kern_step[dom][1],
             "ms_per_step": round(kern_step[dom][0], 4), "peak_source": peak_src,
             "largest_class_in_breakdown": max(bd_step, key=lambda k: bd_step[k][0])}
-    # whole-step view: the path's algorithmic bytes per unit (SURVEY formula) x rate
+    # whole-step view: the path's algorithmic bytes per unit (each layer written and read once, edge arrays once per
+    # launch) x rate
     N_rows, E = sum(s["sizes"]), s.edges()
     if train:
         per_unit = 5 * 4 * N_rows + s["obs_dim"] * 4 + s["n_act"] * 4 + (28 * E + 28 * sum(h.sizes)) / B

@@ -1,7 +1,7 @@
 """Writes the golden fixtures of the hop path from the REFERENCE's own code (run in the build container, where the
 reference project adventure-gpt/flyguy is mounted; its Python imports here, nothing of it is copied).
 
-  python tests/golden/make_golden.py [--ref /root/reference]
+  python tests/golden/make_golden.py [--ref REFERENCE_CHECKOUT]
 
 Each committed fixture tests/golden/<case>.npz holds one network and what the reference computes on it:
   net          the network as NET.bin bytes, written by the reference's flyguy/native/export.py:write_net
