@@ -83,9 +83,9 @@ def args_():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="wall time budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-train", action="store_true", help="default workload: leave out the config-3 training block")
+    ap.add_argument("--no-check", action="store_true", help="leave out the 16-bit argmax-agreement check")
     ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling of a small case only)")
-    ap.add_argument("--hub-tc", action="store_true",
-                    help="16-bit workloads: hops with hub sources on the tensor-core hop (FG_HUB_TC, opt-in)")
     ap.add_argument("--sources", choices=["zipf", "uniform"], default="zipf",
                     help="source distribution of the 3-hop synthetic graph (configs 1-3): Zipf(1.5) ranks, or uniform "
                          "(no L2 locality from hub sources, and every row of every layer feeds the output)")
@@ -198,6 +198,40 @@ def algo_bytes(cls: str, s, B: int, act: int) -> float:
     return 0.0
 
 
+def train_bytes(plan, s, B: int, flat_len: int, redrive: bool) -> dict:
+    """Algorithmic HBM bytes of one fp32 training step per kernel class, counting only what the step's plan visits:
+    the forward touches every row (each layer written once and read once, every edge record once); the backward only
+    the rows whose gradient can be non-zero (live rows), their merged pairs and the edge weights of those pairs; Adam
+    reads P, G, M, V, EMA and writes P, M, V, EMA over the flat parameter buffer."""
+    n, K = s["sizes"], s["hops"]
+    hops = plan["hops"]
+    E = sum(h["edges"] for h in hops)
+    out = {
+        "plug_fwd": (s["obs_dim"] + n[0] * (2 if redrive else 1)) * 4 * B,
+        "hop_fwd": 4 * B * sum(n[k] + n[k + 1] for k in range(K)) + 8 * E + 4 * sum(n[1:]),
+        "out_fwd": (plan["n_dn"] + 2 * s["n_act"]) * 4 * B,
+        "loss": 3 * s["n_act"] * 4 * B,
+        "out_bwd": (s["n_act"] + 2 * plan["n_dn"]) * 4 * B,
+        "act_bwd": 3 * 4 * B * hops[-1]["live_dst"],
+        "sddmm": sum(4 * B * (h["live_dst"] + h["live_src"]) + 8 * h["live_pairs_"] + 8 * h["live_edges"]
+                     for h in hops),
+        # transposed product: read gz of the live rows, write the layer below's live rows (and read its states for
+        # the fused neuron backward, except below the first hop, where gh0 is written as it is)
+        "hop_bwd_t": sum(4 * B * (h["live_dst"] + h["live_src"] * (2 if k else 1)) + 8 * h["tpairs"]
+                         for k, h in enumerate(hops)),
+        "plug_bwd": 4 * B * (3 * plan["plug_live"] + s["obs_dim"]),
+        "adam": 36 * flat_len,
+    }
+    return {k: float(v) for k, v in out.items()}
+
+
+def with_live_pairs(plan):
+    """plan['hops'][k]['live_pairs_']: merged pairs of the live rows (the transposed pairs kept are exactly those)."""
+    for h in plan["hops"]:
+        h["live_pairs_"] = h["tpairs"]
+    return plan
+
+
 # ------------------------------------------------------------------ our arm
 def make_graph(W, sources="zipf"):
     from flyguy_b200 import synth
@@ -208,16 +242,14 @@ def make_graph(W, sources="zipf"):
     return synth.make_synthetic(uniform=sources == "uniform")
 
 
-def run_ours(a, W, rank, world, dev, torch, dist):
+def run_ours(a, W, rank, world, dev, torch, dist, graph=None):
     from flyguy_b200 import native, synth
-    s, P = make_graph(W, a.sources)
+    s, P = graph or make_graph(W, a.sources)
     Bg = (a.batch or W["batch"]) * (world if W["per_gpu"] else 1)
     B = Bg // world
     assert B % 32 == 0 and B * world == Bg, "the batch must split into multiples of 32"
     flags = {"bf16": native.FG_ACT_BF16, "f16": native.FG_ACT_F16, "fp32": native.FG_INFER_ONLY,
              "train": 0}[W["flags"]]
-    if a.hub_tc and W["flags"] in ("bf16", "f16"):
-        flags |= native.FG_HUB_TC
     piece = min(B, PIECE) if W.get("graph") == "full" else B
     h = native.Handle(s, piece, flags, device=dev)
     h.set_params(P, 0)
@@ -296,19 +328,43 @@ def run_ours(a, W, rank, world, dev, torch, dist):
     peak, peak_src = peaks()
     achieved = byts / (kern_step[dom][0] / 1e3) / 1e9 if byts else None
     roof = {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1) if achieved else None, "peak": peak,
-            "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None, "traffic": None if a.hub_tc else traffic_of(dom, W, B, a.sources),
+            "unit": "GB/s", "frac": round(achieved / peak, 4) if achieved else None, "traffic": traffic_of(dom, W, B, a.sources),
             "algorithmic_bytes_per_step": byts, "launches_per_step": kern_step[dom][1],
             "ms_per_step": round(kern_step[dom][0], 4), "peak_source": peak_src,
             "largest_class_in_breakdown": max(bd_step, key=lambda k: bd_step[k][0])}
-    # whole-step view: the path's algorithmic bytes per unit (each layer written and read once, edge arrays once per
-    # launch) x rate
+    # whole-step view. Inference: the path's algorithmic bytes per decision (each layer written and read once, edge
+    # arrays once per launch) x rate. Training: the bytes the step's plan really moves (train_bytes: the backward over
+    # live rows only), per kernel class against that class's measured time, and summed against the step time.
     N_rows, E = sum(s["sizes"]), s.edges()
     if train:
-        per_unit = 5 * 4 * N_rows + s["obs_dim"] * 4 + s["n_act"] * 4 + (28 * E + 28 * sum(h.sizes)) / B
+        plan = with_live_pairs(h.plan())
+        redrive = any((np.asarray(hh["drow"]) >= 0).any() for hh in s["hop"])
+        tb = train_bytes(plan, s, B, int(grad.numel()), bool(redrive))
+        ms_step = t_max / a.steps * 1e3
+        step_roof = {"bytes_per_step": round(sum(tb.values())), "bytes_per_unit": round(sum(tb.values()) / B, 1),
+                     "achieved_gbs_per_gpu": round(sum(tb.values()) / (ms_step / 1e3) / 1e9, 1),
+                     "frac": round(sum(tb.values()) / (ms_step / 1e3) / 1e9 / peak, 4),
+                     "kernels": {k: {"ms": round(bd_step[k][0], 4), "bytes": round(v),
+                                     "frac": round(v / (bd_step[k][0] / 1e3) / 1e9 / peak, 4)}
+                                 for k, v in tb.items() if k in bd_step and bd_step[k][0] > 0},
+                     "live_rows": [hh["live_dst"] for hh in plan["hops"]],
+                     "rows": [hh["rows"] for hh in plan["hops"]],
+                     "live_pairs": [hh["tpairs"] for hh in plan["hops"]],
+                     "pairs": [hh["pairs"] for hh in plan["hops"]],
+                     "how": "algorithmic bytes of what the plan visits (forward: all rows; backward: live rows, their "
+                            "pairs and edge weights; Adam over the flat buffer) / measured time; per-kernel times "
+                            "from the breakdown pass"}
     else:
         per_unit = 2 * act * N_rows + s["obs_dim"] * 4 + s["n_act"] * 4 + (8 * E + 4 * sum(s["sizes"][1:])) / B
-    step_roof = {"bytes_per_unit": round(per_unit, 1), "achieved_gbs_per_gpu": round(per_unit * value / world / 1e9, 1),
-                 "frac": round(per_unit * value / world / 1e9 / peak, 4)}
+        step_roof = {"bytes_per_unit": round(per_unit, 1),
+                     "achieved_gbs_per_gpu": round(per_unit * value / world / 1e9, 1),
+                     "frac": round(per_unit * value / world / 1e9 / peak, 4)}
+    # ---- argmax agreement of the 16-bit path (rank 0): the last step's logits on samples spread over the batch,
+    # against the oracle's emulation of the same 16-bit format (the kernel's error) and its fp32 forward (the
+    # format's error)
+    agreement = None
+    if rank == 0 and W["flags"] in ("bf16", "f16") and not a.no_check:
+        agreement = argmax_agreement(s, P, obs_np, logits.cpu().numpy(), W["flags"])
     # ---- e2e through the host-buffer entry points
     e2e = None if a.no_e2e else run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier,
                                           max_over_ranks, grad, piece)
@@ -333,13 +389,31 @@ def run_ours(a, W, rank, world, dev, torch, dist):
                       "edges": s["n_w"],
                       "edge_steps": E,
                       "pieces_per_step": (B + piece - 1) // piece,
-                      "hop_kernel": ("tensor-core hub product + CUDA-core tail (FG_HUB_TC)"
-                                     if a.hub_tc and W["flags"] in ("bf16", "f16") else "CUDA cores")},
+                      "hop_kernel": "CUDA cores"},
            "roofline": roof, "step_roofline": step_roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks,
+           **({"argmax_agreement": agreement} if agreement else {}),
            "gpu_launches": int(launches),
            "kernels_ms_per_step": {k: round(v[0], 4) for k, v in bd_step.items()},
            "kernels_breakdown": f"separate pass of {n_bd} steps after the timed region, every class timed"}
     return out
+
+
+def argmax_agreement(s, P, obs_np, got, fmt: str, n: int = 2048) -> dict:
+    """Argmax agreement of the GPU's 16-bit-state logits on n samples spread over the batch with the oracle's
+    emulation of that format and with its fp32 forward (the reference's arithmetic)."""
+    from oracle.oracle import Oracle
+    idx = np.unique(np.linspace(0, len(obs_np) - 1, n).astype(np.int64))
+    o = Oracle(s, threads=os.cpu_count() or 1)
+    emu = o.forward(P, obs_np[idx], states=fmt + "+obs")
+    ref = o.forward(P, obs_np[idx])
+    g = got[idx]
+    rel = lambda x, y: float(np.abs(x - y).max() / max(np.abs(y).max(), 1e-30))  # noqa: E731
+    return {"samples": int(len(idx)), "vs_emulation": float(np.mean(g.argmax(1) == emu.argmax(1))),
+            "vs_fp32_reference": float(np.mean(g.argmax(1) == ref.argmax(1))),
+            "emulation_vs_fp32_reference": float(np.mean(emu.argmax(1) == ref.argmax(1))),
+            "rel_vs_emulation": rel(g, emu), "rel_vs_fp32_reference": rel(g, ref),
+            "how": f"oracle/fly_oracle.c: {fmt} emulation (states rounded where the kernels store them) and fp32 "
+                   "forward, on samples spread over the last timed step's batch"}
 
 
 def traffic_of(cls: str, W, B: int, sources: str = "zipf") -> float | None:
@@ -620,7 +694,15 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", torch.cuda.current_device())
     try:
-        out = run_ours(a, W, rank, world, dev, torch, dist)
+        graph = make_graph(W, a.sources)
+        out = run_ours(a, W, rank, world, dev, torch, dist, graph)
+        if a.workload == "infer" and not a.no_train and not a.batch:
+            # config 3 at the same N on the same graph: the training half of BASELINE's metric
+            torch.cuda.empty_cache()
+            tr = run_ours(a, WORKLOADS["train"], rank, world, dev, torch, dist, graph)
+            out["train"] = {k: tr[k] for k in ("metric", "value", "unit", "ms_per_step", "scaling", "dtype", "config",
+                                               "roofline", "step_roofline", "e2e", "cpu_baseline", "clocks",
+                                               "gpu_launches", "kernels_ms_per_step") if k in tr}
         if rank == 0:
             print(json.dumps(out), flush=True)
     finally:

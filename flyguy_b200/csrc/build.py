@@ -20,7 +20,7 @@ REPO = PKG.parent
 LIB = PKG / "libflyguy_b200.so"
 TRAIN = PKG / "fg_train"                             # the trainer executable (a main() over fg_train_main)
 SOURCES = [HERE / "fg_core.cu", HERE / "fg_noalloc.cu", HERE / "fg_hopop.cu", HERE / "fg_train.cu", HERE / "fg_fly.cu"]
-DEPS = SOURCES + [HERE / "fg_kernels.cuh", HERE / "fg_tc.cuh", HERE / "fg_outtc.cuh", REPO / "include" / "flyguy_b200.h"]
+DEPS = SOURCES + [HERE / "fg_kernels.cuh", HERE / "fg_tcgen05.cuh", HERE / "fg_outtc.cuh", REPO / "include" / "flyguy_b200.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -12,7 +12,6 @@
 #include <vector>
 
 #include "fg_kernels.cuh"
-#include "fg_tc.cuh"
 #include "fg_outtc.cuh"
 #include "flyguy_b200.h"
 
@@ -42,6 +41,7 @@ struct Hop {
     long long tbase = 0;                         // first transposed pair of this hop in the concatenated arrays
     int T = 0;                                   // transposed pairs kept for the backward
     int *d_live_dst = nullptr, n_live_dst = 0;   // rows of this hop's layer whose gradient can be non-zero
+    long long live_pairs = 0, live_edges = 0;    // merged pairs / edges of those rows (what the weight gradient visits)
     int2* d_sd_items = nullptr;                  // weight-gradient work items {row, first of up to kSdP pairs}
     int n_sd_items = 0;
     int *d_live_src = nullptr, n_live_src = 0;   // rows of the layer below that this hop's backward writes
@@ -50,11 +50,6 @@ struct Hop {
     int n_segs = 0, n_reds = 0, n_slots = 0;
     void* d_h = nullptr;                     // states [rows, ld]
     bool out_f32 = false;                    // this hop's layer is stored in fp32 (the last layer always is)
-    // tensor-core forward (16-bit states): K hub columns (0: this hop runs on CUDA cores only)
-    int K = 0, n_hub_pairs = 0, row_tiles = 0;
-    int *d_pmid = nullptr, *d_hubs = nullptr;  // per row: first hub pair; hub source rows (-1: padding)
-    int2* d_hubmap = nullptr;                  // hub pair -> element of the weight operand tiles
-    void *wt = nullptr, *xh = nullptr;         // weight operand tiles, gathered hub states
 };
 
 constexpr int kSegLen = 64;                  // pairs per transposed segment (short: hub CTAs retire fast)
@@ -113,7 +108,7 @@ struct Core {
     std::string err;
     std::vector<void*> allocs;
     int device = 0, n_sm = 148;
-    int* d_err = nullptr;                               // device error word of the tensor-core hop (0: none)
+    int* d_err = nullptr;                               // device error word of the tensor-core kernels (0: none)
     int* sv_fired = nullptr;                            // during fg_survey: per-row firing counts and
     float* sv_sq = nullptr;                             //   sums of squared pre-activations (all layers' rows)
     long long launches = 0;
@@ -191,49 +186,15 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
     std::vector<int> pptr(rows + 1, 0), order;
     const long long pbase = (long long)pairs.size();
     h.pbase = pbase;
-    // Hubs (FG_HUB_TC with 16-bit states, inference-only handles): the source rows read by the most merged pairs,
-    // each read by at least 1/64 of the rows (and 16 rows), at most kHubMax of them, at least 8 to be worth a product.
-    std::vector<int> hub_of;
-    if ((c.bf16 || c.f16) && (c.flags & FG_HUB_TC)) {
-        std::vector<int> cnt(h.n_src, 0), cols;
-        for (int t = 0; t < rows; ++t) {
-            cols.assign(col.begin() + crow[t], col.begin() + crow[t + 1]);
-            std::sort(cols.begin(), cols.end());
-            for (size_t i = 0; i < cols.size(); ++i)
-                if (i == 0 || cols[i] != cols[i - 1]) ++cnt[cols[i]];
-        }
-        std::vector<int> cand(h.n_src);
-        std::iota(cand.begin(), cand.end(), 0);
-        std::stable_sort(cand.begin(), cand.end(), [&](int a, int b) { return cnt[a] > cnt[b]; });
-        const int thr = std::max(16, rows / 64);
-        std::vector<int> hubs;
-        for (int s : cand) {
-            if ((int)hubs.size() == kHubMax || cnt[s] < thr) break;
-            hubs.push_back(s);
-        }
-        if (hubs.size() >= 8) {
-            h.K = ((int)hubs.size() + 15) / 16 * 16;
-            hub_of.assign(h.n_src, -1);
-            for (size_t k = 0; k < hubs.size(); ++k) hub_of[hubs[k]] = (int)k;
-            hubs.resize(h.K, -1);
-            h.d_hubs = upload(c, hubs);
-        }
-    }
-    // a row's pairs: tail pairs by source, then (with hubs) hub pairs by hub index
-    auto key = [&](int e) -> long long {
-        const int hb = hub_of.empty() ? -1 : hub_of[col[e]];
-        return hb < 0 ? (long long)col[e] : (1LL << 40) + hb;
-    };
-    std::vector<int> psrc, pmid(rows, 0);
+    // a row's pairs by source (a pair = the row's edges from one source)
+    std::vector<int> psrc;
     for (int t = 0; t < rows; ++t) {
         order.resize(crow[t + 1] - crow[t]);
         std::iota(order.begin(), order.end(), crow[t]);
-        std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return key(a) < key(b); });
-        pmid[t] = -1;
+        std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return col[a] < col[b]; });
         for (size_t i = 0; i < order.size(); ++i) {
             const int e = order[i];
             if (i == 0 || col[e] != col[order[i - 1]]) {
-                if (pmid[t] < 0 && !hub_of.empty() && hub_of[col[e]] >= 0) pmid[t] = (int)psrc.size();
                 psrc.push_back(col[e]);
                 gptr.push_back((int)gw.size());
             }
@@ -242,7 +203,6 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
             mark[widx[e]] = 1;
         }
         pptr[t + 1] = (int)psrc.size();
-        if (pmid[t] < 0) pmid[t] = pptr[t + 1];
     }
     for (int w : widx) mark[w] = 0;
     h.P = (int)psrc.size();
@@ -252,26 +212,6 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
     std::iota(sched.begin(), sched.end(), 0);
     std::stable_sort(sched.begin(), sched.end(),
                      [&](int a, int b) { return pptr[a + 1] - pptr[a] > pptr[b + 1] - pptr[b]; });
-    if (h.K) {
-        // hub pair -> its element in the weight operand tiles: row tile = 128 consecutive schedule slots, each tile
-        // [hi block][lo block] of 128 x K in the K-major core-matrix layout
-        h.row_tiles = (rows + kTcRows - 1) / kTcRows;
-        std::vector<int2> map;
-        const long long tile_elems = 2LL * kTcRows * h.K;
-        if ((long long)h.row_tiles * tile_elems >= (1LL << 31)) throw Err("hub weight tiles exceed 2^31 elements");
-        for (int slot = 0; slot < rows; ++slot) {
-            const int t = sched[slot], rt = slot / kTcRows, j = slot % kTcRows;
-            for (int p = pmid[t]; p < pptr[t + 1]; ++p) {
-                const int k = hub_of[psrc[p]];
-                const long long off = rt * tile_elems + ((long long)(j >> 3) * (h.K >> 3) + (k >> 3)) * 64 +
-                                      (j & 7) * 8 + (k & 7);
-                map.push_back(make_int2((int)(pbase + p), (int)off));
-            }
-        }
-        h.n_hub_pairs = (int)map.size();
-        h.d_hubmap = upload(c, map);
-        h.d_pmid = upload(c, pmid);
-    }
     h.h_psrc = std::move(psrc);
     h.h_pptr = pptr;
     h.d_pptr = upload(c, pptr);
@@ -284,7 +224,12 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
 // nothing written for them (the reference skips zero gradients at run time, warp by warp). Then per hop: the
 // transposed pairs into live rows, by source and destination, cut into segments of at most kSegLen pairs.
 void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, const std::vector<int>& dn,
-                          std::vector<int2>& tpairs, std::vector<int>& tpi) {
+                          const std::vector<int>& gptr, long long n_edges, std::vector<int2>& tpairs,
+                          std::vector<int>& tpi) {
+    // edges of merged pair q (an index into the concatenated pair arrays)
+    auto edges_of = [&](long long q) -> long long {
+        return (q + 1 < (long long)gptr.size() ? gptr[q + 1] : n_edges) - gptr[q];
+    };
     const int K = c.hops;
     std::vector<std::vector<char>> live(K + 1);
     live[K].assign(c.sizes[K], 0);
@@ -314,8 +259,11 @@ void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, c
         h.n_live_dst = (int)ld.size();
         h.n_live_src = (int)ls.size();
         std::vector<int2> items;
-        for (int t : ld)
+        for (int t : ld) {
             for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; p += kSdP) items.push_back(make_int2(t, p));
+            h.live_pairs += h.h_pptr[t + 1] - h.h_pptr[t];
+            for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; ++p) h.live_edges += edges_of(h.pbase + p);
+        }
         h.n_sd_items = (int)items.size();
         h.d_sd_items = upload(c, items);
         h.d_live_dst = upload(c, ld);
@@ -468,7 +416,7 @@ void upload_net(Core& c, NetHost& n) {
     {
         std::vector<std::vector<int>> drows;
         for (auto& hh : n.hop) drows.push_back(hh.drow);
-        build_backward_plans(c, drows, n.dn, tpairs, tpi);
+        build_backward_plans(c, drows, n.dn, gptr, (long long)gw.size(), tpairs, tpi);
     }
     c.Ttot = (long long)tpairs.size();
     gptr.push_back((int)gw.size());
@@ -524,13 +472,6 @@ void alloc_all(Core& c) {
     c.d_err = dalloc<int>(c, 1);
     CK(cudaMemset(c.d_err, 0, sizeof(int)));
     CK(cudaDeviceGetAttribute(&c.n_sm, cudaDevAttrMultiProcessorCount, c.device));
-    for (auto& h : c.hop) {
-        if (!h.K) continue;
-        const size_t w_elems = (size_t)h.row_tiles * 2 * kTcRows * h.K;
-        h.wt = dalloc<uint16_t>(c, w_elems);
-        CK(cudaMemset(h.wt, 0, w_elems * 2));                // rows that do not read a hub keep a zero weight
-        h.xh = dalloc<uint16_t>(c, (size_t)((B + kTcCols - 1) / kTcCols) * kTcCols * h.K);
-    }
     // The slice count depends on the graph only, never on the batch, so a sample's logits are the same bits whatever
     // batch (or piece of one) it is computed in: one slice per ~320 dn columns, at most 8.
     c.out_chunks = (c.n_dn + kOtKC - 1) / kOtKC;
@@ -588,15 +529,7 @@ void plug_limit(const Core& c) {
     CK(cudaFuncSetAttribute(k_plug_fwd<T, SAVE, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
 }
 
-constexpr int tc_smem(int K) { return 2 * kTcRows * K * 2 + 2 * kTcCols * K * 2 + 128; }
-
 void set_smem_limits(const Core& c) {
-    CK(cudaFuncSetAttribute(k_hop_tc<__nv_bfloat16, __nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            tc_smem(kHubMax)));
-    CK(cudaFuncSetAttribute(k_hop_tc<__nv_bfloat16, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            tc_smem(kHubMax)));
-    CK(cudaFuncSetAttribute(k_hop_tc<__half, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(kHubMax)));
-    CK(cudaFuncSetAttribute(k_hop_tc<__half, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(kHubMax)));
     CK(cudaFuncSetAttribute(k_out_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kOtSmem));
     CK(cudaFuncSetAttribute(k_out_bwd_h_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kObSmem));
     CK(cudaFuncSetAttribute(k_out_bwd_w_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kOwSmem));
@@ -616,18 +549,6 @@ void fold(Core& c, int which) {
                                                   c.d_rsig, (int)c.R); });
     if (c.Ptot) {
         launch(c, K_FOLD, [&]() { k_fold_pairs<<<blocks(c.Ptot, kThreads), kThreads, 0, c.st>>>(c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, c.d_tpos, c.d_tpairs, (int)c.Ptot); });
-        for (auto& h : c.hop) {
-            if (!h.n_hub_pairs) continue;
-            launch(c, K_FOLD, [&]() {
-                if (c.bf16)
-                    k_fold_hub<__nv_bfloat16><<<blocks(h.n_hub_pairs), 256, 0, c.st>>>(h.d_hubmap, c.d_pairs,
-                                                                                       (__nv_bfloat16*)h.wt,
-                                                                                       h.n_hub_pairs, h.K);
-                else
-                    k_fold_hub<__half><<<blocks(h.n_hub_pairs), 256, 0, c.st>>>(h.d_hubmap, c.d_pairs, (__half*)h.wt,
-                                                                               h.n_hub_pairs, h.K);
-            });
-        }
     }
     launch(c, K_FOLD, [&]() { k_fold_ow_tc<<<blocks((long long)c.out_chunks * kOtN * kOtKC), 256, 0, c.st>>>(
                                   src + c.off[5], c.ow_tc, c.n_act, c.n_dn, c.out_chunks); });
@@ -678,30 +599,6 @@ void plug_launch(Core& c, const float* Pw, int B) {
     });
 }
 
-// a hop with hub columns, 16-bit states, batch a multiple of 256: hub states gathered into the MMA operand layout,
-// then the tensor-core kernel (hub product + tail pairs + activation), persistent with one CTA per SM over work items
-// of {row tile, run of sample tiles} - about 16 items per CTA, so the CTAs finish together
-template <class T, class TO>
-void tc_hop(Core& c, const Hop& h, const void* hp, int B) {
-    const int NT = B / kTcCols;
-    launch(c, K_HOP_FWD, [&]() {
-        k_gather_hub<T><<<dim3(NT, h.K / 8), 256, 0, c.st>>>((const T*)hp, h.d_hubs, (T*)h.xh, h.K, B);
-    });
-    TcHop a;
-    a.wt = h.wt; a.xh = h.xh; a.hp = hp;
-    a.pairs = c.d_pairs + h.pbase; a.pptr = h.d_pptr; a.pmid = h.d_pmid; a.sched = h.d_sched;
-    a.rgain = c.d_rgain + h.rbase; a.rthr = c.d_rthr + h.rbase; a.drow = h.d_drow; a.drive = c.drive;
-    a.h = h.d_h; a.err = c.d_err;
-    a.n_rows = h.rows; a.ld = B; a.K = h.K; a.n_sample_tiles = NT;
-    const long long want = 16LL * c.n_sm;
-    const int S = (int)std::min<long long>(NT, std::max(1LL, (long long)NT * h.row_tiles / want));
-    a.tiles_per_item = S;
-    a.items_per_row_tile = (NT + S - 1) / S;
-    a.n_items = h.row_tiles * a.items_per_row_tile;
-    const int grid = std::min(a.n_items, c.n_sm);
-    launch(c, K_HOP_FWD, [&]() { k_hop_tc<T, TO><<<grid, kTcThreads, tc_smem(h.K), c.st>>>(a); });
-}
-
 template <class TI, class TO>
 void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
     if (c.sv_fired) {                                     // the firing survey: CUDA-core hop with per-row counters
@@ -718,12 +615,6 @@ void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
                     c.sv_fired + h.rbase, c.sv_sq + h.rbase);
         });
         return;
-    }
-    if constexpr (sizeof(TI) == 2) {
-        if (h.K && B % kTcCols == 0) {
-            tc_hop<TI, TO>(c, h, hp, B);
-            return;
-        }
     }
     constexpr int N = Lane32<TI>::N;                     // samples per lane; the warp's chunk is 32 N
     const dim3 g((h.rows + kWarps - 1) / kWarps, (unsigned)((B + 32 * N - 1) / (32 * N)));
@@ -967,6 +858,7 @@ void* create(const char* path, int max_batch, int flags) {
         if (max_batch <= 0 || max_batch % 32) throw Err("max_batch must be a positive multiple of 32");
         // a state row of max_batch fp32 values must stay below 4 GiB (row offsets are 32 x 32 -> 64-bit products)
         if (max_batch > (1 << 28)) throw Err("max_batch must be at most 268435456");
+        if (flags & ~(FG_ACT_BF16 | FG_INFER_ONLY | FG_ACT_F16)) throw Err("unknown flags " + std::to_string(flags));
         c->maxB = max_batch;
         c->flags = flags;
         c->bf16 = flags & FG_ACT_BF16;
@@ -1022,6 +914,21 @@ int fg_layout(void* h, int* sizes, long long* pairs) {
         for (int k = 0; k <= c.hops; ++k) if (sizes) sizes[k] = c.sizes[k];
         for (int k = 0; k < c.hops; ++k) if (pairs) pairs[k] = c.hop[k].P;
         return c.hops;
+    }, -1);
+}
+
+int fg_plan(void* h, long long* out, int n) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        std::vector<long long> v;
+        for (const Hop& hp : c.hop) {
+            const long long row[8] = {hp.rows, hp.n_src, hp.E, hp.P, hp.T, hp.n_live_dst, hp.n_live_src, hp.live_edges};
+            v.insert(v.end(), row, row + 8);
+        }
+        const long long tail[4] = {c.n_plug_live, c.n_s, c.fan, c.n_dn};
+        v.insert(v.end(), tail, tail + 4);
+        for (int i = 0; i < n && i < (int)v.size(); ++i) out[i] = v[i];
+        return (int)v.size();
     }, -1);
 }
 

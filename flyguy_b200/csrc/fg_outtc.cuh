@@ -20,7 +20,7 @@
 // lanes 32 (w % 4) .., columns 48 (w / 4) ..) into the partial slab. Every wait is bounded (about 2 s): on expiry the
 // CTA records an error code and stops.
 #pragma once
-#include "fg_tc.cuh"
+#include "fg_tcgen05.cuh"
 
 namespace fg {
 

@@ -16,7 +16,7 @@ from .netfile import Structure, read_net, write_net
 
 PKG = Path(__file__).resolve().parent
 LIB_PATH = Path(os.environ.get("FLYGUY_B200_LIB", PKG / "libflyguy_b200.so"))   # (override: a variant build)
-FG_ACT_BF16, FG_INFER_ONLY, FG_ACT_F16, FG_HUB_TC = 1, 2, 4, 8
+FG_ACT_BF16, FG_INFER_ONLY, FG_ACT_F16 = 1, 2, 4
 _lib = None
 
 # the exported symbols and their ctypes signatures: (restype, argtypes)
@@ -41,6 +41,7 @@ SIGNATURES = {
     "fg_flat": (_ci, [_vp, _ci, ctypes.POINTER(_vp), ctypes.POINTER(_cll)]),
     "fg_offsets": (None, [_vp, ctypes.POINTER(_cll)]),
     "fg_layout": (_ci, [_vp, ctypes.POINTER(_ci), ctypes.POINTER(_cll)]),
+    "fg_plan": (_ci, [_vp, ctypes.POINTER(_cll), _ci]),
     "fg_teach": (_ci, [_vp, _vp, _vp, _ci, _cf, _vp, ctypes.POINTER(ctypes.c_double)]),
     "fg_teach_ex": (_ci, [_vp, _vp, _vp, _ci, _cf, _cf, _vp, ctypes.POINTER(ctypes.c_double)]),
     "fg_forward_host": (_ci, [_vp, _vp, _ci, _vp, _ci]),
@@ -160,6 +161,18 @@ class Handle:
         K = self.L.fg_layout(self.h, sizes, pairs)
         self.check()
         return [int(v) for v in sizes[:K + 1]], [int(v) for v in pairs[:K]]
+
+    def plan(self) -> dict:
+        """The work plan's counts (fg_plan): per hop {rows, n_src, edges, pairs, tpairs, live_dst, live_src,
+        live_edges}, and the plug backward's live sensory rows."""
+        buf = (ctypes.c_longlong * 512)()
+        n = self.L.fg_plan(self.h, buf, 512)
+        self.check()
+        keys = ("rows", "n_src", "edges", "pairs", "tpairs", "live_dst", "live_src", "live_edges")
+        hops = [{k: int(buf[8 * i + j]) for j, k in enumerate(keys)} for i in range((n - 4) // 8)]
+        t = n - 4
+        return {"hops": hops, "plug_live": int(buf[t]), "n_s": int(buf[t + 1]), "fan": int(buf[t + 2]),
+                "n_dn": int(buf[t + 3])}
 
     # ---- weights
     def set_params(self, params, which: int = 0) -> None:
@@ -303,10 +316,22 @@ def kl_loss_noalloc(logits, teacher, inv_temp: float, dlogits, stats, stream=Non
     """KL loss and its gradient without any device allocation (fg_kl_loss_noalloc): logits, teacher, dlogits [B, n_act]
     and stats [2] are caller-owned CUDA fp32 tensors; the work is queued on `stream` (default: torch's current)."""
     import torch
+    named = {"logits": logits, "teacher": teacher, "dlogits": dlogits, "stats": stats}
+    for k, t in named.items():
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+            raise FlyguyError(f"{k} must be a contiguous float32 CUDA tensor")
+        if t.device != logits.device:
+            raise FlyguyError(f"{k} is on {t.device}, logits on {logits.device}")
+    if logits.dim() != 2 or teacher.shape != logits.shape or dlogits.shape != logits.shape:
+        raise FlyguyError(f"logits, teacher and dlogits must share one [B, n_act] shape "
+                          f"(got {tuple(logits.shape)}, {tuple(teacher.shape)}, {tuple(dlogits.shape)})")
+    if stats.numel() < 2:
+        raise FlyguyError("stats needs room for 2 floats")
     L = lib()
-    st = (stream or torch.cuda.current_stream(logits.device)).cuda_stream
-    rc = L.fg_kl_loss_noalloc(logits.data_ptr(), teacher.data_ptr(), logits.shape[0], logits.shape[1],
-                              float(inv_temp), dlogits.data_ptr(), stats.data_ptr(), st)
+    with torch.cuda.device(logits.device):                     # the entry point works on the current device
+        st = (stream or torch.cuda.current_stream(logits.device)).cuda_stream
+        rc = L.fg_kl_loss_noalloc(logits.data_ptr(), teacher.data_ptr(), logits.shape[0], logits.shape[1],
+                                  float(inv_temp), dlogits.data_ptr(), stats.data_ptr(), st)
     if rc:
         raise FlyguyError(L.fg_noalloc_last_error().decode())
 

@@ -71,11 +71,9 @@ void fc_sync(void* h);
 #define FG_ACT_BF16 1     /* states stored as bf16 (fp32 accumulation, fp32 weights); forward only */
 #define FG_INFER_ONLY 2   /* no gradient / optimiser buffers: fc_backward and fc_step fail */
 #define FG_ACT_F16 4      /* states stored as IEEE fp16 (the reference's 16-bit "cuda16" states); forward only */
-#define FG_HUB_TC 8       /* 16-bit states: hops with hub sources use the tensor-core hop (opt-in, see below) */
-/* In both 16-bit modes the last layer (the descending neurons the output plug reads) stays fp32. With FG_HUB_TC, 16-bit
-   states and a batch that is a multiple of 256, a hop whose sources include hubs (rows read by many of the hop's rows)
-   sums the hub pairs with tensor cores (weights as 16-bit hi + lo terms, fp32 accumulation) and the rest on CUDA
-   cores. Without it every hop runs on CUDA cores, which is faster on the graphs measured so far. */
+/* In both 16-bit modes every layer but the last is stored in the 16-bit type, rounded to nearest even where it is
+   written; the last layer (the descending neurons the output plug reads) stays fp32, and the input plug reads the
+   observation values rounded to the same 16-bit type. Sums are fp32 throughout. */
 
 /* fc_create with flags (FG_ACT_BF16 and FG_ACT_F16 imply FG_INFER_ONLY). */
 void* fg_create(const char* net_path, int max_batch, int flags);
@@ -96,6 +94,11 @@ int fg_flat(void* h, int which, float** ptr, long long* n);
 void fg_offsets(void* h, long long* off);
 /* Layer sizes: sizes[0..hops] (returns hops); merged (destination, source) pairs per hop into pairs[0..hops-1]. */
 int fg_layout(void* h, int* sizes, long long* pairs);
+/* The work plan's counts, for roofline arithmetic: per hop 8 values {rows, source rows, edges, merged pairs,
+   transposed pairs kept for the backward, rows whose gradient can be non-zero, source rows the backward writes, edges
+   of the live rows' pairs}, then {sensory rows the plug backward visits, sensory rows, plug fan, descending rows}.
+   Writes min(n, count) values into out; returns the count (8 * hops + 4), or -1 on error. */
+int fg_plan(void* h, long long* out, int n);
 
 /* The distillation step's device half, fused: forward with the weights, KL(softmax(teacher * inv_temp) ||
  * softmax(logits)) averaged over the batch, its gradient through the network ADDED to the gradient.

@@ -19,6 +19,7 @@
  * from the reference's FlyActor in this container).
  */
 #include <math.h>
+#include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
 #ifdef _OPENMP
@@ -39,6 +40,31 @@ typedef struct {
     const int* const* drow;                 /* per hop: rows */
 } fo_net;
 
+/* 16-bit state emulation (fo_forward_q): the value a kernel stores for a state of the given format - the fp32 result
+ * rounded to the 16-bit type, round to nearest even. qmode bits 0-1: 0 keep fp32, 1 bf16, 2 fp16; bit 4: the plug's
+ * observation values are rounded to that type as well (a kernel that stages obs in the state type). */
+enum { FO_Q_NONE = 0, FO_Q_BF16 = 1, FO_Q_F16 = 2, FO_Q_OBS = 16 };
+static float q16(float f, int qmode) {
+    switch (qmode & 3) {
+        case FO_Q_BF16: {
+            uint32_t u;
+            memcpy(&u, &f, 4);
+            if ((u & 0x7fffffffu) > 0x7f800000u) return f;                 /* NaN stays NaN */
+            u += 0x7fffu + ((u >> 16) & 1u);
+            u &= 0xffff0000u;
+            memcpy(&f, &u, 4);
+            return f;
+        }
+        case FO_Q_F16: return (float)(_Float16)f;
+        default: return f;
+    }
+}
+
+/* q16 over an array (so tests can pin the rounding against other implementations) */
+void fo_round16(const float* in, float* out, long long n, int qmode) {
+    for (long long i = 0; i < n; ++i) out[i] = q16(in[i], qmode);
+}
+
 static double softplus_d(double x) { return x > 20.0 ? x : log1p(exp(x)); }
 static double sigmoid_d(double x) { return 1.0 / (1.0 + exp(-x)); }
 
@@ -55,16 +81,20 @@ static size_t total_rows(const fo_net* n) {
 
 /* one sample forward; fills drive[n_s], h (all layers back to back: h0, h1, ..., hK) and z (layers 1..K back to
  * back); returns logits[n_act] */
-static void fwd_one(const fo_net* n, const float* const* P, const float* x, double* drive, double* h, double* z,
-                    float* lg) {
+static void fwd_one_q(const fo_net* n, const float* const* P, const float* x, double* drive, double* h, double* z,
+                      float* lg, int qmode) {
     const float *W = P[0], *gain = P[1], *theta = P[2], *in_w = P[3], *in_b = P[4], *ow = P[5], *ob = P[6];
     for (int s = 0; s < n->n_s; ++s) {
         double acc = in_b[s];
-        for (int e = n->in_crow[s]; e < n->in_crow[s + 1]; ++e) acc += (double)in_w[e] * x[n->in_col[e]];
+        for (int e = n->in_crow[s]; e < n->in_crow[s + 1]; ++e) {
+            const float xv = (qmode & FO_Q_OBS) ? q16(x[n->in_col[e]], qmode) : x[n->in_col[e]];
+            acc += (double)in_w[e] * xv;
+        }
         drive[s] = acc;
         int id = n->n0[s];
         double v = (double)gain[id] * acc - softplus_d(theta[id]);
         h[s] = v > 0.0 ? v : 0.0;
+        if (qmode & 3) h[s] = q16((float)h[s], qmode);
     }
     size_t off_prev = 0, off = n->n_s, zoff = 0;
     for (int k = 0; k < n->hops; ++k) {
@@ -79,6 +109,7 @@ static void fwd_one(const fo_net* n, const float* const* P, const float* x, doub
             int id = nid[t];
             double v = (double)gain[id] * acc - softplus_d(theta[id]);
             h[off + t] = v > 0.0 ? v : 0.0;
+            if ((qmode & 3) && k + 1 < n->hops) h[off + t] = q16((float)h[off + t], qmode);   /* last layer: fp32 */
         }
         off_prev = off; off += rows; zoff += rows;
     }
@@ -90,9 +121,16 @@ static void fwd_one(const fo_net* n, const float* const* P, const float* x, doub
     }
 }
 
-/* obs [B, obs_dim] -> logits [B, n_act]; layers (nullable): [B, n_s + sum rows] fp32 = h0, h1, ..., hK */
-int fo_forward(const fo_net* n, const float* const* P, const float* obs, int B, float* logits, float* layers,
-               int threads) {
+static void fwd_one(const fo_net* n, const float* const* P, const float* x, double* drive, double* h, double* z,
+                    float* lg) {
+    fwd_one_q(n, P, x, drive, h, z, lg, FO_Q_NONE);
+}
+
+/* obs [B, obs_dim] -> logits [B, n_act]; layers (nullable): [B, n_s + sum rows] fp32 = h0, h1, ..., hK.
+ * qmode: FO_Q_NONE (the reference's fp32 forward) or a 16-bit state emulation (q16 above): every layer but the last
+ * rounded to the 16-bit type where it is stored, sums still in double. */
+int fo_forward_q(const fo_net* n, const float* const* P, const float* obs, int B, float* logits, float* layers,
+                 int threads, int qmode) {
     size_t R = total_rows(n);
 #ifdef _OPENMP
     if (threads > 0) omp_set_num_threads(threads);
@@ -107,13 +145,18 @@ int fo_forward(const fo_net* n, const float* const* P, const float* obs, int B, 
         else {
 #pragma omp for schedule(static)
             for (int b = 0; b < B; ++b) {
-                fwd_one(n, P, obs + (size_t)b * n->obs_dim, drive, h, z, logits + (size_t)b * n->n_act);
+                fwd_one_q(n, P, obs + (size_t)b * n->obs_dim, drive, h, z, logits + (size_t)b * n->n_act, qmode);
                 if (layers) for (size_t i = 0; i < R; ++i) layers[(size_t)b * R + i] = (float)h[i];
             }
         }
         free(drive); free(h); free(z);
     }
     return bad ? -1 : 0;
+}
+
+int fo_forward(const fo_net* n, const float* const* P, const float* obs, int B, float* logits, float* layers,
+               int threads) {
+    return fo_forward_q(n, P, obs, B, logits, layers, threads, FO_Q_NONE);
 }
 
 /* KL(softmax(teacher * inv_temp) || softmax(logits)) summed over the batch (kl_sum), argmax agreements (agree),

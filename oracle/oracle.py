@@ -41,6 +41,8 @@ def lib():
             L = ctypes.CDLL(str(LIB))
             vp, ci, cf = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
             L.fo_forward.restype, L.fo_forward.argtypes = ci, [vp, vp, vp, ci, vp, vp, ci]
+            L.fo_forward_q.restype, L.fo_forward_q.argtypes = ci, [vp, vp, vp, ci, vp, vp, ci, ci]
+            L.fo_round16.restype, L.fo_round16.argtypes = None, [vp, vp, ctypes.c_longlong, ci]
             L.fo_backward.restype, L.fo_backward.argtypes = ci, [vp, vp, vp, vp, ci, vp, ci]
             L.fo_loss.restype = None
             L.fo_loss.argtypes = [vp, vp, ci, ci, cf, vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
@@ -49,6 +51,10 @@ def lib():
             L.fo_adam.argtypes = [vp] * 6 + [ctypes.c_longlong, cf, cf, cf, cf, cf]
             _lib = L
     return _lib
+
+
+# fo_forward_q's qmode per state format (fly_oracle.c: q16)
+QMODES = {"fp32": 0, "bf16": 1, "f16": 2, "bf16+obs": 1 | 16, "f16+obs": 2 | 16}
 
 
 def _i32(a) -> np.ndarray:
@@ -93,15 +99,19 @@ class Oracle:
         assert [len(p) for p in P] == self.sizes, "weights do not fit this network"
         return P, (ctypes.c_void_p * 7)(*[_ptr(p) for p in P])
 
-    def forward(self, P, obs: np.ndarray, layers: bool = False):
-        """obs [B, obs_dim] -> logits [B, n_act] (and, with layers=True, every layer's firing [B, sum of sizes])."""
+    def forward(self, P, obs: np.ndarray, layers: bool = False, states: str = "fp32"):
+        """obs [B, obs_dim] -> logits [B, n_act] (and, with layers=True, every layer's firing [B, sum of sizes]).
+
+        states: "fp32" - the reference's forward; "bf16" / "f16" - 16-bit state emulation: every layer but the last
+        rounded (to nearest even) to that type where a 16-bit-state kernel stores it, the sums still in double;
+        "bf16+obs" / "f16+obs" - the plug's observation values rounded to that type as well."""
         obs = _f32(obs)
         B = obs.shape[0]
         P, pp = self._params(P)
         out = np.empty((B, self.s["n_act"]), np.float32)
         lay = np.empty((B, int(sum(self.s["sizes"]))), np.float32) if layers else None
-        rc = lib().fo_forward(ctypes.byref(self.net), pp, _ptr(obs), B, _ptr(out), _ptr(lay) if layers else None,
-                              self.threads)
+        rc = lib().fo_forward_q(ctypes.byref(self.net), pp, _ptr(obs), B, _ptr(out), _ptr(lay) if layers else None,
+                                self.threads, QMODES[states])
         assert rc == 0, "oracle forward ran out of memory"
         return (out, lay) if layers else out
 
@@ -114,6 +124,14 @@ class Oracle:
         rc = lib().fo_backward(ctypes.byref(self.net), pp, _ptr(obs), _ptr(dl), obs.shape[0], gp, self.threads)
         assert rc == 0, "oracle backward ran out of memory"
         return G
+
+
+def round16(x: np.ndarray, fmt: str) -> np.ndarray:
+    """x rounded to the 16-bit state format fmt ("bf16" / "f16"), as fp32: the emulation's rounding (fly_oracle.c q16)."""
+    x = _f32(x)
+    out = np.empty_like(x)
+    lib().fo_round16(_ptr(x), _ptr(out), x.size, QMODES[fmt])
+    return out
 
 
 def loss(logits: np.ndarray, teacher: np.ndarray, inv_temp: float = 1.0):

@@ -29,6 +29,7 @@ model.net.bin, model.params.bin and model_ref.npz (obs, teacher, logits, dlogits
 from __future__ import annotations
 
 import argparse
+import os
 import io
 import sys
 import tempfile
@@ -141,7 +142,8 @@ def run_case(f, write_net, params_from_torch, structure, B: int, seed: int, inv_
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("FLYGUY_REF"), required="FLYGUY_REF" not in os.environ,
+                    help="checkout of the reference project (default: the FLYGUY_REF environment variable)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     sys.path.insert(0, str(REPO))

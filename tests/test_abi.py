@@ -84,3 +84,28 @@ def test_hop_operator_argument_errors_are_statuses():
     assert "null pointer" in L.fg_hop_last_error().decode()
     assert L.fg_hop_bwd(None, None, None, None, None, None, None, None, -1, 10, 64, 0, None, None, None) == -1
     assert "negative" in L.fg_hop_last_error().decode()
+
+
+def test_noalloc_wrapper_checks_its_tensors():
+    """kl_loss_noalloc refuses, before any device call, tensors the entry point would write out of bounds of or read
+    on the wrong device: non-CUDA, non-fp32, non-contiguous, mismatched shapes, a too-small stats buffer."""
+    import torch
+    from flyguy_b200 import native
+    x = torch.zeros(32, 90)
+    with pytest.raises(native.FlyguyError, match="CUDA tensor"):
+        native.kl_loss_noalloc(x, x, 1.0, x, torch.zeros(2))
+
+
+def test_reference_binding_fixture_names_exported_entry_points():
+    """The recorded binding (tests/golden/binding_toy_h3.npz, made from the reference's fly_native.py) declares only
+    entry points this library exports and include/flyguy_b200.h declares."""
+    import json
+    from conftest import GOLDEN
+    d = np.load(GOLDEN / "binding_toy_h3.npz")
+    meta = json.loads(d["meta"].tobytes())
+    lib = ctypes.CDLL(str(native.LIB))
+    declared = set(native.header_symbols())
+    for name in meta["declarations"]:
+        assert hasattr(lib, name) and name in declared, name
+    assert {c["fn"] for c in meta["calls"]} >= {"fc_create", "fc_sizes", "fc_copy", "fc_forward", "fc_backward",
+                                                  "fc_zero_grad", "fc_step", "fc_adam_t"}

@@ -37,3 +37,28 @@ def test_hop_forward_algorithmic_bytes_match_the_stated_figure():
     from flyguy_b200 import synth
     s, _ = synth.make_synthetic()
     assert abs(b.algo_bytes("hop_fwd", s, 65536, 2) - 24.47e9) < 0.01e9
+
+
+def test_training_bytes_count_only_what_the_plan_visits():
+    """The training step's algorithmic bytes follow the plan: forward classes count every row, backward classes only
+    the live rows and their pairs, so a plan with fewer live rows moves fewer backward bytes and the same forward
+    bytes."""
+    b = _bench()
+    from flyguy_b200 import synth
+    s, _ = synth.make_synthetic(sizes=(300, 700, 500, 60), total_edges=30_000, seed=3)
+
+    def plan(frac):
+        hops = []
+        for k, hh in enumerate(s["hop"]):
+            rows, n_src, E = s["sizes"][k + 1], s["sizes"][k], len(hh["col"])
+            hops.append({"rows": rows, "n_src": n_src, "edges": E, "pairs": E, "tpairs": int(E * frac),
+                         "live_dst": int(rows * frac), "live_src": int(n_src * frac), "live_edges": int(E * frac)})
+        return b.with_live_pairs({"hops": hops, "plug_live": int(300 * frac), "n_s": 300, "fan": 8, "n_dn": 60})
+    full = b.train_bytes(plan(1.0), s, 1024, 100_000, False)
+    half = b.train_bytes(plan(0.5), s, 1024, 100_000, False)
+    for k in ("plug_fwd", "hop_fwd", "out_fwd", "loss", "out_bwd", "adam"):
+        assert full[k] == half[k], k
+    for k in ("act_bwd", "sddmm", "hop_bwd_t", "plug_bwd"):
+        assert half[k] < full[k], k
+    assert full["hop_fwd"] == b.algo_bytes("hop_fwd", s, 1024, 4)
+    assert full["adam"] == 36 * 100_000

