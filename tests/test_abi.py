@@ -103,7 +103,7 @@ def test_reference_binding_fixture_names_exported_entry_points():
     from conftest import GOLDEN
     d = np.load(GOLDEN / "binding_toy_h3.npz")
     meta = json.loads(d["meta"].tobytes())
-    lib = ctypes.CDLL(str(native.LIB))
+    lib = ctypes.CDLL(str(native.LIB_PATH))
     declared = set(native.header_symbols())
     for name in meta["declarations"]:
         assert hasattr(lib, name) and name in declared, name

@@ -33,7 +33,7 @@ CTYPES = {"c_void_p": ctypes.c_void_p, "c_char_p": ctypes.c_char_p, "c_int": cty
 def _declared(meta):
     """libflyguy_b200.so loaded the way the reference loads its library: ctypes.CDLL by path, with the reference's
     declarations (a CDLL object of its own, so nothing else's declarations interfere)."""
-    lib = ctypes.CDLL(str(native.LIB))
+    lib = ctypes.CDLL(str(native.LIB_PATH))
     for name, d in meta["declarations"].items():
         f = getattr(lib, name)
         f.restype = CTYPES[d["restype"]]
