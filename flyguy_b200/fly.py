@@ -6,11 +6,9 @@ unchanged. The forward pass runs in libflyguy_b200.so for CUDA tensors - with au
 in the library and lands in the parameters' .grad like the reference's torch path (flyguy/fly.py:286-305). There is
 no CPU compute path here: CPU tensors raise (the reference's CPU play path, fly_infer.cpp, stays the reference's).
 
-Structure (flyguy/fly.py:91-126): the neurons that matter after hop k are those within k synapses downstream of a
-sensory neuron AND within hops-k synapses upstream of a descending neuron; hop k keeps the connections from the
-layer-(k-1) set into the layer-k set, in CSR order by destination (sources ascending) and by source. The input plug
-draws, per sensory neuron in play, `fan` distinct observation indices from numpy default_rng(seed) - the same draws
-in the same order as the reference, so that a checkpoint's in_w meets the same observation values.
+The structure comes from flyguy_b200.wiring (the layers, each hop's connections in CSR order by destination and by
+source); this class lays it out under the reference's buffer names (e{k}, r{k}, c{k}, crow{k}, tcrow{k}, tcol{k},
+tperm{k}, ci{k}, tci{k}, n{k}, s{k}, d{k}, n0, dn_rows, in_*), which the NET.bin writer reads.
 """
 from __future__ import annotations
 
@@ -20,37 +18,28 @@ import numpy as np
 import torch
 import torch.nn as nn
 
+from .wiring import by_key, row_starts, wire
+
 ROOT = Path(__file__).resolve().parents[1]
-INHIBITORY = ("gaba", "glutamate", "histamine")
-
-
-def reachable(start: np.ndarray, src: np.ndarray, dst: np.ndarray, n: int, steps: int) -> list[np.ndarray]:
-    """masks[k][i]: neuron i is in `start` or reachable from it in at most k steps along src -> dst."""
-    mask = np.zeros(n, bool)
-    mask[start] = True
-    masks = [mask]
-    for _ in range(steps):
-        nxt = masks[-1].copy()
-        nxt[dst[masks[-1][src]]] = True
-        masks.append(nxt)
-    return masks
-
-
-def row_pointer(rows: np.ndarray, n_rows: int) -> np.ndarray:
-    counts = np.bincount(rows, minlength=n_rows)
-    out = np.zeros(n_rows + 1, np.int64)
-    np.cumsum(counts, out=out[1:])
-    return out
+INHIBITORY = ("gaba", "glutamate", "histamine")     # transmitters whose connections start with a negative strength
 
 
 def plug_columns(n_s: int, obs_dim: int, fan: int, seed: int) -> np.ndarray:
-    """fan distinct observation indices per sensory row, sorted within the row (flyguy/fly.py:141-143: one
-    rng.choice(obs_dim, fan, replace=False) per row from default_rng(seed), in row order)."""
+    """The observation indices each sensory row listens to: per row, in row order, one draw of `fan` distinct indices
+    from numpy default_rng(seed), sorted - the reference's draws (flyguy/fly.py:141-143), so a checkpoint's in_w meets
+    the same observation values."""
     rng = np.random.default_rng(seed)
-    out = np.empty((n_s, fan), np.int64)
-    for i in range(n_s):
-        out[i] = np.sort(rng.choice(obs_dim, size=fan, replace=False))
-    return out.reshape(-1)
+    return np.concatenate([np.sort(rng.choice(obs_dim, size=fan, replace=False)) for _ in range(n_s)]
+                          or [np.zeros(0, np.int64)]).astype(np.int64)
+
+
+def starting_strengths(g, total: np.ndarray) -> np.ndarray:
+    """1.5 x synapse count / the target's incoming synapse count, negative for inhibitory transmitters (the
+    reference's starting point, flyguy/fly.py:134-137)."""
+    pre, post = g["pre"].astype(np.int64), g["post"].astype(np.int64)
+    neg = np.isin(g["nt"], INHIBITORY)[pre]
+    return (np.where(neg, -1.5, 1.5).astype(np.float32) * g["syn"].astype(np.float32)
+            / np.maximum(total[post], 1.0)).astype(np.float32)
 
 
 class FlyActor(nn.Module):
@@ -63,68 +52,52 @@ class FlyActor(nn.Module):
         g = np.load(p if p.is_absolute() or p.exists() else ROOT / p)
         n = len(g["body"])
         pre, post = g["pre"].astype(np.int64), g["post"].astype(np.int64)
-        syn = g["syn"].astype(np.float32)
-        sens, dn = g["sensory"].astype(np.int64), g["descending"].astype(np.int64)
         self.n_neurons, self.n_conn, self.hops, self.obs_dim, self.fan = n, len(pre), hops, obs_dim, fan
         self.whole_graph = "in_total" not in g.files
         self.gather_limit = 60_000_000           # kept for API compatibility (the reference's torch-path switch)
         self.kernel = "b200"                     # every kernel name of the reference maps to the B200 library; for
         #                                          forward without gradients "cuda16" selects fp16 states (as the
         #                                          reference's cuda16 kernels) and "bf16" bf16 states
-        down = reachable(sens, pre, post, n, hops)
-        up = reachable(dn, post, pre, n, hops)
-        layers = [np.flatnonzero(down[k] & up[hops - k]) for k in range(hops + 1)]
-        self.sizes = [len(s) for s in layers]
-        where = []
-        for s in layers:
-            w = np.full(n, -1, np.int64)
-            w[s] = np.arange(len(s))
-            where.append(w)
-        sensory = np.zeros(n, bool)
-        sensory[sens] = True
-        self.used = 0
-        in_play = np.zeros(len(pre), bool)
-        for k in range(1, hops + 1):
-            m = np.flatnonzero((where[k - 1][pre] >= 0) & (where[k][post] >= 0))
-            r, c = where[k][post[m]], where[k - 1][pre[m]]
-            by_dst = np.lexsort((c, r))
-            m, r, c = m[by_dst], r[by_dst], c[by_dst]
-            by_src = np.lexsort((r, c))
-            ids = layers[k]
-            self._buf(f"e{k}", m); self._buf(f"r{k}", r); self._buf(f"c{k}", c)
-            self._buf(f"crow{k}", row_pointer(r, len(ids))); self._buf(f"tcrow{k}", row_pointer(c[by_src], len(layers[k - 1])))
-            self._buf(f"tcol{k}", r[by_src]); self._buf(f"tperm{k}", by_src)
-            self._buf(f"ci{k}", c.astype(np.int32)); self._buf(f"tci{k}", r[by_src].astype(np.int32))
-            self._buf(f"n{k}", ids)
-            self._buf(f"s{k}", np.flatnonzero(sensory[ids]))
-            self._buf(f"d{k}", where[0][ids[sensory[ids]]])
-            self.used += len(m)
-            in_play[m] = True
-        self.in_play = int(in_play.sum())
-        self._buf("n0", layers[0])
-        reach_dn = where[hops][dn] >= 0
-        assert reach_dn.any(), "no descending neuron can be reached in this many hops"
-        self._buf("dn_rows", where[hops][dn[reach_dn]])
-        if "in_total" in g.files:
-            assert hops <= int(g["hops"]), f"this graph file holds the connections of a {int(g['hops'])}-hop network only"
-            total = g["in_total"].astype(np.float32)
+        wiring = wire(pre, post, g["sensory"], g["descending"], n, hops)
+        if not len(wiring.dn_rows):
+            raise ValueError(f"{p.name}: none of the descending neurons is {hops} synapses or fewer from a sensory "
+                             "neuron along the wiring")
+        self.sizes = wiring.sizes
+        for k, hw in enumerate(wiring.hop, start=1):
+            tcol = hw.rows[hw.tperm]
+            for name, a in (("e", hw.edges), ("r", hw.rows), ("c", hw.cols), ("crow", hw.row_ptr),
+                            ("tcrow", hw.tcol_ptr), ("tcol", tcol), ("tperm", hw.tperm),
+                            ("ci", hw.cols.astype(np.int32)), ("tci", tcol.astype(np.int32)), ("n", hw.neurons),
+                            ("s", hw.sensory_rows), ("d", hw.drive_rows)):
+                self._buf(f"{name}{k}", a)
+        self.used = int(sum(len(hw.edges) for hw in wiring.hop))
+        self.in_play = int(wiring.kept(self.n_conn).sum())
+        self._buf("n0", wiring.layers[0])
+        self._buf("dn_rows", wiring.dn_rows)
+        # weights: a strength per connection (normalised by the target's incoming synapses in the WHOLE graph, which
+        # a trimmed file carries as in_total), a gain and a threshold parameter per neuron
+        if self.whole_graph:
+            total = np.bincount(post, weights=g["syn"].astype(np.float64), minlength=n).astype(np.float32)
         else:
-            total = np.zeros(n, np.float32)
-            np.add.at(total, post, syn)
-        sign = np.where(np.isin(g["nt"][pre], INHIBITORY), -1.0, 1.0).astype(np.float32)
-        self.w = nn.Parameter(torch.as_tensor(1.5 * sign * syn / np.maximum(total[post], 1.0)))
+            if hops > int(g["hops"]):
+                raise ValueError(f"{p.name} keeps only the connections of a {int(g['hops'])}-hop network")
+            total = g["in_total"].astype(np.float32)
+        self.w = nn.Parameter(torch.as_tensor(starting_strengths(g, total)))
         self.gain = nn.Parameter(torch.ones(n))
         self.theta = nn.Parameter(torch.full((n,), -4.0))
+        # input plug: sensory row i hears `fan` observation values; output plug: descending rows -> action logits
         n_s = self.sizes[0]
         cols = plug_columns(n_s, obs_dim, fan, seed)
-        rows = np.repeat(np.arange(n_s), fan)
-        t = np.lexsort((rows, cols))
-        self._buf("in_r", rows); self._buf("in_c", cols); self._buf("in_crow", row_pointer(rows, n_s))
-        self._buf("in_tcrow", row_pointer(cols[t], obs_dim)); self._buf("in_tcol", rows[t]); self._buf("in_tperm", t)
-        self._buf("in_ci", cols.astype(np.int32)); self._buf("in_tci", rows[t].astype(np.int32))
+        rows = np.repeat(np.arange(n_s, dtype=np.int64), fan)
+        t = by_key(cols, rows, n_s)
+        for name, a in (("in_r", rows), ("in_c", cols), ("in_crow", row_starts(rows, n_s)),
+                        ("in_tcrow", row_starts(cols[t], obs_dim)), ("in_tcol", rows[t]), ("in_tperm", t),
+                        ("in_ci", cols.astype(np.int32)), ("in_tci", rows[t].astype(np.int32))):
+            self._buf(name, a)
+        # (the order of the random draws below is the reference's, so a seeded run starts from the same numbers)
         self.in_w = nn.Parameter(torch.randn(n_s * fan) / fan ** 0.5)
         self.in_b = nn.Parameter(torch.zeros(n_s))
-        self.out = nn.Linear(len(self.dn_rows), n_actions)
+        self.out = nn.Linear(len(wiring.dn_rows), n_actions)
         nn.init.orthogonal_(self.out.weight, out_gain)
         nn.init.zeros_(self.out.bias)
         self._engine = None
@@ -133,11 +106,11 @@ class FlyActor(nn.Module):
         self.register_buffer(name, torch.as_tensor(np.ascontiguousarray(a)), persistent=False)
 
     def describe(self) -> str:
-        plug = self.in_w.numel() + self.in_b.numel() + sum(p.numel() for p in self.out.parameters())
-        return (f"fly actor: {self.n_neurons:,} neurons and {self.n_conn:,} connections in the graph; {self.hops} hops: "
-                f"{self.in_play:,} connections and {sum(self.sizes):,} neuron states in play (per hop {self.sizes}), "
-                f"{self.used:,} connection steps a decision; learned outside the fly: {plug:,} numbers (each sensory "
-                f"neuron hears {self.fan} observation values; {len(self.dn_rows):,} descending neurons -> actions)")
+        plug = self.in_w.numel() + self.in_b.numel() + sum(q.numel() for q in self.out.parameters())
+        return (f"{self.hops}-hop fly network over a {self.n_neurons:,}-neuron, {self.n_conn:,}-connection graph: "
+                f"layers {self.sizes}, {self.in_play:,} connections used ({self.used:,} connection steps per "
+                f"decision); plugs: {self.fan} observation values per sensory neuron in, {len(self.dn_rows):,} "
+                f"descending neurons out ({plug:,} weights)")
 
     def __deepcopy__(self, memo):
         """Copies share no library handle (two Python objects must not drive one network in the library)."""

@@ -47,7 +47,7 @@ def test_checkpoint_layout(toys):
     assert sd["in_w"].shape == (f.sizes[0] * 5,) and sd["out.weight"].shape == (90, len(f.dn_rows))
     g = FlyActor(toys / "toy.npz", 517, 90, hops=3, fan=5)
     g.load_state_dict(sd)
-    assert "fly actor" in f.describe()
+    assert "fly network" in f.describe() and str(f.used) not in ("", "0")
 
 
 def test_cpu_forward_is_refused(toys):
@@ -61,7 +61,7 @@ def test_trimmed_hops_refused(toys, tmp_path):
     g = dict(np.load(toys / "toy.npz"))
     g["in_total"], g["hops"] = np.ones(80, np.float32), np.array(2)
     np.savez(tmp_path / "trim.npz", **g)
-    with pytest.raises(AssertionError):
+    with pytest.raises(ValueError, match="2-hop network"):
         FlyActor(tmp_path / "trim.npz", 517, 90, hops=3, fan=5)
 
 

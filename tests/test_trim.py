@@ -46,7 +46,7 @@ def test_trimmed_graph_limits(wide, tmp_path):
     for k in range(3):
         assert torch.equal(getattr(a, f"n{k}"), getattr(b, f"n{k}"))
     assert torch.allclose(a.w.detach()[getattr(a, "e1")], b.w.detach()[getattr(b, "e1")])
-    with pytest.raises(AssertionError, match="3-hop network only"):
+    with pytest.raises(ValueError, match="only the connections of a 3-hop network"):
         FlyActor(tmp_path / "h3.npz", 16, 2, hops=4)
 
 
@@ -74,5 +74,5 @@ def test_trim_weights_cuts_checkpoint(wide, tmp_path):
 
 def test_trim_cli(wide, tmp_path, capsys):
     trim_graph.main([str(wide), str(tmp_path / "cli.npz"), "--hops", "2"])
-    assert "of 6,000 connections (2 hops)" in capsys.readouterr().out
+    assert "of 6,000 connections for 2 hops" in capsys.readouterr().out
     assert int(np.load(tmp_path / "cli.npz")["hops"]) == 2
