@@ -36,7 +36,8 @@ struct Hop {
     long long pbase = 0;                     // first merged pair of this hop in the concatenated arrays
     long long rbase = 0;                     // first row of this hop's layer in the per-row arrays
     bool widx_unique = true, redrive = false;
-    int *d_nid = nullptr, *d_drow = nullptr, *d_sched = nullptr, *d_pptr = nullptr;
+    int *d_nid = nullptr, *d_drow = nullptr, *d_pptr = nullptr;
+    int4* d_rows = nullptr;                      // forward schedule: per slot {first pair, end, row, 0}
     std::vector<int> h_psrc, h_pptr;             // host copies of the forward pairs (for the backward plan)
     long long tbase = 0;                         // first transposed pair of this hop in the concatenated arrays
     int T = 0;                                   // transposed pairs kept for the backward
@@ -180,8 +181,8 @@ void check_ptr(const std::vector<int>& p, long long n, const char* what) {
 
 // merged pairs of one hop: pair = the edges of one (row, source); returns host arrays appended to the global ones
 void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::vector<int>& col,
-                    const std::vector<int>& widx, std::vector<int2>& pairs, std::vector<int>& gptr,
-                    std::vector<int>& gw, std::vector<char>& mark) {
+                    const std::vector<int>& widx, const std::vector<int>& drow, std::vector<int2>& pairs,
+                    std::vector<int>& gptr, std::vector<int>& gw, std::vector<char>& mark) {
     const int rows = h.rows;
     std::vector<int> pptr(rows + 1, 0), order;
     const long long pbase = (long long)pairs.size();
@@ -215,7 +216,12 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
     h.h_psrc = std::move(psrc);
     h.h_pptr = pptr;
     h.d_pptr = upload(c, pptr);
-    h.d_sched = upload(c, sched);
+    std::vector<int4> rows4(rows);
+    for (int slot = 0; slot < rows; ++slot) {
+        const int t = sched[slot];
+        rows4[slot] = make_int4(pptr[t], pptr[t + 1], t, 0);
+    }
+    h.d_rows = upload(c, rows4);
 }
 
 // The backward plan. A row's gradient can be non-zero only if the row feeds a row whose gradient can be non-zero
@@ -409,7 +415,7 @@ void upload_net(Core& c, NetHost& n) {
         h.d_nid = upload(c, src.nid);
         h.d_drow = h.redrive ? upload(c, src.drow) : nullptr;
         row_nid.insert(row_nid.end(), src.nid.begin(), src.nid.end());
-        build_hop_plan(c, h, src.crow, src.col, src.widx, pairs, gptr, gw, mark);
+        build_hop_plan(c, h, src.crow, src.col, src.widx, src.drow, pairs, gptr, gw, mark);
         rbase += h.rows;
     }
     c.d_dn = upload(c, n.dn);
@@ -606,11 +612,11 @@ void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
         const dim3 g((h.rows + kWarps - 1) / kWarps, (unsigned)((B + 32 * N - 1) / (32 * N)));
         launch(c, K_HOP_FWD, [&]() {
             if (B % (32 * N) == 0)
-                k_hop_fwd_surv<TI, TO, true><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase,
+                k_hop_fwd_surv<TI, TO, true><<<g, kThreads, 0, c.st>>>(h.d_rows, c.d_pairs + h.pbase,
                     (const TI*)hp, c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive, (TO*)h.d_h, h.rows, B,
                     c.sv_fired + h.rbase, c.sv_sq + h.rbase);
             else
-                k_hop_fwd_surv<TI, TO, false><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase,
+                k_hop_fwd_surv<TI, TO, false><<<g, kThreads, 0, c.st>>>(h.d_rows, c.d_pairs + h.pbase,
                     (const TI*)hp, c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive, (TO*)h.d_h, h.rows, B,
                     c.sv_fired + h.rbase, c.sv_sq + h.rbase);
         });
@@ -621,13 +627,13 @@ void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
     const bool full = B % (32 * N) == 0;
     launch(c, K_HOP_FWD, [&]() {
         if (full)
-            k_hop_fwd<TI, TO, true><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase,
-                                                              (const TI*)hp, c.d_rgain + h.rbase, c.d_rthr + h.rbase,
-                                                              h.d_drow, c.drive, (TO*)h.d_h, h.rows, B);
+            k_hop_fwd<TI, TO, true><<<g, kThreads, 0, c.st>>>(h.d_rows, c.d_pairs + h.pbase, (const TI*)hp,
+                                                              c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow,
+                                                              c.drive, (TO*)h.d_h, h.rows, B);
         else
-            k_hop_fwd<TI, TO, false><<<g, kThreads, 0, c.st>>>(h.d_sched, h.d_pptr, c.d_pairs + h.pbase,
-                                                               (const TI*)hp, c.d_rgain + h.rbase, c.d_rthr + h.rbase,
-                                                               h.d_drow, c.drive, (TO*)h.d_h, h.rows, B);
+            k_hop_fwd<TI, TO, false><<<g, kThreads, 0, c.st>>>(h.d_rows, c.d_pairs + h.pbase, (const TI*)hp,
+                                                               c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow,
+                                                               c.drive, (TO*)h.d_h, h.rows, B);
     });
 }
 
@@ -865,6 +871,11 @@ void* create(const char* path, int max_batch, int flags) {
         c->f16 = (flags & FG_ACT_F16) && !c->bf16;
         c->train = !(flags & (FG_ACT_BF16 | FG_ACT_F16 | FG_INFER_ONLY));
         NetHost n = parse_net(*c, path);     // (a bad file fails here, before the GPU is touched)
+        // the hop kernels address a source row in 16-byte units with 32 bits: one layer of states at most 2^36 bytes
+        for (int v : c->sizes)
+            if ((double)v * max_batch * 4.0 >= 68719476736.0)
+                throw Err("max_batch " + std::to_string(max_batch) + " makes a layer of " + std::to_string(v) +
+                          " rows larger than 2^36 bytes");
         CK(cudaGetDevice(&c->device));
         upload_net(*c, n);
         alloc_all(*c);

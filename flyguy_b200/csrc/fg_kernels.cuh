@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace fg {
 
 constexpr int kWarps = 8;                 // warps per CTA of the row kernels
@@ -359,13 +361,14 @@ __device__ __forceinline__ void st16(TO* o, const float* hv) {
     }
 }
 
-// Per source-state type (measured at batch 65,536 bf16 / 16,384 and 4,096 fp32 on the Zipf graph):
+// Per source-state type (measured at batch 65,536 bf16 / 16,384 and 4,096 fp32 on the Zipf graph; two pairs in flight
+// beat the look-ahead record and one pair at a time for both types: bf16 hop forward 7.14 against 7.37 and 7.53 ms):
 //   NG  16-byte groups per lane per pair - the pair record, its address and the loop are shared by NG x V samples
 //       (16-bit: 4 -> 32 samples a lane, 1,024 a warp; fp32: 8 -> 32 samples a lane, 1,024 a warp);
 //   PF  the next pair's record is loaded before this pair's gathers (fp32 only: with 16-bit states the extra
 //       registers cost more than the shorter dependency chain saves);
+//   UNR (without PF) pairs whose records and gathers are issued before any of their products;
 //   min_blocks  resident CTAs per SM the register allocation is sized for (16-bit: 64 registers, fp32: 80).
-// UNR (without PF): pairs per step whose records and gathers are issued before any of their products.
 #ifndef FG_HOP_NG16
 #define FG_HOP_NG16 4
 #endif
@@ -376,7 +379,13 @@ __device__ __forceinline__ void st16(TO* o, const float* hv) {
 #define FG_HOP_PF16 0
 #endif
 #ifndef FG_HOP_PF32
-#define FG_HOP_PF32 1
+#define FG_HOP_PF32 0
+#endif
+#ifndef FG_HOP_UNR16
+#define FG_HOP_UNR16 2
+#endif
+#ifndef FG_HOP_UNR32
+#define FG_HOP_UNR32 2
 #endif
 #ifndef FG_HOP_MINB16
 #define FG_HOP_MINB16 4
@@ -384,11 +393,9 @@ __device__ __forceinline__ void st16(TO* o, const float* hv) {
 #ifndef FG_HOP_MINB32
 #define FG_HOP_MINB32 3
 #endif
-#ifndef FG_HOP_UNR
-#define FG_HOP_UNR 1
-#endif
 template <class TI> struct HopCfg {
     static constexpr int NG = sizeof(TI) == 2 ? FG_HOP_NG16 : FG_HOP_NG32;
+    static constexpr int UNR = sizeof(TI) == 2 ? FG_HOP_UNR16 : FG_HOP_UNR32;
     static constexpr bool PF = sizeof(TI) == 2 ? FG_HOP_PF16 : FG_HOP_PF32;
     static constexpr int min_blocks = sizeof(TI) == 2 ? FG_HOP_MINB16 : FG_HOP_MINB32;
 };
@@ -414,25 +421,57 @@ __device__ __forceinline__ uint4 ldg16(const char* p) { return __ldg(reinterpret
 __device__ __forceinline__ const char* row_at(const char* base, int r, unsigned row_bytes) {
     return base + (unsigned long long)(unsigned)r * row_bytes;
 }
-// one warp's work: row `slot` of the schedule x sample chunk `chunk`. FULL: the warp's whole chunk lies inside the
-// batch (ld a multiple of 32 N): no per-group validity tests. SURV (the firing survey): also adds, per row, the number
-// of samples whose state is positive to fired[t] and the sum of the squared pre-activations to sq[t] (per-lane atomics:
-// lanes past the batch have already returned).
+// relu(gain * z - thr) of 16 bytes' worth of outputs, stored as the layer's type: 16-bit layers round each pair of
+// values to the type first and take the max with zero on the packed pair (rounding is monotonic and keeps the sign, so
+// this is the value rounded after the relu, as the oracle's emulation stores it)
+template <class TO, int H>
+__device__ __forceinline__ void act_store(TO* o, const float2 (&a)[H], float gn, float th) {
+    const float2 g2 = make_float2(gn, gn), t2 = make_float2(-th, -th);
+    if constexpr (sizeof(TO) == 4) {
+#pragma unroll
+        for (int i = 0; i < H; i += 2) {
+            const float2 u = __ffma2_rn(g2, a[i], t2), v = __ffma2_rn(g2, a[i + 1], t2);
+            *reinterpret_cast<float4*>(o + 2 * i) = make_float4(fmaxf(u.x, 0.f), fmaxf(u.y, 0.f), fmaxf(v.x, 0.f),
+                                                                fmaxf(v.y, 0.f));
+        }
+    } else {
+        static_assert(H == 4, "a 16-bit layer's 16 bytes are 8 values");
+        uint32_t q[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 u = __ffma2_rn(g2, a[i], t2);
+            if constexpr (std::is_same<TO, __nv_bfloat16>::value) {
+                __nv_bfloat162 b = __hmax2(__floats2bfloat162_rn(u.x, u.y), __float2bfloat162_rn(0.f));
+                q[i] = *reinterpret_cast<uint32_t*>(&b);
+            } else {
+                __half2 b = __hmax2(__floats2half2_rn(u.x, u.y), __float2half2_rn(0.f));
+                q[i] = *reinterpret_cast<uint32_t*>(&b);
+            }
+        }
+        *reinterpret_cast<uint4*>(o) = make_uint4(q[0], q[1], q[2], q[3]);
+    }
+}
+// One warp's work: row `slot` of the schedule x sample chunk `chunk`. rows[slot] = {first pair, end, row t, 0}: three
+// independent loads from one 16-byte record. drow[t]: the sensory row whose drive is added again, or -1 (drow is null
+// for a network without sensory re-drive). FULL: the
+// warp's whole chunk lies inside the batch (ld a multiple of 32 N): no per-group validity tests. SURV (the firing
+// survey): also adds, per row, the number of samples whose state is positive to fired[t] and the sum of the squared
+// pre-activations to sq[t] (per-lane atomics: lanes past the batch have already returned).
 template <class TI, class TO, bool FULL, bool SURV = false>
-__device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restrict__ sched,
-                                        const int* __restrict__ pptr, const int2* __restrict__ pairs,
-                                        const TI* __restrict__ hp, const float* __restrict__ rgain,
-                                        const float* __restrict__ rthr, const int* __restrict__ drow,
-                                        const float* __restrict__ drive, TO* __restrict__ h, int n_rows, int ld,
-                                        int* __restrict__ fired = nullptr, float* __restrict__ sq = nullptr) {
-    constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H, U = FG_HOP_UNR, NG = HopCfg<TI>::NG;
+__device__ __forceinline__ void hop_row(int slot, int chunk, const int4* __restrict__ rows,
+                                        const int2* __restrict__ pairs, const TI* __restrict__ hp,
+                                        const float* __restrict__ rgain, const float* __restrict__ rthr,
+                                        const int* __restrict__ drow, const float* __restrict__ drive,
+                                        TO* __restrict__ h, int n_rows, int ld, int* __restrict__ fired = nullptr,
+                                        float* __restrict__ sq = nullptr) {
+    constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H, NG = HopCfg<TI>::NG, U = HopCfg<TI>::UNR;
     constexpr bool PF = HopCfg<TI>::PF;
     constexpr int GB = 32 * 16;                          // byte distance between a lane's groups
     const int lane = threadIdx.x & 31;
     if (slot >= n_rows) return;
-    const int t = __ldg(&sched[slot]);
     const int c0 = chunk * 32 * V * NG + lane * V;      // the lane's group g: samples c0 + 32 V g ...
     if (!FULL && c0 >= ld) return;
+    const int t = __ldg(&rows[slot].z);
     // groups inside the batch (ld is a multiple of 32, so a group is either wholly inside or wholly outside)
     const int ng = FULL ? NG : min(NG, (ld - c0 + 32 * V - 1) / (32 * V));
     float2 a[NG][H];
@@ -440,10 +479,10 @@ __device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restri
     for (int g = 0; g < NG; ++g)
 #pragma unroll
         for (int i = 0; i < H; ++i) a[g][i] = make_float2(0.f, 0.f);
-    const int e0 = __ldg(&pptr[t]), e1 = __ldg(&pptr[t + 1]);
     const unsigned row_bytes = (unsigned)ld * (unsigned)sizeof(TI);
     const char* base = reinterpret_cast<const char*>(hp + c0);
-    int e = e0;
+    int e = __ldg(&rows[slot].x);
+    const int e1 = __ldg(&rows[slot].y);
     if (FULL || ng == NG) {
         for (; !PF && e + U <= e1; e += U) {             // (with the look-ahead below, pairs go one at a time)
             int2 p[U];
@@ -491,7 +530,7 @@ __device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restri
                 if (g < ng) fma16<TI>(ldg16(ap + g * GB), w, a[g]);
         }
     }
-    if (drow) {
+    if (drow) {                                          // (a network with sensory re-drive: z += drive[d])
         const int d = __ldg(&drow[t]);
         if (d >= 0) {
 #pragma unroll
@@ -507,41 +546,48 @@ __device__ __forceinline__ void hop_row(int slot, int chunk, const int* __restri
         }
     }
     const float gn = __ldg(&rgain[t]), th = __ldg(&rthr[t]);
-    int n_on = 0;
-    float s2 = 0.f;
+    if constexpr (!SURV) {
 #pragma unroll
-    for (int g = 0; g < NG; ++g) {
-        if (g >= ng) break;
-        float hv[V];
+        for (int g = 0; g < NG; ++g) {
+            if (g >= ng) break;
+            act_store<TO, H>(h + (size_t)t * ld + c0 + g * 32 * V, a[g], gn, th);
+        }
+    } else {
+        int n_on = 0;
+        float s2 = 0.f;
 #pragma unroll
-        for (int i = 0; i < H; ++i) {
-            hv[2 * i] = fmaxf(fmaf(gn, a[g][i].x, -th), 0.f);
-            hv[2 * i + 1] = fmaxf(fmaf(gn, a[g][i].y, -th), 0.f);
-            if (SURV) {
+        for (int g = 0; g < NG; ++g) {
+            if (g >= ng) break;
+            float hv[V];
+#pragma unroll
+            for (int i = 0; i < H; ++i) {
+                hv[2 * i] = fmaxf(fmaf(gn, a[g][i].x, -th), 0.f);
+                hv[2 * i + 1] = fmaxf(fmaf(gn, a[g][i].y, -th), 0.f);
                 n_on += (hv[2 * i] > 0.f) + (hv[2 * i + 1] > 0.f);
                 s2 = fmaf(a[g][i].x, a[g][i].x, fmaf(a[g][i].y, a[g][i].y, s2));
             }
+            st16<TO, V>(h + (size_t)t * ld + c0 + g * 32 * V, hv);
         }
-        st16<TO, V>(h + (size_t)t * ld + c0 + g * 32 * V, hv);
-    }
-    if (SURV) {
         atomicAdd(&fired[t], n_on);
         atomicAdd(&sq[t], s2);
     }
 }
 
 template <class TI, class TO, bool FULL>
-__global__ void __launch_bounds__(kThreads, HopCfg<TI>::min_blocks) k_hop_fwd(const int* __restrict__ sched, const int* __restrict__ pptr,
-                                                      const int2* __restrict__ pairs, const TI* __restrict__ hp,
-                                                      const float* __restrict__ rgain, const float* __restrict__ rthr,
-                                                      const int* __restrict__ drow, const float* __restrict__ drive,
-                                                      TO* __restrict__ h, int n_rows, int ld) {
-    hop_row<TI, TO, FULL>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, sched, pptr, pairs, hp, rgain, rthr,
-                          drow, drive, h, n_rows, ld);
+__global__ void __launch_bounds__(kThreads, HopCfg<TI>::min_blocks) k_hop_fwd(const int4* __restrict__ rows,
+                                                                               const int2* __restrict__ pairs,
+                                                                               const TI* __restrict__ hp,
+                                                                               const float* __restrict__ rgain,
+                                                                               const float* __restrict__ rthr,
+                                                                               const int* __restrict__ drow,
+                                                                               const float* __restrict__ drive,
+                                                                               TO* __restrict__ h, int n_rows, int ld) {
+    hop_row<TI, TO, FULL>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, rows, pairs, hp, rgain, rthr, drow,
+                          drive, h, n_rows, ld);
 }
 // the same forward hop for the firing survey (fired / sq: this hop's rows)
 template <class TI, class TO, bool FULL>
-__global__ void __launch_bounds__(kThreads) k_hop_fwd_surv(const int* __restrict__ sched, const int* __restrict__ pptr,
+__global__ void __launch_bounds__(kThreads) k_hop_fwd_surv(const int4* __restrict__ rows,
                                                            const int2* __restrict__ pairs, const TI* __restrict__ hp,
                                                            const float* __restrict__ rgain,
                                                            const float* __restrict__ rthr,
@@ -549,8 +595,8 @@ __global__ void __launch_bounds__(kThreads) k_hop_fwd_surv(const int* __restrict
                                                            const float* __restrict__ drive, TO* __restrict__ h,
                                                            int n_rows, int ld, int* __restrict__ fired,
                                                            float* __restrict__ sq) {
-    hop_row<TI, TO, FULL, true>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, sched, pptr, pairs, hp, rgain,
-                                rthr, drow, drive, h, n_rows, ld, fired, sq);
+    hop_row<TI, TO, FULL, true>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, rows, pairs, hp, rgain, rthr,
+                                drow, drive, h, n_rows, ld, fired, sq);
 }
 // the firing survey of the sensory layer: samples with a positive state per row (a warp per row)
 template <class T>

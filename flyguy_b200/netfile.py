@@ -162,6 +162,15 @@ def read_chunk(path: str | Path) -> tuple[np.ndarray, np.ndarray]:
     return obs, teacher
 
 
+def write_batch(obs: np.ndarray, teacher: np.ndarray, path: str | Path) -> None:
+    """A fixed batch for `fg_train --check`: "FLYB", n (int32), obs [n, obs_dim] then teacher [n, n_act] float32 (the
+    layout export.py batch writes, flyguy/native/export.py:142-143)."""
+    obs, teacher = np.ascontiguousarray(obs, np.float32), np.ascontiguousarray(teacher, np.float32)
+    assert obs.shape[0] == teacher.shape[0]
+    with open(path, "wb") as fh:
+        fh.write(b"FLYB" + struct.pack("<i", obs.shape[0]) + obs.tobytes() + teacher.tobytes())
+
+
 def read_opt(path: str | Path, s: Structure) -> tuple[int, int, list[np.ndarray], list[np.ndarray]]:
     """A FLYO optimiser state (flyguy/native/flyguy_train.cu:288-293): "FLYO", step, adam_t (int64), then M and V of
     each of the seven arrays in turn. Returns (step, adam_t, M, V)."""

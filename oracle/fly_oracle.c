@@ -43,7 +43,7 @@ typedef struct {
 /* 16-bit state emulation (fo_forward_q): the value a kernel stores for a state of the given format - the fp32 result
  * rounded to the 16-bit type, round to nearest even. qmode bits 0-1: 0 keep fp32, 1 bf16, 2 fp16; bit 4: the plug's
  * observation values are rounded to that type as well (a kernel that stages obs in the state type). */
-enum { FO_Q_NONE = 0, FO_Q_BF16 = 1, FO_Q_F16 = 2, FO_Q_OBS = 16 };
+enum { FO_Q_NONE = 0, FO_Q_BF16 = 1, FO_Q_F16 = 2, FO_Q_OBS = 16, FO_PRE = 32 };
 static float q16(float f, int qmode) {
     switch (qmode & 3) {
         case FO_Q_BF16: {
@@ -128,7 +128,9 @@ static void fwd_one(const fo_net* n, const float* const* P, const float* x, doub
 
 /* obs [B, obs_dim] -> logits [B, n_act]; layers (nullable): [B, n_s + sum rows] fp32 = h0, h1, ..., hK.
  * qmode: FO_Q_NONE (the reference's fp32 forward) or a 16-bit state emulation (q16 above): every layer but the last
- * rounded to the 16-bit type where it is stored, sums still in double. */
+ * rounded to the 16-bit type where it is stored, sums still in double. With FO_PRE, layers receives the
+ * pre-activations instead of the states: the plug's drive for layer 0, z (sum over the edges + re-drive) for the hop
+ * layers. */
 int fo_forward_q(const fo_net* n, const float* const* P, const float* obs, int B, float* logits, float* layers,
                  int threads, int qmode) {
     size_t R = total_rows(n);
@@ -146,7 +148,12 @@ int fo_forward_q(const fo_net* n, const float* const* P, const float* obs, int B
 #pragma omp for schedule(static)
             for (int b = 0; b < B; ++b) {
                 fwd_one_q(n, P, obs + (size_t)b * n->obs_dim, drive, h, z, logits + (size_t)b * n->n_act, qmode);
-                if (layers) for (size_t i = 0; i < R; ++i) layers[(size_t)b * R + i] = (float)h[i];
+                if (layers && (qmode & FO_PRE)) {
+                    for (int i = 0; i < n->n_s; ++i) layers[(size_t)b * R + i] = (float)drive[i];
+                    for (size_t i = (size_t)n->n_s; i < R; ++i) layers[(size_t)b * R + i] = (float)z[i - n->n_s];
+                } else if (layers) {
+                    for (size_t i = 0; i < R; ++i) layers[(size_t)b * R + i] = (float)h[i];
+                }
             }
         }
         free(drive); free(h); free(z);

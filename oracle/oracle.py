@@ -99,19 +99,20 @@ class Oracle:
         assert [len(p) for p in P] == self.sizes, "weights do not fit this network"
         return P, (ctypes.c_void_p * 7)(*[_ptr(p) for p in P])
 
-    def forward(self, P, obs: np.ndarray, layers: bool = False, states: str = "fp32"):
+    def forward(self, P, obs: np.ndarray, layers: bool = False, states: str = "fp32", pre: bool = False):
         """obs [B, obs_dim] -> logits [B, n_act] (and, with layers=True, every layer's firing [B, sum of sizes]).
 
         states: "fp32" - the reference's forward; "bf16" / "f16" - 16-bit state emulation: every layer but the last
         rounded (to nearest even) to that type where a 16-bit-state kernel stores it, the sums still in double;
-        "bf16+obs" / "f16+obs" - the plug's observation values rounded to that type as well."""
+        "bf16+obs" / "f16+obs" - the plug's observation values rounded to that type as well. pre=True: the layers
+        returned are the pre-activations (the plug's drive for layer 0, z for the hop layers) instead of the states."""
         obs = _f32(obs)
         B = obs.shape[0]
         P, pp = self._params(P)
         out = np.empty((B, self.s["n_act"]), np.float32)
         lay = np.empty((B, int(sum(self.s["sizes"]))), np.float32) if layers else None
         rc = lib().fo_forward_q(ctypes.byref(self.net), pp, _ptr(obs), B, _ptr(out), _ptr(lay) if layers else None,
-                                self.threads, QMODES[states])
+                                self.threads, QMODES[states] | (32 if pre else 0))
         assert rc == 0, "oracle forward ran out of memory"
         return (out, lay) if layers else out
 

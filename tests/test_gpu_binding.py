@@ -108,4 +108,4 @@ def test_reference_binding_replays_against_this_library(cuda):
                 raise AssertionError(f"unexpected call {fn}")
             assert native.lib().fg_status(core) == 0, native.lib().fg_last_error(core).decode()
         native.lib().fg_destroy(core)
-    assert checked.get("fc_forward", 0) == 7 and all(checked.get(f"fc_copy{w}") for w in (0, 1, 2, 3, 4)), checked
+    assert checked.get("fc_forward", 0) == 6 and all(checked.get(f"fc_copy{w}") for w in (0, 1, 2, 3, 4)), checked

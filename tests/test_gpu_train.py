@@ -1,7 +1,9 @@
-"""The standalone teaching trainer (fg_train; the reference's flyguy_train main loop, flyguy/native/flyguy_train.cu:
+"""The standalone teaching trainer (fg_train; the reference's flyguy_train program, flyguy/native/flyguy_train.cu:
 631-788) on a small synthetic network: it learns, writes FLYP / FLYO in the reference's formats, is deterministic,
 matches the same steps driven from Python through the library bit for bit, restarts from its own save with the
-optimiser state, and stops on a STOP file."""
+optimiser state, stops on a STOP file, holds a chunk out and scores it every --eval-every steps, answers --check like
+the reference's export.py batch (against the oracle), and revives silent neurons exactly as the CPU restatement of
+the reference's revive() does (oracle/revival.py)."""
 import os
 import re
 import subprocess
@@ -48,9 +50,9 @@ def _splitmix64(x):
 def test_trainer_learns_and_writes_the_reference_formats(tmp_path, cuda):
     s, P, data = _setup(tmp_path)
     log = _run(tmp_path, tmp_path / "P0.bin", tmp_path / "out", "--steps", 40)
-    kls = [float(m) for m in re.findall(r"^step \d+ \| \d+ samples/s \| kl ([0-9.]+)", log, re.M)]
+    kls = [float(m) for m in re.findall(r"^step \d+ \| kl ([0-9.]+) agree [0-9.]+ \| lr", log, re.M)]
     assert len(kls) == 4 and kls[-1] < kls[0], log
-    assert "eval step 0" in log
+    assert "eval @0 chunk_001.bin (at the start)" in log
     step, W = netfile.read_params(tmp_path / "out.bin", s)
     assert step == 40 and all(np.isfinite(a).all() for a in W)
     assert netfile.read_params(tmp_path / "out.ema.bin", s)[0] == 40
@@ -61,7 +63,7 @@ def test_trainer_learns_and_writes_the_reference_formats(tmp_path, cuda):
     assert (tmp_path / "out.bin").read_bytes() == (tmp_path / "again.bin").read_bytes()
     # a restart from its own save goes on with the running average and the optimiser state
     log2 = _run(tmp_path, tmp_path / "out.bin", tmp_path / "out", "--steps", 10)
-    assert "start step 40, optimiser state restored" in log2
+    assert "from step 40 with its optimiser state" in log2
     assert netfile.read_params(tmp_path / "out.bin", s)[0] == 50
     assert netfile.read_opt(tmp_path / "out.opt.bin", s)[1] == 50
 
@@ -98,7 +100,7 @@ def test_trainer_stops_on_request(tmp_path, cuda):
     s, P, data = _setup(tmp_path)
     (tmp_path / "st.STOP").write_text("")
     log = _run(tmp_path, tmp_path / "P0.bin", tmp_path / "st", "--eval-batches", 0)
-    assert "stopped on request at step 1" in log
+    assert "stopped on request @1" in log
     assert (tmp_path / "st.STOP.done").exists() and netfile.read_params(tmp_path / "st.bin", s)[0] == 1
 
 
@@ -135,17 +137,87 @@ def test_survey_counts_and_squared_inputs(tmp_path, cuda):
 
 
 def test_revive_brings_silent_neurons_back_with_the_output_unchanged(tmp_path, cuda):
+    """Revival with every rate at zero (so the one step after it changes no weight): the saved weights equal the CPU
+    restatement's (oracle/revival.py: the reference's revive() steps on the oracle's forward, the same census draws),
+    the loss before and after is the same, and the planted silent neurons are among those revived."""
+    from conftest import rel
+    from oracle import revival
     s, P, data = _setup(tmp_path)
     n_s = s["sizes"][0]
     P = [a.copy() for a in P]
-    P[2][n_s:n_s + 60] = 20.0                     # 60 layer-1 neurons whose threshold no input reaches: silent
+    planted = np.asarray(s["hop"][0]["nid"])[:60]
+    P[2][planted] = 20.0                          # 60 layer-1 neurons whose threshold no input reaches: silent
     netfile.write_params(P, tmp_path / "Ps.bin", step=0)
-    log = _run(tmp_path, tmp_path / "Ps.bin", tmp_path / "rv", "--steps", 2, "--revive-every", 1,
-               "--revive-batches", 2, "--eval-batches", 1)
-    m = re.search(r"revive step 1 \| (\d+) of \d+ neurons .* \| (\d+) still silent \| kl ([0-9.]+) -> ([0-9.]+) "
-                  r"\(must be equal\)", log)
+    log = _run(tmp_path, tmp_path / "Ps.bin", tmp_path / "rv", "--steps", 1, "--revive-every", 1, "--revive-first", 1,
+               "--revive-batches", 2, "--eval-batches", 1, "--lr", 0, "--lr-neuron", 0, "--lr-plug", 0, "--lr-min", 0)
+    m = re.search(r"revival @0: (\d+) silent of \d+ .* still silent (\d+); kl ([0-9.]+) -> ([0-9.]+)", log)
     assert m, log
     n_dead, still, kl0, kl1 = int(m.group(1)), int(m.group(2)), m.group(3), m.group(4)
     assert n_dead >= 60 and still < n_dead and kl0 == kl1, log
-    assert re.search(r"^eval step 0 \| kl [0-9.]+ agree [0-9.]+ \| raw kl .* \| firing( [0-9.]+){4} \| silent \d+ of",
-                     log, re.M), log
+    assert re.search(r"^eval @0 chunk_001.bin \(at the start\) \| average: kl [0-9.]+ agree [0-9.]+ \| weights: kl "
+                     r"[0-9.]+ agree [0-9.]+ \| firing [0-9.]+(/[0-9.]+){3} \| silent \d+/\d+$", log, re.M), log
+    chunks = [netfile.read_chunk(data / f"chunk_{i:03d}.bin") for i in range(2)]
+    obs_all = np.concatenate([c[0] for c in chunks]).astype(np.float32)
+    tl_all = np.concatenate([c[1] for c in chunks]).astype(np.float32)
+    want, silent = revival.revive(s, P, obs_all, tl_all, seed=12345 + 3, batches=2, B=64, target=0.4)
+    assert len(silent) == n_dead and set(planted) <= set(silent.tolist())
+    got = netfile.read_params(tmp_path / "rv.bin", s)[1]
+    for i in range(7):
+        assert rel(got[i], want[i]) < 1e-4, i
+    assert np.array_equal(np.sign(got[0]), np.sign(want[0]))
+
+
+def test_check_mode_answers_like_the_reference_batch_check(tmp_path, cuda):
+    """fg_train --check NET PARAMS BATCH (a FLYB batch of 40 samples, not a multiple of 32): loss, agreement, the
+    first sample's first logits and every array's gradient norm and sum - against the oracle."""
+    from oracle.oracle import Oracle, loss
+    s, P, data = _setup(tmp_path)
+    obs, teacher = synth.make_batch(40, seed=77)
+    netfile.write_batch(obs, teacher, tmp_path / "batch.bin")
+    r = subprocess.run([str(TRAIN), "--check", str(tmp_path / "NET.bin"), str(tmp_path / "P0.bin"),
+                        str(tmp_path / "batch.bin")], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    out = r.stdout
+    o = Oracle(s)
+    lg = o.forward(P, obs)
+    kl, agree, dl = loss(lg, teacher, 1.0)
+    G = o.backward(P, obs, dl)
+    m = re.search(r"40 samples \| loss ([0-9.]+) agree ([0-9.]+)", out)
+    assert m, out
+    assert abs(float(m.group(1)) - kl / 40) < 1e-5 * max(1.0, kl / 40) and float(m.group(2)) == round(agree / 40, 4)
+    got_lg = [float(v) for v in re.search(r"logits\[0\]\[:5\]((?: -?[0-9.]+)+)", out).group(1).split()]
+    assert np.allclose(got_lg, lg[0, :5], rtol=1e-5, atol=2e-6)
+    for i, name in enumerate(("W", "gain", "theta", "in_w", "in_b", "out_w", "out_b")):
+        m = re.search(rf"grad {name}\s+norm ([0-9.e+-]+) sum ([0-9.e+-]+)", out)
+        norm = float(np.linalg.norm(G[i].astype(np.float64)))
+        assert abs(float(m.group(1)) - norm) <= 1e-4 * norm + 1e-12, (name, m.group(1), norm)
+
+
+def test_holdout_is_scored_every_eval_every_steps_and_never_learned_from(tmp_path, cuda):
+    """--holdout 1: the newest chunk at the start (chunk_001) stays out of the ring - the steps equal the library
+    driven from Python on chunk_000's samples alone - and --eval-every 5 scores it at steps 0, 5 and 10."""
+    import torch
+    s, P, data = _setup(tmp_path)
+    log = _run(tmp_path, tmp_path / "P0.bin", tmp_path / "ho", "--steps", 10, "--holdout", 1, "--eval-every", 5,
+               "--eval-batches", 1)
+    assert [int(v) for v in re.findall(r"^eval @(\d+) chunk_001.bin \(held out\)", log, re.M)] == [0, 5, 10], log
+    assert "ring 1, newest chunk_000.bin" in log
+    obs0, tl0 = netfile.read_chunk(data / "chunk_000.bin")
+    obs0, tl0 = obs0.astype(np.float32), tl0.astype(np.float32)
+    B, seed = 64, 12345
+    h = native.Handle(s, B)
+    h.set_params(P, 0)
+    h.set_params(P, 1)
+    f32 = np.float32
+    lr, lr_n, lr_p, lr_min = f32(1e-3), f32(1e-4), f32(3e-4), f32(3e-5)
+    for step in range(10):
+        sel = [_splitmix64(seed ^ ((step << 32) | b)) % len(obs0) for b in range(B)]
+        h.zero_grad()
+        h.teach(torch.as_tensor(obs0[sel]).cuda(), torch.as_tensor(tl0[sel]).cuda(), 1.0, loss_norm=B)
+        sched = f32(0.5 ** ((step + 1) / 20000.0))
+        rate = lambda base: float(max(lr_min * base / lr, base * sched))  # noqa: E731
+        h.step(rate(lr), rate(lr_n), rate(lr_p), 0.0, 0.999)
+    want = [a.cpu().numpy() for a in h.get(0)]
+    got = netfile.read_params(tmp_path / "ho.bin", s)[1]
+    for i in range(7):
+        assert np.array_equal(got[i], want[i]), i
