@@ -518,8 +518,8 @@ void alloc_all(Core& c) {
 
 template <class T>
 int plug_smem(const Core& c) {
-    const int f = (c.fan % 4 == 0 && c.fan > 0 && c.fan <= 16) ? c.fan : 1;
-    return (c.obs_dim * PlugCfg<T>::cols * (int)sizeof(T) + 15) / 16 * 16 + (kPlugThreads / 32) * 32 * f * 8;
+    const int f = (c.fan % 4 == 0 && c.fan > 0 && c.fan <= 16) ? c.fan : 1;     // (the F the launch instantiates)
+    return (c.obs_dim * PlugCfg<T>::cols * (int)sizeof(T) + 15) / 16 * 16 + (kPlugThreads / 32) * PlugCfg<T>::warp_bytes(f);
 }
 
 template <class T, bool SAVE>

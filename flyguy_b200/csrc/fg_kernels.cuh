@@ -193,7 +193,13 @@ __global__ void k_to_neuron_major(const float* __restrict__ in, float* __restric
 #endif
 constexpr int kPlugThreads = FG_PLUG_THREADS;
 // samples per CTA chunk: 2 per lane for fp32 states, 4 for 16-bit states (517 obs rows x 64 or 128 = 132 KB staged)
-template <class T> struct PlugCfg { static constexpr int cols = sizeof(T) == 4 ? 64 : 128; };
+template <class T> struct PlugCfg {
+    static constexpr int cols = sizeof(T) == 4 ? 64 : 128;
+    // rows a warp stages at a time (fewer for wide fans, so the slices fit beside the staged obs), and a warp's slice:
+    // RW row records {bias, gain, threshold, -} and RW x F columns and weights
+    __host__ __device__ static constexpr int rows(int F) { return F > 8 ? 16 : 32; }
+    __host__ __device__ static constexpr int warp_bytes(int F) { return rows(F) * 16 + rows(F) * F * 8; }
+};
 __device__ __forceinline__ void cvt_store4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
 __device__ __forceinline__ void cvt_store4(__nv_bfloat16* p, float4 v) {
     *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
@@ -225,10 +231,38 @@ __device__ __forceinline__ void st_ns(__half* p, const float (&v)[4]) {
     *reinterpret_cast<uint2*>(p) = make_uint2(pack_f16(v[0], v[1]), pack_f16(v[2], v[3]));
 }
 
+// relu(gain * drive - thr) of one lane's NS samples (as fp32 pairs), stored as the state type: 16-bit states round
+// each pair first and take the max with zero on the packed pair (the same value as rounding after the relu)
+template <class T, int NS>
+__device__ __forceinline__ void plug_store(T* o, const float2 (&d)[NS / 2], float gn, float th) {
+    const float2 g2 = make_float2(gn, gn), t2 = make_float2(-th, -th);
+    if constexpr (sizeof(T) == 4) {
+        static_assert(NS == 2, "fp32 states: two samples a lane");
+        const float2 u = __ffma2_rn(g2, d[0], t2);
+        *reinterpret_cast<float2*>(o) = make_float2(fmaxf(u.x, 0.f), fmaxf(u.y, 0.f));
+    } else {
+        static_assert(NS == 4, "16-bit states: four samples a lane");
+        uint32_t q[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const float2 u = __ffma2_rn(g2, d[k], t2);
+            if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+                __nv_bfloat162 b = __hmax2(__floats2bfloat162_rn(u.x, u.y), __float2bfloat162_rn(0.f));
+                q[k] = *reinterpret_cast<uint32_t*>(&b);
+            } else {
+                __half2 b = __hmax2(__floats2half2_rn(u.x, u.y), __float2half2_rn(0.f));
+                q[k] = *reinterpret_cast<uint32_t*>(&b);
+            }
+        }
+        *reinterpret_cast<uint2*>(o) = make_uint2(q[0], q[1]);
+    }
+}
+
 // A CTA owns one chunk of C samples and a block of rows: x for the chunk is staged once (as the state type for
-// 16-bit states), then each warp takes 32 consecutive rows at a time, stages their plug columns and weights in its own
-// slice of shared memory with one coalesced load, and walks them with broadcast reads - no global-memory latency
-// inside the row loop. FAN: the plug's fan-in (a multiple of 4 up to 16) or 0 for any fan (slower path).
+// 16-bit states), then each warp takes RW consecutive rows at a time and stages, in its own slice of shared memory,
+// their plug columns, weights and {bias, gain, threshold} with coalesced loads; the row loop then reads only shared
+// memory (broadcast reads of the row's record, one 8-byte read of staged x per lane and column). FAN: the plug's
+// fan-in (a multiple of 4 up to 16) or 0 for any fan (slower path).
 template <class T, bool SAVE_DRIVE, int FAN>
 __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict__ in_col,
                                                            const float* __restrict__ in_w,
@@ -242,10 +276,12 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
     constexpr int kWarpsP = kPlugThreads / 32;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T* xs = reinterpret_cast<T*>(smem_raw);                                               // [obs_dim][C]
-    int* rc_all = reinterpret_cast<int*>(smem_raw + ((size_t)obs_dim * C * sizeof(T) + 15) / 16 * 16);
+    unsigned char* warp_base = smem_raw + ((size_t)obs_dim * C * sizeof(T) + 15) / 16 * 16;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int* rc = rc_all + warp * 32 * F * 2;                                                // [32][F] cols
-    float* rw = reinterpret_cast<float*>(rc + 32 * F);                                   // [32][F] weights
+    constexpr int RW = PlugCfg<T>::rows(F);
+    float4* rp = reinterpret_cast<float4*>(warp_base + (size_t)warp * PlugCfg<T>::warp_bytes(F));   // [RW] b, g, thr
+    int* rc = reinterpret_cast<int*>(rp + RW);                                                       // [RW][F] cols
+    float* rw = reinterpret_cast<float*>(rc + RW * F);                                               // [RW][F] weights
     const int b0 = blockIdx.y * C;
     const int r_lo = blockIdx.x * rows_per_cta, r_hi = min(n_s, r_lo + rows_per_cta);
     for (int i = threadIdx.x; i < obs_dim * (C / 4); i += blockDim.x) {
@@ -257,32 +293,31 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
     __syncthreads();
     const int bl = NS * lane;
     const bool on = b0 + bl < ld;
-    for (int r0 = r_lo + warp * 32; r0 < r_hi; r0 += kWarpsP * 32) {
-        const int nrows = min(32, r_hi - r0);
-        if constexpr (FAN > 0) {
-            __syncwarp();
-            if (lane < nrows) {
-                const size_t e = (size_t)(r0 + lane) * FAN;
+    const T* xl = xs + bl;
+    for (int r0 = r_lo + warp * RW; r0 < r_hi; r0 += kWarpsP * RW) {
+        const int nrows = min(RW, r_hi - r0);
+        __syncwarp();
+        if (lane < nrows) {
+            const int r = r0 + lane;
+            rp[lane] = make_float4(__ldg(&in_b[r]), __ldg(&rgain[r]), __ldg(&rthr[r]), 0.f);
+            if constexpr (FAN > 0) {
+                const size_t e = (size_t)r * FAN;
 #pragma unroll
                 for (int j = 0; j < FAN; j += 4) {
                     *reinterpret_cast<int4*>(rc + lane * F + j) = __ldg(reinterpret_cast<const int4*>(in_col + e + j));
                     *reinterpret_cast<float4*>(rw + lane * F + j) = __ldg(reinterpret_cast<const float4*>(in_w + e + j));
                 }
             }
-            __syncwarp();
         }
+        __syncwarp();
         if (!on) continue;
         for (int i = 0; i < nrows; ++i) {
             const int row = r0 + i;
-            float a[NS];
-            const float bias = __ldg(&in_b[row]);
+            const float4 prm = rp[i];
+            float2 a2[NS / 2];
 #pragma unroll
-            for (int k = 0; k < NS; ++k) a[k] = bias;
+            for (int k = 0; k < NS / 2; ++k) a2[k] = make_float2(prm.x, prm.x);
             if constexpr (FAN > 0) {
-                static_assert(NS % 2 == 0, "packed fp32x2 products need an even number of samples per lane");
-                float2 a2[NS / 2];
-#pragma unroll
-                for (int k = 0; k < NS / 2; ++k) a2[k] = make_float2(bias, bias);
 #pragma unroll
                 for (int j = 0; j < FAN; j += 4) {
                     const int4 cc = *reinterpret_cast<const int4*>(rc + i * F + j);
@@ -292,35 +327,32 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         float v[NS];
-                        lds_ns(xs + cs[u] * C + bl, v);
+                        lds_ns(xl + cs[u] * C, v);
                         const float2 w2 = make_float2(ws[u], ws[u]);
 #pragma unroll
                         for (int k = 0; k < NS / 2; ++k)      // the same fp32 FMA per sample, two per instruction
                             a2[k] = __ffma2_rn(w2, make_float2(v[2 * k], v[2 * k + 1]), a2[k]);
                     }
                 }
-#pragma unroll
-                for (int k = 0; k < NS / 2; ++k) { a[2 * k] = a2[k].x; a[2 * k + 1] = a2[k].y; }
             } else {
                 const size_t e0 = (size_t)row * fan;
                 for (int j = 0; j < fan; ++j) {
                     float v[NS];
-                    lds_ns(xs + __ldg(&in_col[e0 + j]) * C + bl, v);
+                    lds_ns(xl + __ldg(&in_col[e0 + j]) * C, v);
                     const float w = __ldg(&in_w[e0 + j]);
 #pragma unroll
-                    for (int k = 0; k < NS; ++k) a[k] = fmaf(w, v[k], a[k]);
+                    for (int k = 0; k < NS / 2; ++k) {
+                        a2[k].x = fmaf(w, v[2 * k], a2[k].x);
+                        a2[k].y = fmaf(w, v[2 * k + 1], a2[k].y);
+                    }
                 }
             }
             const size_t o = (size_t)row * ld + b0 + bl;
             if (SAVE_DRIVE) {
-                if constexpr (NS == 2) *reinterpret_cast<float2*>(drive + o) = make_float2(a[0], a[1]);
-                else *reinterpret_cast<float4*>(drive + o) = make_float4(a[0], a[1], a[2], a[3]);
+                if constexpr (NS == 2) *reinterpret_cast<float2*>(drive + o) = a2[0];
+                else *reinterpret_cast<float4*>(drive + o) = make_float4(a2[0].x, a2[0].y, a2[1].x, a2[1].y);
             }
-            const float g = __ldg(&rgain[row]), th = __ldg(&rthr[row]);
-            float hv[NS];
-#pragma unroll
-            for (int k = 0; k < NS; ++k) hv[k] = fmaxf(fmaf(g, a[k], -th), 0.f);
-            st_ns(h0 + o, hv);
+            plug_store<T, NS>(h0 + o, a2, prm.y, prm.z);
         }
     }
 }
