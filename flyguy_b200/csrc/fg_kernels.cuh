@@ -284,11 +284,23 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
     float* rw = reinterpret_cast<float*>(rc + RW * F);                                               // [RW][F] weights
     const int b0 = blockIdx.y * C;
     const int r_lo = blockIdx.x * rows_per_cta, r_hi = min(n_s, r_lo + rows_per_cta);
-    for (int i = threadIdx.x; i < obs_dim * (C / 4); i += blockDim.x) {
-        const int f = i / (C / 4), q = (i - f * (C / 4)) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (b0 + q < ld) v = __ldg(reinterpret_cast<const float4*>(x + (size_t)f * ld + b0 + q));
-        cvt_store4(xs + f * C + q, v);
+    {                                                     // stage the chunk: four 16-byte loads in flight a thread
+        constexpr int Q = C / 4, U = 4;
+        const int total = obs_dim * Q;
+        for (int i0 = threadIdx.x; i0 < total; i0 += U * blockDim.x) {
+            float4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + u * blockDim.x, f = i / Q, q = (i - f * Q) * 4;
+                v[u] = i < total && b0 + q < ld ? __ldg(reinterpret_cast<const float4*>(x + (size_t)f * ld + b0 + q))
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + u * blockDim.x, f = i / Q, q = (i - f * Q) * 4;
+                if (i < total) cvt_store4(xs + f * C + q, v[u]);
+            }
+        }
     }
     __syncthreads();
     const int bl = NS * lane;
