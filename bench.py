@@ -61,6 +61,22 @@ WORKLOADS = {
                  dtype="f32", desc="playing: one decision for 8 cars per call through the reference's fly_* "
                                    "interface (fly_forward: host observations in, host logits and the first car's "
                                    "firing bytes out), fp32, the config-2 graph; latency-bound"),
+    "model_infer": dict(cfg="model.pt", batch=65536, per_gpu=False, flags="bf16", graph="model",
+                        metric="decisions/sec", unit="decisions/s", dtype="bf16",
+                        desc="the shipped bot/model.pt network (trimmed 3-hop graph, 3,688,058 edge-steps over "
+                             "2,992,734 shared weights, sensory re-drive, plug fan 16): bf16-state forward, global batch "
+                             "65,536 batch-sharded, no collective"),
+    "model_infer32": dict(cfg="model.pt", batch=4096, per_gpu=True, flags="fp32", graph="model",
+                          metric="decisions/sec", unit="decisions/s", dtype="f32",
+                          desc="bot/model.pt network: fp32 forward, batch 4,096 per GPU"),
+    "model_train": dict(cfg="model.pt", batch=16384, per_gpu=False, flags="train", graph="model",
+                        metric="train samples/sec", unit="samples/s", dtype="f32",
+                        desc="bot/model.pt network: distillation step (forward, KL loss, backward over every row - "
+                             "nothing is pruned on this graph - and Adam) fp32, global batch 16,384 data-parallel"),
+    "model_play": dict(cfg=0, batch=1, per_gpu=False, flags="play", graph="model", metric="decisions/sec",
+                       unit="decisions/s", dtype="f32",
+                       desc="config 0 on the GPU: one decision per fly_forward call (batch 1) on the bot/model.pt "
+                            "network, host observations in, host logits and firing bytes out; latency-bound"),
     "full": dict(cfg=4, batch=32768, per_gpu=False, flags="train", graph="full", metric="train samples/sec",
                  unit="samples/s", dtype="f32",
                  desc="config 4: the untrimmed graph (166,700 neurons, 15,283,167 edges, every hop past the first over "
@@ -233,8 +249,18 @@ def with_live_pairs(plan):
 
 
 # ------------------------------------------------------------------ our arm
+MODEL_DIR = Path(os.environ.get("FLYGUY_MODEL_DIR", REPO / "tests" / "golden" / "_model"))
+
+
 def make_graph(W, sources="zipf"):
-    from flyguy_b200 import synth
+    from flyguy_b200 import netfile, synth
+    if W.get("graph") == "model":
+        net, params = MODEL_DIR / "model.net.bin", MODEL_DIR / "model.params.bin"
+        if not (net.exists() and params.exists()):
+            raise SystemExit(f"{net} / {params} are missing: tests/golden/make_golden.py writes them from the "
+                             "reference's bot/model.pt")
+        s = netfile.read_net(net)
+        return s, netfile.read_params(params, s)[1]
     if W.get("graph") == "full":
         return synth.make_full_graph()
     if W.get("graph") == "h4":
@@ -375,7 +401,10 @@ def run_ours(a, W, rank, world, dev, torch, dist, graph=None):
     out = {"metric": W["metric"], "value": round(value, 1), "unit": W["unit"], "n_gpus": world, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": round(t_max / a.steps * 1e3, 4), "higher_is_better": True,
            "scaling": "weak" if W["per_gpu"] else "strong", "vs_baseline": None, "dtype": W["dtype"],
-           "data": ("synthetic: seeded untrimmed graph (166,700 neurons, 15,283,167 edges, lognormal in-degree mean 92, "
+           "data": (f"the reference's bot/model.pt network and weights ({'/'.join(f'{v:,}' for v in s['sizes'])} "
+                    f"neurons, {s['n_w']:,} weights, {E:,} edge-steps, sensory re-drive); synthetic obs ~ N(0,1), "
+                    "teacher ~ N(0,4)" if W.get("graph") == "model" else
+                    "synthetic: seeded untrimmed graph (166,700 neurons, 15,283,167 edges, lognormal in-degree mean 92, "
                     "Zipf(1.5) sources), obs ~ N(0,1), teacher ~ N(0,4)" if W.get("graph") == "full" else
                     f"synthetic: seeded {len(s['sizes']) - 1}-hop graph "
                     f"({'/'.join(f'{v:,}' for v in s['sizes'])} neurons, {s['n_w']:,} edges, lognormal "
@@ -384,7 +413,8 @@ def run_ours(a, W, rank, world, dev, torch, dist, graph=None):
            "config": {"workload": W["desc"], "baseline_config": W["cfg"], "global_batch": Bg, "per_gpu_batch": B,
                       "parallelism": (f"dp{world}" if train else f"batch-sharded x{world}, no collective"),
                       "l2": "flushed between timed steps (256 MiB write, outside the step events)",
-                      "graph": ("synthetic untrimmed 166,700-neuron graph" if W.get("graph") == "full"
+                      "graph": ("bot/model.pt (trimmed male-CNS 3-hop graph)" if W.get("graph") == "model"
+                                else "synthetic untrimmed 166,700-neuron graph" if W.get("graph") == "full"
                                 else f"synthetic flyguy-sized {len(s['sizes']) - 1}-hop, {a.sources} sources"),
                       "edges": s["n_w"],
                       "edge_steps": E,
@@ -650,7 +680,8 @@ def run_play(a, W, reference: bool):
     out = {"metric": W["metric"], "value": round(value, 1), "unit": W["unit"], "n_gpus": 0 if reference else 1,
            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt * CALLS * 1e3, 4),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-           "data": "synthetic: the config-2 graph, obs ~ N(0,1)",
+           "data": ("the reference's bot/model.pt network and weights, obs ~ N(0,1)" if W.get("graph") == "model"
+                    else "synthetic: the config-2 graph, obs ~ N(0,1)"),
            "config": {"workload": W["desc"], "baseline_config": W["cfg"], "cars_per_call": W["batch"],
                       "calls_per_step": CALLS, "timing": "host wall clock per fly_forward call",
                       "latency_ms_per_call": round(dt * 1e3, 4)},
