@@ -101,6 +101,8 @@ def args_():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-train", action="store_true", help="default workload: leave out the config-3 training block")
     ap.add_argument("--no-check", action="store_true", help="leave out the 16-bit argmax-agreement check")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="training at N > 1: one all-reduce after the backward instead of buckets overlapping it")
     ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling of a small case only)")
     ap.add_argument("--sources", choices=["zipf", "uniform"], default="zipf",
                     help="source distribution of the 3-hop synthetic graph (configs 1-3): Zipf(1.5) ranks, or uniform "
@@ -287,14 +289,27 @@ def run_ours(a, W, rank, world, dev, torch, dist, graph=None):
     flush = torch.empty(64 * 2 ** 20, dtype=torch.float32, device=dev)      # 256 MiB > 126 MB L2
     train = W["flags"] == "train"
     grad = h.flat(4) if train else None
+    # data-parallel mean in the library's gradient buckets, each started as soon as the backward finishes it (one
+    # piece a step); otherwise one all-reduce of the whole flat gradient after the backward
+    from flyguy_b200.dist import BucketedMean
+    bucketed = BucketedMean(h) if train and world > 1 and piece == B and not a.no_overlap else None
+
+    def mean_grad():
+        if world == 1:
+            return
+        if bucketed:
+            bucketed.finish()
+        else:
+            dist.all_reduce(grad, op=dist.ReduceOp.AVG)
 
     def step():
         if train:
             h.zero_grad()
             for lo in range(0, B, piece):
                 h.teach(obs[lo:lo + piece], teacher[lo:lo + piece], 1.0, logits=None, stats=False, loss_norm=B)
-            if world > 1:
-                dist.all_reduce(grad, op=dist.ReduceOp.AVG)
+            if bucketed:
+                bucketed.start()
+            mean_grad()
             h.step(LR, 0.3 * LR, LR, 0.0, 0.999)
         else:
             h.forward(obs, 0, out=logits)
@@ -393,7 +408,7 @@ def run_ours(a, W, rank, world, dev, torch, dist, graph=None):
         agreement = argmax_agreement(s, P, obs_np, logits.cpu().numpy(), W["flags"])
     # ---- e2e through the host-buffer entry points
     e2e = None if a.no_e2e else run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier,
-                                          max_over_ranks, grad, piece)
+                                          max_over_ranks, grad, piece, bucketed)
     # ---- CPU baseline (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -411,7 +426,10 @@ def run_ours(a, W, rank, world, dev, torch, dist, graph=None):
                     f"in-degree mean 35, {'Zipf(1.5)' if a.sources == 'zipf' else 'uniform'} sources), obs ~ N(0,1), "
                     "teacher ~ N(0,4)"),
            "config": {"workload": W["desc"], "baseline_config": W["cfg"], "global_batch": Bg, "per_gpu_batch": B,
-                      "parallelism": (f"dp{world}" if train else f"batch-sharded x{world}, no collective"),
+                      "parallelism": ((f"dp{world}, gradient all-reduce in {len(bucketed.early)} early + "
+                                       f"{len(bucketed.late)} late buckets overlapping the backward" if bucketed else
+                                       f"dp{world}, one gradient all-reduce per step") if train
+                                      else f"batch-sharded x{world}, no collective"),
                       "l2": "flushed between timed steps (256 MiB write, outside the step events)",
                       "graph": ("bot/model.pt (trimmed male-CNS 3-hop graph)" if W.get("graph") == "model"
                                 else "synthetic untrimmed 166,700-neuron graph" if W.get("graph") == "full"
@@ -457,7 +475,8 @@ def traffic_of(cls: str, W, B: int, sources: str = "zipf") -> float | None:
     return round(float(v) * B / d["batch"]) if v is not None else None
 
 
-def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier, max_over_ranks, grad, piece):
+def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier, max_over_ranks, grad, piece,
+            bucketed=None):
     train = W["flags"] == "train"
     obs_h = torch.from_numpy(obs_np).pin_memory()
     out_h = torch.empty(B, s["n_act"]).pin_memory()
@@ -475,7 +494,11 @@ def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barr
                 st = h.teach(obs_d[lo:lo + piece], teach_d[lo:lo + piece], 1.0, logits=None, stats=world == 1,
                              loss_norm=B)
             if world > 1:
-                dist.all_reduce(grad, op=dist.ReduceOp.AVG)
+                if bucketed:
+                    bucketed.start()
+                    bucketed.finish()
+                else:
+                    dist.all_reduce(grad, op=dist.ReduceOp.AVG)
                 h.step(LR, 0.3 * LR, LR, 0.0, 0.999)
                 h.sync()                             # the loss sums come back after the step
             else:

@@ -2,6 +2,7 @@
 // include/flyguy_b200.h. The reference's equivalent is the host half of flyguy/native/flyguy_train.cu (load_net
 // 230-256, alloc_batch 308-317, forward_logits 320-332, backward 339-359, fc_* 553-629).
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -33,6 +34,7 @@ thread_local std::string g_create_error;    // fg_last_error(NULL): why the last
 
 struct Hop {
     int rows = 0, n_src = 0, E = 0, P = 0;
+    long long wlo = 0, whi = 0;              // the strength indices this hop's edges use: [wlo, whi)
     long long pbase = 0;                     // first merged pair of this hop in the concatenated arrays
     long long rbase = 0;                     // first row of this hop's layer in the per-row arrays
     bool widx_unique = true, redrive = false;
@@ -114,6 +116,9 @@ struct Core {
     float* sv_sq = nullptr;                             //   sums of squared pre-activations (all layers' rows)
     long long launches = 0;
     Timer timer;
+    // gradient buckets for an all-reduce that overlaps the backward: stage 0 = the output plug's gradient is final,
+    // stage k + 1 = hop k's weight gradient is final; the caller's event for a stage is recorded when it is reached
+    std::vector<cudaEvent_t> stage_ev;
 };
 
 cudaEvent_t pool_event(Core& c) {
@@ -416,6 +421,11 @@ void upload_net(Core& c, NetHost& n) {
         h.d_drow = h.redrive ? upload(c, src.drow) : nullptr;
         row_nid.insert(row_nid.end(), src.nid.begin(), src.nid.end());
         build_hop_plan(c, h, src.crow, src.col, src.widx, src.drow, pairs, gptr, gw, mark);
+        if (!src.widx.empty()) {
+            const auto mm = std::minmax_element(src.widx.begin(), src.widx.end());
+            h.wlo = *mm.first;
+            h.whi = (long long)*mm.second + 1;
+        }
         rbase += h.rows;
     }
     c.d_dn = upload(c, n.dn);
@@ -680,6 +690,37 @@ void forward(Core& c, const float* obs, int B, float* logits, int ema, bool keep
     else forward_t<float>(c, obs, B, logits, ema, keep_lg);
 }
 
+void record_stage(Core& c, int stage) {
+    if (stage < (int)c.stage_ev.size() && c.stage_ev[stage]) CK(cudaEventRecord(c.stage_ev[stage], c.st));
+}
+
+// Ranges of the flat gradient that become final before the backward ends, and the stage at which each does: the
+// output plug's arrays at stage 0; hop k's strengths [wlo, whi) at stage k + 1 when no hop the backward visits later
+// (k - 1 .. 0) uses a strength inside that range (weights shared across hops - the shipped model.pt network - leave
+// no such range). The rest of [0, flat length) is final at the end (stage -1).
+std::vector<std::array<long long, 3>> grad_buckets(const Core& c) {
+    std::vector<std::array<long long, 3>> early{{c.off[5], c.off[7], 0}};
+    for (int k = c.hops - 1; k >= 0; --k) {
+        const Hop& h = c.hop[k];
+        if (h.whi <= h.wlo) continue;
+        bool alone = true;
+        for (int j = 0; j < k; ++j)
+            if (c.hop[j].whi > c.hop[j].wlo && c.hop[j].wlo < h.whi && h.wlo < c.hop[j].whi) alone = false;
+        if (alone) early.push_back({h.wlo, h.whi, k + 1});
+    }
+    std::vector<std::array<long long, 3>> out = early;
+    std::vector<std::pair<long long, long long>> taken;
+    for (auto& b : early) taken.push_back({b[0], b[1]});
+    std::sort(taken.begin(), taken.end());
+    long long at = 0;
+    for (auto& t : taken) {
+        if (t.first > at) out.push_back({at, t.first, -1});
+        at = std::max(at, t.second);
+    }
+    if (at < c.off[7]) out.push_back({at, c.off[7], -1});
+    return out;
+}
+
 // gradient of the loss whose d/dlogits is in c.dl [n_act, B], through the states of the last forward; ADDED to G.
 // Per hop k (top down): the weight gradient of its merged pairs from gz_k and the states below, then the transposed
 // product into the layer below with that layer's neuron backward fused in (for the sensory layer: gh0 for the plug).
@@ -707,6 +748,7 @@ void backward(Core& c, int B) {
                                                                                      c.G + c.off[6], c.n_act, c.n_dn,
                                                                                      splits);
     });
+    record_stage(c, 0);
     float* gz = c.gz_a;                      // gz of the layer being processed
     float* nxt = c.gz_b;                     // gz (or gh0) of the layer below
     // only the output plug's columns of the top layer get a gradient; the other rows of gh / gz are never read
@@ -748,6 +790,7 @@ void backward(Core& c, int B) {
                                                             c.G + c.off[0], h.n_sd_items, B, B);
                 });
         }
+        record_stage(c, k + 1);                          // (hop k's weight gradient is final)
         const bool full = B % 256 == 0;
         auto transposed = [&](auto epi, const NeuronEpi& ep) {
             constexpr bool EPI = decltype(epi)::value;
@@ -925,6 +968,26 @@ int fg_layout(void* h, int* sizes, long long* pairs) {
         for (int k = 0; k <= c.hops; ++k) if (sizes) sizes[k] = c.sizes[k];
         for (int k = 0; k < c.hops; ++k) if (pairs) pairs[k] = c.hop[k].P;
         return c.hops;
+    }, -1);
+}
+
+int fg_set_stage_event(void* h, int stage, void* event) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        if (stage < 0 || stage > c.hops) throw Err("fg_set_stage_event: stage " + std::to_string(stage) + " is not 0.." +
+                                                   std::to_string(c.hops));
+        if ((int)c.stage_ev.size() <= stage) c.stage_ev.resize(stage + 1, nullptr);
+        c.stage_ev[stage] = static_cast<cudaEvent_t>(event);
+        return 0;
+    }, -1);
+}
+
+int fg_grad_buckets(void* h, long long* out, int n) {
+    return guarded(h, [&]() {
+        const auto b = grad_buckets(*as_core(h));
+        for (int i = 0; i < n && i < (int)b.size(); ++i)
+            for (int j = 0; j < 3; ++j) out[3 * i + j] = b[i][j];
+        return (int)b.size();
     }, -1);
 }
 

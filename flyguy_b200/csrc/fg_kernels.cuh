@@ -688,8 +688,9 @@ __global__ void __launch_bounds__(256) k_out_reduce(const float* __restrict__ pa
 // argmax agreement. teacher is the caller's [B, n_act]; lg and dl are neuron-major.
 // A CTA owns kLossS samples: all its threads stage their logit rows ([a][b], coalesced) and teacher rows ([b][a],
 // contiguous) in shared memory (teacher row stride n_act + 1 words: odd for n_act = 90, so the per-sample reads do not
-// conflict), then one thread per sample runs the three passes over its actions in order, writes dl into the staged
-// logits, and the CTA stores dl back row by row.
+// conflict), then a warp per sample computes it with its lanes over the actions and warp reductions (a short
+// dependency chain at small batches, where one thread per sample running the passes in order took 26 us), writes dl
+// into the staged logits, and the CTA stores dl back row by row.
 constexpr int kLossS = 32, kLossT = 256;
 __global__ void __launch_bounds__(kLossT) k_loss(const float* __restrict__ lg, const float* __restrict__ teacher,
                                                  float* __restrict__ dl, float* __restrict__ kl_s,
@@ -709,27 +710,52 @@ __global__ void __launch_bounds__(kLossT) k_loss(const float* __restrict__ lg, c
         stt[r * tw + (i - r * n_act)] = __ldg(&tb[i]);
     }
     __syncthreads();
-    if (threadIdx.x < nb) {
-        const float* t = stt + j * tw;
-        float* s_ = sl + j;
+    // a warp per sample (8 warps, 4 samples each), the lanes over the actions (3 a lane for 90 actions): max with the
+    // first index in action order on ties (the reference's strict '>' scan), the two log-sum-exps, the KL and dl
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int PA = kMaxAct / 32;
+    for (int jj = warp; jj < nb; jj += kLossT / 32) {
+        const float* t = stt + jj * tw;
+        float sv[PA], tv[PA];
         float ms = -INFINITY, mt = -INFINITY;
-        int as = 0, at = 0;
-        for (int a = 0; a < n_act; ++a) {
-            float s = s_[a * kLossS], tv = t[a] * it;
-            if (s > ms) { ms = s; as = a; }
-            if (tv > mt) { mt = tv; at = a; }
+        int as = n_act, at = n_act;
+#pragma unroll
+        for (int k = 0; k < PA; ++k) {
+            const int a = lane + 32 * k;
+            sv[k] = a < n_act ? sl[a * kLossS + jj] : -INFINITY;
+            tv[k] = a < n_act ? t[a] * it : -INFINITY;
+            if (a < n_act && (sv[k] > ms || as == n_act)) { ms = sv[k]; as = a; }
+            if (a < n_act && (tv[k] > mt || at == n_act)) { mt = tv[k]; at = a; }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {                   // (value, first index) maxima over the warp
+            const float ms2 = __shfl_xor_sync(0xffffffffu, ms, o), mt2 = __shfl_xor_sync(0xffffffffu, mt, o);
+            const int as2 = __shfl_xor_sync(0xffffffffu, as, o), at2 = __shfl_xor_sync(0xffffffffu, at, o);
+            if (ms2 > ms || (ms2 == ms && as2 < as)) { ms = ms2; as = as2; }
+            if (mt2 > mt || (mt2 == mt && at2 < at)) { mt = mt2; at = at2; }
         }
         float zs = 0.f, zt = 0.f;
-        for (int a = 0; a < n_act; ++a) { zs += expf(s_[a * kLossS] - ms); zt += expf(t[a] * it - mt); }
+#pragma unroll
+        for (int k = 0; k < PA; ++k)
+            if (lane + 32 * k < n_act) { zs += expf(sv[k] - ms); zt += expf(tv[k] - mt); }
+        zs = warp_sum(zs);
+        zt = warp_sum(zt);
         const float ls = ms + logf(zs), lt = mt + logf(zt);
         float kl = 0.f;
-        for (int a = 0; a < n_act; ++a) {
-            float lps = s_[a * kLossS] - ls, lpt = t[a] * it - lt, pt = expf(lpt);
-            kl += pt * (lpt - lps);
-            s_[a * kLossS] = (expf(lps) - pt) * inv_norm;
+#pragma unroll
+        for (int k = 0; k < PA; ++k) {
+            const int a = lane + 32 * k;
+            if (a < n_act) {
+                const float lps = sv[k] - ls, lpt = tv[k] - lt, pt = expf(lpt);
+                kl += pt * (lpt - lps);
+                sl[a * kLossS + jj] = (expf(lps) - pt) * inv_norm;
+            }
         }
-        kl_s[b0 + j] = kl;
-        ag_s[b0 + j] = as == at ? 1.f : 0.f;
+        kl = warp_sum(kl);
+        if (lane == 0) {
+            kl_s[b0 + jj] = kl;
+            ag_s[b0 + jj] = as == at ? 1.f : 0.f;
+        }
     }
     __syncthreads();
 #pragma unroll 4

@@ -27,3 +27,66 @@ def mean_(tensors) -> None:
         else:                                             # gloo has no AVG
             td.all_reduce(t, op=td.ReduceOp.SUM)
             t.div_(world)
+
+
+class BucketedMean:
+    """The mean of a handle's flat gradient over all ranks, taken in the library's buckets (fg_grad_buckets) so that
+    most of it crosses NVLink while the backward is still running: a bucket whose values are final early (the output
+    plug's arrays, each hop's strengths when no later hop shares them) is all-reduced on a side stream as soon as the
+    backward records its stage event; the rest after the backward returns. The result is the same in-place average as
+    mean_([flat]) (the same reduction on the same values, per range).
+
+        mean = BucketedMean(handle)          # once: buckets, events, the side stream
+        handle.teach(...)                    # enqueues the step; its backward records the stage events
+        mean.start()                         # early buckets wait on their events on the side stream
+        mean.finish()                        # the remaining buckets; the current stream waits for all of them
+    """
+
+    def __init__(self, handle):
+        self.h = handle
+        self.grad = handle.flat(4)
+        self.stream = torch.cuda.Stream(device=handle.device)
+        hops = len(handle.layout()[1])
+        self.events = {}
+        for _, _, st in handle.grad_buckets():
+            if st >= 0 and st not in self.events:
+                ev = torch.cuda.Event()
+                handle.set_stage_event(st, ev)
+                self.events[st] = ev
+        buckets = handle.grad_buckets()
+        # the backward reaches stage 0 (output plug) first, then hops+..., 1 (the hops top down)
+        self.early = sorted([b for b in buckets if b[2] >= 0], key=lambda b: 0 if b[2] == 0 else hops + 1 - b[2])
+        self.late = [b for b in buckets if b[2] < 0]
+        self.works = []
+
+    def _reduce(self, lo, hi):
+        t = self.grad[lo:hi]
+        if td.get_backend() == "nccl":
+            return td.all_reduce(t, op=td.ReduceOp.AVG, async_op=True)
+        w = td.all_reduce(t, op=td.ReduceOp.SUM, async_op=True)
+        w.wait()
+        t.div_(td.get_world_size())
+        return None
+
+    def start(self) -> None:
+        self.works = []
+        if not on():
+            return
+        with torch.cuda.stream(self.stream):
+            for lo, hi, st in self.early:
+                self.stream.wait_event(self.events[st])
+                self.works.append(self._reduce(lo, hi))
+
+    def finish(self) -> None:
+        if not on():
+            return
+        main = torch.cuda.current_stream(self.grad.device)
+        with torch.cuda.stream(self.stream):
+            self.stream.wait_stream(main)
+            for lo, hi, _ in self.late:
+                self.works.append(self._reduce(lo, hi))
+        for w in self.works:
+            if w is not None:
+                w.wait()                                 # the current (main) stream waits for the NCCL work
+        main.wait_stream(self.stream)
+        self.works = []

@@ -42,6 +42,8 @@ SIGNATURES = {
     "fg_offsets": (None, [_vp, ctypes.POINTER(_cll)]),
     "fg_layout": (_ci, [_vp, ctypes.POINTER(_ci), ctypes.POINTER(_cll)]),
     "fg_plan": (_ci, [_vp, ctypes.POINTER(_cll), _ci]),
+    "fg_grad_buckets": (_ci, [_vp, ctypes.POINTER(_cll), _ci]),
+    "fg_set_stage_event": (_ci, [_vp, _ci, _vp]),
     "fg_teach": (_ci, [_vp, _vp, _vp, _ci, _cf, _vp, ctypes.POINTER(ctypes.c_double)]),
     "fg_teach_ex": (_ci, [_vp, _vp, _vp, _ci, _cf, _cf, _vp, ctypes.POINTER(ctypes.c_double)]),
     "fg_forward_host": (_ci, [_vp, _vp, _ci, _vp, _ci]),
@@ -173,6 +175,23 @@ class Handle:
         t = n - 4
         return {"hops": hops, "plug_live": int(buf[t]), "n_s": int(buf[t + 1]), "fan": int(buf[t + 2]),
                 "n_dn": int(buf[t + 3])}
+
+    def grad_buckets(self) -> list[tuple[int, int, int]]:
+        """(first, end, stage) ranges of the flat gradient (fg_grad_buckets): stage s >= 0 final once the backward
+        reaches stage s, -1 at its end."""
+        buf = (ctypes.c_longlong * 96)()
+        n = self.L.fg_grad_buckets(self.h, buf, 32)
+        self.check()
+        return [(int(buf[3 * i]), int(buf[3 * i + 1]), int(buf[3 * i + 2])) for i in range(n)]
+
+    def set_stage_event(self, stage: int, event) -> None:
+        """Record `event` (a torch.cuda.Event, or None) when the backward reaches `stage` (fg_set_stage_event)."""
+        handle = None
+        if event is not None:
+            event.record()                                    # (creates the underlying CUDA event)
+            handle = event.cuda_event
+        if self.L.fg_set_stage_event(self.h, int(stage), handle):
+            self.check()
 
     # ---- weights
     def set_params(self, params, which: int = 0) -> None:

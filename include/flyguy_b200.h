@@ -99,6 +99,16 @@ int fg_layout(void* h, int* sizes, long long* pairs);
    of the live rows' pairs}, then {sensory rows the plug backward visits, sensory rows, plug fan, descending rows}.
    Writes min(n, count) values into out; returns the count (8 * hops + 4), or -1 on error. */
 int fg_plan(void* h, long long* out, int n);
+/* Gradient buckets for a data-parallel all-reduce that overlaps the backward (the reference all-reduces after the
+   whole backward: NativeAdam.step -> dist.mean_, fly_native.py:78-81). Writes up to n triples {first, end, stage} of the
+   flat gradient (fg_flat 4) into out and returns their count: stage 0 = final once the output plug's backward is
+   done, stage k + 1 = final once hop k's weight gradient is done, -1 = final when the backward returns. The ranges
+   cover [0, flat length) once. */
+int fg_grad_buckets(void* h, long long* out, int n);
+/* The caller's cudaEvent_t (NULL: none) that the backward records on the handle's stream when it reaches `stage`
+   (0..hops, as in fg_grad_buckets); a side stream that waits on it can start that bucket's all-reduce. Returns 0, or
+   -1 for a stage out of range. */
+int fg_set_stage_event(void* h, int stage, void* event);
 
 /* The distillation step's device half, fused: forward with the weights, KL(softmax(teacher * inv_temp) ||
  * softmax(logits)) averaged over the batch, its gradient through the network ADDED to the gradient.

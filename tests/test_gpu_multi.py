@@ -19,7 +19,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, out):
+def _rank(rank, world, port, out, bucketed=False):
     import torch
     import torch.distributed as td
     from datetime import timedelta
@@ -35,22 +35,30 @@ def _rank(rank, world, port, out):
         h.set_params(P)
         obs = torch.as_tensor(d["obs"][rank * B:(rank + 1) * B]).cuda()
         teacher = torch.as_tensor(d["teacher"][rank * B:(rank + 1) * B]).cuda()
+        mean = dist.BucketedMean(h) if bucketed else None
         h.zero_grad()
         h.teach(obs, teacher, float(d["inv_temp"]))
         assert dist.on()
-        dist.mean_([h.flat(4)])
+        if bucketed:                                   # buckets started as the backward finishes them
+            mean.start()
+            mean.finish()
+        else:
+            dist.mean_([h.flat(4)])
         G = [g.cpu().numpy() for g in h.get(4)]
         np.savez(Path(out) / f"r{rank}.npz", *G)
     finally:
         td.destroy_process_group()
 
 
-def test_two_gpu_gradient_mean_equals_full_batch(tmp_path, cuda):
+@pytest.mark.parametrize("bucketed", [False, True])
+def test_two_gpu_gradient_mean_equals_full_batch(tmp_path, cuda, bucketed):
+    """One all-reduce after the backward, or the library's buckets each started on a side stream when the backward
+    reaches its stage: either way the averaged gradient is the whole batch's."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
-    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), bucketed), nprocs=2, start_method="spawn")
     # one process, the whole batch: the mean over ranks of per-half gradients (each scaled by 1/half) equals the
     # gradient of the whole batch (scaled by 1/B)
     from flyguy_b200 import native
@@ -64,3 +72,38 @@ def test_two_gpu_gradient_mean_equals_full_batch(tmp_path, cuda):
         got = np.load(tmp_path / f"r{r}.npz")
         for i in range(7):
             assert rel(got[f"arr_{i}"], want[i]) < 1e-4, (r, i)
+
+
+def test_gradient_buckets_cover_the_flat_gradient_and_their_events_fire(cuda):
+    """fg_grad_buckets: the ranges cover [0, flat length) once; on the synthetic graph (hops on disjoint strength
+    ranges) the output plug and every hop's strengths are early buckets, on a graph whose hops share strengths only the
+    output plug is; every stage event of a step has completed once the step has."""
+    import torch
+    from flyguy_b200 import native, synth
+    for s, want_early in ((synth.make_synthetic(sizes=(300, 700, 500, 60), total_edges=30_000, seed=3)[0], 4),
+                          (load_case("toy_h3")[0], None)):
+        P = [np.zeros(n, np.float32) for n in s.param_sizes()]
+        h = native.Handle(s, 64)
+        h.set_params(P)
+        buckets = sorted(h.grad_buckets())
+        n = h.flat(4).numel()
+        at = 0
+        for lo, hi, st in buckets:
+            assert lo == at and hi > lo, buckets
+            at = hi
+        assert at == n
+        early = [b for b in buckets if b[2] >= 0]
+        if want_early is not None:
+            assert len(early) == want_early and {b[2] for b in early} == {0, 1, 2, 3}
+        else:
+            assert 0 in {b[2] for b in early}
+        evs = {st: torch.cuda.Event() for st in {b[2] for b in early}}
+        for st, ev in evs.items():
+            h.set_stage_event(st, ev)
+        obs = torch.randn(64, s["obs_dim"], device="cuda")
+        h.zero_grad()
+        h.teach(obs, torch.randn(64, s["n_act"], device="cuda"), 1.0)
+        torch.cuda.synchronize()
+        assert all(ev.query() for ev in evs.values())
+        with pytest.raises(native.FlyguyError):
+            h.set_stage_event(99, evs[0])
