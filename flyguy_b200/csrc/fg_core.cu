@@ -148,6 +148,29 @@ void launch(Core& c, int cls, F&& f) {
     }
 }
 
+// A kernel of the step on the handle's stream with programmatic dependent launch: the runtime may start its CTAs while
+// the stream's previous kernel finishes its last wave; every kernel of the library begins with pdl_enter(), which
+// waits for the previous grid to complete (its writes visible) before it reads anything, so only the launch and the
+// CTAs' start-up overlap the previous kernel's tail. Stream operations that are not kernels (copies, memsets, event
+// records) keep their ordinary ordering.
+#ifndef FG_PDL
+#define FG_PDL 1
+#endif
+template <class... KArgs, class... Args>
+void pdl(Core& c, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = c.st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = FG_PDL;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    CK(cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...));
+}
+
 template <class X>
 X* dalloc(Core& c, size_t n) {
     void* p = nullptr;
@@ -492,7 +515,7 @@ void alloc_all(Core& c) {
     // batch (or piece of one) it is computed in: one slice per ~320 dn columns, at most 8.
     c.out_chunks = (c.n_dn + kOtKC - 1) / kOtKC;
     {
-        const int want = std::max(1, std::min(8, (c.n_dn + 319) / 320));
+        const int want = std::max(1, std::min(kOutSlices, (c.n_dn + 319) / 320));
         c.out_cps = (c.out_chunks + want - 1) / want;
         c.out_slices = (c.out_chunks + c.out_cps - 1) / c.out_cps;
     }
@@ -561,16 +584,15 @@ static_assert(kOtN == kOutA, "the tensor-core output plug writes the partial sla
 void fold(Core& c, int which) {
     if (c.folded == which) return;
     const float* src = which ? c.EMA : c.P;
-    launch(c, K_FOLD, [&]() { k_fold_neurons<<<blocks(c.R), 256, 0, c.st>>>(c.d_row_nid, src + c.off[1], src + c.off[2], c.d_rgain, c.d_rthr,
+    launch(c, K_FOLD, [&]() { pdl(c, k_fold_neurons, blocks(c.R), 256, 0, c.d_row_nid, src + c.off[1], src + c.off[2], c.d_rgain, c.d_rthr,
                                                   c.d_rsig, (int)c.R); });
     if (c.Ptot) {
-        launch(c, K_FOLD, [&]() { k_fold_pairs<<<blocks(c.Ptot, kThreads), kThreads, 0, c.st>>>(c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, c.d_tpos, c.d_tpairs, (int)c.Ptot); });
+        launch(c, K_FOLD, [&]() { pdl(c, k_fold_pairs, blocks(c.Ptot, kThreads), kThreads, 0, c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, c.d_tpos, c.d_tpairs, (int)c.Ptot); });
     }
-    launch(c, K_FOLD, [&]() { k_fold_ow_tc<<<blocks((long long)c.out_chunks * kOtN * kOtKC), 256, 0, c.st>>>(
+    launch(c, K_FOLD, [&]() { pdl(c, k_fold_ow_tc, blocks((long long)c.out_chunks * kOtN * kOtKC), 256, 0,
                                   src + c.off[5], c.ow_tc, c.n_act, c.n_dn, c.out_chunks); });
     if (c.ow_bt)
-        launch(c, K_FOLD, [&]() { k_fold_owbt<<<blocks((long long)c.ob_tiles * kObChunks * kObN * kOtKC), 256, 0,
-                                                   c.st>>>(src + c.off[5], c.ow_bt, c.n_act, c.n_dn, c.ob_tiles); });
+        launch(c, K_FOLD, [&]() { pdl(c, k_fold_owbt, blocks((long long)c.ob_tiles * kObChunks * kObN * kOtKC), 256, 0, src + c.off[5], c.ow_bt, c.n_act, c.n_dn, c.ob_tiles); });
     c.folded = which;
 }
 
@@ -598,19 +620,19 @@ void plug_launch(Core& c, const float* Pw, int B) {
     const dim3 g(nblk, chunks);
     launch(c, K_PLUG_FWD, [&]() {
         if (c.fan == 8)
-            k_plug_fwd<T, SAVE, 8><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+            pdl(c, k_plug_fwd<T, SAVE, 8>, g, kPlugThreads, smem, c.d_in_col, Pw + c.off[3], Pw + c.off[4],
                 c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
         else if (c.fan == 16)
-            k_plug_fwd<T, SAVE, 16><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+            pdl(c, k_plug_fwd<T, SAVE, 16>, g, kPlugThreads, smem, c.d_in_col, Pw + c.off[3], Pw + c.off[4],
                 c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
         else if (c.fan == 4)
-            k_plug_fwd<T, SAVE, 4><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+            pdl(c, k_plug_fwd<T, SAVE, 4>, g, kPlugThreads, smem, c.d_in_col, Pw + c.off[3], Pw + c.off[4],
                 c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
         else if (c.fan == 12)
-            k_plug_fwd<T, SAVE, 12><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+            pdl(c, k_plug_fwd<T, SAVE, 12>, g, kPlugThreads, smem, c.d_in_col, Pw + c.off[3], Pw + c.off[4],
                 c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
         else
-            k_plug_fwd<T, SAVE, 0><<<g, kPlugThreads, smem, c.st>>>(c.d_in_col, Pw + c.off[3], Pw + c.off[4],
+            pdl(c, k_plug_fwd<T, SAVE, 0>, g, kPlugThreads, smem, c.d_in_col, Pw + c.off[3], Pw + c.off[4],
                 c.d_rgain, c.d_rthr, c.x, c.drive, (T*)c.h0, c.n_s, c.fan, rows, c.obs_dim, B);
     });
 }
@@ -622,11 +644,11 @@ void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
         const dim3 g((h.rows + kWarps - 1) / kWarps, (unsigned)((B + 32 * N - 1) / (32 * N)));
         launch(c, K_HOP_FWD, [&]() {
             if (B % (32 * N) == 0)
-                k_hop_fwd_surv<TI, TO, true><<<g, kThreads, 0, c.st>>>(h.d_rows, c.d_pairs + h.pbase,
+                pdl(c, k_hop_fwd_surv<TI, TO, true>, g, kThreads, 0, h.d_rows, c.d_pairs + h.pbase,
                     (const TI*)hp, c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive, (TO*)h.d_h, h.rows, B,
                     c.sv_fired + h.rbase, c.sv_sq + h.rbase);
             else
-                k_hop_fwd_surv<TI, TO, false><<<g, kThreads, 0, c.st>>>(h.d_rows, c.d_pairs + h.pbase,
+                pdl(c, k_hop_fwd_surv<TI, TO, false>, g, kThreads, 0, h.d_rows, c.d_pairs + h.pbase,
                     (const TI*)hp, c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive, (TO*)h.d_h, h.rows, B,
                     c.sv_fired + h.rbase, c.sv_sq + h.rbase);
         });
@@ -637,11 +659,11 @@ void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
     const bool full = B % (32 * N) == 0;
     launch(c, K_HOP_FWD, [&]() {
         if (full)
-            k_hop_fwd<TI, TO, true><<<g, kThreads, 0, c.st>>>(h.d_rows, c.d_pairs + h.pbase, (const TI*)hp,
+            pdl(c, k_hop_fwd<TI, TO, true>, g, kThreads, 0, h.d_rows, c.d_pairs + h.pbase, (const TI*)hp,
                                                               c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow,
                                                               c.drive, (TO*)h.d_h, h.rows, B);
         else
-            k_hop_fwd<TI, TO, false><<<g, kThreads, 0, c.st>>>(h.d_rows, c.d_pairs + h.pbase, (const TI*)hp,
+            pdl(c, k_hop_fwd<TI, TO, false>, g, kThreads, 0, h.d_rows, c.d_pairs + h.pbase, (const TI*)hp,
                                                                c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow,
                                                                c.drive, (TO*)h.d_h, h.rows, B);
     });
@@ -654,7 +676,7 @@ void forward_t(Core& c, const float* obs, int B, float* logits, int ema, bool ke
     const float* Pw = ema ? c.EMA : c.P;
     if (obs) {
         launch(c, K_TRANSPOSE, [&]() {
-            k_to_neuron_major<<<dim3((B + 31) / 32, (c.obs_dim + 31) / 32), dim3(32, 8), 0, c.st>>>(obs, c.x, c.obs_dim,
+            pdl(c, k_to_neuron_major, dim3((B + 31) / 32, (c.obs_dim + 31) / 32), dim3(32, 8), 0, obs, c.x, c.obs_dim,
                                                                                                 B, B);
         });
     }
@@ -675,10 +697,10 @@ void forward_t(Core& c, const float* obs, int B, float* logits, int ema, bool ke
     ot.wt = c.ow_tc; ot.dn = c.d_dn; ot.hK = (const float*)hp; ot.part = c.out_part; ot.err = c.d_err;
     ot.n_dn = c.n_dn; ot.B = B; ot.ld = B; ot.chunks = c.out_chunks; ot.cps = c.out_cps;
     launch(c, K_OUT_FWD, [&]() {
-        k_out_tc<<<dim3((B + kOtM - 1) / kOtM, c.out_slices), kOtThreads, kOtSmem, c.st>>>(ot);
+        pdl(c, k_out_tc, dim3((B + kOtM - 1) / kOtM, c.out_slices), kOtThreads, kOtSmem, ot);
     });
     launch(c, K_OUT_FWD, [&]() {
-        k_out_reduce<<<(B + 31) / 32, 256, 0, c.st>>>(c.out_part, Pw + c.off[6], keep_lg ? c.lg : nullptr, logits,
+        pdl(c, k_out_reduce, (B + 31) / 32, 256, 0, c.out_part, Pw + c.off[6], keep_lg ? c.lg : nullptr, logits,
                                                       c.out_slices, c.n_act, B, B);
     });
     c.lastB = B;
@@ -741,10 +763,10 @@ void backward(Core& c, int B) {
         OutBw ow;
         ow.dl = c.dl; ow.hK = hK; ow.dn = c.d_dn; ow.part = c.part; ow.err = c.d_err;
         ow.n_act = c.n_act; ow.n_dn = c.n_dn; ow.B = B; ow.ld = B; ow.slice_len = split_len;
-        launch(c, K_OUT_BWD, [&]() { k_out_bwd_w_tc<<<dim3(wtiles, splits), kOtThreads, kOwSmem, c.st>>>(ow); });
+        launch(c, K_OUT_BWD, [&]() { pdl(c, k_out_bwd_w_tc, dim3(wtiles, splits), kOtThreads, kOwSmem, ow); });
     }
     launch(c, K_OUT_BWD, [&]() {
-        k_out_bwd_reduce<<<blocks((long long)c.n_act * (c.n_dn + 1)), 256, 0, c.st>>>(c.part, c.G + c.off[5],
+        pdl(c, k_out_bwd_reduce, blocks((long long)c.n_act * (c.n_dn + 1)), 256, 0, c.part, c.G + c.off[5],
                                                                                      c.G + c.off[6], c.n_act, c.n_dn,
                                                                                      splits);
     });
@@ -761,11 +783,11 @@ void backward(Core& c, int B) {
         const int groups = std::max(1, std::min(c.ob_tiles, c.n_sm / st));
         ob.tpg = (c.ob_tiles + groups - 1) / groups;
         const int ng = (c.ob_tiles + ob.tpg - 1) / ob.tpg;
-        launch(c, K_OUT_BWD, [&]() { k_out_bwd_h_tc<<<dim3(st, ng), kOtThreads, kObSmem, c.st>>>(ob); });
+        launch(c, K_OUT_BWD, [&]() { pdl(c, k_out_bwd_h_tc, dim3(st, ng), kOtThreads, kObSmem, ob); });
     }
     if (top.n_live_dst)
     launch(c, K_ACT_BWD, [&]() {
-        k_act_bwd<float><<<top.n_live_dst, kThreads, 0, c.st>>>(nxt, hK, top.d_nid, top.d_drow,
+        pdl(c, k_act_bwd<float>, top.n_live_dst, kThreads, 0, nxt, hK, top.d_nid, top.d_drow,
                                                                 c.d_rgain + top.rbase, c.d_rthr + top.rbase,
                                                                 c.d_rsig + top.rbase, gz, c.G + c.off[1],
                                                                 c.G + c.off[2], c.gdrive, c.live, top.d_live_dst, B,
@@ -779,13 +801,13 @@ void backward(Core& c, int B) {
             const unsigned g = (unsigned)((h.n_sd_items + kWarps - 1) / kWarps);
             if (h.widx_unique)
                 launch(c, K_SDDMM, [&]() {
-                    k_sddmm<false><<<g, kThreads, 0, c.st>>>(h.d_sd_items, h.d_pptr, c.d_pairs + h.pbase,
+                    pdl(c, k_sddmm<false>, g, kThreads, 0, h.d_sd_items, h.d_pptr, c.d_pairs + h.pbase,
                                                              c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live,
                                                              c.G + c.off[0], h.n_sd_items, B, B);
                 });
             else
                 launch(c, K_SDDMM, [&]() {
-                    k_sddmm<true><<<g, kThreads, 0, c.st>>>(h.d_sd_items, h.d_pptr, c.d_pairs + h.pbase,
+                    pdl(c, k_sddmm<true>, g, kThreads, 0, h.d_sd_items, h.d_pptr, c.d_pairs + h.pbase,
                                                             c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live,
                                                             c.G + c.off[0], h.n_sd_items, B, B);
                 });
@@ -798,11 +820,11 @@ void backward(Core& c, int B) {
             if (h.n_segs == 0) return;
             launch(c, K_HOP_BWD, [&]() {
                 if (full)
-                    k_hop_bwd_t<EPI, true><<<gs, kThreads, 0, c.st>>>(h.d_segs, h.d_seg_red, h.d_reds, c.seg_done,
+                    pdl(c, k_hop_bwd_t<EPI, true>, gs, kThreads, 0, h.d_segs, h.d_seg_red, h.d_reds, c.seg_done,
                                                                       c.d_tpairs + h.tbase, gz, nxt, c.seg_part,
                                                                       h.n_segs, B, ep);
                 else
-                    k_hop_bwd_t<EPI, false><<<gs, kThreads, 0, c.st>>>(h.d_segs, h.d_seg_red, h.d_reds, c.seg_done,
+                    pdl(c, k_hop_bwd_t<EPI, false>, gs, kThreads, 0, h.d_segs, h.d_seg_red, h.d_reds, c.seg_done,
                                                                        c.d_tpairs + h.tbase, gz, nxt, c.seg_part,
                                                                        h.n_segs, B, ep);
             });
@@ -813,7 +835,7 @@ void backward(Core& c, int B) {
             transposed(std::true_type{}, ep);
             if (h.n_live_src)
             launch(c, K_ACT_BWD, [&]() {
-                k_neuron_reduce<<<blocks(h.n_live_src), 256, 0, c.st>>>(c.nsum, h.d_live_src, lo.d_nid,
+                pdl(c, k_neuron_reduce, blocks(h.n_live_src), 256, 0, c.nsum, h.d_live_src, lo.d_nid,
                                                                        c.d_rsig + lo.rbase, c.G + c.off[1],
                                                                        c.G + c.off[2], c.live, h.n_live_src, chunks);
             });
@@ -828,15 +850,15 @@ void backward(Core& c, int B) {
     launch(c, K_PLUG_BWD, [&]() {
         const dim3 g((c.n_plug_live + kWarps - 1) / kWarps);
         if (c.fan == 8)
-            k_plug_bwd<8><<<g, kThreads, 0, c.st>>>(c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
+            pdl(c, k_plug_bwd<8>, g, kThreads, 0, c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
                                                     c.x, c.d_rgain, c.d_rthr, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
                                                     c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
         else if (c.fan == 16)
-            k_plug_bwd<16><<<g, kThreads, 0, c.st>>>(c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
+            pdl(c, k_plug_bwd<16>, g, kThreads, 0, c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
                                                      c.x, c.d_rgain, c.d_rthr, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
                                                      c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
         else
-            k_plug_bwd<0><<<g, kThreads, 0, c.st>>>(c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
+            pdl(c, k_plug_bwd<0>, g, kThreads, 0, c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
                                                     c.x, c.d_rgain, c.d_rthr, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
                                                     c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
     });
@@ -846,8 +868,8 @@ void backward(Core& c, int B) {
 void grad_norm_launch(Core& c, float max_norm) {
     const long long n = c.off[7];
     const int nb = (int)std::min<long long>(1024, std::max<long long>(1, blocks(n)));
-    launch(c, K_NORM, [&]() { k_sumsq<<<nb, 256, 0, c.st>>>(c.G, n, c.norm_part); });
-    launch(c, K_NORM, [&]() { k_norm_final<<<1, 256, 0, c.st>>>(c.norm_part, nb, max_norm, c.norm); });
+    launch(c, K_NORM, [&]() { pdl(c, k_sumsq, nb, 256, 0, c.G, n, c.norm_part); });
+    launch(c, K_NORM, [&]() { pdl(c, k_norm_final, 1, 256, 0, c.norm_part, nb, max_norm, c.norm); });
 }
 float read_norm(Core& c) {
     float g = 0.f;
@@ -1062,7 +1084,7 @@ void fc_backward(void* h, const float* dlogits, int B) {
         Core& c = *as_core(h);
         check_batch(c, B);
         if (!c.train) throw Err("this handle was created for inference only");
-        launch(c, K_TRANSPOSE, [&]() { k_to_neuron_major<<<dim3((B + 31) / 32, (c.n_act + 31) / 32), dim3(32, 8), 0, c.st>>>(dlogits, c.dl, c.n_act,
+        launch(c, K_TRANSPOSE, [&]() { pdl(c, k_to_neuron_major, dim3((B + 31) / 32, (c.n_act + 31) / 32), dim3(32, 8), 0, dlogits, c.dl, c.n_act,
                                                                                             B, B); });
         backward(c, B);
         return 0;
@@ -1087,7 +1109,7 @@ float fc_step(void* h, float lr, float lr_neuron, float lr_plug, float max_norm,
         const long long tc = std::min<long long>(c.adam_t, 100000);
         const float c1 = 1.f - (float)pow(0.9, (double)tc), c2 = 1.f - (float)pow(0.999, (double)tc);
         const long long n = c.off[7];
-        launch(c, K_ADAM, [&]() { k_adam<<<(unsigned)std::min<long long>(blocks((n + 3) / 4), 148 * 8), 256, 0, c.st>>>(
+        launch(c, K_ADAM, [&]() { pdl(c, k_adam, (unsigned)std::min<long long>(blocks((n + 3) / 4), 148 * 8), 256, 0,
             c.P, c.G, c.M, c.V, c.EMA, n, c.off[1], c.off[3], lr, lr_neuron, lr_plug, c1, c2, scale, ema); });
         c.folded = -1;
         // the update is queued behind the norm on the device; the host reads the norm afterwards
@@ -1130,8 +1152,8 @@ int fg_teach_ex(void* h, const float* obs, const float* teacher, int B, float in
         if (!c.train) throw Err("this handle was created for inference only");
         forward(c, obs, B, logits, 0, true);
         CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
-        launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, kLossS), kLossT, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp, 1.f / loss_norm); });
-        launch(c, K_LOSS, [&]() { k_loss_stats<<<1, kStatsT, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
+        launch(c, K_LOSS, [&]() { pdl(c, k_loss, blocks(B, kLossS), kLossT, 0, c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, inv_temp, 1.f / loss_norm); });
+        launch(c, K_LOSS, [&]() { pdl(c, k_loss_stats, 1, kStatsT, 0, c.kl_s, c.ag_s, c.stats, B); });
         backward(c, B);
         if (stats) {
             float s[2];
@@ -1164,14 +1186,14 @@ int fg_survey(void* h, const float* obs, const float* teacher, int B, int ema, i
         c.sv_sq = nullptr;
         launch(c, K_HOP_FWD, [&]() {
             const unsigned g = (unsigned)((c.n_s + kWarps - 1) / kWarps);
-            if (c.bf16) k_count_fired<__nv_bfloat16><<<g, kThreads, 0, c.st>>>((const __nv_bfloat16*)c.h0, fired, c.n_s, B, B);
-            else if (c.f16) k_count_fired<__half><<<g, kThreads, 0, c.st>>>((const __half*)c.h0, fired, c.n_s, B, B);
-            else k_count_fired<float><<<g, kThreads, 0, c.st>>>((const float*)c.h0, fired, c.n_s, B, B);
+            if (c.bf16) pdl(c, k_count_fired<__nv_bfloat16>, g, kThreads, 0, (const __nv_bfloat16*)c.h0, fired, c.n_s, B, B);
+            else if (c.f16) pdl(c, k_count_fired<__half>, g, kThreads, 0, (const __half*)c.h0, fired, c.n_s, B, B);
+            else pdl(c, k_count_fired<float>, g, kThreads, 0, (const float*)c.h0, fired, c.n_s, B, B);
         });
         if (loss) {
             CK(cudaMemsetAsync(c.stats, 0, 16, c.st));
-            launch(c, K_LOSS, [&]() { k_loss<<<blocks(B, kLossS), kLossT, 0, c.st>>>(c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, 1.f, 1.f / B); });
-            launch(c, K_LOSS, [&]() { k_loss_stats<<<1, kStatsT, 0, c.st>>>(c.kl_s, c.ag_s, c.stats, B); });
+            launch(c, K_LOSS, [&]() { pdl(c, k_loss, blocks(B, kLossS), kLossT, 0, c.lg, teacher, c.dl, c.kl_s, c.ag_s, c.n_act, B, B, 1.f, 1.f / B); });
+            launch(c, K_LOSS, [&]() { pdl(c, k_loss_stats, 1, kStatsT, 0, c.kl_s, c.ag_s, c.stats, B); });
             float s[2];
             CK(cudaMemcpyAsync(s, c.stats, 8, cudaMemcpyDeviceToHost, c.st));
             CK(cudaStreamSynchronize(c.st));

@@ -20,6 +20,15 @@ constexpr int kWarps = 8;                 // warps per CTA of the row kernels
 constexpr int kThreads = 32 * kWarps;
 constexpr int kMaxAct = 96;                // actions at most (the output plug's tiles pad to 96)
 
+// First statement of every kernel. Launched with programmatic dependent launch (the library's step kernels), a kernel
+// can start while the stream's previous kernel is still running: griddepcontrol.wait blocks until that grid has
+// completed and its memory is visible, and launch_dependents lets the next kernel's launch begin once every CTA of
+// this one has started. Launched without it, both are no-ops.
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 
 // ---- 16-byte vector loads / stores of V activations as fp32
 __device__ __forceinline__ void ld_act(const float* p, float (&v)[4]) {
@@ -123,6 +132,7 @@ __device__ __forceinline__ void block_sum(float (&v)[N], float* red) {
 __global__ void k_fold_neurons(const int* __restrict__ nid, const float* __restrict__ gain,
                                const float* __restrict__ theta, float* __restrict__ rgain, float* __restrict__ rthr,
                                float* __restrict__ rsig, int n) {
+    pdl_enter();
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     int id = nid[i];
@@ -140,6 +150,7 @@ __global__ void __launch_bounds__(kThreads) k_fold_pairs(const int* __restrict__
                                                          const float* __restrict__ W, int2* __restrict__ pairs,
                                                          const int* __restrict__ tpos, int2* __restrict__ tpairs,
                                                          int n) {
+    pdl_enter();
     __shared__ float buf[kWarps][kFoldBuf];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int p0 = (blockIdx.x * kWarps + warp) * 32;
@@ -170,6 +181,7 @@ __global__ void __launch_bounds__(kThreads) k_fold_pairs(const int* __restrict__
 // ---------------------------------------------------------------- layout changes at the API boundary
 // in [B, D] (sample-major, the caller's) -> out [D, ld] (neuron-major); 32x32 tiles through shared memory
 __global__ void k_to_neuron_major(const float* __restrict__ in, float* __restrict__ out, int D, int B, int ld) {
+    pdl_enter();
     __shared__ float tile[32][33];
     int b0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
@@ -271,6 +283,7 @@ __global__ void __launch_bounds__(kPlugThreads) k_plug_fwd(const int* __restrict
                                                            const float* __restrict__ rthr, const float* __restrict__ x,
                                                            float* __restrict__ drive, T* __restrict__ h0, int n_s,
                                                            int fan, int rows_per_cta, int obs_dim, int ld) {
+    pdl_enter();
     constexpr int C = PlugCfg<T>::cols, NS = C / 32;
     constexpr int F = FAN > 0 ? FAN : 1;
     constexpr int kWarpsP = kPlugThreads / 32;
@@ -626,6 +639,7 @@ __global__ void __launch_bounds__(kThreads, HopCfg<TI>::min_blocks) k_hop_fwd(co
                                                                                const int* __restrict__ drow,
                                                                                const float* __restrict__ drive,
                                                                                TO* __restrict__ h, int n_rows, int ld) {
+    pdl_enter();
     hop_row<TI, TO, FULL>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, rows, pairs, hp, rgain, rthr, drow,
                           drive, h, n_rows, ld);
 }
@@ -639,6 +653,7 @@ __global__ void __launch_bounds__(kThreads) k_hop_fwd_surv(const int4* __restric
                                                            const float* __restrict__ drive, TO* __restrict__ h,
                                                            int n_rows, int ld, int* __restrict__ fired,
                                                            float* __restrict__ sq) {
+    pdl_enter();
     hop_row<TI, TO, FULL, true>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, rows, pairs, hp, rgain, rthr,
                                 drow, drive, h, n_rows, ld, fired, sq);
 }
@@ -646,6 +661,7 @@ __global__ void __launch_bounds__(kThreads) k_hop_fwd_surv(const int4* __restric
 template <class T>
 __global__ void __launch_bounds__(kThreads) k_count_fired(const T* __restrict__ h0, int* __restrict__ fired, int n_s,
                                                           int B, int ld) {
+    pdl_enter();
     const int r = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (r >= n_s) return;
     int c = 0;
@@ -658,17 +674,27 @@ __global__ void __launch_bounds__(kThreads) k_count_fired(const T* __restrict__ 
 // output plug: the forward and backward products are the tensor-core kernels of fg_outtc.cuh; kOutA is the padded
 // action count of the forward's partial slabs
 constexpr int kOutA = 96;
+constexpr int kOutSlices = 8;                           // most split-K slices of the output plug's dn columns
 // the slices' partial logits added in slice order + bias -> lg [n_act, ld] and/or out [B, n_act]; a CTA per 32 samples
 __global__ void __launch_bounds__(256) k_out_reduce(const float* __restrict__ part, const float* __restrict__ ob,
                                                     float* __restrict__ lg, float* __restrict__ out, int slices,
                                                     int n_act, int B, int ld) {
+    pdl_enter();
     __shared__ float st[32][kOutA + 1];
     const int b0 = blockIdx.x * 32;
+    // every slice's partial of 4 (action, sample) items loaded before any is added (slices <= kOutSlices), so a
+    // thread waits for memory once per 4 items, not once per partial; the sum is the bias, then slice 0, 1, ...
+#pragma unroll 4
     for (int i = threadIdx.x; i < n_act * 32; i += 256) {
         const int a = i >> 5, bb = i & 31, b = b0 + bb;
         if (b >= B) continue;
+        float p[kOutSlices];
+#pragma unroll
+        for (int s = 0; s < kOutSlices; ++s) p[s] = s < slices ? __ldg(&part[((size_t)s * kOutA + a) * ld + b]) : 0.f;
         float v = __ldg(&ob[a]);
-        for (int s = 0; s < slices; ++s) v += __ldg(&part[((size_t)s * kOutA + a) * ld + b]);
+#pragma unroll
+        for (int s = 0; s < kOutSlices; ++s)
+            if (s < slices) v += p[s];
         if (lg) lg[(size_t)a * ld + b] = v;
         st[bb][a] = v;
     }
@@ -696,6 +722,7 @@ __global__ void __launch_bounds__(kLossT) k_loss(const float* __restrict__ lg, c
                                                  float* __restrict__ dl, float* __restrict__ kl_s,
                                                  float* __restrict__ ag_s, int n_act, int B, int ld, float it,
                                                  float inv_norm) {
+    pdl_enter();
     __shared__ float sl[kMaxAct * kLossS];
     __shared__ float stt[kLossS * (kMaxAct + 1)];
     const int b0 = blockIdx.x * kLossS, nb = min(kLossS, B - b0), tw = n_act + 1;
@@ -767,6 +794,7 @@ __global__ void __launch_bounds__(kLossT) k_loss(const float* __restrict__ lg, c
 constexpr int kStatsT = 1024;
 __global__ void __launch_bounds__(kStatsT) k_loss_stats(const float* __restrict__ kl_s, const float* __restrict__ ag_s,
                                                          float* __restrict__ stats, int B) {
+    pdl_enter();
     __shared__ float red[2][kStatsT / 32];
     float v0 = 0.f, v1 = 0.f;
 #pragma unroll 4
@@ -792,10 +820,12 @@ __global__ void __launch_bounds__(kStatsT) k_loss_stats(const float* __restrict_
 // G_out_w[a*n_dn + j] += sum_s part[s][a][j]; G_out_b[a] += sum_s part[s][a][n_dn]
 __global__ void k_out_bwd_reduce(const float* __restrict__ part, float* __restrict__ gow, float* __restrict__ gob,
                                  int n_act, int n_dn, int splits) {
+    pdl_enter();
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int n_col = n_dn + 1;
     if (i >= n_act * n_col) return;
     float s = 0.f;
+#pragma unroll 8
     for (int k = 0; k < splits; ++k) s += part[(size_t)k * n_act * n_col + i];
     int a = i / n_col, j = i - a * n_col;
     if (j < n_dn) gow[(size_t)a * n_dn + j] += s; else gob[a] += s;
@@ -813,6 +843,7 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
                                                       float* __restrict__ ggain, float* __restrict__ gtheta,
                                                       float* __restrict__ gdrive, int* __restrict__ live,
                                                       const int* __restrict__ rows, int B, int ld) {
+    pdl_enter();
     __shared__ float red[3 * kWarps];
     const int t = __ldg(&rows[blockIdx.x]);             // a row whose gradient can be non-zero (an output-plug column)
     const float gn = rgain[t], th = rthr[t];
@@ -865,6 +896,7 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ ite
                                                     const int* __restrict__ gw, const float* __restrict__ gz,
                                                     const float* __restrict__ hp, const int* __restrict__ live,
                                                     float* __restrict__ gW, int n_items, int B, int ld) {
+    pdl_enter();
     const int wi = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (wi >= n_items) return;
     const int2 it = __ldg(&items[wi]);
@@ -989,6 +1021,7 @@ __global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__
                                                         const int2* __restrict__ tpairs, const float* __restrict__ gz,
                                                         float* __restrict__ out, float* __restrict__ part, int n_segs,
                                                         int ld, NeuronEpi ep) {
+    pdl_enter();
     const int sidx = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (sidx >= n_segs) return;
     const int4 sg = __ldg(&segs[sidx]);
@@ -1078,6 +1111,7 @@ __global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __res
                                 const int* __restrict__ nid, const float* __restrict__ rsig,
                                 float* __restrict__ ggain, float* __restrict__ gtheta, int* __restrict__ live, int n,
                                 int chunks) {
+    pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int s = __ldg(&list[i]);
@@ -1107,6 +1141,7 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ l
                                                        const float* __restrict__ rsig, float* __restrict__ ggain,
                                                        float* __restrict__ gtheta, float* __restrict__ gin_w,
                                                        float* __restrict__ gin_b, int n_list, int fan, int B, int ld) {
+    pdl_enter();
     constexpr int F = FAN > 0 ? FAN : kPlugFan;
     const int i = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (i >= n_list) return;
@@ -1166,6 +1201,7 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ l
 // ---------------------------------------------------------------- optimiser
 // partial sums of squares of the flat gradient (one per CTA); the host or k_norm_final adds them in order
 __global__ void k_sumsq(const float* __restrict__ g, long long n, float* __restrict__ part) {
+    pdl_enter();
     __shared__ float red[kWarps];
     float v[1] = {0.f};
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
@@ -1175,6 +1211,7 @@ __global__ void k_sumsq(const float* __restrict__ g, long long n, float* __restr
 }
 // norm[0] = sqrt(sum of part); norm[1] = gradient scale for clipping to max_norm (1 if not clipping)
 __global__ void k_norm_final(const float* __restrict__ part, int n, float max_norm, float* __restrict__ norm) {
+    pdl_enter();
     __shared__ float red[kWarps];
     float v[1] = {0.f};
     for (int i = threadIdx.x; i < n; i += blockDim.x) v[0] += part[i];
@@ -1198,6 +1235,7 @@ __device__ __forceinline__ void adam1(float& p, float g, float& m, float& v, flo
 __global__ void k_adam(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m, float* __restrict__ v,
                        float* __restrict__ ema, long long n, long long seg1, long long seg2, float lr0, float lr1,
                        float lr2, float c1, float c2, const float* __restrict__ scale, float decay) {
+    pdl_enter();
     const float gs = scale ? scale[1] : 1.f;
     const long long n4 = n >> 2, stride = (long long)gridDim.x * blockDim.x;
     for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < n4; q += stride) {

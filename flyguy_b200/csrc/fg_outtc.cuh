@@ -20,6 +20,7 @@
 // lanes 32 (w % 4) .., columns 48 (w / 4) ..) into the partial slab. Every wait is bounded (about 2 s): on expiry the
 // CTA records an error code and stops.
 #pragma once
+#include "fg_kernels.cuh"
 #include "fg_tcgen05.cuh"
 
 namespace fg {
@@ -52,6 +53,7 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b
 
 // out_w [n_act][n_dn] -> wt [chunk][hi, lo][96 x 32] in the operand layout (zero past n_act actions and n_dn columns)
 __global__ void k_fold_ow_tc(const float* __restrict__ ow, float* __restrict__ wt, int n_act, int n_dn, int chunks) {
+    pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= chunks * kOtN * kOtKC) return;
     const int c = i / (kOtN * kOtKC), r = i - c * (kOtN * kOtKC), a = r / kOtKC, k = r - a * kOtKC;
@@ -74,6 +76,7 @@ struct OutTc {
 };
 
 __global__ void __launch_bounds__(kOtThreads, 1) k_out_tc(const OutTc a) {
+    pdl_enter();
     extern __shared__ __align__(1024) unsigned char smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOtStages * kOtStage);
     // bars: 0..2 stage full, 3..5 stage empty, 6 accumulator complete
@@ -230,6 +233,7 @@ __device__ __forceinline__ constexpr uint32_t ob_idesc() {
 
 // out_w [n_act][n_dn] -> wt [column tile][chunk][hi, lo][128 columns x 32 actions] in the K-major operand layout
 __global__ void k_fold_owbt(const float* __restrict__ ow, float* __restrict__ wt, int n_act, int n_dn, int n_tiles) {
+    pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_tiles * kObChunks * kObN * kOtKC) return;
     const int blk = i / (kObN * kOtKC), r = i - blk * (kObN * kOtKC);
@@ -254,6 +258,7 @@ struct OutBh {
 };
 
 __global__ void __launch_bounds__(kOtThreads, 1) k_out_bwd_h_tc(const OutBh a) {
+    pdl_enter();
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* sa = smem;                                      // A: [chunk][hi, lo] of kObA bytes
     unsigned char* sw = smem + kObChunks * 2 * kObA;               // W ring: 3 stages of [hi, lo]
@@ -430,6 +435,7 @@ struct OutBw {
 };
 
 __global__ void __launch_bounds__(kOtThreads, 1) k_out_bwd_w_tc(const OutBw a) {
+    pdl_enter();
     extern __shared__ __align__(1024) unsigned char smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOwStages * kOwStage);
     // bars: 0..2 stage full, 3..5 stage empty, 6 accumulator complete
