@@ -584,15 +584,18 @@ static_assert(kOtN == kOutA, "the tensor-core output plug writes the partial sla
 void fold(Core& c, int which) {
     if (c.folded == which) return;
     const float* src = which ? c.EMA : c.P;
-    launch(c, K_FOLD, [&]() { pdl(c, k_fold_neurons, blocks(c.R), 256, 0, c.d_row_nid, src + c.off[1], src + c.off[2], c.d_rgain, c.d_rthr,
-                                                  c.d_rsig, (int)c.R); });
-    if (c.Ptot) {
-        launch(c, K_FOLD, [&]() { pdl(c, k_fold_pairs, blocks(c.Ptot, kThreads), kThreads, 0, c.d_gptr, c.d_gw, src + c.off[0], c.d_pairs, c.d_tpos, c.d_tpairs, (int)c.Ptot); });
-    }
-    launch(c, K_FOLD, [&]() { pdl(c, k_fold_ow_tc, blocks((long long)c.out_chunks * kOtN * kOtKC), 256, 0,
-                                  src + c.off[5], c.ow_tc, c.n_act, c.n_dn, c.out_chunks); });
-    if (c.ow_bt)
-        launch(c, K_FOLD, [&]() { pdl(c, k_fold_owbt, blocks((long long)c.ob_tiles * kObChunks * kObN * kOtKC), 256, 0, src + c.off[5], c.ow_bt, c.n_act, c.n_dn, c.ob_tiles); });
+    FoldArgs f;
+    f.nid = c.d_row_nid; f.gain = src + c.off[1]; f.theta = src + c.off[2];
+    f.rgain = c.d_rgain; f.rthr = c.d_rthr; f.rsig = c.d_rsig; f.n_rows = (int)c.R;
+    f.gptr = c.d_gptr; f.gw = c.d_gw; f.W = src + c.off[0]; f.pairs = c.d_pairs; f.tpos = c.d_tpos;
+    f.tpairs = c.d_tpairs; f.n_pairs = (int)c.Ptot;
+    f.ow = src + c.off[5]; f.ow_tc = c.ow_tc; f.ow_bt = c.ow_bt;
+    f.n_act = c.n_act; f.n_dn = c.n_dn; f.chunks = c.out_chunks; f.ob_tiles = c.ob_tiles;
+    f.nb_pairs = (int)blocks(c.Ptot, kWarps * 32);                     // a warp per 32 pairs
+    f.nb_rows = (int)blocks(c.R, kThreads);
+    f.nb_ow = (int)blocks((long long)c.out_chunks * kOtN * kOtKC, kThreads);
+    const int nb_bt = c.ow_bt ? (int)blocks((long long)c.ob_tiles * kObChunks * kObN * kOtKC, kThreads) : 0;
+    launch(c, K_FOLD, [&]() { pdl(c, k_fold, f.nb_pairs + f.nb_rows + f.nb_ow + nb_bt, kThreads, 0, f); });
     c.folded = which;
 }
 

@@ -128,12 +128,11 @@ __device__ __forceinline__ void block_sum(float (&v)[N], float* red) {
 }
 
 // ---------------------------------------------------------------- weight-version folds
+// (one launch, k_fold in fg_outtc.cuh, runs the four folds side by side in separate block ranges)
 // per row of every layer: its neuron's gain and threshold softplus(theta)
-__global__ void k_fold_neurons(const int* __restrict__ nid, const float* __restrict__ gain,
-                               const float* __restrict__ theta, float* __restrict__ rgain, float* __restrict__ rthr,
-                               float* __restrict__ rsig, int n) {
-    pdl_enter();
-    int i = blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void fold_neuron(int i, const int* __restrict__ nid, const float* __restrict__ gain,
+                                            const float* __restrict__ theta, float* __restrict__ rgain,
+                                            float* __restrict__ rthr, float* __restrict__ rsig, int n) {
     if (i >= n) return;
     int id = nid[i];
     float th = theta[id];
@@ -143,17 +142,15 @@ __global__ void k_fold_neurons(const int* __restrict__ nid, const float* __restr
 }
 // merged pair weight = sum of the weights of its edges (edges of one (row, source) pair are contiguous)
 // A warp owns 32 consecutive pairs: it gathers the weights of their edges (a contiguous range of gw) into shared memory
-// with all lanes, 256 at a time, then each lane adds its own pair's edges from there in edge order. The sum is also
+// with all lanes, 256 at a time, then each lane adds its own pair's edges from there. The sum is also
 // written to the pair's place among the transposed pairs (tpos[p] >= 0) when there are any.
 constexpr int kFoldBuf = 256;
-__global__ void __launch_bounds__(kThreads) k_fold_pairs(const int* __restrict__ gptr, const int* __restrict__ gw,
-                                                         const float* __restrict__ W, int2* __restrict__ pairs,
-                                                         const int* __restrict__ tpos, int2* __restrict__ tpairs,
-                                                         int n) {
-    pdl_enter();
-    __shared__ float buf[kWarps][kFoldBuf];
+__device__ __forceinline__ void fold_pairs(int blk, float (*buf)[kFoldBuf], const int* __restrict__ gptr,
+                                           const int* __restrict__ gw, const float* __restrict__ W,
+                                           int2* __restrict__ pairs, const int* __restrict__ tpos,
+                                           int2* __restrict__ tpairs, int n) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int p0 = (blockIdx.x * kWarps + warp) * 32;
+    const int p0 = (blk * kWarps + warp) * 32;
     if (p0 >= n) return;
     const int p = p0 + lane, pend = min(p0 + 32, n);
     const int e_lo = __ldg(&gptr[p0]), e_hi = __ldg(&gptr[pend]);
@@ -166,8 +163,18 @@ __global__ void __launch_bounds__(kThreads) k_fold_pairs(const int* __restrict__
         for (int i = lane; i < kFoldBuf; i += 32)
             if (i < cnt) sb[i] = __ldg(&W[__ldg(&gw[base + i])]);
         __syncwarp();
-        const int lo = max(my_lo, base), hi = min(my_hi, base + cnt);
-        for (int e = lo; e < hi; ++e) s += sb[e - base];
+        // the lane's edges in this window into four interleaved sums, added pairwise (a fixed order: the same bits
+        // in every run): a pair of many duplicate edges (hundreds on a hub source) waits on a quarter of the adds
+        const int lo = max(my_lo, base) - base, hi = min(my_hi, base + cnt) - base;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int e = lo;
+        for (; e + 4 <= hi; e += 4) {
+            a0 += sb[e]; a1 += sb[e + 1]; a2 += sb[e + 2]; a3 += sb[e + 3];
+        }
+        if (e < hi) a0 += sb[e];
+        if (e + 1 < hi) a1 += sb[e + 1];
+        if (e + 2 < hi) a2 += sb[e + 2];
+        if (lo < hi) s += (a0 + a1) + (a2 + a3);
         __syncwarp();
     }
     if (p < n) {
@@ -716,8 +723,12 @@ __global__ void __launch_bounds__(256) k_out_reduce(const float* __restrict__ pa
 // contiguous) in shared memory (teacher row stride n_act + 1 words: odd for n_act = 90, so the per-sample reads do not
 // conflict), then a warp per sample computes it with its lanes over the actions and warp reductions (a short
 // dependency chain at small batches, where one thread per sample running the passes in order took 26 us), writes dl
-// into the staged logits, and the CTA stores dl back row by row.
-constexpr int kLossS = 32, kLossT = 256;
+// into the staged logits, and the CTA stores dl back row by row. kLossS = 8 samples a CTA (one per warp; each staged row
+// one 32-byte sector): a batch of 2,048 gives 256 CTAs for the 148 SMs, not 64.
+#ifndef FG_LOSS_S
+#define FG_LOSS_S 8
+#endif
+constexpr int kLossS = FG_LOSS_S, kLossT = 256;
 __global__ void __launch_bounds__(kLossT) k_loss(const float* __restrict__ lg, const float* __restrict__ teacher,
                                                  float* __restrict__ dl, float* __restrict__ kl_s,
                                                  float* __restrict__ ag_s, int n_act, int B, int ld, float it,
@@ -737,7 +748,7 @@ __global__ void __launch_bounds__(kLossT) k_loss(const float* __restrict__ lg, c
         stt[r * tw + (i - r * n_act)] = __ldg(&tb[i]);
     }
     __syncthreads();
-    // a warp per sample (8 warps, 4 samples each), the lanes over the actions (3 a lane for 90 actions): max with the
+    // a warp per sample, the lanes over the actions (3 a lane for 90 actions): max with the
     // first index in action order on ties (the reference's strict '>' scan), the two log-sum-exps, the KL and dl
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int PA = kMaxAct / 32;

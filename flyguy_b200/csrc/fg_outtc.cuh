@@ -52,9 +52,8 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b
 }
 
 // out_w [n_act][n_dn] -> wt [chunk][hi, lo][96 x 32] in the operand layout (zero past n_act actions and n_dn columns)
-__global__ void k_fold_ow_tc(const float* __restrict__ ow, float* __restrict__ wt, int n_act, int n_dn, int chunks) {
-    pdl_enter();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void fold_ow_tc(int i, const float* __restrict__ ow, float* __restrict__ wt, int n_act,
+                                           int n_dn, int chunks) {
     if (i >= chunks * kOtN * kOtKC) return;
     const int c = i / (kOtN * kOtKC), r = i - c * (kOtN * kOtKC), a = r / kOtKC, k = r - a * kOtKC;
     const int j = c * kOtKC + k;
@@ -232,9 +231,8 @@ __device__ __forceinline__ constexpr uint32_t ob_idesc() {
 }
 
 // out_w [n_act][n_dn] -> wt [column tile][chunk][hi, lo][128 columns x 32 actions] in the K-major operand layout
-__global__ void k_fold_owbt(const float* __restrict__ ow, float* __restrict__ wt, int n_act, int n_dn, int n_tiles) {
-    pdl_enter();
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+__device__ __forceinline__ void fold_owbt(int i, const float* __restrict__ ow, float* __restrict__ wt, int n_act,
+                                          int n_dn, int n_tiles) {
     if (i >= n_tiles * kObChunks * kObN * kOtKC) return;
     const int blk = i / (kObN * kOtKC), r = i - blk * (kObN * kOtKC);
     const int t = blk / kObChunks, c = blk - t * kObChunks;
@@ -586,6 +584,38 @@ __global__ void __launch_bounds__(kOtThreads, 1) k_out_bwd_w_tc(const OutBw a) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128) : "memory");
     }
+}
+
+// ---------------------------------------------------------------- the folds of one weight version, one launch
+// Block ranges, the longest first: merged pair weights (fold_pairs), per-row gain / threshold / sigmoid
+// (fold_neuron), out_w in the forward's tensor-core operand layout (fold_ow_tc) and, when training, in the backward's
+// (fold_owbt). The four read the weights only and write disjoint arrays.
+struct FoldArgs {
+    const int* nid; const float* gain; const float* theta; float* rgain; float* rthr; float* rsig; int n_rows;
+    const int* gptr; const int* gw; const float* W; int2* pairs; const int* tpos; int2* tpairs; int n_pairs;
+    const float* ow; float* ow_tc; float* ow_bt; int n_act, n_dn, chunks, ob_tiles;
+    int nb_pairs, nb_rows, nb_ow;                    // blocks of each range (the rest: fold_owbt)
+};
+__global__ void __launch_bounds__(kThreads) k_fold(const FoldArgs a) {
+    pdl_enter();
+    __shared__ float buf[kWarps][kFoldBuf];
+    int b = blockIdx.x;
+    if (b < a.nb_pairs) {
+        fold_pairs(b, buf, a.gptr, a.gw, a.W, a.pairs, a.tpos, a.tpairs, a.n_pairs);
+        return;
+    }
+    b -= a.nb_pairs;
+    if (b < a.nb_rows) {
+        fold_neuron(b * kThreads + threadIdx.x, a.nid, a.gain, a.theta, a.rgain, a.rthr, a.rsig, a.n_rows);
+        return;
+    }
+    b -= a.nb_rows;
+    if (b < a.nb_ow) {
+        fold_ow_tc(b * kThreads + threadIdx.x, a.ow, a.ow_tc, a.n_act, a.n_dn, a.chunks);
+        return;
+    }
+    b -= a.nb_ow;
+    if (a.ow_bt) fold_owbt(b * kThreads + threadIdx.x, a.ow, a.ow_bt, a.n_act, a.n_dn, a.ob_tiles);
 }
 
 }  // namespace fg
