@@ -1128,6 +1128,7 @@ __global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __res
     const int s = __ldg(&list[i]);
     float a = 0.f, b = 0.f, nz = 0.f;
     const float* p = nsum + (size_t)s * chunks * 3;
+#pragma unroll 4
     for (int k = 0; k < chunks; ++k) { a += p[3 * k]; b += p[3 * k + 1]; nz += p[3 * k + 2]; }
     const int id = nid[s];
     ggain[id] += a;
@@ -1170,6 +1171,8 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ l
         float v[F + 3];
 #pragma unroll
         for (int u = 0; u < F + 3; ++u) v[u] = 0.f;
+        // (two steps' loads in flight: a warp per live row is few warps a SM, so each waits on memory latency)
+#pragma unroll 2
         for (int b = lane * 4; b < B; b += 128) {
             const float4 gh = ghv ? __ldg(reinterpret_cast<const float4*>(gh0 + o + b)) : make_float4(0.f, 0.f, 0.f, 0.f);
             const float4 hh = __ldg(reinterpret_cast<const float4*>(h0 + o + b));
