@@ -15,8 +15,8 @@ flyguy_b200.synth, obs ~ N(0,1), teacher logits ~ N(0,2^2)):
 A step is one pass of the hop path over the rank's batch with its inputs resident in HBM; the L2 is flushed (a 256 MiB
 write) between timed steps, outside the timed events. `value` = all ranks' units / the max over ranks of the summed
 per-step device time. `e2e` = the same metric through the library's host-buffer entry points (fg_forward_host; for
-train: pinned H2D of obs + teacher, fg_teach, all-reduce, fc_step, D2H of the loss), host copies inside the timed
-region. `roofline` = the dominant kernel class's algorithmic bytes / its CUDA-event time over the timed region.
+train: pinned H2D of obs + teacher, the next step's copied on a side stream while this step computes, fg_teach,
+all-reduce, fc_step, D2H of the loss), host copies inside the timed region. `roofline` = the dominant kernel class's algorithmic bytes / its CUDA-event time over the timed region.
 `--impl reference` times the reference's own CPU implementation (flyguy/native/fly_infer.cpp built from source into
 oracle/_ref; for training, which the reference does in torch on the CPU, the oracle's C port) on the host cores.
 """
@@ -481,17 +481,31 @@ def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barr
     obs_h = torch.from_numpy(obs_np).pin_memory()
     out_h = torch.empty(B, s["n_act"]).pin_memory()
     if train:
+        # a training loop's input pipeline: step i's obs and teacher cross PCIe on a copy stream while step i - 1
+        # computes (two device buffers); the first step's copy is not hidden, and every copy is inside the timed loop
         teach_h = torch.from_numpy(teacher_np).pin_memory()
-        obs_d = torch.empty_like(obs_h, device=dev)
-        teach_d = torch.empty_like(teach_h, device=dev)
+        obs_d = [torch.empty_like(obs_h, device=dev) for _ in range(2)]
+        teach_d = [torch.empty_like(teach_h, device=dev) for _ in range(2)]
+        cs = torch.cuda.Stream(device=dev)
+        ready = [torch.cuda.Event() for _ in range(2)]
+        main = torch.cuda.current_stream(dev)
 
-        def step():
-            obs_d.copy_(obs_h, non_blocking=True)
-            teach_d.copy_(teach_h, non_blocking=True)
+        def upload(i):
+            cs.wait_stream(main)                     # the buffer's last reader (step i - 2) is queued before this
+            with torch.cuda.stream(cs):
+                obs_d[i % 2].copy_(obs_h, non_blocking=True)
+                teach_d[i % 2].copy_(teach_h, non_blocking=True)
+                ready[i % 2].record(cs)
+
+        def step(i, last):
+            if not last:
+                upload(i + 1)
+            main.wait_event(ready[i % 2])
+            od, td = obs_d[i % 2], teach_d[i % 2]
             h.zero_grad()
             st = None
             for lo in range(0, B, piece):
-                st = h.teach(obs_d[lo:lo + piece], teach_d[lo:lo + piece], 1.0, logits=None, stats=world == 1,
+                st = h.teach(od[lo:lo + piece], td[lo:lo + piece], 1.0, logits=None, stats=world == 1,
                              loss_norm=B)
             if world > 1:
                 if bucketed:
@@ -507,23 +521,28 @@ def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barr
             return st
         h2d, d2h = (obs_np.nbytes + teacher_np.nbytes), 16
     else:
-        def step():
+        def upload(i):
+            pass
+
+        def step(i, last):
             h.forward_host(obs_h, out_h)
         h2d, d2h = obs_np.nbytes, out_h.numel() * 4
-    for _ in range(2):
-        step()
+    upload(0)
+    for i in range(2):
+        step(i, i == 1)
     torch.cuda.synchronize(dev)
     barrier()
-    t = 0.0
-    for _ in range(a.steps):
-        t0 = time.perf_counter()
-        step()
-        t += time.perf_counter() - t0
+    t0 = time.perf_counter()
+    upload(0)
+    for i in range(a.steps):
+        step(i, i + 1 == a.steps)
+    t = time.perf_counter() - t0
     barrier()
     t = max_over_ranks(t)
     return {"value": round(Bg * a.steps / t, 1), "unit": W["unit"], "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h),
-            "path": ("obs/teacher H2D (pinned) + fg_teach + fc_step + D2H loss" if train
+            "path": ("obs/teacher H2D (pinned; the next step's on a copy stream during this step) + fg_teach + "
+                     "fc_step + D2H loss" if train
                      else "fg_forward_host (pinned host obs -> host logits, copies overlapped in 4 chunks)")}
 
 
