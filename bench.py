@@ -491,7 +491,7 @@ def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barr
         main = torch.cuda.current_stream(dev)
 
         def upload(i):
-            cs.wait_stream(main)                     # the buffer's last reader (step i - 2) is queued before this
+            # (the buffer's last reader, step i - 2, has finished: every step ends with the host waiting for it)
             with torch.cuda.stream(cs):
                 obs_d[i % 2].copy_(obs_h, non_blocking=True)
                 teach_d[i % 2].copy_(teach_h, non_blocking=True)

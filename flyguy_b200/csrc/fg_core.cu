@@ -47,6 +47,7 @@ struct Hop {
     long long live_pairs = 0, live_edges = 0;    // merged pairs / edges of those rows (what the weight gradient visits)
     int2* d_sd_items = nullptr;                  // weight-gradient work items {row, first of up to kSdP pairs}
     int n_sd_items = 0;
+    bool sd_skip = true;                         // the SDDMM skips silent sample steps (no hub-heavy sources)
     int *d_live_src = nullptr, n_live_src = 0;   // rows of the layer below that this hop's backward writes
     int4 *d_segs = nullptr, *d_reds = nullptr;   // transposed product: segments of source rows, split-row reductions
     int* d_seg_red = nullptr;                    // per segment: its split row's reduction index, or -1
@@ -300,6 +301,16 @@ void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, c
         }
         h.n_sd_items = (int)items.size();
         h.d_sd_items = upload(c, items);
+        {   // the share of the live pairs whose source is one of the 32 busiest: above a fifth, the source gathers
+            // mostly hit L1 and the SDDMM issues them without waiting for the silent-step test
+            std::vector<int> per_src(h.n_src, 0);
+            for (int t : ld)
+                for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; ++p) ++per_src[h.h_psrc[p]];
+            const int top = std::min<int>(32, (int)per_src.size());
+            std::partial_sort(per_src.begin(), per_src.begin() + top, per_src.end(), std::greater<int>());
+            const long long busy = std::accumulate(per_src.begin(), per_src.begin() + top, 0LL);
+            h.sd_skip = !(h.live_pairs > 0 && busy * 5 > h.live_pairs);
+        }
         h.d_live_dst = upload(c, ld);
         h.d_live_src = upload(c, ls);
         // transposed pairs into live rows: by source, destinations ascending
@@ -802,18 +813,20 @@ void backward(Core& c, int B) {
         const float* hprev = k ? (const float*)c.hop[k - 1].d_h : (const float*)c.h0;
         if (h.n_sd_items) {
             const unsigned g = (unsigned)((h.n_sd_items + kWarps - 1) / kWarps);
-            if (h.widx_unique)
+            auto sddmm = [&](auto atomic, auto skip) {
                 launch(c, K_SDDMM, [&]() {
-                    pdl(c, k_sddmm<false>, g, kThreads, 0, h.d_sd_items, h.d_pptr, c.d_pairs + h.pbase,
-                                                             c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live,
-                                                             c.G + c.off[0], h.n_sd_items, B, B);
+                    pdl(c, k_sddmm<decltype(atomic)::value, decltype(skip)::value>, g, kThreads, 0, h.d_sd_items,
+                        h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live, c.G + c.off[0],
+                        h.n_sd_items, B, B);
                 });
-            else
-                launch(c, K_SDDMM, [&]() {
-                    pdl(c, k_sddmm<true>, g, kThreads, 0, h.d_sd_items, h.d_pptr, c.d_pairs + h.pbase,
-                                                            c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live,
-                                                            c.G + c.off[0], h.n_sd_items, B, B);
-                });
+            };
+            if (h.widx_unique) {
+                if (h.sd_skip) sddmm(std::false_type{}, std::true_type{});
+                else sddmm(std::false_type{}, std::false_type{});
+            } else {
+                if (h.sd_skip) sddmm(std::true_type{}, std::true_type{});
+                else sddmm(std::true_type{}, std::false_type{});
+            }
         }
         record_stage(c, k + 1);                          // (hop k's weight gradient is final)
         const bool full = B % 256 == 0;

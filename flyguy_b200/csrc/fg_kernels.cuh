@@ -901,7 +901,11 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
 #define FG_SDDMM_P 4
 #endif
 constexpr int kSdP = FG_SDDMM_P;
-template <bool ATOMIC>
+// SKIP: a 4-sample step whose gz values are all zero loads no source states (worth it where the gathers miss L1: a
+// graph without hub sources, sparse activity); without it the gz and source loads of a step are issued together
+// (worth it where the sources are few hubs that hit L1: the loads' latency, not their bytes, is the cost). The sums
+// are the same bits either way: a skipped step adds exact zeros.
+template <bool ATOMIC, bool SKIP>
 __global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ items, const int* __restrict__ pptr,
                                                     const int2* __restrict__ pairs, const int* __restrict__ gptr,
                                                     const int* __restrict__ gw, const float* __restrict__ gz,
@@ -924,7 +928,7 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ ite
 #pragma unroll 2
     for (int b = lane * 4; b < B; b += 128) {
         const float4 q = __ldg(reinterpret_cast<const float4*>(g + b));
-        if (q.x == 0.f && q.y == 0.f && q.z == 0.f && q.w == 0.f) continue;       // silent samples: nothing to add
+        if (SKIP && q.x == 0.f && q.y == 0.f && q.z == 0.f && q.w == 0.f) continue;  // silent samples: nothing to add
 #pragma unroll
         for (int u = 0; u < kSdP; ++u) {
             if (u < np) {
