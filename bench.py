@@ -543,7 +543,7 @@ def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barr
             "d2h_bytes_per_step": int(d2h),
             "path": ("obs/teacher H2D (pinned; the next step's on a copy stream during this step) + fg_teach + "
                      "fc_step + D2H loss" if train
-                     else "fg_forward_host (pinned host obs -> host logits, copies overlapped in 4 chunks)")}
+                     else "fg_forward_host (pinned host obs -> host logits; pieces growing from 1/32 of the batch, each upload hidden behind the previous piece's forward)")}
 
 
 # ------------------------------------------------------------------ CPU baseline / reference arm

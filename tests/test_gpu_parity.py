@@ -318,8 +318,9 @@ def test_errors_leave_the_handle_usable(cuda):
 
 @pytest.mark.parametrize("B", [8192, 33024])
 def test_host_buffer_forward_matches_device_forward(flygraph, B, cuda):
-    """fg_forward_host (pinned host buffers, copies overlapped with compute; 33,024 runs as two pieces of 16,640 and
-    16,384 samples) gives the device forward's logits bit for bit."""
+    """fg_forward_host (pinned host buffers, copies overlapped with compute; 8,192 runs as pieces of 1,024 / 3,072 /
+    4,096 samples, 33,024 as 2,048 / 6,144 / 18,432 / 6,400 - the last not a whole 1,024-sample hop chunk) gives the
+    device forward's logits bit for bit."""
     import torch
     s, P = flygraph
     obs, _ = synth.make_batch(B, seed=14)
