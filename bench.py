@@ -224,6 +224,7 @@ def train_bytes(plan, s, B: int, flat_len: int, redrive: bool) -> dict:
     n, K = s["sizes"], s["hops"]
     hops = plan["hops"]
     E = sum(h["edges"] for h in hops)
+    chunks = (B + 255) // 256                           # the backward's 256-sample chunks
     out = {
         "plug_fwd": (s["obs_dim"] + n[0] * (2 if redrive else 1)) * 4 * B,
         "hop_fwd": 4 * B * sum(n[k] + n[k + 1] for k in range(K)) + 8 * E + 4 * sum(n[1:]),
@@ -231,12 +232,14 @@ def train_bytes(plan, s, B: int, flat_len: int, redrive: bool) -> dict:
         "loss": 3 * s["n_act"] * 4 * B,
         "out_bwd": (s["n_act"] + 2 * plan["n_dn"]) * 4 * B,
         "act_bwd": 3 * 4 * B * hops[-1]["live_dst"],
-        "sddmm": sum(4 * B * (h["live_dst"] + h["live_src"]) + 8 * h["live_pairs_"] + 8 * h["live_edges"]
-                     for h in hops),
-        # transposed product: read gz of the live rows, write the layer below's live rows (and read its states for
-        # the fused neuron backward, except below the first hop, where gh0 is written as it is)
-        "hop_bwd_t": sum(4 * B * (h["live_dst"] + h["live_src"] * (2 if k else 1)) + 8 * h["tpairs"]
-                         for k, h in enumerate(hops)),
+        # the weight gradient's last step (k_sd_reduce): each live pair's per-chunk partials, its forward pair and edge
+        # range, and each of its edges' weight-gradient word read and written
+        "sddmm": sum(4 * h["live_pairs_"] * chunks + 12 * h["live_pairs_"] + 12 * h["live_edges"] for h in hops),
+        # transposed product with the weight-gradient products fused in: read gz of the live rows and the live source
+        # rows' states (the products and the fused neuron backward), write the layer below's live rows (gz, or gh0
+        # below the first hop), read the pair records, write the per-chunk weight-gradient partials
+        "hop_bwd_t": sum(4 * B * (h["live_dst"] + 2 * h["live_src"]) + 8 * h["tpairs"] + 4 * h["tpairs"] * chunks
+                         for h in hops),
         "plug_bwd": 4 * B * (3 * plan["plug_live"] + s["obs_dim"]),
         "adam": 36 * flat_len,
     }

@@ -16,6 +16,7 @@
 #include "fg_outtc.cuh"
 #include "flyguy_b200.h"
 
+
 using namespace fg;
 
 namespace {
@@ -38,17 +39,16 @@ struct Hop {
     long long pbase = 0;                     // first merged pair of this hop in the concatenated arrays
     long long rbase = 0;                     // first row of this hop's layer in the per-row arrays
     bool widx_unique = true, redrive = false;
-    int *d_nid = nullptr, *d_drow = nullptr, *d_pptr = nullptr;
+    int *d_nid = nullptr, *d_drow = nullptr;
     int4* d_rows = nullptr;                      // forward schedule: per slot {first pair, end, row, 0}
     std::vector<int> h_psrc, h_pptr;             // host copies of the forward pairs (for the backward plan)
     long long tbase = 0;                         // first transposed pair of this hop in the concatenated arrays
     int T = 0;                                   // transposed pairs kept for the backward
     int *d_live_dst = nullptr, n_live_dst = 0;   // rows of this hop's layer whose gradient can be non-zero
     long long live_pairs = 0, live_edges = 0;    // merged pairs / edges of those rows (what the weight gradient visits)
-    int2* d_sd_items = nullptr;                  // weight-gradient work items {row, first of up to kSdP pairs}
-    int n_sd_items = 0;
-    bool sd_skip = true;                         // the SDDMM skips silent sample steps (no hub-heavy sources)
     int *d_live_src = nullptr, n_live_src = 0;   // rows of the layer below that this hop's backward writes
+    int2* d_sde = nullptr;                       // live edges {edge, transposed pair} in transposed-pair order
+    int n_sde = 0;
     int4 *d_segs = nullptr, *d_reds = nullptr;   // transposed product: segments of source rows, split-row reductions
     int* d_seg_red = nullptr;                    // per segment: its split row's reduction index, or -1
     int n_segs = 0, n_reds = 0, n_slots = 0;
@@ -93,6 +93,7 @@ struct Core {
     float *d_rgain = nullptr, *d_rthr = nullptr, *d_rsig = nullptr;
     int2 *d_pairs = nullptr, *d_tpairs = nullptr;
     int *d_gptr = nullptr, *d_gw = nullptr, *d_tpos = nullptr;   // d_tpos: pair -> transposed pair, or -1
+    float* sd_part = nullptr;                            // weight-gradient partials [256-sample chunk][transposed pair]
     long long off[8] = {0};                             // segment starts in the flat arrays (256-byte aligned)
     long long psize[7] = {0};                           // the seven arrays' true lengths
     float *P = nullptr, *G = nullptr, *M = nullptr, *V = nullptr, *EMA = nullptr;
@@ -244,7 +245,6 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
                      [&](int a, int b) { return pptr[a + 1] - pptr[a] > pptr[b + 1] - pptr[b]; });
     h.h_psrc = std::move(psrc);
     h.h_pptr = pptr;
-    h.d_pptr = upload(c, pptr);
     std::vector<int4> rows4(rows);
     for (int slot = 0; slot < rows; ++slot) {
         const int t = sched[slot];
@@ -293,23 +293,9 @@ void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, c
         for (int s = 0; s < h.n_src; ++s) if (live[k - 1][s]) ls.push_back(s);
         h.n_live_dst = (int)ld.size();
         h.n_live_src = (int)ls.size();
-        std::vector<int2> items;
         for (int t : ld) {
-            for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; p += kSdP) items.push_back(make_int2(t, p));
             h.live_pairs += h.h_pptr[t + 1] - h.h_pptr[t];
             for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; ++p) h.live_edges += edges_of(h.pbase + p);
-        }
-        h.n_sd_items = (int)items.size();
-        h.d_sd_items = upload(c, items);
-        {   // the share of the live pairs whose source is one of the 32 busiest: above a fifth, the source gathers
-            // mostly hit L1 and the SDDMM issues them without waiting for the silent-step test
-            std::vector<int> per_src(h.n_src, 0);
-            for (int t : ld)
-                for (int p = h.h_pptr[t]; p < h.h_pptr[t + 1]; ++p) ++per_src[h.h_psrc[p]];
-            const int top = std::min<int>(32, (int)per_src.size());
-            std::partial_sort(per_src.begin(), per_src.begin() + top, per_src.end(), std::greater<int>());
-            const long long busy = std::accumulate(per_src.begin(), per_src.begin() + top, 0LL);
-            h.sd_skip = !(h.live_pairs > 0 && busy * 5 > h.live_pairs);
         }
         h.d_live_dst = upload(c, ld);
         h.d_live_src = upload(c, ls);
@@ -334,6 +320,14 @@ void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, c
         }
         tpairs.insert(tpairs.end(), tp.begin(), tp.end());
         tpi.insert(tpi.end(), ti.begin(), ti.end());
+        {   // the weight gradient's edges, pair by pair in transposed order
+            std::vector<int2> sde;
+            for (int q = 0; q < h.T; ++q)
+                for (int j = gptr[ti[q]]; j < (ti[q] + 1 < (long long)gptr.size() ? gptr[ti[q] + 1] : (int)n_edges); ++j)
+                    sde.push_back(make_int2(j, q));
+            h.n_sde = (int)sde.size();
+            if (h.n_sde) h.d_sde = upload(c, sde);
+        }
         std::vector<int4> segs, reds;
         std::vector<int> seg_red;
         for (int s : ls) {
@@ -551,6 +545,9 @@ void alloc_all(Core& c) {
         int slots = 0;
         for (auto& h : c.hop) slots = std::max(slots, h.n_slots);
         c.seg_part = dalloc<float>(c, (size_t)slots * B);
+        long long tmax = 1;
+        for (auto& h : c.hop) tmax = std::max<long long>(tmax, h.T);
+        c.sd_part = dalloc<float>(c, (size_t)tmax * ((B + 255) / 256));
         int reds = 0;
         for (auto& h : c.hop) reds = std::max(reds, h.n_reds);
         const size_t n_done = std::max<size_t>(1, (size_t)reds * ((B + 255) / 256));
@@ -811,25 +808,9 @@ void backward(Core& c, int B) {
     for (int k = c.hops - 1; k >= 0; --k) {
         const Hop& h = c.hop[k];
         const float* hprev = k ? (const float*)c.hop[k - 1].d_h : (const float*)c.h0;
-        if (h.n_sd_items) {
-            const unsigned g = (unsigned)((h.n_sd_items + kWarps - 1) / kWarps);
-            auto sddmm = [&](auto atomic, auto skip) {
-                launch(c, K_SDDMM, [&]() {
-                    pdl(c, k_sddmm<decltype(atomic)::value, decltype(skip)::value>, g, kThreads, 0, h.d_sd_items,
-                        h.d_pptr, c.d_pairs + h.pbase, c.d_gptr + h.pbase, c.d_gw, gz, hprev, c.live, c.G + c.off[0],
-                        h.n_sd_items, B, B);
-                });
-            };
-            if (h.widx_unique) {
-                if (h.sd_skip) sddmm(std::false_type{}, std::true_type{});
-                else sddmm(std::false_type{}, std::false_type{});
-            } else {
-                if (h.sd_skip) sddmm(std::true_type{}, std::true_type{});
-                else sddmm(std::true_type{}, std::false_type{});
-            }
-        }
-        record_stage(c, k + 1);                          // (hop k's weight gradient is final)
         const bool full = B % 256 == 0;
+        // the transposed product, which also forms the weight gradient's per-chunk partials; k_sd_reduce then adds
+        // them up into the edges' weight gradients
         auto transposed = [&](auto epi, const NeuronEpi& ep) {
             constexpr bool EPI = decltype(epi)::value;
             const dim3 gs((h.n_segs + kWarps - 1) / kWarps, chunks);
@@ -837,13 +818,21 @@ void backward(Core& c, int B) {
             launch(c, K_HOP_BWD, [&]() {
                 if (full)
                     pdl(c, k_hop_bwd_t<EPI, true>, gs, kThreads, 0, h.d_segs, h.d_seg_red, h.d_reds, c.seg_done,
-                                                                      c.d_tpairs + h.tbase, gz, nxt, c.seg_part,
-                                                                      h.n_segs, B, ep);
+                        c.d_tpairs + h.tbase, gz, nxt, c.seg_part, h.n_segs, B, ep, hprev, c.sd_part, (int)h.T);
                 else
                     pdl(c, k_hop_bwd_t<EPI, false>, gs, kThreads, 0, h.d_segs, h.d_seg_red, h.d_reds, c.seg_done,
-                                                                       c.d_tpairs + h.tbase, gz, nxt, c.seg_part,
-                                                                       h.n_segs, B, ep);
+                        c.d_tpairs + h.tbase, gz, nxt, c.seg_part, h.n_segs, B, ep, hprev, c.sd_part, (int)h.T);
             });
+            if (h.n_sde) {
+                launch(c, K_SDDMM, [&]() {
+                    if (h.widx_unique)
+                        pdl(c, k_sd_reduce<false>, blocks(h.n_sde), 256, 0, (const float*)c.sd_part, (int)h.T, chunks,
+                            (const int2*)h.d_sde, h.n_sde, (const int*)c.d_gw, c.G + c.off[0]);
+                    else
+                        pdl(c, k_sd_reduce<true>, blocks(h.n_sde), 256, 0, (const float*)c.sd_part, (int)h.T, chunks,
+                            (const int2*)h.d_sde, h.n_sde, (const int*)c.d_gw, c.G + c.off[0]);
+                });
+            }
         };
         if (k >= 1) {                        // the layer below is a hop's: its neuron backward rides along
             const Hop& lo = c.hop[k - 1];
@@ -859,6 +848,7 @@ void backward(Core& c, int B) {
             NeuronEpi ep{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, chunks};
             transposed(std::false_type{}, ep);
         }
+        record_stage(c, k + 1);                          // (hop k's weight gradient is final)
         std::swap(gz, nxt);
     }
     // gz now holds gh0 (the sensory layer's incoming gradient)

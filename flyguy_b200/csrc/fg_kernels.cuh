@@ -892,68 +892,6 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
     }
 }
 
-// per merged pair p of row t: gp = sum_b gz[t,b] * hp[src_p, b], added to the gradient of every edge weight of the
-// pair. One warp per work item {row, first pair} - up to kSdP consecutive pairs of one row whose gradient can be
-// non-zero (the gz row is read once for all of them) - over the whole batch, 4 samples per lane per step; a
-// warp-shuffle reduction in a fixed order (no block barriers, no atomics for weights used once per hop); the edge
-// weights' gradients are then updated by all lanes. A pair's sum does not depend on kSdP.
-#ifndef FG_SDDMM_P
-#define FG_SDDMM_P 4
-#endif
-constexpr int kSdP = FG_SDDMM_P;
-// SKIP: a 4-sample step whose gz values are all zero loads no source states (worth it where the gathers miss L1: a
-// graph without hub sources, sparse activity); without it the gz and source loads of a step are issued together
-// (worth it where the sources are few hubs that hit L1: the loads' latency, not their bytes, is the cost). The sums
-// are the same bits either way: a skipped step adds exact zeros.
-template <bool ATOMIC, bool SKIP>
-__global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ items, const int* __restrict__ pptr,
-                                                    const int2* __restrict__ pairs, const int* __restrict__ gptr,
-                                                    const int* __restrict__ gw, const float* __restrict__ gz,
-                                                    const float* __restrict__ hp, const int* __restrict__ live,
-                                                    float* __restrict__ gW, int n_items, int B, int ld) {
-    pdl_enter();
-    const int wi = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (wi >= n_items) return;
-    const int2 it = __ldg(&items[wi]);
-    const int t = it.x, p0 = it.y;
-    if (!__ldg(&live[t])) return;
-    const int np = min(kSdP, __ldg(&pptr[t + 1]) - p0);
-    const float* hs[kSdP];
-#pragma unroll
-    for (int u = 0; u < kSdP; ++u) hs[u] = hp + (size_t)(u < np ? __ldg(&pairs[p0 + u].x) : 0) * ld;
-    const float* g = gz + (size_t)t * ld;
-    float acc[kSdP];
-#pragma unroll
-    for (int u = 0; u < kSdP; ++u) acc[u] = 0.f;
-#pragma unroll 2
-    for (int b = lane * 4; b < B; b += 128) {
-        const float4 q = __ldg(reinterpret_cast<const float4*>(g + b));
-        if (SKIP && q.x == 0.f && q.y == 0.f && q.z == 0.f && q.w == 0.f) continue;  // silent samples: nothing to add
-#pragma unroll
-        for (int u = 0; u < kSdP; ++u) {
-            if (u < np) {
-                const float4 hq = __ldg(reinterpret_cast<const float4*>(hs[u] + b));
-                acc[u] = fmaf(q.x, hq.x, fmaf(q.y, hq.y, fmaf(q.z, hq.z, fmaf(q.w, hq.w, acc[u]))));
-            }
-        }
-    }
-#pragma unroll
-    for (int u = 0; u < kSdP; ++u) acc[u] = warp_sum(acc[u]);
-    // the item's edges are one contiguous range of gw (pair after pair): every lane adds a pair's sum into the
-    // gradient of one edge weight at a time; each weight is used once per hop unless ATOMIC
-    const int e0 = __ldg(&gptr[p0]), e1 = __ldg(&gptr[p0 + np]);
-    int m[kSdP];                                         // m[u]: the first edge of pair u (u >= 1)
-#pragma unroll
-    for (int u = 1; u < kSdP; ++u) m[u] = u < np ? __ldg(&gptr[p0 + u]) : e1;
-    for (int j = e0 + lane; j < e1; j += 32) {
-        float v = acc[0];
-#pragma unroll
-        for (int u = 1; u < kSdP; ++u) v = j >= m[u] ? acc[u] : v;
-        const int w = __ldg(&gw[j]);
-        if (ATOMIC) atomicAdd(&gW[w], v); else gW[w] += v;
-    }
-}
-
 // transposed hop: gh[s, b] = sum over merged pairs (dst, w) of source row s of w * gz[dst, b]. The source rows are
 // cut into segments of at most a fixed number of pairs (hub sources have tens of thousands); a segment of a row that
 // has one finishes the row, the others write partial rows that the last of them to finish adds up in slot order.
@@ -964,6 +902,12 @@ __global__ void __launch_bounds__(kThreads) k_sddmm(const int2* __restrict__ ite
 // Finishing a row (EPI): the source layer's neuron backward is fused in - g = gh * [h > 0]; gz = g * gain is written
 // (not gh), gdrive[drow] += gz, and the row's per-chunk sums of g*z (z = (h + thr) / gain where h > 0), of g and of
 // [g != 0] go to nsum[row][chunk][3] for k_neuron_reduce. Without EPI (the sensory layer) gh itself is written.
+// The weight gradient (the reference's SDDMM, flyguy_train.cu:158-167) is fused in: the warp loads its source row's
+// states for its chunk once (hs) and, per pair, adds gz[dst] * hs[src] over the chunk's 256 samples into
+// wpart[chunk][pair] (two pairs' warp sums at once: each half-warp reduces one); k_sd_reduce then adds a pair's chunks
+// in order into its edges' weight gradients. The gz rows each pair loads serve both products, and no source row is
+// gathered per pair (the separate SDDMM gathered one per pair over the whole batch: on the model.pt network the
+// training step went 56.6 -> 39.1 ms with the fusion, on the Zipf graph 5.08 -> 4.79 ms).
 struct NeuronEpi {
     const float* h;          // the source layer's states [rows, ld]
     const float* rgain;      // per row
@@ -1030,12 +974,15 @@ __device__ __forceinline__ void finish_row(int s, int chunk, int c0, int c1, boo
 // A segment of a split row writes its partial row to part[slot], then counts itself in done[red][chunk]; the last of
 // the row's segments to arrive (no waiting: the others just leave) adds all the row's partials in slot order through
 // L2 and finishes the row, then resets the counter for the next call. Deterministic: the sum order is fixed.
+// (5 CTAs a SM: 48 registers, a few bytes spilled; 58 registers at 4 CTAs measured slower: training steps of 4.89
+// against 4.83 ms on the Zipf graph, 43.1 against 38.9 ms on model.pt.)
 template <bool EPI, bool FULL>
-__global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__ segs, const int* __restrict__ seg_red,
+__global__ void __launch_bounds__(kThreads, 5) k_hop_bwd_t(const int4* __restrict__ segs, const int* __restrict__ seg_red,
                                                         const int4* __restrict__ reds, int* __restrict__ done,
                                                         const int2* __restrict__ tpairs, const float* __restrict__ gz,
                                                         float* __restrict__ out, float* __restrict__ part, int n_segs,
-                                                        int ld, NeuronEpi ep) {
+                                                        int ld, NeuronEpi ep, const float* __restrict__ hs,
+                                                        float* __restrict__ wpart, int T) {
     pdl_enter();
     const int sidx = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (sidx >= n_segs) return;
@@ -1047,41 +994,61 @@ __global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__
     float2 a0[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)}, a1[2] = {a0[0], a0[1]};
     const unsigned row_bytes = (unsigned)ld * 4u;
     const char* base = reinterpret_cast<const char*>(gz + (v0 ? c0 : 0));
-    if (v0 && v1) {
+    {
+        // every lane runs every pair (the warp sums need the whole warp); lanes past the batch load nothing
+        const float2 z2 = make_float2(0.f, 0.f);
+        float2 h0[2] = {z2, z2}, h1[2] = {z2, z2};
+        if (v0) ld16<float>(hs + (size_t)sg.x * ld + c0, h0);
+        if (v1) ld16<float>(hs + (size_t)sg.x * ld + c1, h1);
+        float* wp = wpart + (size_t)chunk * T;
+        auto dot = [&](const float2 (&u0)[2], const float2 (&u1)[2]) {
+            float2 d = __fmul2_rn(u0[0], h0[0]);
+            d = __ffma2_rn(u0[1], h0[1], d);
+            d = __ffma2_rn(u1[0], h1[0], d);
+            d = __ffma2_rn(u1[1], h1[1], d);
+            return d.x + d.y;
+        };
         int e = sg.y;
         for (; e + 2 <= sg.z; e += 2) {
             const int2 p = __ldg(&tpairs[e]), q = __ldg(&tpairs[e + 1]);
             const char* ap = row_at(base, p.x, row_bytes);
             const char* aq = row_at(base, q.x, row_bytes);
-            float2 x0[2], x1[2], y0[2], y1[2];
-            ld16<float>(reinterpret_cast<const float*>(ap), x0);
-            ld16<float>(reinterpret_cast<const float*>(ap + 512), x1);
-            ld16<float>(reinterpret_cast<const float*>(aq), y0);
-            ld16<float>(reinterpret_cast<const float*>(aq + 512), y1);
-            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
-            const float2 wq = make_float2(__int_as_float(q.y), __int_as_float(q.y));
-            a0[0] = __ffma2_rn(wp, x0[0], a0[0]); a0[1] = __ffma2_rn(wp, x0[1], a0[1]);
-            a1[0] = __ffma2_rn(wp, x1[0], a1[0]); a1[1] = __ffma2_rn(wp, x1[1], a1[1]);
-            a0[0] = __ffma2_rn(wq, y0[0], a0[0]); a0[1] = __ffma2_rn(wq, y0[1], a0[1]);
-            a1[0] = __ffma2_rn(wq, y1[0], a1[0]); a1[1] = __ffma2_rn(wq, y1[1], a1[1]);
+            float2 x0[2] = {z2, z2}, x1[2] = {z2, z2}, y0[2] = {z2, z2}, y1[2] = {z2, z2};
+            if (v0) {
+                ld16<float>(reinterpret_cast<const float*>(ap), x0);
+                ld16<float>(reinterpret_cast<const float*>(aq), y0);
+            }
+            if (v1) {
+                ld16<float>(reinterpret_cast<const float*>(ap + 512), x1);
+                ld16<float>(reinterpret_cast<const float*>(aq + 512), y1);
+            }
+            const float2 wp2 = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+            const float2 wq2 = make_float2(__int_as_float(q.y), __int_as_float(q.y));
+            a0[0] = __ffma2_rn(wp2, x0[0], a0[0]); a0[1] = __ffma2_rn(wp2, x0[1], a0[1]);
+            a1[0] = __ffma2_rn(wp2, x1[0], a1[0]); a1[1] = __ffma2_rn(wp2, x1[1], a1[1]);
+            a0[0] = __ffma2_rn(wq2, y0[0], a0[0]); a0[1] = __ffma2_rn(wq2, y0[1], a0[1]);
+            a1[0] = __ffma2_rn(wq2, y1[0], a1[0]); a1[1] = __ffma2_rn(wq2, y1[1], a1[1]);
+            const float sp = dot(x0, x1), sq = dot(y0, y1);
+            // lanes 0-15 end with the warp's sum of sp, lanes 16-31 with that of sq
+            float v = lane < 16 ? sp : sq;
+            v += __shfl_xor_sync(0xffffffffu, lane < 16 ? sq : sp, 16);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            if ((lane & 15) == 0) wp[e + (lane >> 4)] = v;
         }
         if (e < sg.z) {
             const int2 p = __ldg(&tpairs[e]);
             const char* ap = row_at(base, p.x, row_bytes);
-            float2 x0[2], x1[2];
-            ld16<float>(reinterpret_cast<const float*>(ap), x0);
-            ld16<float>(reinterpret_cast<const float*>(ap + 512), x1);
-            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
-            a0[0] = __ffma2_rn(wp, x0[0], a0[0]); a0[1] = __ffma2_rn(wp, x0[1], a0[1]);
-            a1[0] = __ffma2_rn(wp, x1[0], a1[0]); a1[1] = __ffma2_rn(wp, x1[1], a1[1]);
-        }
-    } else if (v0) {
-        for (int e = sg.y; e < sg.z; ++e) {
-            const int2 p = __ldg(&tpairs[e]);
-            float2 x0[2];
-            ld16<float>(reinterpret_cast<const float*>(row_at(base, p.x, row_bytes)), x0);
-            const float2 wp = make_float2(__int_as_float(p.y), __int_as_float(p.y));
-            a0[0] = __ffma2_rn(wp, x0[0], a0[0]); a0[1] = __ffma2_rn(wp, x0[1], a0[1]);
+            float2 x0[2] = {z2, z2}, x1[2] = {z2, z2};
+            if (v0) ld16<float>(reinterpret_cast<const float*>(ap), x0);
+            if (v1) ld16<float>(reinterpret_cast<const float*>(ap + 512), x1);
+            const float2 wp2 = make_float2(__int_as_float(p.y), __int_as_float(p.y));
+            a0[0] = __ffma2_rn(wp2, x0[0], a0[0]); a0[1] = __ffma2_rn(wp2, x0[1], a0[1]);
+            a1[0] = __ffma2_rn(wp2, x1[0], a1[0]); a1[1] = __ffma2_rn(wp2, x1[1], a1[1]);
+            const float v = warp_sum(dot(x0, x1));
+            if (lane == 0) wp[e] = v;
         }
     }
     float r0[4] = {a0[0].x, a0[0].y, a0[1].x, a0[1].y}, r1[4] = {a1[0].x, a1[0].y, a1[1].x, a1[1].y};
@@ -1118,6 +1085,25 @@ __global__ void __launch_bounds__(kThreads) k_hop_bwd_t(const int4* __restrict__
     }
     finish_row<EPI>(sg.x, chunk, c0, c1, v0, v1, ld, r0, r1, out, ep);
     if (lane == 0) done[(size_t)ri * gridDim.y + chunk] = 0;
+}
+
+// per live edge {j, q} of a hop (sde, in transposed-pair order): the weight gradient of its pair q = the sum of the
+// pair's chunk partials in chunk order, added to the edge's weight gradient gW[gw[j]] - a thread per edge, so a pair
+// of hundreds of duplicate edges (a hub source) is spread over as many threads; ATOMIC when a weight is used by more
+// than one pair of the hop
+template <bool ATOMIC>
+__global__ void __launch_bounds__(256) k_sd_reduce(const float* __restrict__ wpart, int T, int chunks,
+                                                   const int2* __restrict__ sde, int n, const int* __restrict__ gw,
+                                                   float* __restrict__ gW) {
+    pdl_enter();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int2 e = __ldg(&sde[i]);
+    float v = 0.f;
+#pragma unroll 8
+    for (int c = 0; c < chunks; ++c) v += __ldg(&wpart[(size_t)c * T + e.y]);
+    const int w = __ldg(&gw[e.x]);
+    if (ATOMIC) atomicAdd(&gW[w], v); else gW[w] += v;
 }
 
 // per listed row of a layer (the rows the transposed hop finished): gain grad += sum over chunks of g*z, theta grad +=
