@@ -974,10 +974,11 @@ __device__ __forceinline__ void finish_row(int s, int chunk, int c0, int c1, boo
 // A segment of a split row writes its partial row to part[slot], then counts itself in done[red][chunk]; the last of
 // the row's segments to arrive (no waiting: the others just leave) adds all the row's partials in slot order through
 // L2 and finishes the row, then resets the counter for the next call. Deterministic: the sum order is fixed.
-// (5 CTAs a SM: 48 registers, a few bytes spilled; 58 registers at 4 CTAs measured slower: training steps of 4.89
-// against 4.83 ms on the Zipf graph, 43.1 against 38.9 ms on model.pt.)
+// (Four pairs' gathers in flight, 64 registers, 4 CTAs a SM: against two pairs at 5 CTAs (48 registers) the training
+// step measured 38.1 / 38.8 ms on model.pt, 4.73 / 4.77 ms on the Zipf graph, 0.802 / 0.820 ms at batch 2,048; four
+// pairs at 80 registers (3 CTAs) 40.7 ms on model.pt.)
 template <bool EPI, bool FULL>
-__global__ void __launch_bounds__(kThreads, 5) k_hop_bwd_t(const int4* __restrict__ segs, const int* __restrict__ seg_red,
+__global__ void __launch_bounds__(kThreads, 4) k_hop_bwd_t(const int4* __restrict__ segs, const int* __restrict__ seg_red,
                                                         const int4* __restrict__ reds, int* __restrict__ done,
                                                         const int2* __restrict__ tpairs, const float* __restrict__ gz,
                                                         float* __restrict__ out, float* __restrict__ part, int n_segs,
@@ -1008,7 +1009,43 @@ __global__ void __launch_bounds__(kThreads, 5) k_hop_bwd_t(const int4* __restric
             d = __ffma2_rn(u1[1], h1[1], d);
             return d.x + d.y;
         };
+        // the warp sums of two pairs' products at once: lanes 0-15 end with a's, 16-31 with b's
+        auto sum2 = [&](float a, float b) {
+            float v = lane < 16 ? a : b;
+            v += __shfl_xor_sync(0xffffffffu, lane < 16 ? b : a, 16);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            return v;
+        };
         int e = sg.y;
+        for (; e + 4 <= sg.z; e += 4) {                  // four pairs' loads in flight
+            int2 r[4];
+            float2 x[4][2][2];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) r[u] = __ldg(&tpairs[e + u]);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const char* ap = row_at(base, r[u].x, row_bytes);
+                x[u][0][0] = x[u][0][1] = x[u][1][0] = x[u][1][1] = z2;
+                if (v0) ld16<float>(reinterpret_cast<const float*>(ap), x[u][0]);
+                if (v1) ld16<float>(reinterpret_cast<const float*>(ap + 512), x[u][1]);
+            }
+            float d[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float2 w2 = make_float2(__int_as_float(r[u].y), __int_as_float(r[u].y));
+                a0[0] = __ffma2_rn(w2, x[u][0][0], a0[0]); a0[1] = __ffma2_rn(w2, x[u][0][1], a0[1]);
+                a1[0] = __ffma2_rn(w2, x[u][1][0], a1[0]); a1[1] = __ffma2_rn(w2, x[u][1][1], a1[1]);
+                d[u] = dot(x[u][0], x[u][1]);
+            }
+            const float v01 = sum2(d[0], d[1]), v23 = sum2(d[2], d[3]);
+            if ((lane & 15) == 0) {
+                wp[e + (lane >> 4)] = v01;
+                wp[e + 2 + (lane >> 4)] = v23;
+            }
+        }
         for (; e + 2 <= sg.z; e += 2) {
             const int2 p = __ldg(&tpairs[e]), q = __ldg(&tpairs[e + 1]);
             const char* ap = row_at(base, p.x, row_bytes);
@@ -1028,14 +1065,7 @@ __global__ void __launch_bounds__(kThreads, 5) k_hop_bwd_t(const int4* __restric
             a1[0] = __ffma2_rn(wp2, x1[0], a1[0]); a1[1] = __ffma2_rn(wp2, x1[1], a1[1]);
             a0[0] = __ffma2_rn(wq2, y0[0], a0[0]); a0[1] = __ffma2_rn(wq2, y0[1], a0[1]);
             a1[0] = __ffma2_rn(wq2, y1[0], a1[0]); a1[1] = __ffma2_rn(wq2, y1[1], a1[1]);
-            const float sp = dot(x0, x1), sq = dot(y0, y1);
-            // lanes 0-15 end with the warp's sum of sp, lanes 16-31 with that of sq
-            float v = lane < 16 ? sp : sq;
-            v += __shfl_xor_sync(0xffffffffu, lane < 16 ? sq : sp, 16);
-            v += __shfl_xor_sync(0xffffffffu, v, 8);
-            v += __shfl_xor_sync(0xffffffffu, v, 4);
-            v += __shfl_xor_sync(0xffffffffu, v, 2);
-            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            const float v = sum2(dot(x0, x1), dot(y0, y1));
             if ((lane & 15) == 0) wp[e + (lane >> 4)] = v;
         }
         if (e < sg.z) {
