@@ -203,12 +203,6 @@ def algo_bytes(cls: str, s, B: int, act: int) -> float:
     rows = sum(n[1:])
     if cls == "hop_fwd":
         return act * B * sum(n[k] + n[k + 1] for k in range(K)) + 8 * E + 4 * rows
-    if cls == "hop_bwd_t":                       # read gz of layer k, write gh of layer k-1
-        return 4 * B * sum(n[k] + n[k + 1] for k in range(K)) + 8 * E + 4 * sum(n[:K])
-    if cls == "sddmm":                           # read gz of layer k and the states of layer k-1, write the grads
-        return 4 * B * sum(n[k] + n[k + 1] for k in range(K)) + 12 * E
-    if cls == "act_bwd":                         # read gh and h, write gz
-        return 3 * 4 * B * rows
     if cls == "plug_fwd":
         return (s["obs_dim"] * 4 + n[0] * act) * B
     if cls == "out_fwd":
