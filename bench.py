@@ -102,7 +102,8 @@ def args_():
     ap.add_argument("--no-train", action="store_true", help="default workload: leave out the config-3 training block")
     ap.add_argument("--no-check", action="store_true", help="leave out the 16-bit argmax-agreement check")
     ap.add_argument("--no-overlap", action="store_true",
-                    help="training at N > 1: one all-reduce after the backward instead of buckets overlapping it")
+                    help="training at N > 1: one all-reduce of the whole gradient after the backward instead of the "
+                         "packed gradient or buckets overlapping the backward")
     ap.add_argument("--batch", type=int, default=0, help="override the global batch (profiling of a small case only)")
     ap.add_argument("--sources", choices=["zipf", "uniform"], default="zipf",
                     help="source distribution of the 3-hop synthetic graph (configs 1-3): Zipf(1.5) ranks, or uniform "
@@ -228,7 +229,7 @@ def train_bytes(plan, s, B: int, flat_len: int, redrive: bool) -> dict:
         "act_bwd": 3 * 4 * B * hops[-1]["live_dst"],
         # the weight gradient's last step (k_sd_reduce): each live pair's per-chunk partials, its forward pair and edge
         # range, and each of its edges' weight-gradient word read and written
-        "sddmm": sum(4 * h["live_pairs_"] * chunks + 12 * h["live_pairs_"] + 12 * h["live_edges"] for h in hops),
+        "wgrad": sum(4 * h["live_pairs_"] * chunks + 12 * h["live_pairs_"] + 12 * h["live_edges"] for h in hops),
         # transposed product with the weight-gradient products fused in: read gz of the live rows and the live source
         # rows' states (the products and the fused neuron backward), write the layer below's live rows (gz, or gh0
         # below the first hop), read the pair records, write the per-chunk weight-gradient partials
@@ -286,15 +287,24 @@ def run_ours(a, W, rank, world, dev, torch, dist, graph=None):
     flush = torch.empty(64 * 2 ** 20, dtype=torch.float32, device=dev)      # 256 MiB > 126 MB L2
     train = W["flags"] == "train"
     grad = h.flat(4) if train else None
-    # data-parallel mean in the library's gradient buckets, each started as soon as the backward finishes it (one
-    # piece a step); otherwise one all-reduce of the whole flat gradient after the backward
-    from flyguy_b200.dist import BucketedMean
-    bucketed = BucketedMean(h) if train and world > 1 and piece == B and not a.no_overlap else None
+    # data-parallel mean: where the gradient's structural zeros are at least half of it (a graph whose backward
+    # reaches few rows), one all-reduce of the packed gradient after the backward; otherwise the library's gradient
+    # buckets, each started as soon as the backward finishes it (one piece a step); --no-overlap: one all-reduce of
+    # the whole flat gradient after the backward
+    from flyguy_b200.dist import BucketedMean, PackedMean
+    packed = bucketed = None
+    if train and world > 1 and not a.no_overlap:
+        packed = PackedMean(h)
+        if not packed.worth_it():
+            packed = None
+            bucketed = BucketedMean(h) if piece == B else None
 
     def mean_grad():
         if world == 1:
             return
-        if bucketed:
+        if packed:
+            packed()
+        elif bucketed:
             bucketed.finish()
         else:
             dist.all_reduce(grad, op=dist.ReduceOp.AVG)
@@ -405,7 +415,7 @@ def run_ours(a, W, rank, world, dev, torch, dist, graph=None):
         agreement = argmax_agreement(s, P, obs_np, logits.cpu().numpy(), W["flags"])
     # ---- e2e through the host-buffer entry points
     e2e = None if a.no_e2e else run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier,
-                                          max_over_ranks, grad, piece, bucketed)
+                                          max_over_ranks, grad, piece, bucketed, packed)
     # ---- CPU baseline (rank 0, N = 1)
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -423,7 +433,9 @@ def run_ours(a, W, rank, world, dev, torch, dist, graph=None):
                     f"in-degree mean 35, {'Zipf(1.5)' if a.sources == 'zipf' else 'uniform'} sources), obs ~ N(0,1), "
                     "teacher ~ N(0,4)"),
            "config": {"workload": W["desc"], "baseline_config": W["cfg"], "global_batch": Bg, "per_gpu_batch": B,
-                      "parallelism": ((f"dp{world}, gradient all-reduce in {len(bucketed.early)} early + "
+                      "parallelism": ((f"dp{world}, one all-reduce of the packed gradient ({packed.n:,} of "
+                                       f"{packed.flat_len:,} floats: its structural zeros left out)" if packed else
+                                       f"dp{world}, gradient all-reduce in {len(bucketed.early)} early + "
                                        f"{len(bucketed.late)} late buckets overlapping the backward" if bucketed else
                                        f"dp{world}, one gradient all-reduce per step") if train
                                       else f"batch-sharded x{world}, no collective"),
@@ -473,7 +485,7 @@ def traffic_of(cls: str, W, B: int, sources: str = "zipf") -> float | None:
 
 
 def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barrier, max_over_ranks, grad, piece,
-            bucketed=None):
+            bucketed=None, packed=None):
     train = W["flags"] == "train"
     obs_h = torch.from_numpy(obs_np).pin_memory()
     out_h = torch.empty(B, s["n_act"]).pin_memory()
@@ -505,7 +517,9 @@ def run_e2e(a, W, h, s, obs_np, teacher_np, B, Bg, world, dev, torch, dist, barr
                 st = h.teach(od[lo:lo + piece], td[lo:lo + piece], 1.0, logits=None, stats=world == 1,
                              loss_norm=B)
             if world > 1:
-                if bucketed:
+                if packed:
+                    packed()
+                elif bucketed:
                     bucketed.start()
                     bucketed.finish()
                 else:

@@ -49,6 +49,7 @@ struct Hop {
     int *d_live_src = nullptr, n_live_src = 0;   // rows of the layer below that this hop's backward writes
     int2* d_sde = nullptr;                       // live edges {edge, transposed pair} in transposed-pair order
     int n_sde = 0;
+    std::vector<int2> h_sde;                     // (host copy, until the packed-gradient list is built)
     int4 *d_segs = nullptr, *d_reds = nullptr;   // transposed product: segments of source rows, split-row reductions
     int* d_seg_red = nullptr;                    // per segment: its split row's reduction index, or -1
     int n_segs = 0, n_reds = 0, n_slots = 0;
@@ -59,7 +60,7 @@ struct Hop {
 constexpr int kSegLen = 64;                  // pairs per transposed segment (short: hub CTAs retire fast)
 
 // kernel classes timed by fg_timing (CUDA events around every launch of the class, on the handle's stream)
-enum KClass { K_TRANSPOSE, K_FOLD, K_PLUG_FWD, K_HOP_FWD, K_OUT_FWD, K_LOSS, K_OUT_BWD, K_ACT_BWD, K_SDDMM, K_HOP_BWD,
+enum KClass { K_TRANSPOSE, K_FOLD, K_PLUG_FWD, K_HOP_FWD, K_OUT_FWD, K_LOSS, K_OUT_BWD, K_ACT_BWD, K_WGRAD, K_HOP_BWD,
               K_PLUG_BWD, K_ADAM, K_NORM, K_NCLASS };
 
 struct Timer {
@@ -94,6 +95,8 @@ struct Core {
     int2 *d_pairs = nullptr, *d_tpairs = nullptr;
     int *d_gptr = nullptr, *d_gw = nullptr, *d_tpos = nullptr;   // d_tpos: pair -> transposed pair, or -1
     float* sd_part = nullptr;                            // weight-gradient partials [256-sample chunk][transposed pair]
+    int* d_wlive = nullptr;                              // strengths a live edge can change, ascending (fg_grad_pack)
+    int n_wlive = 0;
     long long off[8] = {0};                             // segment starts in the flat arrays (256-byte aligned)
     long long psize[7] = {0};                           // the seven arrays' true lengths
     float *P = nullptr, *G = nullptr, *M = nullptr, *V = nullptr, *EMA = nullptr;
@@ -327,6 +330,7 @@ void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, c
                     sde.push_back(make_int2(j, q));
             h.n_sde = (int)sde.size();
             if (h.n_sde) h.d_sde = upload(c, sde);
+            h.h_sde = std::move(sde);
         }
         std::vector<int4> segs, reds;
         std::vector<int> seg_red;
@@ -476,6 +480,16 @@ void upload_net(Core& c, NetHost& n) {
     c.d_tpairs = upload(c, tpairs);
     c.d_gptr = upload(c, gptr);
     c.d_gw = upload(c, gw);
+    {   // the strengths whose gradient can be non-zero: those of the edges of pairs into live rows
+        std::vector<char> on(std::max(c.n_w, 1), 0);
+        for (const Hop& h : c.hop)
+            for (const int2& e : h.h_sde) on[gw[e.x]] = 1;
+        std::vector<int> wl;
+        for (int w = 0; w < c.n_w; ++w) if (on[w]) wl.push_back(w);
+        c.n_wlive = (int)wl.size();
+        if (c.n_wlive) c.d_wlive = upload(c, wl);
+        for (Hop& h : c.hop) std::vector<int2>().swap(h.h_sde);
+    }
     if (c.Ttot) {
         std::vector<int> tpos(c.Ptot, -1);
         for (long long q = 0; q < c.Ttot; ++q) tpos[tpi[q]] = (int)q;
@@ -824,7 +838,7 @@ void backward(Core& c, int B) {
                         c.d_tpairs + h.tbase, gz, nxt, c.seg_part, h.n_segs, B, ep, hprev, c.sd_part, (int)h.T);
             });
             if (h.n_sde) {
-                launch(c, K_SDDMM, [&]() {
+                launch(c, K_WGRAD, [&]() {
                     if (h.widx_unique)
                         pdl(c, k_sd_reduce<false>, blocks(h.n_sde), 256, 0, (const float*)c.sd_part, (int)h.T, chunks,
                             (const int2*)h.d_sde, h.n_sde, (const int*)c.d_gw, c.G + c.off[0]);
@@ -1017,6 +1031,27 @@ int fg_grad_buckets(void* h, long long* out, int n) {
             for (int j = 0; j < 3; ++j) out[3 * i + j] = b[i][j];
         return (int)b.size();
     }, -1);
+}
+
+long long fg_grad_pack(void* h, float* buf, long long cap, int unpack) {
+    return guarded(h, [&]() {
+        Core& c = *as_core(h);
+        if (!c.train) throw Err("this handle was created for inference only");
+        const long long tail = c.off[7] - c.off[1];
+        const long long n = c.n_wlive + tail;
+        if (!buf || cap == 0) return n;
+        if (cap < n) throw Err("fg_grad_pack: the buffer holds " + std::to_string(cap) + " floats, the packed gradient " +
+                               std::to_string(n));
+        if (c.n_wlive)
+            launch(c, K_NORM, [&]() {
+                pdl(c, k_grad_pack, blocks(c.n_wlive), 256, 0, c.G, (const int*)c.d_wlive, buf, c.n_wlive, unpack);
+            });
+        float* g = c.G + c.off[1];
+        float* b = buf + c.n_wlive;
+        if (unpack) CK(cudaMemcpyAsync(g, b, (size_t)tail * 4, cudaMemcpyDeviceToDevice, c.st));
+        else CK(cudaMemcpyAsync(b, g, (size_t)tail * 4, cudaMemcpyDeviceToDevice, c.st));
+        return n;
+    }, (long long)-1);
 }
 
 int fg_plan(void* h, long long* out, int n) {

@@ -1136,6 +1136,16 @@ __global__ void __launch_bounds__(256) k_sd_reduce(const float* __restrict__ wpa
     if (ATOMIC) atomicAdd(&gW[w], v); else gW[w] += v;
 }
 
+// packed gradient: buf[i] = g[idx[i]] (unpack: g[idx[i]] = buf[i])
+__global__ void k_grad_pack(float* __restrict__ g, const int* __restrict__ idx, float* __restrict__ buf, int n,
+                            int unpack) {
+    pdl_enter();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int w = __ldg(&idx[i]);
+    if (unpack) g[w] = buf[i]; else buf[i] = g[w];
+}
+
 // per listed row of a layer (the rows the transposed hop finished): gain grad += sum over chunks of g*z, theta grad +=
 // -(sum of g) * sigmoid(theta); live = any g
 __global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __restrict__ list,

@@ -44,6 +44,7 @@ SIGNATURES = {
     "fg_plan": (_ci, [_vp, ctypes.POINTER(_cll), _ci]),
     "fg_grad_buckets": (_ci, [_vp, ctypes.POINTER(_cll), _ci]),
     "fg_set_stage_event": (_ci, [_vp, _ci, _vp]),
+    "fg_grad_pack": (_cll, [_vp, _vp, _cll, _ci]),
     "fg_teach": (_ci, [_vp, _vp, _vp, _ci, _cf, _vp, ctypes.POINTER(ctypes.c_double)]),
     "fg_teach_ex": (_ci, [_vp, _vp, _vp, _ci, _cf, _cf, _vp, ctypes.POINTER(ctypes.c_double)]),
     "fg_forward_host": (_ci, [_vp, _vp, _ci, _vp, _ci]),
@@ -67,7 +68,7 @@ SIGNATURES = {
     "fly_free": (None, [_vp]),
     "fg_fly_last_error": (ctypes.c_char_p, []),
 }
-KERNEL_CLASSES = ("layout", "fold", "plug_fwd", "hop_fwd", "out_fwd", "loss", "out_bwd", "act_bwd", "sddmm",
+KERNEL_CLASSES = ("layout", "fold", "plug_fwd", "hop_fwd", "out_fwd", "loss", "out_bwd", "act_bwd", "wgrad",
                   "hop_bwd_t", "plug_bwd", "adam", "norm")
 
 
@@ -175,6 +176,20 @@ class Handle:
         t = n - 4
         return {"hops": hops, "plug_live": int(buf[t]), "n_s": int(buf[t + 1]), "fan": int(buf[t + 2]),
                 "n_dn": int(buf[t + 3])}
+
+    def grad_pack(self, buf=None, unpack: bool = False) -> int:
+        """fg_grad_pack: the gradient without its structural zeros into `buf` (a float32 device tensor; unpack: back
+        from it). Without buf, the packed length."""
+        self.bind_stream()
+        if buf is None:
+            n = self.L.fg_grad_pack(self.h, None, 0, 0)
+        else:
+            if buf.dtype != self.torch.float32 or not buf.is_contiguous() or buf.device != self.device:
+                raise FlyguyError("grad_pack: buf must be a contiguous float32 tensor on the handle's device")
+            n = self.L.fg_grad_pack(self.h, buf.data_ptr(), buf.numel(), 1 if unpack else 0)
+        if n < 0:
+            self.check()
+        return int(n)
 
     def grad_buckets(self) -> list[tuple[int, int, int]]:
         """(first, end, stage) ranges of the flat gradient (fg_grad_buckets): stage s >= 0 final once the backward

@@ -109,6 +109,12 @@ int fg_grad_buckets(void* h, long long* out, int n);
    (0..hops, as in fg_grad_buckets); a side stream that waits on it can start that bucket's all-reduce. Returns 0, or
    -1 for a stage out of range. */
 int fg_set_stage_event(void* h, int stage, void* event);
+/* The gradient packed without its structural zeros, for a smaller data-parallel all-reduce: the connection strengths
+   that a live edge can change (every other strength's gradient is exactly zero on every rank: the backward never
+   writes it after fc_zero_grad), then the other six arrays whole. unpack = 0: buf (device, cap floats) <- the
+   gradient; unpack = 1: the gradient <- buf (the strengths outside the packed set keep their zero). Queued on the
+   handle's stream. Returns the packed length (buf NULL or cap 0: the length only), or -1. */
+long long fg_grad_pack(void* h, float* buf, long long cap, int unpack);
 
 /* The distillation step's device half, fused: forward with the weights, KL(softmax(teacher * inv_temp) ||
  * softmax(logits)) averaged over the batch, its gradient through the network ADDED to the gradient.

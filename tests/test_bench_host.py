@@ -58,7 +58,7 @@ def test_training_bytes_count_only_what_the_plan_visits():
     half = b.train_bytes(plan(0.5), s, 1024, 100_000, False)
     for k in ("plug_fwd", "hop_fwd", "out_fwd", "loss", "out_bwd", "adam"):
         assert full[k] == half[k], k
-    for k in ("act_bwd", "sddmm", "hop_bwd_t", "plug_bwd"):
+    for k in ("act_bwd", "wgrad", "hop_bwd_t", "plug_bwd"):
         assert half[k] < full[k], k
     assert full["hop_fwd"] == b.algo_bytes("hop_fwd", s, 1024, 4)
     assert full["adam"] == 36 * 100_000

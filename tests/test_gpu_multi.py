@@ -19,7 +19,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, out, bucketed=False):
+def _rank(rank, world, port, out, mode="one"):
     import torch
     import torch.distributed as td
     from datetime import timedelta
@@ -35,13 +35,15 @@ def _rank(rank, world, port, out, bucketed=False):
         h.set_params(P)
         obs = torch.as_tensor(d["obs"][rank * B:(rank + 1) * B]).cuda()
         teacher = torch.as_tensor(d["teacher"][rank * B:(rank + 1) * B]).cuda()
-        mean = dist.BucketedMean(h) if bucketed else None
+        mean = dist.BucketedMean(h) if mode == "bucketed" else dist.PackedMean(h) if mode == "packed" else None
         h.zero_grad()
         h.teach(obs, teacher, float(d["inv_temp"]))
         assert dist.on()
-        if bucketed:                                   # buckets started as the backward finishes them
+        if mode == "bucketed":                         # buckets started as the backward finishes them
             mean.start()
             mean.finish()
+        elif mode == "packed":                         # one all-reduce of the gradient without its structural zeros
+            mean()
         else:
             dist.mean_([h.flat(4)])
         G = [g.cpu().numpy() for g in h.get(4)]
@@ -50,15 +52,15 @@ def _rank(rank, world, port, out, bucketed=False):
         td.destroy_process_group()
 
 
-@pytest.mark.parametrize("bucketed", [False, True])
-def test_two_gpu_gradient_mean_equals_full_batch(tmp_path, cuda, bucketed):
-    """One all-reduce after the backward, or the library's buckets each started on a side stream when the backward
-    reaches its stage: either way the averaged gradient is the whole batch's."""
+@pytest.mark.parametrize("mode", ["one", "bucketed", "packed"])
+def test_two_gpu_gradient_mean_equals_full_batch(tmp_path, cuda, mode):
+    """One all-reduce after the backward, the library's buckets each started on a side stream when the backward
+    reaches its stage, or one all-reduce of the packed gradient: each way the averaged gradient is the whole batch's."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
-    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), bucketed), nprocs=2, start_method="spawn")
+    mp.start_processes(_rank, args=(2, _free_port(), str(tmp_path), mode), nprocs=2, start_method="spawn")
     # one process, the whole batch: the mean over ranks of per-half gradients (each scaled by 1/half) equals the
     # gradient of the whole batch (scaled by 1/B)
     from flyguy_b200 import native
@@ -107,3 +109,33 @@ def test_gradient_buckets_cover_the_flat_gradient_and_their_events_fire(cuda):
         assert all(ev.query() for ev in evs.values())
         with pytest.raises(native.FlyguyError):
             h.set_stage_event(99, evs[0])
+
+
+def test_packed_gradient_leaves_out_only_zeros(cuda):
+    """fg_grad_pack: after a teaching step, packing the gradient, zeroing it and unpacking gives the same gradient bit
+    for bit - the strengths left out of the packed set had an exactly zero gradient; on a Zipf-source graph (most rows
+    unread, so the backward reaches few) the packed gradient is a fraction of the flat one."""
+    import torch
+    from flyguy_b200 import native, synth
+    for s, smaller in ((synth.make_synthetic(sizes=(300, 700, 500, 60), total_edges=30_000, seed=3)[0], True),
+                       (load_case("toy_h3")[0], False)):
+        P = [np.random.default_rng(1).normal(size=n).astype(np.float32) * 0.1 for n in s.param_sizes()]
+        h = native.Handle(s, 64)
+        h.set_params(P)
+        obs = torch.randn(64, s["obs_dim"], device="cuda")
+        h.zero_grad()
+        h.teach(obs, torch.randn(64, s["n_act"], device="cuda"), 1.0)
+        flat = h.flat(4)
+        want = flat.clone()
+        n = h.grad_pack()
+        if smaller:                                    # (about 54% here: 10,928 of 30,000 strengths + the rest)
+            assert n < 0.6 * flat.numel(), (n, flat.numel())
+        buf = torch.full((n,), float("nan"), device="cuda")
+        assert h.grad_pack(buf) == n
+        h.zero_grad()
+        h.grad_pack(buf, unpack=True)
+        torch.cuda.synchronize()
+        assert torch.equal(flat, want)
+        with pytest.raises(native.FlyguyError):
+            h.grad_pack(torch.empty(max(n - 1, 1), device="cuda"))
+
