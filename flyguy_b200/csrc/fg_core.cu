@@ -106,7 +106,6 @@ struct Core {
     float *gz_a = nullptr, *gz_b = nullptr, *gdrive = nullptr, *part = nullptr;
     float* nsum = nullptr;
     float *kl_s = nullptr, *ag_s = nullptr, *stats = nullptr, *norm_part = nullptr, *norm = nullptr;
-    int* live = nullptr;
     int out_splits = 1;
     float *obs_dev = nullptr, *logits_dev = nullptr;   // fg_forward_host staging
     cudaStream_t st = 0, h2d = nullptr, d2h = nullptr;
@@ -551,8 +550,7 @@ void alloc_all(Core& c) {
         c.gz_a = dalloc<float>(c, (size_t)max_rows * B);
         c.gz_b = dalloc<float>(c, (size_t)max_rows * B);
         c.gdrive = dalloc<float>(c, (size_t)c.n_s * B);
-        c.live = dalloc<int>(c, max_rows);
-        c.nsum = dalloc<float>(c, (size_t)max_rows * ((B + 255) / 256) * 3);
+        c.nsum = dalloc<float>(c, (size_t)max_rows * ((B + 255) / 256) * 2);
         c.out_splits = std::max(1, std::min(64, (int)(B / 128)));     // batch slices of the output-plug backward
         c.part = dalloc<float>(c, (size_t)c.out_splits * c.n_act * (c.n_dn + 1));
         c.kl_s = dalloc<float>(c, B);
@@ -815,7 +813,7 @@ void backward(Core& c, int B) {
         pdl(c, k_act_bwd<float>, top.n_live_dst, kThreads, 0, nxt, hK, top.d_nid, top.d_drow,
                                                                 c.d_rgain + top.rbase, c.d_rthr + top.rbase,
                                                                 c.d_rsig + top.rbase, gz, c.G + c.off[1],
-                                                                c.G + c.off[2], c.gdrive, c.live, top.d_live_dst, B,
+                                                                c.G + c.off[2], c.gdrive, top.d_live_dst, B,
                                                                 B);
     });
     const int chunks = (B + 255) / 256;
@@ -856,7 +854,7 @@ void backward(Core& c, int B) {
             launch(c, K_ACT_BWD, [&]() {
                 pdl(c, k_neuron_reduce, blocks(h.n_live_src), 256, 0, c.nsum, h.d_live_src, lo.d_nid,
                                                                        c.d_rsig + lo.rbase, c.G + c.off[1],
-                                                                       c.G + c.off[2], c.live, h.n_live_src, chunks);
+                                                                       c.G + c.off[2], h.n_live_src, chunks);
             });
         } else {
             NeuronEpi ep{nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, chunks};

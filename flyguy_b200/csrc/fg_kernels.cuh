@@ -844,16 +844,15 @@ __global__ void k_out_bwd_reduce(const float* __restrict__ part, float* __restri
 
 // ---------------------------------------------------------------- backward: through the neurons
 // one CTA per listed row of the top layer: g = gh * [h > 0]; gz = g * gain -> gz; gain grad += sum g*z with z = (h + thr) / gain (exact where
-// h > 0, the only place it counts); theta grad += sum -g * sigmoid(theta); gdrive[drow] += gz. Returns through
-// `live[row]` whether any g was non-zero (rows that never fire are skipped by the weight gradient).
+// h > 0, the only place it counts); theta grad += sum -g * sigmoid(theta); gdrive[drow] += gz.
 template <class T>
 __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ gh, const T* __restrict__ h,
                                                       const int* __restrict__ nid, const int* __restrict__ drow,
                                                       const float* __restrict__ rgain, const float* __restrict__ rthr,
                                                       const float* __restrict__ rsig, float* __restrict__ gz,
                                                       float* __restrict__ ggain, float* __restrict__ gtheta,
-                                                      float* __restrict__ gdrive, int* __restrict__ live,
-                                                      const int* __restrict__ rows, int B, int ld) {
+                                                      float* __restrict__ gdrive, const int* __restrict__ rows, int B,
+                                                      int ld) {
     pdl_enter();
     __shared__ float red[3 * kWarps];
     const int t = __ldg(&rows[blockIdx.x]);             // a row whose gradient can be non-zero (an output-plug column)
@@ -861,7 +860,7 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
     const float inv_g = gn != 0.f ? 1.f / gn : 0.f;
     const int d = drow ? drow[t] : -1;
     const size_t o = (size_t)t * ld;
-    float s[3] = {0.f, 0.f, 0.f};                        // sum g*z, sum g, any
+    float s[2] = {0.f, 0.f};                             // sum g*z, sum g
     for (int b = threadIdx.x * 4; b < B; b += kThreads * 4) {
         float4 q = __ldg(reinterpret_cast<const float4*>(gh + o + b));
         float hv[4] = {ld1(h + o + b), ld1(h + o + b + 1), ld1(h + o + b + 2), ld1(h + o + b + 3)};
@@ -872,7 +871,6 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
             float g = hv[i] > 0.f ? gv[i] : 0.f;
             s[0] = fmaf(g, (hv[i] + th) * inv_g, s[0]);
             s[1] += g;
-            s[2] += g != 0.f ? 1.f : 0.f;
             zo[i] = g * gn;
         }
         *reinterpret_cast<float4*>(gz + o + b) = make_float4(zo[0], zo[1], zo[2], zo[3]);
@@ -883,12 +881,11 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
             *gd = c;
         }
     }
-    block_sum<3>(s, red);
+    block_sum<2>(s, red);
     if (threadIdx.x == 0) {
         const int id = nid[t];
         ggain[id] += s[0];
         gtheta[id] += -s[1] * rsig[t];
-        live[t] = s[2] > 0.f;
     }
 }
 
@@ -900,8 +897,8 @@ __global__ void __launch_bounds__(kThreads) k_act_bwd(const float* __restrict__ 
 // Chunk-major launch order and hub rows cut into short segments keep the few chunks in flight inside L2 (a hub row
 // reaches every destination row, so each chunk reads its whole gz column slab).
 // Finishing a row (EPI): the source layer's neuron backward is fused in - g = gh * [h > 0]; gz = g * gain is written
-// (not gh), gdrive[drow] += gz, and the row's per-chunk sums of g*z (z = (h + thr) / gain where h > 0), of g and of
-// [g != 0] go to nsum[row][chunk][3] for k_neuron_reduce. Without EPI (the sensory layer) gh itself is written.
+// (not gh), gdrive[drow] += gz, and the row's per-chunk sums of g*z (z = (h + thr) / gain where h > 0) and of g
+// go to nsum[row][chunk][2] for k_neuron_reduce. Without EPI (the sensory layer) gh itself is written.
 // The weight gradient (the reference's SDDMM, flyguy_train.cu:158-167) is fused in: the warp loads its source row's
 // states for its chunk once (hs) and, per pair, adds gz[dst] * hs[src] over the chunk's 256 samples into
 // wpart[chunk][pair] (two pairs' warp sums at once: each half-warp reduces one); k_sd_reduce then adds a pair's chunks
@@ -914,13 +911,13 @@ struct NeuronEpi {
     const float* rthr;
     const int* drow;         // re-drive rows (nullable)
     float* gdrive;           // [n_s, ld]
-    float* nsum;             // [rows][chunks][3]
+    float* nsum;             // [rows][chunks][2]
     int chunks;
 };
-// one 4-sample group of a finished row: stores, and adds the group's neuron sums into s[3]
+// one 4-sample group of a finished row: stores, and adds the group's neuron sums into sum[2]
 template <bool EPI>
 __device__ __forceinline__ void finish_group(int s, int c, int ld, const float (&a)[4], float* out,
-                                             const NeuronEpi& ep, float gn, float th, float inv_g, float (&sum)[3]) {
+                                             const NeuronEpi& ep, float gn, float th, float inv_g, float (&sum)[2]) {
     float* o = out + (size_t)s * ld + c;
     if (!EPI) {
         *reinterpret_cast<float4*>(o) = make_float4(a[0], a[1], a[2], a[3]);
@@ -935,7 +932,6 @@ __device__ __forceinline__ void finish_group(int s, int c, int ld, const float (
         gz[i] = g * gn;
         sum[0] = fmaf(g, (hv[i] + th) * inv_g, sum[0]);
         sum[1] += g;
-        sum[2] += g != 0.f ? 1.f : 0.f;
     }
     *reinterpret_cast<float4*>(o) = make_float4(gz[0], gz[1], gz[2], gz[3]);
     if (ep.drow) {
@@ -953,7 +949,7 @@ template <bool EPI>
 __device__ __forceinline__ void finish_row(int s, int chunk, int c0, int c1, bool v0, bool v1, int ld,
                                            const float (&a0)[4], const float (&a1)[4], float* out,
                                            const NeuronEpi& ep) {
-    float sum[3] = {0.f, 0.f, 0.f};
+    float sum[2] = {0.f, 0.f};
     float gn = 0.f, th = 0.f, inv_g = 0.f;
     if (EPI) {
         gn = __ldg(&ep.rgain[s]);
@@ -963,10 +959,10 @@ __device__ __forceinline__ void finish_row(int s, int chunk, int c0, int c1, boo
     if (v0) finish_group<EPI>(s, c0, ld, a0, out, ep, gn, th, inv_g, sum);
     if (v1) finish_group<EPI>(s, c1, ld, a1, out, ep, gn, th, inv_g, sum);
     if (EPI) {
-        sum[0] = warp_sum(sum[0]); sum[1] = warp_sum(sum[1]); sum[2] = warp_sum(sum[2]);
+        sum[0] = warp_sum(sum[0]); sum[1] = warp_sum(sum[1]);
         if ((threadIdx.x & 31) == 0) {
-            float* ns = ep.nsum + ((size_t)s * ep.chunks + chunk) * 3;
-            ns[0] = sum[0]; ns[1] = sum[1]; ns[2] = sum[2];
+            float* ns = ep.nsum + ((size_t)s * ep.chunks + chunk) * 2;
+            ns[0] = sum[0]; ns[1] = sum[1];
         }
     }
 }
@@ -1147,23 +1143,21 @@ __global__ void k_grad_pack(float* __restrict__ g, const int* __restrict__ idx, 
 }
 
 // per listed row of a layer (the rows the transposed hop finished): gain grad += sum over chunks of g*z, theta grad +=
-// -(sum of g) * sigmoid(theta); live = any g
+// -(sum of g) * sigmoid(theta)
 __global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __restrict__ list,
                                 const int* __restrict__ nid, const float* __restrict__ rsig,
-                                float* __restrict__ ggain, float* __restrict__ gtheta, int* __restrict__ live, int n,
-                                int chunks) {
+                                float* __restrict__ ggain, float* __restrict__ gtheta, int n, int chunks) {
     pdl_enter();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int s = __ldg(&list[i]);
-    float a = 0.f, b = 0.f, nz = 0.f;
-    const float* p = nsum + (size_t)s * chunks * 3;
+    float a = 0.f, b = 0.f;
+    const float* p = nsum + (size_t)s * chunks * 2;
 #pragma unroll 4
-    for (int k = 0; k < chunks; ++k) { a += p[3 * k]; b += p[3 * k + 1]; nz += p[3 * k + 2]; }
+    for (int k = 0; k < chunks; ++k) { a += p[2 * k]; b += p[2 * k + 1]; }
     const int id = nid[s];
     ggain[id] += a;
     gtheta[id] += -b * rsig[s];
-    live[s] = nz > 0.f;
 }
 
 // sensory layer and plug, one warp per listed sensory row s (the rows with a possibly non-zero gradient) over the

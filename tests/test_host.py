@@ -96,6 +96,60 @@ def test_dist_mean_over_two_gloo_ranks(tmp_path):
         assert torch.allclose(d["b"], torch.arange(7, dtype=torch.float32) * 1.5)
 
 
+class _FakePackHandle:
+    """The host side of fg_grad_pack on the CPU: a flat gradient whose entries 0..63 outside `idx` are structural
+    zeros, packed as flat[idx] then flat[64:] (the library's layout: the strengths that can change, then the rest)."""
+
+    def __init__(self, rank):
+        self.device = torch.device("cpu")
+        self.idx = torch.tensor([3, 5, 17, 40, 41, 63])
+        self.g = torch.zeros(100)
+        self.g[self.idx] = torch.arange(6, dtype=torch.float32) * (rank + 1)
+        self.g[64:] = torch.linspace(-1, 1, 36) * (rank + 1)
+
+    def flat(self, which):
+        return self.g
+
+    def grad_pack(self, buf=None, unpack=False):
+        n = len(self.idx) + 36
+        if buf is None:
+            return n
+        if unpack:
+            self.g[self.idx] = buf[:len(self.idx)]
+            self.g[64:] = buf[len(self.idx):n]
+        else:
+            buf[:len(self.idx)] = self.g[self.idx]
+            buf[len(self.idx):n] = self.g[64:]
+        return n
+
+
+def _packed_worker(rank, world, port, out):
+    import torch.distributed as td
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+    td.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    from flyguy_b200 import dist
+    h = _FakePackHandle(rank)
+    mean = dist.PackedMean(h)
+    assert mean.n == 42 and mean.worth_it()
+    mean()
+    torch.save(h.g, Path(out) / f"r{rank}.pt")
+    td.destroy_process_group()
+
+
+def test_dist_packed_mean_over_two_gloo_ranks(tmp_path):
+    """dist.PackedMean: pack, all-reduce (average), unpack - the same mean as all-reducing the whole flat gradient, and
+    the structural zeros left out stay zero."""
+    import torch.multiprocessing as mp
+    world = 2
+    mp.start_processes(_packed_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
+    want = (_FakePackHandle(0).g + _FakePackHandle(1).g) / 2
+    for r in range(world):
+        got = torch.load(tmp_path / f"r{r}.pt")
+        assert torch.allclose(got, want)
+        assert torch.count_nonzero(got[:64]) == 5          # idx entries (the first is 0 * 1.5) and nothing else
+
+
 def test_dist_off_without_a_group():
     from flyguy_b200 import dist
     t = torch.ones(3)
