@@ -437,6 +437,7 @@ def run_ours(a, W, rank, world, dev, torch, dist, graph=None):
                                        f"{packed.flat_len:,} floats: its structural zeros left out)" if packed else
                                        f"dp{world}, gradient all-reduce in {len(bucketed.early)} early + "
                                        f"{len(bucketed.late)} late buckets overlapping the backward" if bucketed else
+                                       "dp1 (one GPU: no all-reduce)" if world == 1 else
                                        f"dp{world}, one gradient all-reduce per step") if train
                                       else f"batch-sharded x{world}, no collective"),
                       "l2": "flushed between timed steps (256 MiB write, outside the step events)",

@@ -25,7 +25,9 @@
 
 namespace fg {
 
-constexpr int kOtM = 128, kOtN = 96, kOtKC = 32, kOtStages = 3, kOtProd = 8;
+// Two stages (115 KB of shared memory) so that two CTAs share a SM and cover each other's gather latency: the forward
+// output plug at batch 65,536 took 0.198 ms against 0.287 with three stages at one CTA a SM.
+constexpr int kOtM = 128, kOtN = 96, kOtKC = 32, kOtStages = 2, kOtProd = 8;
 constexpr int kOtThreads = 32 * (kOtProd + 1);
 constexpr uint32_t kOtA = kOtM * kOtKC * 4;            // one term of a chunk of hK (16 KB)
 constexpr uint32_t kOtB = kOtN * kOtKC * 4;            // one term of a chunk of out_w (12 KB)
@@ -74,7 +76,7 @@ struct OutTc {
     int n_dn, B, ld, chunks, cps;    // cps: chunks per slice
 };
 
-__global__ void __launch_bounds__(kOtThreads, 1) k_out_tc(const OutTc a) {
+__global__ void __launch_bounds__(kOtThreads, 2) k_out_tc(const OutTc a) {
     pdl_enter();
     extern __shared__ __align__(1024) unsigned char smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOtStages * kOtStage);
