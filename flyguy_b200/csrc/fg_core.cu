@@ -47,6 +47,7 @@ struct Hop {
     int *d_live_dst = nullptr, n_live_dst = 0;   // rows of this hop's layer whose gradient can be non-zero
     long long live_pairs = 0, live_edges = 0;    // merged pairs / edges of those rows (what the weight gradient visits)
     int *d_live_src = nullptr, n_live_src = 0;   // rows of the layer below that this hop's backward writes
+    bool narrow = false;                         // fp32 forward in the narrow configuration (no hub sources)
     int2* d_sde = nullptr;                       // live edges {edge, transposed pair} in transposed-pair order
     int n_sde = 0;
     std::vector<int2> h_sde;                     // (host copy, until the packed-gradient list is built)
@@ -240,6 +241,14 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
     for (int w : widx) mark[w] = 0;
     h.P = (int)psrc.size();
     for (int p = 0; p < h.P; ++p) pairs.push_back(make_int2(psrc[p], 0));
+    {   // no hub sources (the 32 busiest carry under a fifth of the pairs): the narrow fp32 forward (HopCfg)
+        std::vector<int> per_src(h.n_src, 0);
+        for (int s : psrc) ++per_src[s];
+        const int top = std::min<int>(32, (int)per_src.size());
+        std::partial_sort(per_src.begin(), per_src.begin() + top, per_src.end(), std::greater<int>());
+        const long long busy = std::accumulate(per_src.begin(), per_src.begin() + top, 0LL);
+        h.narrow = h.P > 0 && busy * 5 < (long long)h.P;
+    }
     // schedule: rows with most pairs first, so the long ones start early
     std::vector<int> sched(rows);
     std::iota(sched.begin(), sched.end(), 0);
@@ -677,19 +686,22 @@ void hop_launch(Core& c, const Hop& h, const void* hp, int B) {
         });
         return;
     }
-    constexpr int N = Lane32<TI>::N;                     // samples per lane; the warp's chunk is 32 N
-    const dim3 g((h.rows + kWarps - 1) / kWarps, (unsigned)((B + 32 * N - 1) / (32 * N)));
-    const bool full = B % (32 * N) == 0;
-    launch(c, K_HOP_FWD, [&]() {
-        if (full)
-            pdl(c, k_hop_fwd<TI, TO, true>, g, kThreads, 0, h.d_rows, c.d_pairs + h.pbase, (const TI*)hp,
-                                                              c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow,
-                                                              c.drive, (TO*)h.d_h, h.rows, B);
-        else
-            pdl(c, k_hop_fwd<TI, TO, false>, g, kThreads, 0, h.d_rows, c.d_pairs + h.pbase, (const TI*)hp,
-                                                               c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow,
-                                                               c.drive, (TO*)h.d_h, h.rows, B);
-    });
+    auto go = [&](auto narrow) {
+        constexpr bool NW = decltype(narrow)::value;
+        constexpr int N = Lane32<TI, NW>::N;             // samples per lane; the warp's chunk is 32 N
+        const dim3 g((h.rows + kWarps - 1) / kWarps, (unsigned)((B + 32 * N - 1) / (32 * N)));
+        const bool full = B % (32 * N) == 0;
+        launch(c, K_HOP_FWD, [&]() {
+            if (full)
+                pdl(c, k_hop_fwd<TI, TO, true, NW>, g, kThreads, 0, h.d_rows, c.d_pairs + h.pbase, (const TI*)hp,
+                    c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive, (TO*)h.d_h, h.rows, B);
+            else
+                pdl(c, k_hop_fwd<TI, TO, false, NW>, g, kThreads, 0, h.d_rows, c.d_pairs + h.pbase, (const TI*)hp,
+                    c.d_rgain + h.rbase, c.d_rthr + h.rbase, h.d_drow, c.drive, (TO*)h.d_h, h.rows, B);
+        });
+    };
+    if (sizeof(TI) == 4 && h.narrow) go(std::true_type{});
+    else go(std::false_type{});
 }
 
 // obs == nullptr: the states start from c.x as it is

@@ -457,14 +457,21 @@ __device__ __forceinline__ void st16(TO* o, const float* hv) {
 #ifndef FG_HOP_MINB32
 #define FG_HOP_MINB32 3
 #endif
-template <class TI> struct HopCfg {
-    static constexpr int NG = sizeof(TI) == 2 ? FG_HOP_NG16 : FG_HOP_NG32;
+// NARROW (fp32 states on a hop without hub sources, where the gathers miss L1): four groups (16 samples a lane,
+// 512-sample warp chunks) at 64 registers and 4 CTAs a SM, more warps to cover the L2 latency - on the model.pt network
+// the training step's hop forward took 13.0 ms against 14.1 with eight groups at 3 CTAs a SM; on the Zipf graph eight
+// groups stay faster (2.96 against 3.12 ms)
+template <class TI, bool NARROW = false> struct HopCfg {
+    static constexpr bool W = NARROW && sizeof(TI) == 4;
+    static constexpr int NG = W ? 4 : sizeof(TI) == 2 ? FG_HOP_NG16 : FG_HOP_NG32;
     static constexpr int UNR = sizeof(TI) == 2 ? FG_HOP_UNR16 : FG_HOP_UNR32;
     static constexpr bool PF = sizeof(TI) == 2 ? FG_HOP_PF16 : FG_HOP_PF32;
-    static constexpr int min_blocks = sizeof(TI) == 2 ? FG_HOP_MINB16 : FG_HOP_MINB32;
+    static constexpr int min_blocks = W ? 4 : sizeof(TI) == 2 ? FG_HOP_MINB16 : FG_HOP_MINB32;
 };
 // states per lane per pair (the warp's chunk is 32 N samples)
-template <class T> struct Lane32 { static constexpr int N = HopCfg<T>::NG * 16 / (int)sizeof(T); };
+template <class T, bool NARROW = false> struct Lane32 {
+    static constexpr int N = HopCfg<T, NARROW>::NG * 16 / (int)sizeof(T);
+};
 // the 16 raw bytes of a gather, unpacked to fp32 and multiplied into a (same FMA per sample as one at a time)
 template <class TI>
 __device__ __forceinline__ void fma16(const uint4& r, float2 w, float2 (&a)[Vec16<TI>::H]) {
@@ -521,15 +528,15 @@ __device__ __forceinline__ void act_store(TO* o, const float2 (&a)[H], float gn,
 // warp's whole chunk lies inside the batch (ld a multiple of 32 N): no per-group validity tests. SURV (the firing
 // survey): also adds, per row, the number of samples whose state is positive to fired[t] and the sum of the squared
 // pre-activations to sq[t] (per-lane atomics: lanes past the batch have already returned).
-template <class TI, class TO, bool FULL, bool SURV = false>
+template <class TI, class TO, bool FULL, bool SURV = false, bool NARROW = false>
 __device__ __forceinline__ void hop_row(int slot, int chunk, const int4* __restrict__ rows,
                                         const int2* __restrict__ pairs, const TI* __restrict__ hp,
                                         const float* __restrict__ rgain, const float* __restrict__ rthr,
                                         const int* __restrict__ drow, const float* __restrict__ drive,
                                         TO* __restrict__ h, int n_rows, int ld, int* __restrict__ fired = nullptr,
                                         float* __restrict__ sq = nullptr) {
-    constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H, NG = HopCfg<TI>::NG, U = HopCfg<TI>::UNR;
-    constexpr bool PF = HopCfg<TI>::PF;
+    constexpr int V = Vec16<TI>::V, H = Vec16<TI>::H, NG = HopCfg<TI, NARROW>::NG, U = HopCfg<TI, NARROW>::UNR;
+    constexpr bool PF = HopCfg<TI, NARROW>::PF;
     constexpr int GB = 32 * 16;                          // byte distance between a lane's groups
     const int lane = threadIdx.x & 31;
     if (slot >= n_rows) return;
@@ -637,8 +644,8 @@ __device__ __forceinline__ void hop_row(int slot, int chunk, const int4* __restr
     }
 }
 
-template <class TI, class TO, bool FULL>
-__global__ void __launch_bounds__(kThreads, HopCfg<TI>::min_blocks) k_hop_fwd(const int4* __restrict__ rows,
+template <class TI, class TO, bool FULL, bool NARROW = false>
+__global__ void __launch_bounds__(kThreads, HopCfg<TI, NARROW>::min_blocks) k_hop_fwd(const int4* __restrict__ rows,
                                                                                const int2* __restrict__ pairs,
                                                                                const TI* __restrict__ hp,
                                                                                const float* __restrict__ rgain,
@@ -647,8 +654,8 @@ __global__ void __launch_bounds__(kThreads, HopCfg<TI>::min_blocks) k_hop_fwd(co
                                                                                const float* __restrict__ drive,
                                                                                TO* __restrict__ h, int n_rows, int ld) {
     pdl_enter();
-    hop_row<TI, TO, FULL>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, rows, pairs, hp, rgain, rthr, drow,
-                          drive, h, n_rows, ld);
+    hop_row<TI, TO, FULL, false, NARROW>(blockIdx.x * kWarps + (threadIdx.x >> 5), blockIdx.y, rows, pairs, hp, rgain,
+                                         rthr, drow, drive, h, n_rows, ld);
 }
 // the same forward hop for the firing survey (fired / sq: this hop's rows)
 template <class TI, class TO, bool FULL>
