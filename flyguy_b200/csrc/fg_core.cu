@@ -96,6 +96,7 @@ struct Core {
     int2 *d_pairs = nullptr, *d_tpairs = nullptr;
     int *d_gptr = nullptr, *d_gw = nullptr, *d_tpos = nullptr;   // d_tpos: pair -> transposed pair, or -1
     float* sd_part = nullptr;                            // weight-gradient partials [256-sample chunk][transposed pair]
+    float* plug_part = nullptr;                          // plug backward's per-split sums [live row][split][fan + 3]
     int* d_wlive = nullptr;                              // strengths a live edge can change, ascending (fg_grad_pack)
     int n_wlive = 0;
     long long off[8] = {0};                             // segment starts in the flat arrays (256-byte aligned)
@@ -569,6 +570,7 @@ void alloc_all(Core& c) {
         long long tmax = 1;
         for (auto& h : c.hop) tmax = std::max<long long>(tmax, h.T);
         c.sd_part = dalloc<float>(c, (size_t)tmax * ((B + 255) / 256));
+        c.plug_part = dalloc<float>(c, (size_t)std::max(1, c.n_plug_live) * kPlugSplits * (c.fan + 3));
         int reds = 0;
         for (auto& h : c.hop) reds = std::max(reds, h.n_reds);
         const size_t n_done = std::max<size_t>(1, (size_t)reds * ((B + 255) / 256));
@@ -877,21 +879,30 @@ void backward(Core& c, int B) {
     }
     // gz now holds gh0 (the sensory layer's incoming gradient)
     if (c.n_plug_live)
-    launch(c, K_PLUG_BWD, [&]() {
-        const dim3 g((c.n_plug_live + kWarps - 1) / kWarps);
-        if (c.fan == 8)
-            pdl(c, k_plug_bwd<8>, g, kThreads, 0, c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
-                                                    c.x, c.d_rgain, c.d_rthr, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
-                                                    c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
-        else if (c.fan == 16)
-            pdl(c, k_plug_bwd<16>, g, kThreads, 0, c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
-                                                     c.x, c.d_rgain, c.d_rthr, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
-                                                     c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
-        else
-            pdl(c, k_plug_bwd<0>, g, kThreads, 0, c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive, c.d_n0, c.d_in_col,
-                                                    c.x, c.d_rgain, c.d_rthr, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
-                                                    c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B);
-    });
+    {
+        // the batch split over up to 8 warps a row (2,048 samples or more each): a warp per live sensory row alone is
+        // few warps a SM; the splits' sums are added in order by k_plug_bwd_reduce
+        const int splits = std::max(1, std::min(kPlugSplits, B / 2048));
+        const int span = ((B + splits - 1) / splits + 127) / 128 * 128;
+        float* part = splits > 1 ? c.plug_part : nullptr;
+        launch(c, K_PLUG_BWD, [&]() {
+            const dim3 g((c.n_plug_live + kWarps - 1) / kWarps, splits);
+            auto go = [&](auto kern) {
+                pdl(c, kern, g, kThreads, 0, c.d_plug_live, c.d_gh0_valid, gz, (const float*)c.h0, c.drive, c.gdrive,
+                    c.d_n0, c.d_in_col, c.x, c.d_rgain, c.d_rthr, c.d_rsig, c.G + c.off[1], c.G + c.off[2],
+                    c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, B, B, part, span);
+            };
+            if (c.fan == 8) go(k_plug_bwd<8>);
+            else if (c.fan == 16) go(k_plug_bwd<16>);
+            else go(k_plug_bwd<0>);
+        });
+        if (part)
+            launch(c, K_PLUG_BWD, [&]() {
+                pdl(c, k_plug_bwd_reduce, blocks((long long)c.n_plug_live * (c.fan + 3)), 256, 0, (const float*)part,
+                    (const int*)c.d_plug_live, (const int*)c.d_n0, (const float*)c.d_rsig, c.G + c.off[1],
+                    c.G + c.off[2], c.G + c.off[3], c.G + c.off[4], c.n_plug_live, c.fan, splits);
+            });
+    }
 }
 
 // the gradient norm and the clipping scale into c.norm (device)

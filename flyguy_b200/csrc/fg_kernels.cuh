@@ -1174,6 +1174,7 @@ __global__ void k_neuron_reduce(const float* __restrict__ nsum, const int* __res
 // a fixed order and added to the gradients of gain, theta, in_b and in_w. Without a saved drive (a network with no
 // sensory re-drive keeps none) the pre-activation is recovered where it counts, h0 > 0: drive = (h0 + thr) / gain.
 constexpr int kPlugFan = 16;
+constexpr int kPlugSplits = 8;                   // most batch splits of the plug backward
 template <int FAN>
 __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ list, const int* __restrict__ gh_valid,
                                                        const float* __restrict__ gh0, const float* __restrict__ h0,
@@ -1183,11 +1184,15 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ l
                                                        const float* __restrict__ rthr,
                                                        const float* __restrict__ rsig, float* __restrict__ ggain,
                                                        float* __restrict__ gtheta, float* __restrict__ gin_w,
-                                                       float* __restrict__ gin_b, int n_list, int fan, int B, int ld) {
+                                                       float* __restrict__ gin_b, int n_list, int fan, int B, int ld,
+                                                       float* __restrict__ part, int span) {
     pdl_enter();
     constexpr int F = FAN > 0 ? FAN : kPlugFan;
     const int i = blockIdx.x * kWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (i >= n_list) return;
+    // part: the batch is split over gridDim.y warps a row (span samples each, a multiple of 128), each writing its
+    // sums to part[(row * splits + split) * (fan + 3) ..] for k_plug_bwd_reduce to add in split order
+    const int b_lo = part ? blockIdx.y * span : 0, b_hi = part ? min(B, b_lo + span) : B;
     const int s = __ldg(&list[i]);
     const bool ghv = __ldg(&gh_valid[s]) != 0;      // rows the transposed hop did not write have gh0 = 0
     const float gn = __ldg(&rgain[s]), th = __ldg(&rthr[s]), inv_g = gn != 0.f ? 1.f / gn : 0.f;
@@ -1204,7 +1209,7 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ l
         for (int u = 0; u < F + 3; ++u) v[u] = 0.f;
         // (two steps' loads in flight: a warp per live row is few warps a SM, so each waits on memory latency)
 #pragma unroll 2
-        for (int b = lane * 4; b < B; b += 128) {
+        for (int b = b_lo + lane * 4; b < b_hi; b += 128) {
             const float4 gh = ghv ? __ldg(reinterpret_cast<const float4*>(gh0 + o + b)) : make_float4(0.f, 0.f, 0.f, 0.f);
             const float4 hh = __ldg(reinterpret_cast<const float4*>(h0 + o + b));
             const float4 gr = __ldg(reinterpret_cast<const float4*>(gdrive + o + b));
@@ -1230,7 +1235,13 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ l
         }
 #pragma unroll
         for (int u = 0; u < F + 3; ++u) v[u] = warp_sum(v[u]);
-        if (lane == 0) {
+        if (part) {
+            if (lane == 0) {
+                float* pp = part + ((size_t)i * gridDim.y + blockIdx.y) * (fan + 3);
+                for (int u = 0; u < nf; ++u) pp[f0 + u] = v[u];
+                if (first) { pp[fan] = v[F]; pp[fan + 1] = v[F + 1]; pp[fan + 2] = v[F + 2]; }
+            }
+        } else if (lane == 0) {
             if (first) {
                 const int id = __ldg(&n0[s]);
                 ggain[id] += v[F];
@@ -1241,6 +1252,26 @@ __global__ void __launch_bounds__(kThreads) k_plug_bwd(const int* __restrict__ l
         }
         if (fan == 0) break;
     }
+}
+
+// the plug backward's per-split sums added in split order: a thread per (listed row, column of the row's fan + 3
+// sums) - in_w of each plug column, then gain, theta and in_b
+__global__ void __launch_bounds__(256) k_plug_bwd_reduce(const float* __restrict__ part, const int* __restrict__ list,
+                                                         const int* __restrict__ n0, const float* __restrict__ rsig,
+                                                         float* __restrict__ ggain, float* __restrict__ gtheta,
+                                                         float* __restrict__ gin_w, float* __restrict__ gin_b,
+                                                         int n_list, int fan, int splits) {
+    pdl_enter();
+    const int k = blockIdx.x * blockDim.x + threadIdx.x, w = fan + 3;
+    if (k >= n_list * w) return;
+    const int i = k / w, col = k - i * w;
+    float v = 0.f;
+    for (int sp = 0; sp < splits; ++sp) v += part[((size_t)i * splits + sp) * w + col];
+    const int s = __ldg(&list[i]);
+    if (col < fan) gin_w[(size_t)s * fan + col] += v;
+    else if (col == fan) ggain[__ldg(&n0[s])] += v;
+    else if (col == fan + 1) gtheta[__ldg(&n0[s])] += -v * __ldg(&rsig[s]);
+    else gin_b[s] += v;
 }
 
 // ---------------------------------------------------------------- optimiser
