@@ -47,7 +47,7 @@ struct Hop {
     int *d_live_dst = nullptr, n_live_dst = 0;   // rows of this hop's layer whose gradient can be non-zero
     long long live_pairs = 0, live_edges = 0;    // merged pairs / edges of those rows (what the weight gradient visits)
     int *d_live_src = nullptr, n_live_src = 0;   // rows of the layer below that this hop's backward writes
-    bool narrow = false;                         // fp32 forward in the narrow configuration (no hub sources)
+    bool narrow = false;                         // no hub sources: narrow fp32 forward, longer transposed segments
     int2* d_sde = nullptr;                       // live edges {edge, transposed pair} in transposed-pair order
     int n_sde = 0;
     std::vector<int2> h_sde;                     // (host copy, until the packed-gradient list is built)
@@ -58,7 +58,10 @@ struct Hop {
     bool out_f32 = false;                    // this hop's layer is stored in fp32 (the last layer always is)
 };
 
-constexpr int kSegLen = 64;                  // pairs per transposed segment (short: hub CTAs retire fast)
+// pairs per transposed segment: short on a hop with hub sources (their long rows' CTAs retire fast), longer on a hop
+// without (fewer split rows and partial rows: model.pt training 37.2 -> 35.5 ms with 128; with 128 everywhere the Zipf
+// graph at batch 2,048 went 0.797 -> 0.822 ms, so hub hops keep 64)
+constexpr int kSegLen = 64, kSegLenNarrow = 128;
 
 // kernel classes timed by fg_timing (CUDA events around every launch of the class, on the handle's stream)
 enum KClass { K_TRANSPOSE, K_FOLD, K_PLUG_FWD, K_HOP_FWD, K_OUT_FWD, K_LOSS, K_OUT_BWD, K_ACT_BWD, K_WGRAD, K_HOP_BWD,
@@ -269,7 +272,8 @@ void build_hop_plan(Core& c, Hop& h, const std::vector<int>& crow, const std::ve
 // (the descending rows of the last layer start it): rows of the synthetic graph that no later row reads from get an
 // exactly zero gradient, so the backward skips them - no transposed pairs into them, no weight gradients from them,
 // nothing written for them (the reference skips zero gradients at run time, warp by warp). Then per hop: the
-// transposed pairs into live rows, by source and destination, cut into segments of at most kSegLen pairs.
+// transposed pairs into live rows, by source and destination, cut into segments of at most kSegLen pairs
+// (kSegLenNarrow on a hop without hub sources).
 void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, const std::vector<int>& dn,
                           const std::vector<int>& gptr, long long n_edges, std::vector<int2>& tpairs,
                           std::vector<int>& tpi) {
@@ -343,17 +347,18 @@ void build_backward_plans(Core& c, const std::vector<std::vector<int>>& drows, c
         }
         std::vector<int4> segs, reds;
         std::vector<int> seg_red;
+        const int seg_len = h.narrow ? kSegLenNarrow : kSegLen;
         for (int s : ls) {
             const int n = tptr[s + 1] - tptr[s];
-            if (n <= kSegLen) {
+            if (n <= seg_len) {
                 segs.push_back(make_int4(s, tptr[s], tptr[s + 1], -1));
                 seg_red.push_back(-1);
                 continue;
             }
-            const int nseg = (n + kSegLen - 1) / kSegLen;
+            const int nseg = (n + seg_len - 1) / seg_len;
             for (int i = 0; i < nseg; ++i) {
-                segs.push_back(make_int4(s, tptr[s] + i * kSegLen,
-                                         std::min(tptr[s + 1], tptr[s] + (i + 1) * kSegLen), h.n_slots + i));
+                segs.push_back(make_int4(s, tptr[s] + i * seg_len,
+                                         std::min(tptr[s + 1], tptr[s] + (i + 1) * seg_len), h.n_slots + i));
                 seg_red.push_back((int)reds.size());
             }
             reds.push_back(make_int4(s, h.n_slots, nseg, 0));
