@@ -59,9 +59,9 @@ struct Hop {
 };
 
 // pairs per transposed segment: short on a hop with hub sources (their long rows' CTAs retire fast), longer on a hop
-// without (fewer split rows and partial rows: model.pt training 37.2 -> 35.5 ms with 128; with 128 everywhere the Zipf
-// graph at batch 2,048 went 0.797 -> 0.822 ms, so hub hops keep 64)
-constexpr int kSegLen = 64, kSegLenNarrow = 128;
+// without (fewer split rows and partial rows: model.pt training 37.2 -> 35.5 -> 35.1 -> 34.9 ms with 128 / 256 / 512;
+// with 128 everywhere the Zipf graph at batch 2,048 went 0.797 -> 0.822 ms, so hub hops keep 64)
+constexpr int kSegLen = 64, kSegLenNarrow = 256;
 
 // kernel classes timed by fg_timing (CUDA events around every launch of the class, on the handle's stream)
 enum KClass { K_TRANSPOSE, K_FOLD, K_PLUG_FWD, K_HOP_FWD, K_OUT_FWD, K_LOSS, K_OUT_BWD, K_ACT_BWD, K_WGRAD, K_HOP_BWD,
